@@ -1,0 +1,402 @@
+// Public entry points of libflash_engine_b200.so: the extern "C" ABI declared in
+// include/flash_engine_c.h and the C++ launchers declared in include/*.cuh with
+// the reference's namespaces and signatures. Argument validation happens here;
+// the kernels live in paged_decode.cu, attention_fp32.cu and prefill_sm100.cu.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <limits.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "../../include/flash_engine.h"
+#include "fp32_kernels.h"
+#include "internal.h"
+#include "paged_decode.h"
+#include "prefill.h"
+#include "ptx.cuh"
+
+namespace {
+
+inline float resolve_scale(float s, int d) { return s > 0.f ? s : 1.0f / sqrtf(static_cast<float>(d)); }
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+constexpr int kMaxSeqsPerLaunch = 4096;
+constexpr int kErr = static_cast<int>(cudaErrorInvalidValue);
+
+bool dense_args_ok(int B, int H, int N, int M, int d) {
+  return B >= 0 && H >= 0 && N >= 0 && M >= 1 && d >= 1;
+}
+
+struct PagedArgs {
+  const void* q;
+  const void* kc;
+  const void* vc;
+  void* out;
+  const int* bt;
+  const int* lens;
+  int S, H, Hkv, d, bs, max_ctx, maxb, num_blocks;
+  float scale;
+};
+
+int paged_check(const PagedArgs& a, bool tensor_core) {
+  if (a.S < 0 || a.H <= 0 || a.Hkv <= 0 || a.H % a.Hkv != 0 || a.d <= 0 || a.bs <= 0 ||
+      a.maxb < 0)
+    return kErr;
+  if (tensor_core) {
+    if (!(a.d == 64 || a.d == 128) || !(a.bs == 16 || a.bs == 32)) return kErr;
+    if (!aligned(a.kc, 16) || !aligned(a.vc, 16) || !aligned(a.q, 4) || !aligned(a.out, 2))
+      return kErr;
+    if (a.num_blocks > 0 &&
+        static_cast<long long>(a.num_blocks) * a.Hkv * a.bs > static_cast<long long>(INT_MAX))
+      return kErr;
+  } else {
+    if (a.d > 256 || a.d % 4 != 0) return kErr;
+  }
+  return 0;
+}
+
+// Runs the tensor-core decode over all sequences, in chunks of kMaxSeqsPerLaunch.
+// part_o/part_ml may be null when every sequence is a single split.
+template <typename T>
+int paged_tc_run(const PagedArgs& a, int tok_begin, int tok_end, int pps, int max_splits,
+                 int direct_final, float* part_o, float* part_ml, cudaStream_t st) {
+  const int G = a.H / a.Hkv;
+  const int nt = G <= 8 ? 1 : 2;
+  const int head_chunks = (G + 8 * nt - 1) / (8 * nt);
+  const long long kv_rows = a.num_blocks > 0
+                                ? static_cast<long long>(a.num_blocks) * a.Hkv * a.bs
+                                : static_cast<long long>(INT_MAX);
+  for (int s0 = 0; s0 < a.S; s0 += kMaxSeqsPerLaunch) {
+    const int n = a.S - s0 < kMaxSeqsPerLaunch ? a.S - s0 : kMaxSeqsPerLaunch;
+    fe::paged::Params p{};
+    p.q = static_cast<const T*>(a.q) + static_cast<size_t>(s0) * a.H * a.d;
+    p.out = a.out ? static_cast<T*>(a.out) + static_cast<size_t>(s0) * a.H * a.d : nullptr;
+    p.block_tables = a.bt + static_cast<size_t>(s0) * a.maxb;
+    p.context_lens = a.lens + s0;
+    p.part_o = part_o ? part_o + static_cast<size_t>(s0) * a.H * max_splits * a.d : nullptr;
+    p.part_ml = part_ml ? part_ml + static_cast<size_t>(s0) * a.H * max_splits * 2 : nullptr;
+    p.num_seqs = n;
+    p.num_heads = a.H;
+    p.num_kv_heads = a.Hkv;
+    p.max_blocks_per_seq = a.maxb;
+    p.num_phys_blocks = a.num_blocks;
+    p.head_chunks = head_chunks;
+    p.tok_begin = tok_begin;
+    p.tok_end = tok_end;
+    p.pages_per_split = pps;
+    p.max_splits = max_splits;
+    p.direct_final = direct_final;
+    p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;
+    p.err = fe::device_error_word();
+    if (!p.err) return static_cast<int>(cudaErrorInitializationError);
+    cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, st);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return 0;
+}
+
+int default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
+  (void)d;
+  (void)H;
+  const int max_pages = max_ctx > 0 ? (max_ctx + bs - 1) / bs : 1;
+  const long long units = static_cast<long long>(S > 0 ? S : 1) * Hkv;
+  // ~8 units of work per SM slot (2 resident CTAs per SM), pages of >= 16.
+  const long long target = 16LL * fe::sm_count();
+  long long splits = (target + units - 1) / units;
+  const long long max_by_pages = (max_pages + 15) / 16;
+  if (splits > max_by_pages) splits = max_by_pages;
+  if (splits < 1) splits = 1;
+  if (splits > 256) splits = 256;
+  return static_cast<int>(splits);
+}
+
+template <typename T>
+int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
+  const int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (a.S == 0) return 0;
+  // One split per sequence whatever its length: every unit writes its final row.
+  return paged_tc_run<T>(a, 0, INT_MAX, INT_MAX / 2, 1, 1, nullptr, nullptr, st);
+}
+
+template <typename T>
+int paged_v2_tc(const PagedArgs& a, float* sout, float* sstats, int splits, cudaStream_t st) {
+  const int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (splits < 1 || !sout || !sstats) return kErr;
+  if (a.S == 0) return 0;
+  const int max_pages = a.max_ctx > 0 ? (a.max_ctx + a.bs - 1) / a.bs : 1;
+  const int pps = fe::paged::pages_per_split_for(max_pages, splits);
+  int e = paged_tc_run<T>(a, 0, INT_MAX, pps, splits, 1, sout, sstats, st);
+  if (e) return e;
+  fe::paged::MergeParams mp{};
+  mp.part_out = sout;
+  mp.part_stats = sstats;
+  mp.rows = a.S * a.H;
+  mp.ranks = 1;
+  mp.parts_per_rank = splits;
+  mp.context_lens = a.lens;
+  mp.heads = a.H;
+  mp.tok_begin = 0;
+  mp.tok_end = INT_MAX;
+  mp.block_size = a.bs;
+  mp.pages_per_split = pps;
+  mp.skip_single = 1;
+  mp.out = a.out;
+  mp.out_stats = nullptr;
+  mp.out_dtype = std::is_same<T, __nv_bfloat16>::value ? 1 : 3;
+  return static_cast<int>(fe::paged::launch_merge(mp, a.d, st));
+}
+
+}  // namespace
+
+// =========================================================================
+// extern "C"
+extern "C" {
+
+int fe_flash_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
+                                    int B, int H, int N, int M, int d, int causal, float scale,
+                                    void* stream) {
+  if (!dense_args_ok(B, H, N, M, d) || d > 128) return kErr;
+  if (B * H == 0 || N == 0) return 0;
+  return static_cast<int>(fe::simt::launch_fa2_fp32(q, k, v, o, B, H, N, M, d,
+                                                    resolve_scale(scale, d), causal,
+                                                    as_stream(stream)));
+}
+
+int fe_naive_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
+                                    int B, int H, int N, int M, int d, int causal, float scale,
+                                    void* stream) {
+  if (!dense_args_ok(B, H, N, M, d) || d > 256) return kErr;
+  if (B * H == 0 || N == 0) return 0;
+  return static_cast<int>(fe::simt::launch_naive_fp32(q, k, v, o, B, H, N, M, d,
+                                                      resolve_scale(scale, d), causal,
+                                                      as_stream(stream)));
+}
+
+int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v, void* o, int B,
+                                    int H, int N, int M, int d, int causal, float scale,
+                                    void* stream) {
+  if (!dense_args_ok(B, H, N, M, d)) return kErr;
+  if (B * H == 0 || N == 0) return 0;
+  return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
+                                                      resolve_scale(scale, d), true,
+                                                      as_stream(stream)));
+}
+
+int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v, void* o, int B,
+                                    int H, int N, int M, int d, int causal, float scale,
+                                    void* stream) {
+  if (!dense_args_ok(B, H, N, M, d)) return kErr;
+  if (B * H == 0 || N == 0) return 0;
+  return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
+                                                      resolve_scale(scale, d), false,
+                                                      as_stream(stream)));
+}
+
+int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc, float* out,
+                               const int* bt, const int* lens, int S, int H, int Hkv, int d,
+                               int bs, int max_ctx, int maxb, int num_blocks, float scale,
+                               void* stream) {
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  const int rc = paged_check(a, false);
+  if (rc) return rc;
+  if (S == 0) return 0;
+  return static_cast<int>(fe::simt::launch_paged_fp32(q, kc, vc, out, bt, lens, S, H, Hkv, d, bs,
+                                                      maxb, num_blocks, resolve_scale(scale, d),
+                                                      as_stream(stream)));
+}
+
+int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, void* out,
+                               const int* bt, const int* lens, int S, int H, int Hkv, int d,
+                               int bs, int max_ctx, int maxb, int num_blocks, float scale,
+                               void* stream) {
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  return paged_v1_tc<half>(a, as_stream(stream));
+}
+
+int fe_paged_attention_v1_bf16(const void* q, const void* kc, const void* vc, void* out,
+                               const int* bt, const int* lens, int S, int H, int Hkv, int d,
+                               int bs, int max_ctx, int maxb, int num_blocks, float scale,
+                               void* stream) {
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  return paged_v1_tc<__nv_bfloat16>(a, as_stream(stream));
+}
+
+int fe_paged_attention_v2_bf16(const void* q, const void* kc, const void* vc, void* out,
+                               const int* bt, const int* lens, int S, int H, int Hkv, int d,
+                               int bs, int max_ctx, int maxb, int num_blocks, float scale,
+                               float* sout, float* sstats, int splits, void* stream) {
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  return paged_v2_tc<__nv_bfloat16>(a, sout, sstats, splits, as_stream(stream));
+}
+
+int fe_paged_attention_v2_default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
+  if (H <= 0 || Hkv <= 0 || bs <= 0) return 1;
+  return default_splits(S, H, Hkv, d, bs, max_ctx);
+}
+
+int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* v, float* out,
+                                   float* sout, float* sstats, int B, int H, int M, int d,
+                                   int splits, float scale, void* stream) {
+  if (B < 0 || H < 0 || M < 1 || d < 1 || d > 256 || d % 4 != 0 || splits < 1) return kErr;
+  if (B * H == 0) return 0;
+  cudaStream_t st = as_stream(stream);
+  cudaError_t e = fe::simt::launch_decode_split_fp32(q, k, v, sout, sstats, B * H, M, d, splits,
+                                                     resolve_scale(scale, d), st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  fe::paged::MergeParams mp{};
+  mp.part_out = sout;
+  mp.part_stats = sstats;
+  mp.rows = B * H;
+  mp.ranks = 1;
+  mp.parts_per_rank = splits;
+  mp.out = out;
+  mp.out_dtype = 0;
+  return static_cast<int>(fe::paged::launch_merge(mp, d, st));
+}
+
+int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc, const int* bt,
+                                  const int* lens, int S, int H, int Hkv, int d, int bs, int maxb,
+                                  int num_blocks, float scale, int tb, int te, int splits,
+                                  float* sout, float* sstats, float* mout, float* mstats,
+                                  void* stream) {
+  PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
+  int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (splits < 1 || tb < 0 || te < tb || !sout || !sstats || !mout || !mstats || tb % bs != 0)
+    return kErr;
+  if (S == 0) return 0;
+  const int range_pages = (te - tb + bs - 1) / bs;
+  const int pps = fe::paged::pages_per_split_for(range_pages > 0 ? range_pages : 1, splits);
+  cudaStream_t st = as_stream(stream);
+  rc = paged_tc_run<__nv_bfloat16>(a, tb, te, pps, splits, 0, sout, sstats, st);
+  if (rc) return rc;
+  fe::paged::MergeParams mp{};
+  mp.part_out = sout;
+  mp.part_stats = sstats;
+  mp.rows = S * H;
+  mp.ranks = 1;
+  mp.parts_per_rank = splits;
+  mp.context_lens = lens;
+  mp.heads = H;
+  mp.tok_begin = tb;
+  mp.tok_end = te;
+  mp.block_size = bs;
+  mp.pages_per_split = pps;
+  mp.skip_single = 0;
+  mp.out = mout;
+  mp.out_stats = mstats;
+  mp.out_dtype = 2;
+  return static_cast<int>(fe::paged::launch_merge(mp, d, st));
+}
+
+int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,
+                      int parts_per_rank, int d, void* out, float* out_stats, int out_dtype,
+                      void* stream) {
+  if (rows < 0 || ranks < 1 || parts_per_rank < 1 || d < 1 || d > 256 || out_dtype < 0 ||
+      out_dtype > 3 || (out_dtype == 2 && !out_stats))
+    return kErr;
+  fe::paged::MergeParams mp{};
+  mp.part_out = part_out;
+  mp.part_stats = part_stats;
+  mp.rows = rows;
+  mp.ranks = ranks;
+  mp.parts_per_rank = parts_per_rank;
+  mp.out = out;
+  mp.out_stats = out_stats;
+  mp.out_dtype = out_dtype;
+  return static_cast<int>(fe::paged::launch_merge(mp, d, as_stream(stream)));
+}
+
+}  // extern "C"
+
+// =========================================================================
+// C++ API with the reference's namespaces and signatures.
+namespace flash_engine {
+
+void print_device_info(int device_id) { fe_print_device_info(device_id); }
+
+namespace attention {
+
+cudaError_t launch_flash_attention_forward_fp32(const float* q, const float* k, const float* v,
+                                                float* o, const AttentionConfig& c,
+                                                cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_flash_attention_forward_fp32(
+      q, k, v, o, c.batch_size, c.num_heads, c.seq_len_q, c.seq_len_kv, c.head_dim, c.is_causal,
+      c.softmax_scale, s));
+}
+cudaError_t launch_flash_attention_forward_fp16(const half* q, const half* k, const half* v,
+                                                half* o, const AttentionConfig& c,
+                                                cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_flash_attention_forward_fp16(
+      q, k, v, o, c.batch_size, c.num_heads, c.seq_len_q, c.seq_len_kv, c.head_dim, c.is_causal,
+      c.softmax_scale, s));
+}
+cudaError_t launch_flash_attention_forward_bf16(const __nv_bfloat16* q, const __nv_bfloat16* k,
+                                                const __nv_bfloat16* v, __nv_bfloat16* o,
+                                                const AttentionConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_flash_attention_forward_bf16(
+      q, k, v, o, c.batch_size, c.num_heads, c.seq_len_q, c.seq_len_kv, c.head_dim, c.is_causal,
+      c.softmax_scale, s));
+}
+cudaError_t launch_naive_attention_forward_fp32(const float* q, const float* k, const float* v,
+                                                float* o, const AttentionConfig& c,
+                                                cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_naive_attention_forward_fp32(
+      q, k, v, o, c.batch_size, c.num_heads, c.seq_len_q, c.seq_len_kv, c.head_dim, c.is_causal,
+      c.softmax_scale, s));
+}
+
+}  // namespace attention
+
+namespace paged_attention {
+
+cudaError_t launch_paged_attention_v1_fp16(const half* q, const half* kc, const half* vc,
+                                           half* out, const int* bt, const int* lens,
+                                           const PagedAttentionConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_paged_attention_v1_fp16(
+      q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
+      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, s));
+}
+cudaError_t launch_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc,
+                                           float* out, const int* bt, const int* lens,
+                                           const PagedAttentionConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_paged_attention_v1_fp32(
+      q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
+      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, s));
+}
+cudaError_t launch_paged_attention_v1_bf16(const __nv_bfloat16* q, const __nv_bfloat16* kc,
+                                           const __nv_bfloat16* vc, __nv_bfloat16* out,
+                                           const int* bt, const int* lens,
+                                           const PagedAttentionConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_paged_attention_v1_bf16(
+      q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
+      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, s));
+}
+cudaError_t launch_paged_attention_v2_bf16(const __nv_bfloat16* q, const __nv_bfloat16* kc,
+                                           const __nv_bfloat16* vc, __nv_bfloat16* out,
+                                           const int* bt, const int* lens,
+                                           const PagedAttentionConfig& c, float* sout,
+                                           float* sstats, int splits, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_paged_attention_v2_bf16(
+      q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
+      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, sout, sstats, splits, s));
+}
+
+}  // namespace paged_attention
+
+namespace decoding {
+
+cudaError_t launch_flash_decoding_forward_fp32(const float* q, const float* k, const float* v,
+                                               float* out, float* sout, float* sstats,
+                                               const FlashDecodingConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_flash_decoding_forward_fp32(
+      q, k, v, out, sout, sstats, c.batch_size, c.num_heads, c.seq_len_kv, c.head_dim,
+      c.num_splits, c.scale, s));
+}
+
+}  // namespace decoding
+}  // namespace flash_engine

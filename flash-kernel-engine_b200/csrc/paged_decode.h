@@ -1,0 +1,59 @@
+// Internal interface of the tensor-core paged decode kernels (paged_decode.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace fe {
+namespace paged {
+
+struct Params {
+  const void* q;           // [S, H, D] (T)
+  void* out;               // [S, H, D] (T), written for single-split sequences
+  const int* block_tables; // [S, max_blocks_per_seq]
+  const int* context_lens; // [S]
+  float* part_o;           // [S, H, max_splits, D] fp32 partial O (unnormalised)
+  float* part_ml;          // [S, H, max_splits, 2] (m in log2 units, l)
+  int num_seqs, num_heads, num_kv_heads, max_blocks_per_seq;
+  int num_phys_blocks;     // 0 = unknown (no range check)
+  int head_chunks;         // ceil(G / (8 * NT))
+  int tok_begin, tok_end;  // token window [tok_begin, tok_end) of every sequence
+  int pages_per_split;
+  int max_splits;          // partial slots per (seq, head)
+  int direct_final;        // 1: sequences with one split write `out` directly
+  float scale_log2;        // softmax scale * log2(e)
+  unsigned* err;           // device error word
+};
+
+struct MergeParams {
+  const float* part_out;
+  const float* part_stats;
+  int rows;
+  int ranks;
+  int parts_per_rank;      // slot stride per (rank, row)
+  // ctx mode (context_lens != nullptr): number of valid slots from the split rule
+  const int* context_lens;
+  int heads;
+  int tok_begin, tok_end, block_size, pages_per_split;
+  int skip_single;         // rows with <= 1 split were finalised by the decode kernel
+  void* out;
+  float* out_stats;
+  int out_dtype;           // 0 f32 final, 1 bf16 final, 2 merged partial, 3 fp16 final
+  int head_dim;            // set by launch_merge
+};
+
+// Splits of the page range [0, pages) into `splits` pieces of pages_per_split.
+inline int pages_per_split_for(int max_pages, int splits) {
+  if (splits < 1) splits = 1;
+  return (max_pages + splits - 1) / splits;
+}
+
+template <typename T>
+cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* k_cache,
+                          const void* v_cache, long long kv_rows, int nt, cudaStream_t stream);
+
+cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
+
+}  // namespace paged
+}  // namespace fe

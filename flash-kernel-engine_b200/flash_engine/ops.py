@@ -1,0 +1,263 @@
+"""Inference-attention operators over CUDA tensors -- the B200 counterpart of the
+reference's ``python/flash_engine/ops.py:15-143``.
+
+Same function names, argument order and meaning as the reference:
+
+* ``flash_attention(q, k, v, is_causal=False, scale=None)``       (ops.py:15-57)
+* ``paged_attention(query, key_cache, value_cache, block_tables,
+  context_lens, block_size=16, scale=None)``                       (ops.py:59-101)
+* ``flash_decoding(query, key, value, num_splits=4, scale=None)`` (ops.py:103-143)
+
+Differences, all deliberate:
+
+* Inputs must be CUDA tensors; there is no NumPy/torch fallback (the reference's
+  CPU code is the test oracle under ``oracle/``). Non-CUDA inputs raise TypeError.
+* ``paged_attention`` supports GQA (num_heads a multiple of num_kv_heads, query
+  head h reading KV head h // (H / Hkv), as src/paged_attention.cu:33-35) and
+  bf16 / fp16 / fp32 caches.
+* Every kernel runs on the current torch CUDA stream; tensors must be contiguous.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_lib_c = _lib.lib
+
+
+def _stream():
+    return ctypes_stream(torch.cuda.current_stream())
+
+
+def ctypes_stream(s) -> int:
+    return int(s.cuda_stream)
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return int(t.data_ptr())
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise TypeError("flash_engine operators take CUDA tensors; the CPU reference "
+                            "implementation is test infrastructure, not a fallback")
+        if not t.is_contiguous():
+            raise ValueError("tensors must be contiguous")
+
+
+def _scale_arg(scale, d):
+    return float(scale) if scale is not None else 1.0 / math.sqrt(d)
+
+
+# --------------------------------------------------------------------------- prefill
+def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None):
+    """FA2 forward: softmax(q k^T * scale [+ top-left causal mask]) v.
+
+    q: [B, H, N, d]; k, v: [B, H, M, d]; dtype float32, bfloat16 or float16.
+    """
+    _require_cuda(q, k, v)
+    B, H, N, d = q.shape
+    M = k.shape[2]
+    if k.shape != (B, H, M, d) or v.shape != k.shape:
+        raise ValueError("k and v must be [B, H, M, d] matching q")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    out = torch.empty_like(q)
+    fn = {torch.float32: _lib_c.fe_flash_attention_forward_fp32,
+          torch.bfloat16: _lib_c.fe_flash_attention_forward_bf16,
+          torch.float16: _lib_c.fe_flash_attention_forward_fp16}.get(q.dtype)
+    if fn is None:
+        raise TypeError(f"unsupported dtype {q.dtype}")
+    with torch.cuda.device(q.device):
+        _lib.check(fn(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
+                      _scale_arg(scale, d), _stream()), "flash_attention")
+    return out
+
+
+def naive_attention(q, k, v, is_causal: bool = False, scale: float | None = None):
+    """Row-per-thread fp32 attention (the reference's naive baseline kernel)."""
+    _require_cuda(q, k, v)
+    if q.dtype != torch.float32:
+        raise TypeError("naive_attention is fp32 only")
+    B, H, N, d = q.shape
+    M = k.shape[2]
+    out = torch.empty_like(q)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib_c.fe_naive_attention_forward_fp32(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
+            _scale_arg(scale, d), _stream()), "naive_attention")
+    return out
+
+
+# --------------------------------------------------------------------------- paged
+def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, block_size):
+    S, H, d = query.shape
+    nb, Hkv, bs, d2 = key_cache.shape
+    if bs != block_size or d2 != d or value_cache.shape != key_cache.shape:
+        raise ValueError("cache must be [num_blocks, Hkv, block_size, d] matching query")
+    if H % Hkv:
+        raise ValueError("num_heads must be a multiple of num_kv_heads")
+    if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
+        raise TypeError("block_tables and context_lens must be int32")
+    if block_tables.dim() != 2 or block_tables.shape[0] != S or context_lens.shape != (S,):
+        raise ValueError("block_tables [S, max_blocks] and context_lens [S] expected")
+    return S, H, Hkv, d, nb, block_tables.shape[1]
+
+
+def paged_attention_splits(num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                           max_context_len) -> int:
+    """Default split count of the split-KV (v2) bf16 kernel."""
+    return int(_lib_c.fe_paged_attention_v2_default_splits(
+        num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_context_len))
+
+
+def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
+                    block_size: int = 16, scale: float | None = None, *,
+                    max_context_len: int | None = None, num_splits: int | None = None,
+                    out=None, workspace=None, version: str = "auto"):
+    """Paged-KV decode attention (one query token per sequence).
+
+    query [S, H, d]; key_cache/value_cache [num_blocks, Hkv, block_size, d];
+    block_tables [S, max_blocks] int32; context_lens [S] int32. Returns [S, H, d].
+
+    ``max_context_len`` sizes the split-KV work split (default: max_blocks *
+    block_size, which needs no device sync); ``version`` "v1" forces the
+    single-pass kernel, "v2" the split-KV kernel with scratch (bf16 only).
+    ``workspace`` optionally passes a preallocated (scratch_out, scratch_stats)
+    pair sized [S*H*splits*d] and [S*H*splits*2] float32.
+    """
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
+    S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
+                                           context_lens, block_size)
+    if out is None:
+        out = torch.empty_like(query)
+    sc = _scale_arg(scale, d)
+    if max_context_len is None:
+        max_context_len = maxb * block_size
+    args_head = (_ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out),
+                 _ptr(block_tables), _ptr(context_lens), S, H, Hkv, d, block_size,
+                 int(max_context_len), maxb, nb, sc)
+    with torch.cuda.device(query.device):
+        if query.dtype == torch.float32:
+            _lib.check(_lib_c.fe_paged_attention_v1_fp32(*args_head, _stream()), "paged_attention")
+        elif query.dtype == torch.float16:
+            _lib.check(_lib_c.fe_paged_attention_v1_fp16(*args_head, _stream()), "paged_attention")
+        elif query.dtype == torch.bfloat16:
+            if version == "v1":
+                _lib.check(_lib_c.fe_paged_attention_v1_bf16(*args_head, _stream()),
+                           "paged_attention")
+            else:
+                splits = num_splits or paged_attention_splits(S, H, Hkv, d, block_size,
+                                                              int(max_context_len))
+                if workspace is None:
+                    so = torch.empty(max(1, S * H * splits * d), dtype=torch.float32,
+                                     device=query.device)
+                    ss = torch.empty(max(1, S * H * splits * 2), dtype=torch.float32,
+                                     device=query.device)
+                else:
+                    so, ss = workspace
+                    if so.numel() < S * H * splits * d or ss.numel() < S * H * splits * 2:
+                        raise ValueError("workspace too small for the split count")
+                _lib.check(_lib_c.fe_paged_attention_v2_bf16(*args_head, _ptr(so), _ptr(ss),
+                                                             splits, _stream()),
+                           "paged_attention")
+        else:
+            raise TypeError(f"unsupported dtype {query.dtype}")
+    return out
+
+
+def paged_decode_partials(query, key_cache, value_cache, block_tables, context_lens,
+                          token_begin: int, token_end: int, num_splits: int,
+                          block_size: int = 16, scale: float | None = None, workspace=None,
+                          out=None, out_stats=None):
+    """Partial attention of every (sequence, query head) over the token window
+    [token_begin, token_end) (bf16 cache; token_begin a multiple of block_size).
+
+    Returns (O [S, H, d] f32 unnormalised, stats [S, H, 2] f32 = (m log2, l)); an
+    empty window gives (0, (-inf, 0)). ``num_splits`` pieces of the window run in
+    parallel and are merged on the device; ``workspace`` optionally passes their
+    (scratch_out, scratch_stats) buffers [S*H*splits*d], [S*H*splits*2]."""
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
+    S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
+                                           context_lens, block_size)
+    dev = query.device
+    if workspace is None:
+        so = torch.empty(max(1, S * H * num_splits * d), dtype=torch.float32, device=dev)
+        ss = torch.empty(max(1, S * H * num_splits * 2), dtype=torch.float32, device=dev)
+    else:
+        so, ss = workspace
+    if out is None:
+        out = torch.empty((S, H, d), dtype=torch.float32, device=dev)
+    if out_stats is None:
+        out_stats = torch.empty((S, H, 2), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib_c.fe_paged_decode_partials_bf16(
+            _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+            _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
+            int(token_begin), int(token_end), int(num_splits), _ptr(so), _ptr(ss), _ptr(out),
+            _ptr(out_stats), _stream()), "paged_decode_partials")
+    return out, out_stats
+
+
+def merge_partials(part_out, part_stats, ranks: int, parts_per_rank: int, out_dtype: str = "bf16",
+                   out=None, out_stats=None):
+    """Log-sum-exp combine of partials laid out [ranks, rows, parts_per_rank, d]
+    (and [..., 2] stats). out_dtype: "fp32" | "bf16" | "fp16" (final output rows
+    [rows, d]) or "partial" (returns (O, stats) merged partials)."""
+    _require_cuda(part_out, part_stats)
+    d = part_out.shape[-1]
+    rows = part_out.numel() // (d * ranks * parts_per_rank)
+    code = {"fp32": 0, "bf16": 1, "partial": 2, "fp16": 3}[out_dtype]
+    dt = {0: torch.float32, 1: torch.bfloat16, 2: torch.float32, 3: torch.float16}[code]
+    if out is None:
+        out = torch.empty((rows, d), dtype=dt, device=part_out.device)
+    if code == 2 and out_stats is None:
+        out_stats = torch.empty((rows, 2), dtype=torch.float32, device=part_out.device)
+    with torch.cuda.device(part_out.device):
+        _lib.check(_lib_c.fe_merge_partials(
+            _ptr(part_out), _ptr(part_stats), rows, ranks, parts_per_rank, d, _ptr(out),
+            _ptr(out_stats) if out_stats is not None else None, code, _stream()),
+            "merge_partials")
+    return (out, out_stats) if code == 2 else out
+
+
+# --------------------------------------------------------------------------- decoding
+def flash_decoding(query, key, value, num_splits: int = 4, scale: float | None = None,
+                   scratch=None):
+    """Two-stage split-KV decoding over a dense cache (fp32).
+
+    query [B, H, 1, d]; key/value [B, H, M, d]. Returns [B, H, 1, d]. Split s
+    covers [s*ceil(M/S), min(M, (s+1)*ceil(M/S))) (ops.py:112-121).
+    """
+    _require_cuda(query, key, value)
+    B, H, one, d = query.shape
+    M = key.shape[2]
+    if one != 1 or key.shape != (B, H, M, d) or value.shape != key.shape:
+        raise ValueError("query [B,H,1,d] and key/value [B,H,M,d] expected")
+    if query.dtype != torch.float32:
+        raise TypeError("flash_decoding takes float32 tensors (as the reference's kernel)")
+    out = torch.empty_like(query)
+    if scratch is None:
+        so = torch.empty((B, H, num_splits, d), dtype=torch.float32, device=query.device)
+        ss = torch.empty((B, H, num_splits, 2), dtype=torch.float32, device=query.device)
+    else:
+        so, ss = scratch
+    with torch.cuda.device(query.device):
+        _lib.check(_lib_c.fe_flash_decoding_forward_fp32(
+            _ptr(query), _ptr(key), _ptr(value), _ptr(out), _ptr(so), _ptr(ss), B, H, M, d,
+            int(num_splits), _scale_arg(scale, d), _stream()), "flash_decoding")
+    return out
+
+
+def device_errors() -> int:
+    """Synchronise, then return and clear the device error word (0 = no error)."""
+    return _lib.device_errors()
+
+
+def get_version() -> str:
+    return _lib_c.fe_get_version().decode()

@@ -1,0 +1,186 @@
+/*
+ * flash_engine_c.h -- C ABI of the B200 (sm_100a) inference-attention library
+ * (libflash_engine_b200.so).
+ *
+ * Plain pointers, ints and floats only; no C++ or torch types. Every entry point
+ * is stream-ordered on `stream` (a cudaStream_t passed as void*, NULL = legacy
+ * default stream), never allocates, never frees and never synchronises. The
+ * caller owns every device buffer, exactly as with the reference's launchers.
+ *
+ * Return value: a cudaError_t as int. 0 = cudaSuccess; 1 = cudaErrorInvalidValue
+ * for arguments the kernels do not support (the reference silently mis-dispatches
+ * those: src/flash_attention.cu:339-342, src/flash_decoding.cu:244-262); any other
+ * value is the launch status from cudaGetLastError(), as the reference returns
+ * (src/flash_attention.cu:344).
+ *
+ * Layouts (row-major, contiguous):
+ *   dense attention  Q,O [B, H, N, d]; K,V [B, H, M, d]
+ *   paged decode     q,out [S, H, d]; k_cache,v_cache [num_blocks, Hkv, block_size, d];
+ *                    block_tables [S, max_blocks_per_seq] int32; context_lens [S] int32
+ *   split-KV scratch scratch_out [S, H, num_splits, d] f32; scratch_stats
+ *                    [S, H, num_splits, 2] f32 = (m, l) with m in log2 units of the
+ *                    scaled score, l = sum 2^(s*log2e - m)
+ *
+ * bf16 / fp16 buffers are passed as `const void*` (__nv_bfloat16 / half in C++).
+ */
+#ifndef FLASH_ENGINE_C_H_
+#define FLASH_ENGINE_C_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Version string, "1.2.0-b200". Replaces flash_engine::get_version()
+ * (include/flash_engine.h:24-26). */
+const char* fe_get_version(void);
+
+/* Prints device properties. Replaces flash_engine::print_device_info
+ * (include/flash_engine.h:29, src/flash_engine_api.cu:7-27). */
+int fe_print_device_info(int device_id);
+
+/* Reads and clears the library's device error word on the current device
+ * (bit 0: a bounded wait timed out; bit 1: a block-table entry was out of range;
+ * bit 2: tensor-memory allocation failed). Synchronises the device. The reference
+ * has no device-side checking; this is new. */
+int fe_get_device_errors(unsigned int* errors_out);
+
+/* ---------------------------------------------------------------- prefill
+ * FA2 online-softmax forward O = softmax(Q K^T * scale [+ causal mask]) V.
+ * Causal masking is top-left aligned (query row i sees keys j <= i), as
+ * src/flash_attention.cu:224 and python/flash_engine/ops.py:43-45.
+ * softmax_scale <= 0 selects 1/sqrt(d) (AttentionConfig, include/flash_attention.cuh:19-21).
+ */
+
+/* fp32. Replaces launch_flash_attention_forward_fp32 (include/flash_attention.cuh:60-67,
+ * src/flash_attention.cu:304-345). Any head_dim in 1..256 with head_dim % 4 == 0. */
+int fe_flash_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
+                                    int batch, int heads, int seq_q, int seq_kv, int head_dim,
+                                    int is_causal, float softmax_scale, void* stream);
+
+/* fp16 in/out, fp32 accumulate. Replaces launch_flash_attention_forward_fp16
+ * (include/flash_attention.cuh:69-76, src/flash_attention.cu:486-524). head_dim 64 or 128. */
+int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v, void* o,
+                                    int batch, int heads, int seq_q, int seq_kv, int head_dim,
+                                    int is_causal, float softmax_scale, void* stream);
+
+/* bf16 in/out, fp32 accumulate (tcgen05 / TMEM / TMA kernel). New sibling of the fp16
+ * entry with identical parameters. head_dim 64 or 128. */
+int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v, void* o,
+                                    int batch, int heads, int seq_q, int seq_kv, int head_dim,
+                                    int is_causal, float softmax_scale, void* stream);
+
+/* Row-per-thread fp32 attention. Replaces launch_naive_attention_forward_fp32
+ * (include/flash_attention.cuh:79-86, src/flash_attention.cu:86-104). */
+int fe_naive_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
+                                    int batch, int heads, int seq_q, int seq_kv, int head_dim,
+                                    int is_causal, float softmax_scale, void* stream);
+
+/* ---------------------------------------------------------------- paged decode
+ * out[s, h] = softmax(q[s, h] . K[s, h/(H/Hkv)]^T * scale) V[...] over context_lens[s]
+ * tokens; token t of sequence s is row t % block_size of physical block
+ * block_tables[s, t / block_size] (src/paged_attention.cu:54-84). A sequence
+ * with context_len <= 0 gets a zero output row (python/flash_engine/ops.py:74-78).
+ * num_blocks > 0 enables a device-side range check of every block-table entry
+ * (bad entries are skipped and flagged in the device error word); 0 = unknown.
+ * scale <= 0 selects 1/sqrt(head_dim).
+ */
+
+/* fp32 cache. Replaces launch_paged_attention_v1_fp32 (include/paged_attention.cuh:39-48,
+ * src/paged_attention.cu:181-215). Any block_size >= 1, head_dim % 4 == 0, <= 256. */
+int fe_paged_attention_v1_fp32(const float* q, const float* k_cache, const float* v_cache,
+                               float* out, const int* block_tables, const int* context_lens,
+                               int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                               int block_size, int max_context_len, int max_blocks_per_seq,
+                               int num_blocks, float scale, void* stream);
+
+/* fp16 cache in the same [num_blocks, Hkv, block_size, d] layout as the fp32 entry.
+ * Replaces the launch_paged_attention_v1_fp16 stub (include/paged_attention.cuh:27-36,
+ * src/paged_attention.cu:218-230, which launches nothing). block_size 16 or 32,
+ * head_dim 64 or 128. */
+int fe_paged_attention_v1_fp16(const void* q, const void* k_cache, const void* v_cache,
+                               void* out, const int* block_tables, const int* context_lens,
+                               int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                               int block_size, int max_context_len, int max_blocks_per_seq,
+                               int num_blocks, float scale, void* stream);
+
+/* bf16 cache, single pass, no scratch: one unit of work per (sequence, KV head),
+ * its pages spread over the CTA's consumer warps and merged in shared memory.
+ * New bf16 sibling of launch_paged_attention_v1_fp32. block_size 16 or 32,
+ * head_dim 64 or 128. */
+int fe_paged_attention_v1_bf16(const void* q, const void* k_cache, const void* v_cache,
+                               void* out, const int* block_tables, const int* context_lens,
+                               int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                               int block_size, int max_context_len, int max_blocks_per_seq,
+                               int num_blocks, float scale, void* stream);
+
+/* bf16 cache, split-KV with caller-owned scratch (the v2 form of vLLM's paged
+ * attention; the reference has only v1). num_splits >= 1 (see
+ * fe_paged_attention_v2_default_splits for a choice sized to the GPU); each
+ * sequence's pages are cut into pieces of ceil(ceil(max_context_len/block_size) /
+ * num_splits) pages and a sequence needing one piece is finalised directly.
+ * Scratch sizes: scratch_out
+ * num_seqs*num_heads*num_splits*head_dim floats, scratch_stats
+ * num_seqs*num_heads*num_splits*2 floats. */
+int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v_cache,
+                               void* out, const int* block_tables, const int* context_lens,
+                               int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                               int block_size, int max_context_len, int max_blocks_per_seq,
+                               int num_blocks, float scale, float* scratch_out,
+                               float* scratch_stats, int num_splits, void* stream);
+
+/* Split count fe_paged_attention_v2_bf16 uses when passed num_splits <= 0. */
+int fe_paged_attention_v2_default_splits(int num_seqs, int num_heads, int num_kv_heads,
+                                         int head_dim, int block_size, int max_context_len);
+
+/* ---------------------------------------------------------------- split-KV decoding
+ * Dense [B, H, M, d] fp32 flash decoding with caller-owned scratch. Replaces
+ * launch_flash_decoding_forward_fp32 (include/flash_decoding.cuh:22-31,
+ * src/flash_decoding.cu:225-263). Split s covers [s*ceil(M/S), min(M, (s+1)*ceil(M/S)))
+ * (src/flash_decoding.cu:29-32; python/flash_engine/ops.py:112-121). Any head_dim
+ * % 4 == 0 up to 256 (the reference launches nothing for d not in {64,128}). */
+int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* v, float* out,
+                                   float* scratch_out, float* scratch_stats, int batch, int heads,
+                                   int seq_kv, int head_dim, int num_splits, float scale,
+                                   void* stream);
+
+/* Paged, GQA split-KV partial over the logical token window [token_begin, token_end)
+ * of every sequence (clipped to its context length), bf16 cache: the window is cut
+ * into num_splits page-aligned pieces written to scratch_out / scratch_stats
+ * (layouts above), which are then merged into ONE partial per (sequence, query
+ * head): merged_out [S, H, d] f32 (unnormalised O) and merged_stats [S, H, 2]
+ * (m in log2 units, l); a sequence whose window is empty gets (0, -inf, 0).
+ * token_begin must be a multiple of block_size. Used for KV-range sharding across
+ * GPUs: each GPU runs its own window, the merged partials are all-gathered and
+ * fe_merge_partials combines them. New (the reference has no paged split-KV). */
+int fe_paged_decode_partials_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                  const int* block_tables, const int* context_lens, int num_seqs,
+                                  int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                  int max_blocks_per_seq, int num_blocks, float scale,
+                                  int token_begin, int token_end, int num_splits,
+                                  float* scratch_out, float* scratch_stats, float* merged_out,
+                                  float* merged_stats, void* stream);
+
+/* Log-sum-exp combine of partials -- the stage-2 reduction of
+ * src/flash_decoding.cu:151-223 / python/flash_engine/ops.py:133-143:
+ * g = max m_p; L = sum l_p 2^(m_p-g); O = sum O_p 2^(m_p-g) / L.
+ * The partials of output row `row` from rank r, split p live at index
+ * ((r * rows + row) * parts_per_rank + p) of part_out (times head_dim) and of
+ * part_stats (times 2): ranks = 1 is the plain [rows, P, ...] scratch of one
+ * launch; ranks > 1 is the [ranks, rows, P, ...] buffer an all-gather produces.
+ * Output:
+ *   out_dtype 0: fp32 final  [rows, d] in out
+ *   out_dtype 1: bf16 final  [rows, d] in out
+ *   out_dtype 2: merged partial, out = O (fp32, unnormalised) [rows, d] and
+ *                out_stats = (g, L) [rows, 2].
+ * Rows whose partials are all empty (l = 0) produce zeros (and (-inf, 0)). */
+int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,
+                      int parts_per_rank, int head_dim, void* out, float* out_stats,
+                      int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* FLASH_ENGINE_C_H_ */

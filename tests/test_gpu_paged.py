@@ -1,0 +1,133 @@
+"""Paged decode on the GPU (C-ABI through flash_engine.ops) against the CPU oracle
+and the reference-generated golden vectors."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_bf16_close, assert_fp32_close, cuda, host
+from oracle import attention_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(p, dtype, version="auto", bs=16, num_splits=None, num_blocks_check=True):
+    import flash_engine
+    q = cuda(p["q"], dtype)
+    kc = cuda(p["k_cache"], dtype)
+    vc = cuda(p["v_cache"], dtype)
+    bt = cuda(p["block_tables"])
+    lens = cuda(p["context_lens"])
+    out = flash_engine.paged_attention(q, kc, vc, bt, lens, bs, version=version,
+                                       num_splits=num_splits)
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    return host(out)
+
+
+def test_paged_fp32_reference_case(golden):
+    g = golden("paged_fp32")
+    out = _run({"q": g["q"], "k_cache": g["k_cache"], "v_cache": g["v_cache"],
+                "block_tables": g["block_tables"], "context_lens": g["context_lens"]},
+               torch.float32)
+    assert_fp32_close(out, g["out"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_paged_kat_constant_inputs(golden, dtype):
+    g = golden("paged_kat")
+    out = _run(g, dtype)
+    np.testing.assert_array_equal(out, np.full_like(out, 0.25))
+
+
+@pytest.mark.parametrize("version", ["v1", "v2"])
+def test_paged_bf16_golden_gqa(golden, version):
+    g = golden("paged_gqa_bf16")
+    out = _run(g, torch.bfloat16, version)
+    assert_bf16_close(out, g["out"])
+    assert np.all(out[3] == 0)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("bs", [16, 32])
+@pytest.mark.parametrize("H,Hkv", [(8, 8), (32, 8), (64, 8), (16, 1), (48, 2)])
+@pytest.mark.parametrize("version", ["v1", "v2"])
+def test_paged_bf16_random(d, bs, H, Hkv, version):
+    lens = [0, 1, bs - 1, bs, bs + 1, 3 * bs + 7, 300, 1000]
+    p = O.make_paged_problem(11 + d + bs + H, len(lens), H, Hkv, d, lens, block_size=bs,
+                             extra_blocks=5)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"], bs)
+    out = _run(p, torch.bfloat16, version, bs=bs, num_splits=3 if version == "v2" else None)
+    assert_bf16_close(out, ref)
+
+
+@pytest.mark.parametrize("H,Hkv", [(8, 8), (32, 8)])
+def test_paged_fp16_random(H, Hkv):
+    lens = [0, 17, 64, 555]
+    p = O.make_paged_problem(5, len(lens), H, Hkv, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    out = _run(p, torch.float16)
+    assert_bf16_close(out, ref, atol=5e-3)
+
+
+@pytest.mark.parametrize("H,Hkv,d", [(8, 2, 64), (32, 8, 128), (12, 4, 96)])
+def test_paged_fp32_random(H, Hkv, d):
+    lens = [0, 1, 16, 33, 300]
+    p = O.make_paged_problem(9, len(lens), H, Hkv, d, lens, bf16=False)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    out = _run(p, torch.float32)
+    assert_fp32_close(out, ref)
+
+
+@pytest.mark.parametrize("version", ["v1", "v2"])
+def test_block_table_gather_is_bit_exact(version):
+    """One-hot attention: token j of each sequence carries a key that dominates by
+    e^45, so the output row must equal V[token j] bit for bit. Checks the
+    (block table, block offset, KV head) address of every selected row."""
+    rng = np.random.default_rng(1)
+    S, H, Hkv, d, bs = 24, 32, 8, 128, 16
+    lens = rng.integers(1, 700, size=S).astype(np.int32)
+    p = O.make_paged_problem(2, S, H, Hkv, d, lens, extra_blocks=7)
+    kc = np.zeros_like(p["k_cache"])
+    q = np.zeros_like(p["q"])
+    q[:, :, 0] = 8.0
+    sel = np.array([rng.integers(0, c) for c in lens])
+    for s in range(S):
+        j = sel[s]
+        kc[p["block_tables"][s, j // bs], :, j % bs, 0] = 64.0
+    p2 = dict(p, q=q, k_cache=kc)
+    out = _run(p2, torch.bfloat16, version, num_splits=4 if version == "v2" else None)
+    for s in range(S):
+        j = sel[s]
+        vrow = p["v_cache"][p["block_tables"][s, j // bs], :, j % bs, :]  # [Hkv, d]
+        expect = np.repeat(vrow, H // Hkv, axis=0)
+        np.testing.assert_array_equal(out[s], expect)
+
+
+def test_bad_block_index_is_flagged_not_read():
+    import flash_engine
+    lens = [40, 40]
+    p = O.make_paged_problem(3, 2, 8, 2, 128, lens)
+    nb = p["k_cache"].shape[0]
+    bt = p["block_tables"].copy()
+    bt[1, 1] = nb + 1000  # outside the pool
+    q = cuda(p["q"], torch.bfloat16)
+    kc = cuda(p["k_cache"], torch.bfloat16)
+    vc = cuda(p["v_cache"], torch.bfloat16)
+    flash_engine.paged_attention(q, kc, vc, cuda(bt), cuda(p["context_lens"]), 16,
+                                 version="v1")
+    assert flash_engine.device_errors() & 2
+    assert flash_engine.device_errors() == 0  # cleared by the read
+
+
+def test_config3_shape_parity():
+    """BASELINE config 3 shape (B64, 32q/8kv, d128, ctx U[512,4096], bs 16), on a
+    seeded subset of 8 sequences for oracle speed, with the full split logic."""
+    lens = O.config3_context_lens(0)[:8]
+    p = O.make_paged_problem(0, 8, 32, 8, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    out = _run(p, torch.bfloat16)
+    assert_bf16_close(out, ref)
