@@ -72,7 +72,7 @@ def _traffic(name):
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML (read-only) every 20 ms."""
+    """Samples SM clock and throttle reasons through NVML (read-only) every 5 ms."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -104,7 +104,7 @@ class ClockSampler:
                 self.samples.append((time.perf_counter(), mhz, rs))
             except Exception:
                 pass
-            time.sleep(0.02)
+            time.sleep(0.005)
 
     def start(self):
         if self.ok:

@@ -92,6 +92,20 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   return v;
 }
 
+// Page gi of a CTA (its running page counter) belongs to consumer warp gi % NCW
+// and lives in that warp's own ring of DEPTH stages. Every stage therefore has a
+// single consumer that takes its pages in order, so a parity wait can never be
+// satisfied by an older phase of the same stage.
+template <int NCW, int DEPTH>
+struct StageOf {
+  int s, round;
+  __device__ __forceinline__ explicit StageOf(int gi) {
+    const int j = gi / NCW;
+    s = (j % DEPTH) * NCW + (gi - j * NCW);
+    round = j / DEPTH;
+  }
+};
+
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
 struct Cfg {
   static constexpr int HPC = 8 * NT;       // query heads per CTA
@@ -234,7 +248,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
           const int vd = __shfl_sync(0xffffffffu, valid, k);
           int good = 1;
           if (lane == 0) {
-            const int s = gi % NSTAGE, rnd = gi / NSTAGE;
+            const StageOf<NCW, NSTAGE / NCW> so(gi);
+            const int s = so.s, rnd = so.round;
             if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1)) {
               atomicOr(p.err, kErrWaitTimeout);
               good = 0;
@@ -245,6 +260,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
               if (vd) {
                 mbar_arrive_expect_tx(&full[s], STAGE);
                 const int y = (ph * Hkv + kvh) * BS;
+#ifdef FE_DEBUG_CHECKS
+                if (static_cast<long long>(y) + BS > p.dbg_kv_rows) atomicOr(p.err, 1u << 8);
+#endif
 #pragma unroll
                 for (int h = 0; h < HALVES; ++h) {
                   tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
@@ -267,7 +285,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     // Drain: no bulk copy of this CTA may still be in flight when it exits.
     if (lane == 0) {
       for (int j = max(0, gi - NSTAGE); j < gi; ++j) {
-        if (!mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1)) {
+        const StageOf<NCW, NSTAGE / NCW> so(j);
+        if (!mbar_wait(&full[so.s], so.round & 1)) {
           atomicOr(p.err, kErrWaitTimeout);
           break;
         }
@@ -331,8 +350,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     const int first = ((warp - gbase) % NCW + NCW) % NCW;
     for (int i = first; i < npg && ok; i += NCW) {
       const int gi = gbase + i;
-      const int s = gi % NSTAGE;
-      const bool waited = mbar_wait(&full[s], (gi / NSTAGE) & 1);
+      const StageOf<NCW, NSTAGE / NCW> so(gi);
+      const int s = so.s;
+      const bool waited = mbar_wait(&full[s], so.round & 1);
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
         ok = false;
@@ -464,6 +484,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         r0[8] = o[nt][mt][2];
         r0[CSTRIDE + 8] = o[nt][mt][3];
       }
+    __syncwarp();
     named_bar(1, NCW * 32);
 
     const int nsplit_seq =
@@ -487,6 +508,14 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         O += comb_o[(w * HPC + hl) * CSTRIDE + dim] * wt;
       }
       const size_t row = static_cast<size_t>(seq) * p.num_heads + kvh * G + gh;
+#ifdef FE_DEBUG_CHECKS
+      if (row >= static_cast<size_t>(p.num_seqs) * p.num_heads ||
+          (!final_out && (split < 0 || split >= p.max_splits || !p.part_o)) ||
+          (final_out && !p.out)) {
+        atomicOr(p.err, 1u << 9);
+        continue;
+      }
+#endif
       if (final_out) {
         reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(L > 0.f ? O / L : 0.f);
       } else {
@@ -498,6 +527,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         }
       }
     }
+    __syncwarp();
     named_bar(2, NCW * 32);
   }
 }
@@ -596,7 +626,10 @@ template <typename T, int D, int BS, int NT>
 static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, long long kv_rows,
                               cudaStream_t stream) {
   constexpr int NCW = 4;
-  constexpr int NSTAGE = (D == 128 && BS == 32) ? 5 : (D == 64 && BS == 16) ? 20 : 10;
+  // NCW consumer warps x DEPTH private stages each; ~64 KB of stages per CTA.
+  constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
+  constexpr int NSTAGE = NCW * DEPTH;
+  static_assert(NSTAGE % NCW == 0, "stages must split evenly over the consumer warps");
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
   auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE>;
   const int smem = C::smem_bytes(p.num_seqs);
@@ -613,7 +646,9 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
   const int grid = sm_count() * occ;
-  kern<<<grid, C::NTHREADS, smem, stream>>>(km, vm, p);
+  Params pp = p;
+  pp.dbg_kv_rows = kv_rows;
+  kern<<<grid, C::NTHREADS, smem, stream>>>(km, vm, pp);
   return cudaGetLastError();
 }
 

@@ -24,6 +24,7 @@ struct Params {
   int direct_final;        // 1: sequences with one split write `out` directly
   float scale_log2;        // softmax scale * log2(e)
   unsigned* err;           // device error word
+  long long dbg_kv_rows;   // rows of the K/V tensor maps (bounds checks in debug builds)
 };
 
 struct MergeParams {

@@ -11,7 +11,10 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libflash_engine_b200.so")
+# FLASH_ENGINE_LIB may point at another build of the same library (e.g. one
+# compiled with -DFE_DEBUG_CHECKS, which adds device-side bounds checks).
+LIB_PATH = os.environ.get("FLASH_ENGINE_LIB") or os.path.join(_HERE, "lib",
+                                                              "libflash_engine_b200.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
