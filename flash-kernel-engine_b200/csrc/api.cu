@@ -8,6 +8,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "../../include/flash_engine.h"
@@ -236,6 +237,51 @@ int fe_paged_attention_v2_bf16(const void* q, const void* kc, const void* vc, vo
 int fe_paged_attention_v2_default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
   if (H <= 0 || Hkv <= 0 || bs <= 0) return 1;
   return default_splits(S, H, Hkv, d, bs, max_ctx);
+}
+
+// ---- no-alloc split-KV decode ------------------------------------------------
+// Scratch for callers that cannot allocate: one array per device that loads the
+// library, shared by every call (see flash_engine_c.h for the contract).
+static __device__ __align__(256) float g_noalloc_scratch[FE_NOALLOC_SCRATCH_FLOATS];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per
+// device. In host code the array's name only stands in for the symbol, so it is
+// never passed to a kernel directly.
+static int noalloc_scratch_ptr(float** out) {
+  static std::mutex mu;
+  static float* ptrs[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *out = ptrs[dev];
+  return 0;
+}
+
+int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* kc, const void* vc, void* out,
+                                       const int* bt, const int* lens, int S, int H, int Hkv,
+                                       int d, int bs, int max_ctx, int maxb, int num_blocks,
+                                       float scale, int splits, void* stream) {
+  if (S < 0 || H <= 0 || d <= 0 || splits < 1) return kErr;
+  const long long need = static_cast<long long>(S) * H * splits * (d + 2);
+  if (need > FE_NOALLOC_SCRATCH_FLOATS) return kErr;
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  const int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (S == 0) return 0;
+  float* base = nullptr;
+  const int e = noalloc_scratch_ptr(&base);
+  if (e) return e;
+  float* sout = base;
+  float* sstats = base + static_cast<size_t>(S) * H * splits * d;
+  return paged_v2_tc<__nv_bfloat16>(a, sout, sstats, splits, as_stream(stream));
 }
 
 int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* v, float* out,

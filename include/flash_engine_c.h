@@ -130,6 +130,33 @@ int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v
                                int num_blocks, float scale, float* scratch_out,
                                float* scratch_stats, int num_splits, void* stream);
 
+/* Maximum scratch of fe_paged_attention_v2_bf16_noalloc, in floats (16 MiB): the call
+ * needs num_seqs * num_heads * num_splits * (head_dim + 2) floats of it. */
+#define FE_NOALLOC_SCRATCH_FLOATS (4 * 1024 * 1024)
+
+/* The split-KV bf16 decode of fe_paged_attention_v2_bf16 for callers that cannot
+ * allocate device memory: plugin hosts that own every device buffer and hand a
+ * library only its inputs and outputs, and serving loops that may not call
+ * cudaMalloc because it synchronises the whole device. The split partials live in
+ * a fixed 16 MiB array inside this library (FE_NOALLOC_SCRATCH_FLOATS), which
+ * every GPU that loads the library holds until the process exits; nothing is
+ * allocated or freed by this call. It has no counterpart in the reference.
+ *   - Returns cudaErrorInvalidValue (1), before touching the GPU, when
+ *     num_seqs * num_heads * num_splits * (head_dim + 2) > FE_NOALLOC_SCRATCH_FLOATS.
+ *   - The first call on a device looks up the array's device address on the
+ *     current device; make that first call before any stream capture.
+ *   - All calls share the one array: calls that can overlap on the GPU (other
+ *     streams, other threads) race on it and must be serialised by the caller.
+ *     No part of it needs to start at zero; a call writes every slot it reads.
+ * Other arguments and limits are those of fe_paged_attention_v2_bf16. */
+int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       void* out, const int* block_tables,
+                                       const int* context_lens, int num_seqs, int num_heads,
+                                       int num_kv_heads, int head_dim, int block_size,
+                                       int max_context_len, int max_blocks_per_seq,
+                                       int num_blocks, float scale, int num_splits,
+                                       void* stream);
+
 /* Split count fe_paged_attention_v2_bf16 uses when passed num_splits <= 0. */
 int fe_paged_attention_v2_default_splits(int num_seqs, int num_heads, int num_kv_heads,
                                          int head_dim, int block_size, int max_context_len);
