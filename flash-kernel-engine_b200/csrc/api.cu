@@ -58,41 +58,87 @@ int paged_check(const PagedArgs& a, bool tensor_core) {
   return 0;
 }
 
-// Runs the tensor-core decode over all sequences, in chunks of kMaxSeqsPerLaunch.
-// part_o/part_ml may be null when every sequence is a single split.
+// How the tensor-core decode cuts and finishes the work.
+struct DecodePlan {
+  int tok_begin = 0, tok_end = INT_MAX;
+  bool flat = false;          // stream-K chunking with partials (needs scratch)
+  int pps = INT_MAX / 2;      // unit mode: pages per segment; flat: minimum chunk
+  int max_splits = 1;         // partial slots per (seq, head)
+  bool direct_final = true;   // single-slot rows write the final output
+  int merge_dtype = -1;       // -1: no merge; else MergeParams::out_dtype
+  float* merged_out = nullptr;
+  float* merged_stats = nullptr;
+};
+
+// Runs the tensor-core decode (and, if planned, the log-sum-exp merge) over all
+// sequences, in chunks of kMaxSeqsPerLaunch sequences.
 template <typename T>
-int paged_tc_run(const PagedArgs& a, int tok_begin, int tok_end, int pps, int max_splits,
-                 int direct_final, float* part_o, float* part_ml, cudaStream_t st) {
+int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float* part_ml,
+                 cudaStream_t st) {
   const int G = a.H / a.Hkv;
   const int nt = G <= 8 ? 1 : 2;
-  const int head_chunks = (G + 8 * nt - 1) / (8 * nt);
+  const int hpc = 8 * nt;
+  const int head_chunks = (G + hpc - 1) / hpc;
   const long long kv_rows = a.num_blocks > 0
                                 ? static_cast<long long>(a.num_blocks) * a.Hkv * a.bs
                                 : static_cast<long long>(INT_MAX);
+  unsigned* err = fe::device_error_word();
+  if (!err) return static_cast<int>(cudaErrorInitializationError);
   for (int s0 = 0; s0 < a.S; s0 += kMaxSeqsPerLaunch) {
     const int n = a.S - s0 < kMaxSeqsPerLaunch ? a.S - s0 : kMaxSeqsPerLaunch;
+    const size_t row0 = static_cast<size_t>(s0) * a.H;
     fe::paged::Params p{};
-    p.q = static_cast<const T*>(a.q) + static_cast<size_t>(s0) * a.H * a.d;
-    p.out = a.out ? static_cast<T*>(a.out) + static_cast<size_t>(s0) * a.H * a.d : nullptr;
+    p.q = static_cast<const T*>(a.q) + row0 * a.d;
+    p.out = a.out ? static_cast<T*>(a.out) + row0 * a.d : nullptr;
     p.block_tables = a.bt + static_cast<size_t>(s0) * a.maxb;
     p.context_lens = a.lens + s0;
-    p.part_o = part_o ? part_o + static_cast<size_t>(s0) * a.H * max_splits * a.d : nullptr;
-    p.part_ml = part_ml ? part_ml + static_cast<size_t>(s0) * a.H * max_splits * 2 : nullptr;
+    p.part_o = part_o ? part_o + row0 * pl.max_splits * a.d : nullptr;
+    p.part_ml = part_ml ? part_ml + row0 * pl.max_splits * 2 : nullptr;
     p.num_seqs = n;
     p.num_heads = a.H;
     p.num_kv_heads = a.Hkv;
     p.max_blocks_per_seq = a.maxb;
     p.num_phys_blocks = a.num_blocks;
     p.head_chunks = head_chunks;
-    p.tok_begin = tok_begin;
-    p.tok_end = tok_end;
-    p.pages_per_split = pps;
-    p.max_splits = max_splits;
-    p.direct_final = direct_final;
+    p.tok_begin = pl.tok_begin;
+    p.tok_end = pl.tok_end;
+    p.pages_per_split = pl.pps;
+    p.max_splits = pl.max_splits;
+    p.flat = pl.flat ? 1 : 0;
+    p.direct_final = pl.direct_final ? 1 : 0;
     p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;
-    p.err = fe::device_error_word();
-    if (!p.err) return static_cast<int>(cudaErrorInitializationError);
-    cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, st);
+    p.err = err;
+    int grid = 0;
+    cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, &grid, st);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (pl.merge_dtype < 0) continue;
+    fe::paged::MergeParams mp{};
+    mp.part_out = p.part_o;
+    mp.part_stats = p.part_ml;
+    mp.rows = n * a.H;
+    mp.ranks = 1;
+    mp.parts_per_rank = pl.max_splits;
+    mp.context_lens = p.context_lens;
+    mp.num_seqs = n;
+    mp.heads = a.H;
+    mp.kv_heads = a.Hkv;
+    mp.heads_per_chunk = hpc;
+    mp.head_chunks = head_chunks;
+    mp.groups = a.Hkv * head_chunks;
+    mp.tok_begin = pl.tok_begin;
+    mp.tok_end = pl.tok_end;
+    mp.block_size = a.bs;
+    mp.decode_ctas = grid;
+    mp.chunk_min = pl.pps;
+    mp.skip_single = pl.direct_final ? 1 : 0;
+    if (pl.merge_dtype == 2) {
+      mp.out = pl.merged_out + row0 * a.d;
+      mp.out_stats = pl.merged_stats + row0 * 2;
+    } else {
+      mp.out = p.out;
+    }
+    mp.out_dtype = pl.merge_dtype;
+    e = fe::paged::launch_merge(mp, a.d, st);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
@@ -100,17 +146,25 @@ int paged_tc_run(const PagedArgs& a, int tok_begin, int tok_end, int pps, int ma
 
 int default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
   (void)d;
-  (void)H;
+  const int G = H / (Hkv > 0 ? Hkv : 1);
+  const int head_chunks = (G + (G <= 8 ? 8 : 16) - 1) / (G <= 8 ? 8 : 16);
   const int max_pages = max_ctx > 0 ? (max_ctx + bs - 1) / bs : 1;
-  const long long units = static_cast<long long>(S > 0 ? S : 1) * Hkv;
-  // ~8 units of work per SM slot (2 resident CTAs per SM), pages of >= 16.
-  const long long target = 16LL * fe::sm_count();
-  long long splits = (target + units - 1) / units;
-  const long long max_by_pages = (max_pages + 15) / 16;
-  if (splits > max_by_pages) splits = max_by_pages;
-  if (splits < 1) splits = 1;
-  if (splits > 256) splits = 256;
+  const long long groups = static_cast<long long>(S > 0 ? S : 1) * Hkv * head_chunks;
+  // Enough partial slots for a sequence to be spread over ~2x as many CTAs as its
+  // share of the GPU (2 persistent CTAs per SM), plus the two chunk-boundary pieces.
+  const long long ctas = 2LL * fe::sm_count();
+  long long splits = (2 * ctas + groups - 1) / groups + 2;
+  if (splits > max_pages + 1) splits = max_pages + 1;
+  if (splits < 2) splits = 2;
+  if (splits > 64) splits = 64;
   return static_cast<int>(splits);
+}
+
+// Flat-mode minimum chunk so that a sequence of up to max_pages pages touches at
+// most `splits` chunks.
+inline int flat_chunk_min(int max_pages, int splits) {
+  if (max_pages < 1) max_pages = 1;
+  return (max_pages + splits - 2) / (splits - 1);
 }
 
 template <typename T>
@@ -118,8 +172,10 @@ int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
   const int rc = paged_check(a, true);
   if (rc) return rc;
   if (a.S == 0) return 0;
-  // One split per sequence whatever its length: every unit writes its final row.
-  return paged_tc_run<T>(a, 0, INT_MAX, INT_MAX / 2, 1, 1, nullptr, nullptr, st);
+  // Unit mode, one segment per sequence whatever its length: every segment
+  // writes its final rows, no scratch.
+  DecodePlan pl;
+  return paged_tc_run<T>(a, pl, nullptr, nullptr, st);
 }
 
 template <typename T>
@@ -128,27 +184,15 @@ int paged_v2_tc(const PagedArgs& a, float* sout, float* sstats, int splits, cuda
   if (rc) return rc;
   if (splits < 1 || !sout || !sstats) return kErr;
   if (a.S == 0) return 0;
+  if (splits == 1) return paged_v1_tc<T>(a, st);
   const int max_pages = a.max_ctx > 0 ? (a.max_ctx + a.bs - 1) / a.bs : 1;
-  const int pps = fe::paged::pages_per_split_for(max_pages, splits);
-  int e = paged_tc_run<T>(a, 0, INT_MAX, pps, splits, 1, sout, sstats, st);
-  if (e) return e;
-  fe::paged::MergeParams mp{};
-  mp.part_out = sout;
-  mp.part_stats = sstats;
-  mp.rows = a.S * a.H;
-  mp.ranks = 1;
-  mp.parts_per_rank = splits;
-  mp.context_lens = a.lens;
-  mp.heads = a.H;
-  mp.tok_begin = 0;
-  mp.tok_end = INT_MAX;
-  mp.block_size = a.bs;
-  mp.pages_per_split = pps;
-  mp.skip_single = 1;
-  mp.out = a.out;
-  mp.out_stats = nullptr;
-  mp.out_dtype = std::is_same<T, __nv_bfloat16>::value ? 1 : 3;
-  return static_cast<int>(fe::paged::launch_merge(mp, a.d, st));
+  DecodePlan pl;
+  pl.flat = true;
+  pl.pps = flat_chunk_min(max_pages, splits);
+  pl.max_splits = splits;
+  pl.direct_final = true;
+  pl.merge_dtype = std::is_same<T, __nv_bfloat16>::value ? 1 : 3;
+  return paged_tc_run<T>(a, pl, sout, sstats, st);
 }
 
 }  // namespace
@@ -316,27 +360,19 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
     return kErr;
   if (S == 0) return 0;
   const int range_pages = (te - tb + bs - 1) / bs;
-  const int pps = fe::paged::pages_per_split_for(range_pages > 0 ? range_pages : 1, splits);
-  cudaStream_t st = as_stream(stream);
-  rc = paged_tc_run<__nv_bfloat16>(a, tb, te, pps, splits, 0, sout, sstats, st);
-  if (rc) return rc;
-  fe::paged::MergeParams mp{};
-  mp.part_out = sout;
-  mp.part_stats = sstats;
-  mp.rows = S * H;
-  mp.ranks = 1;
-  mp.parts_per_rank = splits;
-  mp.context_lens = lens;
-  mp.heads = H;
-  mp.tok_begin = tb;
-  mp.tok_end = te;
-  mp.block_size = bs;
-  mp.pages_per_split = pps;
-  mp.skip_single = 0;
-  mp.out = mout;
-  mp.out_stats = mstats;
-  mp.out_dtype = 2;
-  return static_cast<int>(fe::paged::launch_merge(mp, d, st));
+  DecodePlan pl;
+  pl.tok_begin = tb;
+  pl.tok_end = te;
+  pl.direct_final = false;
+  pl.max_splits = splits;
+  pl.merge_dtype = 2;
+  pl.merged_out = mout;
+  pl.merged_stats = mstats;
+  if (splits >= 2) {
+    pl.flat = true;
+    pl.pps = flat_chunk_min(range_pages, splits);
+  }
+  return paged_tc_run<__nv_bfloat16>(a, pl, sout, sstats, as_stream(stream));
 }
 
 int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,

@@ -8,23 +8,30 @@
 // [num_blocks, Hkv, BS, d], the one the reference's fp32 kernel implements.
 //
 // Design (B200):
-//  * Persistent CTAs (SMs x occupancy). Work units are (sequence, split, KV head,
-//    head chunk); every CTA builds the compact unit list itself with a block-wide
-//    prefix scan of the per-sequence split counts (read from context_lens), so no
-//    host synchronisation or scratch is needed to skip empty work.
-//  * One producer warp streams each (block, KV head) page of K and V into a ring of
-//    shared-memory stages with 2-D TMA bulk-tensor loads (128-byte swizzle, L2
-//    evict-first, no multicast), completing on mbarriers. Block-table entries are
-//    fetched 32 at a time by the warp.
-//  * NCW consumer warps take pages round-robin. Per 16 tokens a warp computes
-//    S^T = K Q^T with mma.m16n8k16 (tokens x query heads: all G query heads of the
-//    group share every K/V byte fetched), does the online-softmax update in the
-//    log2 domain, turns P^T into the B operand with movmatrix, and accumulates
-//    O^T += V^T P^T (V^T fragments via ldmatrix.trans from the swizzled tile).
-//  * The consumer warps merge their (m, l, O) in shared memory at the end of a
-//    unit and write either the final output (single-split sequences) or an fp32
-//    partial (O, m, l) for the log-sum-exp merge kernel.
-#include <cooperative_groups.h>
+//  * Persistent CTAs (SMs x occupancy). Two ways to cut the work into segments
+//    (a contiguous page range of one (sequence, KV-head group)):
+//      - unit mode (no scratch): one segment per (sequence, KV-head group),
+//        dealt round-robin to the CTAs;
+//      - flat mode (split-KV with partials): the (KV-head group, sequence, page)
+//        space is cut into gridDim.x equal contiguous chunks (stream-K style), one
+//        per CTA, so every CTA streams the same number of pages. A sequence cut by
+//        a chunk boundary leaves one fp32 partial per chunk; merge_kernel combines
+//        them. A sequence inside one chunk is finalised directly.
+//    Both modes read context_lens and build the page prefix with a block-wide scan
+//    in every CTA, so no host synchronisation or scratch is needed to skip or
+//    place work.
+//  * One producer warp streams each (block, KV head) page of K and V into shared
+//    memory with 2-D TMA bulk-tensor loads (128-byte swizzle, L2 evict-first, no
+//    multicast), completing on mbarriers. Block-table entries are fetched 32 at a
+//    time, one 32-page group ahead of the loads they feed.
+//  * NCW consumer warps, each with a private ring of DEPTH stages (page gi of the
+//    CTA belongs to warp gi % NCW). Per 16 tokens a warp computes S^T = K Q^T with
+//    mma.m16n8k16 (tokens x query heads: all G query heads of the group share
+//    every K/V byte fetched), does the online-softmax update in the log2 domain,
+//    turns P^T into the B operand with movmatrix and accumulates O^T += V^T P^T
+//    (V^T fragments via ldmatrix.trans from the swizzled tile).
+//  * At the end of a segment the consumer warps merge their (m, l, O) in shared
+//    memory and write the final row or a partial.
 #include <limits.h>
 
 #include <type_traits>
@@ -57,29 +64,16 @@ struct Elem<half> {
   static __device__ __forceinline__ half cvt(float x) { return __float2half_rn(x); }
 };
 
-// Page range of split `split` of sequence `ctx` inside the token window.
-struct SplitRange {
-  int p0, p1;  // pages [p0, p1)
-  int lo, hi;  // valid tokens [lo, hi)
-};
-__device__ __forceinline__ SplitRange split_range(int ctx, int tb, int te, int bs, int pps,
-                                                  int split) {
-  SplitRange r;
-  r.lo = max(tb, 0);
-  r.hi = min(te, ctx);
-  if (r.hi <= r.lo) {
-    r.p0 = r.p1 = 0;
-    return r;
-  }
-  const int pb = r.lo / bs, pe = (r.hi + bs - 1) / bs;
-  r.p0 = pb + split * pps;
-  r.p1 = min(pe, r.p0 + pps);
-  if (r.p1 < r.p0) r.p1 = r.p0;
-  return r;
-}
+constexpr float NEG_INF = -__builtin_huge_valf();
 
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ int warp_incl_scan(int v) {
@@ -91,6 +85,141 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   }
   return v;
 }
+
+// Token window of a sequence: [lo, hi) = [tok_begin, min(tok_end, ctx)); its pages
+// [lo / bs, ceil(hi / bs)).
+struct Window {
+  int lo, hi, pb, np;
+};
+__device__ __forceinline__ Window seq_window(int ctx, int tb, int te, int bs) {
+  Window w;
+  w.lo = max(tb, 0);
+  w.hi = min(te, ctx);
+  if (w.hi <= w.lo) {
+    w.pb = 0;
+    w.np = 0;
+  } else {
+    w.pb = w.lo / bs;
+    w.np = (w.hi + bs - 1) / bs - w.pb;
+  }
+  return w;
+}
+
+// Number of unit-mode segments of a sequence: one per pages_per_split pages (at
+// least one, so that an empty sequence still gets its zero output row).
+__device__ __forceinline__ int unit_splits(const Window& w, int pps) {
+  return w.np == 0 ? 1 : (w.np + pps - 1) / pps;
+}
+
+// Block-wide exclusive prefix over S per-sequence counts into pre[0..S] (pre[S] =
+// total). `count(i)` must be cheap and pure; every thread of the block calls this.
+template <int NTH, typename Count>
+__device__ __forceinline__ void block_prefix(int* pre, int S, int* warp_tot, Count count) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NW = NTH / 32;
+  const int per = (S + NTH - 1) / NTH;
+  const int beg = min(S, tid * per), end = min(S, beg + per);
+  int local = 0;
+  for (int i = beg; i < end; ++i) local += count(i);
+  const int incl = warp_incl_scan(local);
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = lane < NW ? warp_tot[lane] : 0;
+    v = warp_incl_scan(v);
+    if (lane < NW) warp_tot[lane] = v;
+  }
+  __syncthreads();
+  int run = incl - local + (warp > 0 ? warp_tot[warp - 1] : 0);
+  for (int i = beg; i < end; ++i) {
+    pre[i] = run;
+    run += count(i);
+  }
+  if (tid == 0) pre[S] = warp_tot[NW - 1];
+  __syncthreads();
+}
+
+// Largest s in [0, S) with pre[s] <= r.
+__device__ __forceinline__ int find_seq(const int* pre, int S, long long r) {
+  int lo = 0, hi = S;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (pre[mid] <= r) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Flat-mode chunk length in pages (identical in the decode and merge kernels).
+__device__ __forceinline__ long long flat_chunk(long long T, int ctas, int chunk_min) {
+  long long c = (T + ctas - 1) / ctas;
+  if (c < chunk_min) c = chunk_min;
+  return c < 1 ? 1 : c;
+}
+
+struct Seg {
+  int seq, kvh, hc;
+  int p0, p1;     // absolute pages [p0, p1)
+  int lo, hi;     // valid tokens [lo, hi)
+  int slot;       // partial slot of this segment
+  int nslots;     // segments of this (sequence, head group); 1 = write final output
+};
+
+// Walks the segments of one CTA. Producer and consumers run identical copies.
+struct SegIter {
+  const Params* p;
+  const int* pre;
+  int S, Y, HC, BS;
+  bool flat;
+  // unit mode
+  int u, total_units;
+  // flat mode
+  long long P, Pend, chunk;
+  int Ptot;
+
+  __device__ __forceinline__ bool next(Seg& g) {
+    if (!flat) {
+      if (u >= total_units) return false;
+      const int cu = u / Y, y = u - cu * Y;
+      u += gridDim.x;
+      const int seq = find_seq(pre, S, cu);
+      const Window w = seq_window(__ldg(p->context_lens + seq), p->tok_begin, p->tok_end, BS);
+      const int split = cu - pre[seq];
+      g.seq = seq;
+      g.kvh = y / HC;
+      g.hc = y - g.kvh * HC;
+      g.p0 = w.pb + split * p->pages_per_split;
+      g.p1 = min(w.pb + w.np, g.p0 + p->pages_per_split);
+      if (g.p1 < g.p0) g.p1 = g.p0;
+      g.lo = w.lo;
+      g.hi = w.hi;
+      g.slot = split;
+      g.nslots = pre[seq + 1] - pre[seq];
+      return true;
+    }
+    if (P >= Pend) return false;
+    const int y = static_cast<int>(P / Ptot);
+    const int r = static_cast<int>(P - static_cast<long long>(y) * Ptot);
+    const int seq = find_seq(pre, S, r);
+    const Window w = seq_window(__ldg(p->context_lens + seq), p->tok_begin, p->tok_end, BS);
+    const int in0 = r - pre[seq];
+    const long long left = Pend - P;
+    const int n = static_cast<int>(min(static_cast<long long>(w.np - in0), left));
+    const long long gstart = static_cast<long long>(y) * Ptot + pre[seq];
+    const long long gend = gstart + w.np - 1;
+    g.seq = seq;
+    g.kvh = y / HC;
+    g.hc = y - g.kvh * HC;
+    g.p0 = w.pb + in0;
+    g.p1 = g.p0 + n;
+    g.lo = w.lo;
+    g.hi = w.hi;
+    const int cfirst = static_cast<int>(gstart / chunk);
+    g.nslots = static_cast<int>(gend / chunk) - cfirst + 1;
+    g.slot = static_cast<int>(blockIdx.x) - cfirst;
+    P += n;
+    return true;
+  }
+};
 
 // Page gi of a CTA (its running page counter) belongs to consumer warp gi % NCW
 // and lives in that warp's own ring of DEPTH stages. Every stage therefore has a
@@ -120,16 +249,6 @@ struct Cfg {
   static int smem_bytes(int num_seqs) { return FIXED_SMEM + (num_seqs + 1) * 4; }
 };
 
-// Number of work splits of one sequence (0 if its token window is empty; 1 for an
-// empty sequence when the final output must still be written).
-__device__ __forceinline__ int seq_splits(int ctx, int tb, int te, int bs, int pps,
-                                          bool direct_final) {
-  const int lo = max(tb, 0), hi = min(te, ctx);
-  if (hi <= lo) return direct_final ? 1 : 0;
-  const int np = (hi + bs - 1) / bs - lo / bs;
-  return (np + pps - 1) / pps;
-}
-
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
 __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -137,7 +256,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
   constexpr int HPC = C::HPC, HALVES = C::HALVES, TILE = C::TILE, STAGE = C::STAGE;
   constexpr int CSTRIDE = C::CSTRIDE, NTH = C::NTHREADS;
-  constexpr float NEG_INF = -__builtin_huge_valf();
+  using SO = StageOf<NCW, NSTAGE / NCW>;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -148,13 +267,18 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE + C::COMB_BYTES);
   uint64_t* empty = full + NSTAGE;
   int* stage_valid = reinterpret_cast<int*>(empty + NSTAGE);
-  int* prefix = stage_valid + NSTAGE;  // [num_seqs + 1]
+  int* pre = stage_valid + NSTAGE;  // [num_seqs + 1]
   __shared__ int warp_tot[NCW + 1];
+
+  // Let the merge kernel that follows (programmatic dependent launch) start its
+  // prologue; it waits for this grid's results before reading them.
+  griddep_launch_dependents();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = p.num_seqs;
   const int Hkv = p.num_kv_heads, G = p.num_heads / p.num_kv_heads;
-  const int HC = p.head_chunks;
+  const int HC = p.head_chunks, Y = Hkv * HC;
+  const bool flat = p.flat != 0;
   const bool direct_final = p.direct_final != 0;
 
   if (tid == 0) {
@@ -165,56 +289,35 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     fence_mbar_init();
   }
 
-  // ---- compact unit list: prefix[s] = first compact (sequence, split) index of s.
-  {
-    const int per = (S + NTH - 1) / NTH;
-    const int beg = min(S, tid * per), end = min(S, beg + per);
-    int local = 0;
-    for (int i = beg; i < end; ++i) {
-      const int n = seq_splits(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS,
-                               p.pages_per_split, direct_final);
-      // More splits than partial slots means context_len > max_context_len: the
-      // tail is dropped and the error word says so.
-      if (n > p.max_splits && blockIdx.x == 0) atomicOr(p.err, kErrBadBlock);
-      local += min(n, p.max_splits);
-    }
-    const int incl = warp_incl_scan(local);
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      int v = lane <= NCW ? warp_tot[lane] : 0;
-      v = warp_incl_scan(v);
-      if (lane <= NCW) warp_tot[lane] = v;
-    }
-    __syncthreads();
-    int run = incl - local + (warp > 0 ? warp_tot[warp - 1] : 0);
-    for (int i = beg; i < end; ++i) {
-      prefix[i] = run;
-      run += min(seq_splits(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS,
-                            p.pages_per_split, direct_final),
-                 p.max_splits);
-    }
-    if (tid == 0) prefix[S] = warp_tot[NCW];
-    __syncthreads();
+  SegIter it;
+  it.p = &p;
+  it.pre = pre;
+  it.S = S;
+  it.Y = Y;
+  it.HC = HC;
+  it.BS = BS;
+  it.flat = flat;
+  if (flat) {
+    block_prefix<NTH>(pre, S, warp_tot, [&](int i) {
+      return seq_window(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS).np;
+    });
+    it.Ptot = pre[S];
+    const long long total_pages = static_cast<long long>(Y) * it.Ptot;
+    it.chunk = flat_chunk(total_pages, gridDim.x, p.pages_per_split);
+    it.P = min(total_pages, static_cast<long long>(blockIdx.x) * it.chunk);
+    it.Pend = min(total_pages, it.P + it.chunk);
+    it.u = it.total_units = 0;
+  } else {
+    block_prefix<NTH>(pre, S, warp_tot, [&](int i) {
+      return unit_splits(seq_window(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS),
+                         p.pages_per_split);
+    });
+    it.u = blockIdx.x;
+    it.total_units = pre[S] * Y;
+    it.P = it.Pend = 0;
+    it.chunk = 1;
+    it.Ptot = 0;
   }
-  const int units_per_cu = Hkv * HC;
-  const int total_units = prefix[S] * units_per_cu;
-
-  // unit -> (seq, split, kvh, hc, page range)
-  auto decode_unit = [&](int u, int& seq, int& split, int& kvh, int& hc, SplitRange& r) {
-    const int cu = u / units_per_cu, y = u - cu * units_per_cu;
-    kvh = y / HC;
-    hc = y - kvh * HC;
-    int lo = 0, hi = S;  // largest s with prefix[s] <= cu
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (prefix[mid] <= cu) lo = mid; else hi = mid;
-    }
-    seq = lo;
-    split = cu - prefix[lo];
-    r = split_range(__ldg(p.context_lens + seq), p.tok_begin, p.tok_end, BS, p.pages_per_split,
-                    split);
-  };
 
   if (warp == NCW) {
     // ===================================================== producer warp
@@ -223,69 +326,89 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
       prefetch_tensormap(&vmap);
     }
     const uint64_t pol = l2_policy_evict_first();
-    int gi = 0;  // pages issued by this CTA so far (identical count on every lane)
-    bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-      int seq, split, kvh, hc;
-      SplitRange r;
-      decode_unit(u, seq, split, kvh, hc, r);
-      const int npg = r.p1 - r.p0;
-      const int* bt = p.block_tables + static_cast<size_t>(seq) * p.max_blocks_per_seq;
-      for (int base = 0; base < npg && ok; base += 32) {
-        int phys = 0, valid = 0;
-        if (base + lane < npg && r.p0 + base + lane >= p.max_blocks_per_seq) {
-          atomicOr(p.err, kErrBadBlock);  // context longer than the block table row
-        } else if (base + lane < npg) {
-          phys = __ldg(bt + r.p0 + base + lane);
-          const long long row = (static_cast<long long>(phys) * Hkv + kvh) * BS;
+    // Block-table entries of one 32-page group of a segment (lane i: page base+i).
+    auto load_group = [&](const Seg& g, int base, int& phys, int& valid) {
+      phys = 0;
+      valid = 0;
+      const int page = g.p0 + base + lane;
+      if (page < g.p1) {
+        if (page >= p.max_blocks_per_seq) {
+          atomicOr(p.err, kErrBadBlock);  // context longer than the block-table row
+        } else {
+          phys = __ldg(p.block_tables + static_cast<size_t>(g.seq) * p.max_blocks_per_seq + page);
+          const long long row = (static_cast<long long>(phys) * Hkv + g.kvh) * BS;
           valid = phys >= 0 && (p.num_phys_blocks <= 0 || phys < p.num_phys_blocks) &&
                   row + BS <= static_cast<long long>(INT_MAX);
           if (!valid) atomicOr(p.err, kErrBadBlock);
         }
-        const int cnt = min(32, npg - base);
-        for (int k = 0; k < cnt; ++k) {
-          const int ph = __shfl_sync(0xffffffffu, phys, k);
-          const int vd = __shfl_sync(0xffffffffu, valid, k);
-          int good = 1;
-          if (lane == 0) {
-            const StageOf<NCW, NSTAGE / NCW> so(gi);
-            const int s = so.s, rnd = so.round;
-            if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1)) {
-              atomicOr(p.err, kErrWaitTimeout);
-              good = 0;
-            } else {
-              stage_valid[s] = vd;
-              uint8_t* ks = smem + s * STAGE;
-              uint8_t* vs = ks + TILE;
-              if (vd) {
-                mbar_arrive_expect_tx(&full[s], STAGE);
-                const int y = (ph * Hkv + kvh) * BS;
+      }
+    };
+    int gi = 0;
+    bool ok = true;
+    Seg cur;
+    bool have = it.next(cur);
+    int base = 0;
+    int ph_cur = 0, vd_cur = 0;
+    if (have) load_group(cur, 0, ph_cur, vd_cur);
+    while (have && ok) {
+      // Look one 32-page group ahead and start its block-table loads now.
+      Seg ns = cur;
+      int nbase = base + 32;
+      bool have_n = true;
+      if (cur.p0 + nbase >= cur.p1) {
+        have_n = it.next(ns);
+        nbase = 0;
+      }
+      int ph_n = 0, vd_n = 0;
+      if (have_n) load_group(ns, nbase, ph_n, vd_n);
+      const int cnt = max(0, min(32, cur.p1 - cur.p0 - base));
+      for (int k = 0; k < cnt; ++k) {
+        const int ph = __shfl_sync(0xffffffffu, ph_cur, k);
+        const int vd = __shfl_sync(0xffffffffu, vd_cur, k);
+        int good = 1;
+        if (lane == 0) {
+          const SO so(gi);
+          const int s = so.s;
+          if (so.round > 0 && !mbar_wait(&empty[s], (so.round - 1) & 1)) {
+            atomicOr(p.err, kErrWaitTimeout);
+            good = 0;
+          } else {
+            stage_valid[s] = vd;
+            uint8_t* ks = smem + s * STAGE;
+            uint8_t* vs = ks + TILE;
+            if (vd) {
+              mbar_arrive_expect_tx(&full[s], STAGE);
+              const int y = (ph * Hkv + cur.kvh) * BS;
 #ifdef FE_DEBUG_CHECKS
-                if (static_cast<long long>(y) + BS > p.dbg_kv_rows) atomicOr(p.err, 1u << 8);
+              if (static_cast<long long>(y) + BS > p.dbg_kv_rows) atomicOr(p.err, 1u << 8);
 #endif
 #pragma unroll
-                for (int h = 0; h < HALVES; ++h) {
-                  tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
-                  tma_load_2d(vs + h * BS * 128, &vmap, h * 64, y, &full[s], pol);
-                }
-              } else {
-                mbar_arrive(&full[s]);  // nothing to load; consumers skip the page
+              for (int h = 0; h < HALVES; ++h) {
+                tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
+                tma_load_2d(vs + h * BS * 128, &vmap, h * 64, y, &full[s], pol);
               }
+            } else {
+              mbar_arrive(&full[s]);  // nothing to load; consumers skip the page
             }
           }
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) {
-            ok = false;
-            break;
-          }
-          ++gi;
         }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        ++gi;
       }
+      cur = ns;
+      base = nbase;
+      ph_cur = ph_n;
+      vd_cur = vd_n;
+      have = have_n;
     }
     // Drain: no bulk copy of this CTA may still be in flight when it exits.
     if (lane == 0) {
       for (int j = max(0, gi - NSTAGE); j < gi; ++j) {
-        const StageOf<NCW, NSTAGE / NCW> so(j);
+        const SO so(j);
         if (!mbar_wait(&full[so.s], so.round & 1)) {
           atomicOr(p.err, kErrWaitTimeout);
           break;
@@ -304,15 +427,13 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
 
   uint32_t qf[NT][D / 16][2];
   uint32_t qn[NT][D / 16][2];
-  auto load_q = [&](uint32_t (&dst)[NT][D / 16][2], int u) {
-    int seq, split, kvh, hc;
-    SplitRange r;
-    decode_unit(u, seq, split, kvh, hc, r);
+  auto load_q = [&](uint32_t (&dst)[NT][D / 16][2], const Seg& sg) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int gh = hc * HPC + nt * 8 + g;
+      const int gh = sg.hc * HPC + nt * 8 + g;
       const bool v = gh < G;
-      const T* qp = qbase + (static_cast<size_t>(seq) * p.num_heads + kvh * G + (v ? gh : 0)) * D;
+      const T* qp =
+          qbase + (static_cast<size_t>(sg.seq) * p.num_heads + sg.kvh * G + (v ? gh : 0)) * D;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
         dst[nt][ks][0] = v ? __ldg(reinterpret_cast<const unsigned*>(qp + ks * 16 + 2 * c)) : 0u;
@@ -321,13 +442,16 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     }
   };
 
-  int gbase = 0;  // pages consumed by this CTA before the current unit
+  int gbase = 0;  // pages consumed by this CTA before the current segment
   bool ok = true;
-  if (blockIdx.x < total_units) load_q(qn, blockIdx.x);
-  for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
-    int seq, split, kvh, hc;
-    SplitRange r;
-    decode_unit(u, seq, split, kvh, hc, r);
+  Seg sg, sn;
+  bool have = it.next(sg);
+  bool have_n = false;
+  if (have) {
+    load_q(qn, sg);
+    have_n = it.next(sn);
+  }
+  while (have) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -335,7 +459,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         qf[nt][ks][0] = qn[nt][ks][0];
         qf[nt][ks][1] = qn[nt][ks][1];
       }
-    if (u + gridDim.x < total_units) load_q(qn, u + gridDim.x);  // prefetch the next unit's q
+    if (have_n) load_q(qn, sn);  // prefetch the next segment's q
 
     float m_run[NT][2], l_run[NT][2], o[NT][D / 16][4];
 #pragma unroll
@@ -346,11 +470,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
       for (int mt = 0; mt < D / 16; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
     }
 
-    const int npg = r.p1 - r.p0;
+    const int npg = max(0, sg.p1 - sg.p0);
     const int first = ((warp - gbase) % NCW + NCW) % NCW;
     for (int i = first; i < npg && ok; i += NCW) {
       const int gi = gbase + i;
-      const StageOf<NCW, NSTAGE / NCW> so(gi);
+      const SO so(gi);
       const int s = so.s;
       const bool waited = mbar_wait(&full[s], so.round & 1);
       if (!__all_sync(0xffffffffu, waited)) {
@@ -358,8 +482,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         ok = false;
         break;
       }
-      const int t0 = (r.p0 + i) * BS;
-      const int vlo = max(r.lo - t0, 0), vhi = min(r.hi - t0, BS);
+      const int t0 = (sg.p0 + i) * BS;
+      const int vlo = max(sg.lo - t0, 0), vhi = min(sg.hi - t0, BS);
       const uint32_t ks = ring + s * STAGE, vs = ks + TILE;
       bool zeroed = false;
       if (stage_valid[s]) {
@@ -454,7 +578,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     }
     gbase += npg;
 
-    // ---- merge the NCW warp states of this unit
+    // ---- merge the NCW warp states of this segment
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -487,14 +611,14 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     __syncwarp();
     named_bar(1, NCW * 32);
 
-    const int nsplit_seq =
-        min(seq_splits(__ldg(p.context_lens + seq), p.tok_begin, p.tok_end, BS,
-                       p.pages_per_split, direct_final),
-            p.max_splits);
-    const bool final_out = direct_final && nsplit_seq == 1;
-    for (int idx = tid; idx < HPC * D; idx += NCW * 32) {
+    const bool final_out = direct_final && sg.nslots == 1;
+    // A sequence longer than max_context_len would need more partial slots than the
+    // scratch holds; such a segment is dropped and flagged.
+    const bool slot_ok = final_out || (sg.slot >= 0 && sg.slot < p.max_splits);
+    if (!slot_ok && tid == 0) atomicOr(p.err, kErrBadBlock);
+    for (int idx = tid; idx < HPC * D && slot_ok; idx += NCW * 32) {
       const int hl = idx / D, dim = idx - hl * D;
-      const int gh = hc * HPC + hl;
+      const int gh = sg.hc * HPC + hl;
       if (gh >= G) continue;
       float M = NEG_INF;
 #pragma unroll
@@ -507,19 +631,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         L += comb_l[w * HPC + hl] * wt;
         O += comb_o[(w * HPC + hl) * CSTRIDE + dim] * wt;
       }
-      const size_t row = static_cast<size_t>(seq) * p.num_heads + kvh * G + gh;
-#ifdef FE_DEBUG_CHECKS
-      if (row >= static_cast<size_t>(p.num_seqs) * p.num_heads ||
-          (!final_out && (split < 0 || split >= p.max_splits || !p.part_o)) ||
-          (final_out && !p.out)) {
-        atomicOr(p.err, 1u << 9);
-        continue;
-      }
-#endif
+      const size_t row = static_cast<size_t>(sg.seq) * p.num_heads + sg.kvh * G + gh;
       if (final_out) {
         reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(L > 0.f ? O / L : 0.f);
       } else {
-        const size_t part = row * p.max_splits + split;
+        const size_t part = row * p.max_splits + sg.slot;
         p.part_o[part * D + dim] = O;
         if (dim == 0) {
           p.part_ml[part * 2 + 0] = M;
@@ -529,93 +645,118 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     }
     __syncwarp();
     named_bar(2, NCW * 32);
+    sg = sn;
+    have = have_n;
+    if (have) have_n = it.next(sn);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Log-sum-exp merge of split partials. One warp per output row.
-//   ctx mode (context_lens != nullptr): row = seq * H + h, its valid partials are the
-//     seq_splits(...) first slots of [rows, max_splits]; rows with a single split
-//     were already finalised by the decode kernel when skip_single is set.
+//   ctx mode (context_lens != nullptr): row = seq * H + h; its valid slots follow
+//     from the decode kernel's flat chunking (same prefix, same chunk length);
+//     rows with one slot were finalised by the decode kernel (skip_single), rows
+//     with none are empty (zeros / (-inf, 0)).
 //   all mode: every (rank, part) slot is a partial (possibly empty: l = 0).
-template <int DMAX>
-__global__ void __launch_bounds__(128) merge_kernel(const MergeParams mp) {
-  constexpr float NEG_INF = -__builtin_huge_valf();
+template <int DMAX, int ROWS>
+__global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
   constexpr int PER = DMAX / 32;
+  extern __shared__ int msmem[];
+  __shared__ int warp_tot[8];
   const int D = mp.head_dim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 4 + warp;
-  if (row >= mp.rows) return;
-  int nparts, ranks;
+  int* pre = msmem;
+  long long chunk = 1;
+  int Ptot = 0;
   if (mp.context_lens) {
-    const int seq = row / mp.heads;
-    nparts = min(seq_splits(__ldg(mp.context_lens + seq), mp.tok_begin, mp.tok_end,
-                            mp.block_size, mp.pages_per_split, false),
-                 mp.parts_per_rank);
-    if (mp.skip_single && nparts <= 1) return;
-    ranks = 1;
-  } else {
-    nparts = mp.parts_per_rank;
-    ranks = mp.ranks;
+    block_prefix<256>(pre, mp.num_seqs, warp_tot, [&](int i) {
+      return seq_window(__ldg(mp.context_lens + i), mp.tok_begin, mp.tok_end, mp.block_size).np;
+    });
+    Ptot = pre[mp.num_seqs];
+    chunk = flat_chunk(static_cast<long long>(mp.groups) * Ptot, mp.decode_ctas, mp.chunk_min);
   }
-  // pass 1: global max
-  float M = NEG_INF;
-  for (int rk = 0; rk < ranks; ++rk)
-    for (int j = lane; j < nparts; j += 32) {
-      const size_t slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
-      const float l = mp.part_stats[slot * 2 + 1];
-      if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
-    }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float L = 0.f, acc[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) acc[k] = 0.f;
-  for (int rk = 0; rk < ranks; ++rk)
-    for (int j0 = 0; j0 < nparts; j0 += 32) {
-      const int j = j0 + lane;
-      float wt = 0.f, l = 0.f;
-      size_t slot = 0;
-      if (j < nparts) {
-        slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
-        l = mp.part_stats[slot * 2 + 1];
-        if (l > 0.f) wt = ex2(mp.part_stats[slot * 2] - M);
+  griddep_wait();  // the decode grid's partials are complete and visible
+  for (int rr = warp; rr < ROWS; rr += 8) {
+    const int row = blockIdx.x * ROWS + rr;
+    if (row >= mp.rows) break;
+    int nparts, ranks;
+    if (mp.context_lens) {
+      const int seq = row / mp.heads, h = row - seq * mp.heads;
+      const int G = mp.heads / mp.kv_heads;
+      const int kvh = h / G, hc = (h - kvh * G) / mp.heads_per_chunk;
+      const int y = kvh * mp.head_chunks + hc;
+      const int np = pre[seq + 1] - pre[seq];
+      if (np == 0) {
+        nparts = 0;
+      } else {
+        const long long gstart = static_cast<long long>(y) * Ptot + pre[seq];
+        nparts = static_cast<int>((gstart + np - 1) / chunk - gstart / chunk + 1);
       }
-      L += l * wt;
-      const int cnt = min(32, nparts - j0);
-      for (int k = 0; k < cnt; ++k) {
-        const float w = __shfl_sync(0xffffffffu, wt, k);
-        if (w == 0.f) continue;
-        const size_t sl = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j0 + k;
-        const float* po = mp.part_out + sl * D;
+      if (mp.skip_single && nparts == 1) continue;
+      if (nparts > mp.parts_per_rank) nparts = mp.parts_per_rank;
+      ranks = 1;
+    } else {
+      nparts = mp.parts_per_rank;
+      ranks = mp.ranks;
+    }
+    // pass 1: global max
+    float M = NEG_INF;
+    for (int rk = 0; rk < ranks; ++rk)
+      for (int j = lane; j < nparts; j += 32) {
+        const size_t slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
+        const float l = mp.part_stats[slot * 2 + 1];
+        if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
+      }
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-          const int dim = lane + 32 * e;
-          if (dim < D) acc[e] += po[dim] * w;
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f, acc[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+    for (int rk = 0; rk < ranks; ++rk)
+      for (int j0 = 0; j0 < nparts; j0 += 32) {
+        const int j = j0 + lane;
+        float wt = 0.f, l = 0.f;
+        if (j < nparts) {
+          const size_t slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
+          l = mp.part_stats[slot * 2 + 1];
+          if (l > 0.f) wt = ex2(mp.part_stats[slot * 2] - M);
+        }
+        L += l * wt;
+        const int cnt = min(32, nparts - j0);
+        const size_t base = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j0;
+#pragma unroll 4
+        for (int k = 0; k < cnt; ++k) {
+          const float w = __shfl_sync(0xffffffffu, wt, k);
+          const float* po = mp.part_out + (base + k) * D;
+#pragma unroll
+          for (int e = 0; e < PER; ++e) {
+            const int dim = lane + 32 * e;
+            if (dim < D && w != 0.f) acc[e] += po[dim] * w;
+          }
         }
       }
-    }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int dim = lane + 32 * e;
-    if (dim >= D) continue;
-    const size_t oi = static_cast<size_t>(row) * D + dim;
-    if (mp.out_dtype == 0) {
-      reinterpret_cast<float*>(mp.out)[oi] = acc[e] * inv;
-    } else if (mp.out_dtype == 1) {
-      reinterpret_cast<__nv_bfloat16*>(mp.out)[oi] = __float2bfloat16_rn(acc[e] * inv);
-    } else if (mp.out_dtype == 3) {
-      reinterpret_cast<half*>(mp.out)[oi] = __float2half_rn(acc[e] * inv);
-    } else {
-      reinterpret_cast<float*>(mp.out)[oi] = acc[e];
+    for (int e = 0; e < PER; ++e) {
+      const int dim = lane + 32 * e;
+      if (dim >= D) continue;
+      const size_t oi = static_cast<size_t>(row) * D + dim;
+      if (mp.out_dtype == 0) {
+        reinterpret_cast<float*>(mp.out)[oi] = acc[e] * inv;
+      } else if (mp.out_dtype == 1) {
+        reinterpret_cast<__nv_bfloat16*>(mp.out)[oi] = __float2bfloat16_rn(acc[e] * inv);
+      } else if (mp.out_dtype == 3) {
+        reinterpret_cast<half*>(mp.out)[oi] = __float2half_rn(acc[e] * inv);
+      } else {
+        reinterpret_cast<float*>(mp.out)[oi] = acc[e];
+      }
     }
-  }
-  if (mp.out_dtype == 2 && lane == 0) {
-    mp.out_stats[static_cast<size_t>(row) * 2] = L > 0.f ? M : NEG_INF;
-    mp.out_stats[static_cast<size_t>(row) * 2 + 1] = L;
+    if (mp.out_dtype == 2 && lane == 0) {
+      mp.out_stats[static_cast<size_t>(row) * 2] = L > 0.f ? M : NEG_INF;
+      mp.out_stats[static_cast<size_t>(row) * 2 + 1] = L;
+    }
   }
 }
 
@@ -624,12 +765,11 @@ __global__ void __launch_bounds__(128) merge_kernel(const MergeParams mp) {
 
 template <typename T, int D, int BS, int NT>
 static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, long long kv_rows,
-                              cudaStream_t stream) {
+                              int* grid_out, cudaStream_t stream) {
   constexpr int NCW = 4;
   // NCW consumer warps x DEPTH private stages each; ~64 KB of stages per CTA.
   constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
   constexpr int NSTAGE = NCW * DEPTH;
-  static_assert(NSTAGE % NCW == 0, "stages must split evenly over the consumer warps");
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
   auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE>;
   const int smem = C::smem_bytes(p.num_seqs);
@@ -646,6 +786,7 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
   const int grid = sm_count() * occ;
+  if (grid_out) *grid_out = grid;
   Params pp = p;
   pp.dbg_kv_rows = kv_rows;
   kern<<<grid, C::NTHREADS, smem, stream>>>(km, vm, pp);
@@ -654,10 +795,11 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
 
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* kc,
-                          const void* vc, long long kv_rows, int nt, cudaStream_t stream) {
+                          const void* vc, long long kv_rows, int nt, int* grid_out,
+                          cudaStream_t stream) {
 #define FE_CASE(D_, BS_, NT_)                                                     \
   if (head_dim == D_ && block_size == BS_ && nt == NT_)                           \
-    return launch_cfg<T, D_, BS_, NT_>(p, kc, vc, kv_rows, stream);
+    return launch_cfg<T, D_, BS_, NT_>(p, kc, vc, kv_rows, grid_out, stream);
   FE_CASE(128, 16, 1)
   FE_CASE(128, 16, 2)
   FE_CASE(64, 16, 1)
@@ -671,21 +813,37 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
 }
 
 template cudaError_t launch_decode<__nv_bfloat16>(const Params&, int, int, const void*, const void*,
-                                                  long long, int, cudaStream_t);
+                                                  long long, int, int*, cudaStream_t);
 template cudaError_t launch_decode<half>(const Params&, int, int, const void*, const void*,
-                                         long long, int, cudaStream_t);
+                                         long long, int, int*, cudaStream_t);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream) {
   if (mp.rows <= 0) return cudaSuccess;
-  const int grid = (mp.rows + 3) / 4;
+  constexpr int ROWS = 32;
   MergeParams m2 = mp;
   m2.head_dim = head_dim;
   if (head_dim < 1) return cudaErrorInvalidValue;
-  if (head_dim <= 64) merge_kernel<64><<<grid, 128, 0, stream>>>(m2);
-  else if (head_dim <= 128) merge_kernel<128><<<grid, 128, 0, stream>>>(m2);
-  else if (head_dim <= 256) merge_kernel<256><<<grid, 128, 0, stream>>>(m2);
+  const int smem = mp.context_lens ? (mp.num_seqs + 1) * 4 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((mp.rows + ROWS - 1) / ROWS);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void (*kern)(MergeParams) = nullptr;
+  if (head_dim <= 64) kern = merge_kernel<64, ROWS>;
+  else if (head_dim <= 128) kern = merge_kernel<128, ROWS>;
+  else if (head_dim <= 256) kern = merge_kernel<256, ROWS>;
   else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  if (smem > 48 * 1024) {
+    cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, m2);
 }
 
 }  // namespace paged

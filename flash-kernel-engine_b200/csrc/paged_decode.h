@@ -19,8 +19,9 @@ struct Params {
   int num_phys_blocks;     // 0 = unknown (no range check)
   int head_chunks;         // ceil(G / (8 * NT))
   int tok_begin, tok_end;  // token window [tok_begin, tok_end) of every sequence
-  int pages_per_split;
+  int pages_per_split;     // unit mode: pages per segment; flat mode: minimum chunk
   int max_splits;          // partial slots per (seq, head)
+  int flat;                // 1: flat (stream-K) chunking, 0: unit mode
   int direct_final;        // 1: sequences with one split write `out` directly
   float scale_log2;        // softmax scale * log2(e)
   unsigned* err;           // device error word
@@ -33,11 +34,13 @@ struct MergeParams {
   int rows;
   int ranks;
   int parts_per_rank;      // slot stride per (rank, row)
-  // ctx mode (context_lens != nullptr): number of valid slots from the split rule
+  // ctx mode (context_lens != nullptr): the valid slots of a row follow from the
+  // decode kernel's flat chunking, rebuilt from the same inputs
   const int* context_lens;
-  int heads;
-  int tok_begin, tok_end, block_size, pages_per_split;
-  int skip_single;         // rows with <= 1 split were finalised by the decode kernel
+  int num_seqs, heads, kv_heads, heads_per_chunk, head_chunks, groups;
+  int tok_begin, tok_end, block_size;
+  int decode_ctas, chunk_min;
+  int skip_single;         // rows with one slot were finalised by the decode kernel
   void* out;
   float* out_stats;
   int out_dtype;           // 0 f32 final, 1 bf16 final, 2 merged partial, 3 fp16 final
@@ -50,9 +53,12 @@ inline int pages_per_split_for(int max_pages, int splits) {
   return (max_pages + splits - 1) / splits;
 }
 
+// Launches the decode kernel; *grid_out receives its CTA count (needed by the
+// ctx-mode merge to rebuild the flat chunking).
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* k_cache,
-                          const void* v_cache, long long kv_rows, int nt, cudaStream_t stream);
+                          const void* v_cache, long long kv_rows, int nt, int* grid_out,
+                          cudaStream_t stream);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
 

@@ -131,3 +131,21 @@ def test_config3_shape_parity():
                                 p["context_lens"])
     out = _run(p, torch.bfloat16)
     assert_bf16_close(out, ref)
+
+
+def test_config3_full_batch_split_sweep():
+    """All 64 sequences of BASELINE config 3 (seed 0) against the oracle, through the
+    single-pass kernel and the split-KV kernel at several split counts (the flat
+    chunking then cuts sequences at different places)."""
+    import flash_engine
+    lens = O.config3_context_lens(0)
+    p = O.make_paged_problem(0, 64, 32, 8, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+    bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
+    for version, splits in [("v1", None), ("v2", 2), ("v2", 3), ("v2", 9), ("v2", 64)]:
+        out = flash_engine.paged_attention(q, kc, vc, bt, cl, 16, version=version,
+                                           num_splits=splits, max_context_len=int(lens.max()))
+        assert flash_engine.device_errors() == 0
+        assert_bf16_close(host(out), ref)
