@@ -699,42 +699,56 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
       nparts = mp.parts_per_rank;
       ranks = mp.ranks;
     }
-    // pass 1: global max
+    // Stats of every (rank, part) slot of the row, 32 slots per pass; the O rows of
+    // a pass are loaded together so each pass costs about two memory round trips.
+    const int total = ranks * nparts;
+    const size_t rstride = static_cast<size_t>(mp.rows) * mp.parts_per_rank;
+    const size_t rbase = static_cast<size_t>(row) * mp.parts_per_rank;
     float M = NEG_INF;
-    for (int rk = 0; rk < ranks; ++rk)
-      for (int j = lane; j < nparts; j += 32) {
-        const size_t slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
-        const float l = mp.part_stats[slot * 2 + 1];
-        if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
-      }
+    for (int j = lane; j < total; j += 32) {
+      const int rk = j / nparts, pj = j - rk * nparts;
+      const size_t slot = rk * rstride + rbase + pj;
+      const float l = mp.part_stats[slot * 2 + 1];
+      if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float L = 0.f, acc[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) acc[k] = 0.f;
-    for (int rk = 0; rk < ranks; ++rk)
-      for (int j0 = 0; j0 < nparts; j0 += 32) {
-        const int j = j0 + lane;
-        float wt = 0.f, l = 0.f;
-        if (j < nparts) {
-          const size_t slot = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j;
-          l = mp.part_stats[slot * 2 + 1];
-          if (l > 0.f) wt = ex2(mp.part_stats[slot * 2] - M);
-        }
-        L += l * wt;
-        const int cnt = min(32, nparts - j0);
-        const size_t base = (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + j0;
-#pragma unroll 4
-        for (int k = 0; k < cnt; ++k) {
-          const float w = __shfl_sync(0xffffffffu, wt, k);
-          const float* po = mp.part_out + (base + k) * D;
+    for (int j0 = 0; j0 < total; j0 += 32) {
+      const int j = j0 + lane;
+      float wt = 0.f, l = 0.f;
+      size_t myslot = 0;
+      if (j < total) {
+        const int rk = j / nparts, pj = j - rk * nparts;
+        myslot = rk * rstride + rbase + pj;
+        l = mp.part_stats[myslot * 2 + 1];
+        if (l > 0.f) wt = ex2(mp.part_stats[myslot * 2] - M);
+      }
+      L += l * wt;
+      const int cnt = min(32, total - j0);
+      for (int k0 = 0; k0 < cnt; k0 += 8) {
+        float v[8][PER];
+        float w8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int kk = min(k0 + k, cnt - 1);
+          w8[k] = __shfl_sync(0xffffffffu, wt, kk);
+          const size_t sl = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(myslot), kk);
+          const float* po = mp.part_out + sl * D;
 #pragma unroll
           for (int e = 0; e < PER; ++e) {
             const int dim = lane + 32 * e;
-            if (dim < D && w != 0.f) acc[e] += po[dim] * w;
+            v[k][e] = (k0 + k < cnt && dim < D && w8[k] != 0.f) ? po[dim] : 0.f;
           }
         }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+          for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * (k0 + k < cnt ? w8[k] : 0.f);
       }
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
     const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -819,7 +833,7 @@ template cudaError_t launch_decode<half>(const Params&, int, int, const void*, c
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream) {
   if (mp.rows <= 0) return cudaSuccess;
-  constexpr int ROWS = 32;
+  constexpr int ROWS = 8;  // one row per warp
   MergeParams m2 = mp;
   m2.head_dim = head_dim;
   if (head_dim < 1) return cudaErrorInvalidValue;
