@@ -27,6 +27,13 @@ cudaError_t encode_tma_2d_b16(CUtensorMap* map, const void* base, bool bf16, uin
                               uint64_t rows, uint64_t row_stride_elems, uint32_t box_cols,
                               uint32_t box_rows, bool swizzle128 = true);
 
+// 3-D tiled TMA descriptor, 128-byte swizzle, over a contiguous [outer, rows, cols]
+// tensor of 2-byte elements; box = {box_cols, box_rows, 1}. Rows past `rows` of an
+// outer index read as zeros (they do not spill into the next outer slice).
+cudaError_t encode_tma_3d_b16(CUtensorMap* map, const void* base, bool bf16, uint64_t cols,
+                              uint64_t rows, uint64_t outer, uint32_t box_cols,
+                              uint32_t box_rows);
+
 // Calls cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per
 // (function, device).
 cudaError_t ensure_smem_optin(const void* func, int bytes);

@@ -1,12 +1,429 @@
-// tcgen05 FA2 prefill (placeholder until the kernel lands).
+// FA2 online-softmax prefill forward on the 5th-generation tensor core (sm_100a).
+//
+// O = softmax(Q K^T * scale [+ causal mask]) V for bf16 / fp16 Q, K, V, O of shape
+// [B, H, N|M, d] with fp32 accumulation -- the computation of the reference's
+// launch_flash_attention_forward_fp16 (src/flash_attention.cu:350-524), causal mask
+// top-left aligned (query row i sees keys j <= i, src/flash_attention.cu:224).
+//
+// One CTA (3 warpgroups) computes two 128-row query tiles (Q0, Q1) of one
+// (batch, head). It is launched at 168 registers per thread; setmaxnreg then
+// moves registers from warpgroup 2 (56 each) to the softmax warpgroups (224
+// each): 384 x 168 = 256 x 224 + 128 x 56.
+//  * warp 8 (TMA): loads Q0/Q1 once, then K_j and V_j tiles (128 keys x d) into
+//    two-stage rings with 3-D TMA (128-byte swizzle; out-of-range rows zero-fill).
+//  * warp 9 (MMA): allocates 512 tensor-memory columns
+//    [S0 | S1 | O0 | O1] and, from one thread, issues
+//      S_t = Q_t K_j^T   (tcgen05.mma, A and B from shared memory)
+//      O_t += P_t V_j    (tcgen05.mma, A = P_t from tensor memory, B = V_j)
+//    in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ..., so the tensor
+//    core works on one tile while the other tile's softmax runs.
+//  * warps 0-3 / 4-7 (softmax for Q0 / Q1): thread i owns row i of its tile. It
+//    reads its S row from tensor memory, applies mask and scale, and updates the
+//    running max m and sum l in the log2 domain. It writes P = 2^(s - m) as 16-bit
+//    values over the first half of the S columns. O is rescaled in tensor memory
+//    only when the row max grows by more than 2^8 (the stale max is exact for the
+//    final O / l). At the end it reads O, divides by l and stores the row.
+// Every wait is bounded (mbar_wait); on a timeout the CTA records an error, drains
+// its TMA and MMA work, frees tensor memory and exits.
+#include <limits.h>
+
+#include <type_traits>
+
+#include "internal.h"
 #include "prefill.h"
+#include "ptx.cuh"
+#include "tcgen05.cuh"
 
 namespace fe {
 namespace prefill {
 
-cudaError_t launch_prefill(const void*, const void*, const void*, void*, int, int, int, int, int,
-                           int, float, bool, cudaStream_t) {
-  return cudaErrorNotSupported;
+constexpr float NEG_INF = -__builtin_huge_valf();
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
+
+template <int D>
+struct PCfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int HALVES = D / 64;
+  static constexpr int TILE_BYTES = BM * D * 2;  // one 128-row tile of Q, K or V
+  static constexpr int HALF_BYTES = BM * 128;    // one 64-column swizzle atom column
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int NBARS = 16;
+  static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static constexpr int NTHREADS = 384;
+};
+
+struct PParams {
+  void* out;
+  int N, M, BH;
+  int causal;
+  float scale_log2;
+  unsigned* err;
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  return pack_bf16x2(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<half>(float lo, float hi) {
+  return pack_f16x2(lo, hi);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const PParams p) {
+  using C = PCfg<D>;
+  constexpr int BM = C::BM, BN = C::BN, HALVES = C::HALVES;
+  constexpr int TILE = C::TILE_BYTES, HALF = C::HALF_BYTES;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2] per query tile
+  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* o_done = bars + 13;  // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int npairs = (p.N + 2 * BM - 1) / (2 * BM);
+  const int pair = npairs - 1 - static_cast<int>(blockIdx.x);  // longest causal rows first
+  int m0[2], nkv[2];
+  const int kv_tiles = (p.M + BN - 1) / BN;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    m0[t] = pair * 2 * BM + t * BM;
+    if (m0[t] >= p.N) {
+      nkv[t] = 0;
+    } else if (p.causal) {
+      const int last_row = min(p.N - 1, m0[t] + BM - 1);
+      const int last_key = min(p.M - 1, last_row);
+      nkv[t] = last_key / BN + 1;
+    } else {
+      nkv[t] = kv_tiles;
+    }
+  }
+  const int nmax = max(nkv[0], nkv[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tc::tmem_alloc<512>(tmem_slot);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+   if (warp == 8) {
+    // ========================================================= TMA producer
+    if (lane == 0 && nmax > 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const uint64_t pol_keep = l2_policy_evict_last();   // K/V are re-read by other CTAs
+      const uint64_t pol_once = l2_policy_evict_first();  // Q is read once
+      int nq = (nkv[0] > 0) + (nkv[1] > 0);
+      mbar_arrive_expect_tx(q_full, nq * TILE);
+      for (int t = 0; t < 2; ++t) {
+        if (nkv[t] == 0) continue;
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::Q_OFF + t * TILE + h * HALF, &qmap, h * 64, m0[t], bh, q_full,
+                      pol_once);
+      }
+      bool ok = true;
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < nmax && ok; ++j) {
+        const int st = j & 1, rnd = j >> 1;
+        if (rnd > 0 && !mbar_wait(&k_empty[st], (rnd - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[st], TILE);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::K_OFF + st * TILE + h * HALF, &kmap, h * 64, j * BN, bh,
+                      &k_full[st], pol_keep);
+        ++issued_k;
+        if (rnd > 0 && !mbar_wait(&v_empty[st], (rnd - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[st], TILE);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::V_OFF + st * TILE + h * HALF, &vmap, h * 64, j * BN, bh,
+                      &v_full[st], pol_keep);
+        ++issued_v;
+      }
+      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: every bulk copy issued here has landed before the CTA can exit.
+      mbar_wait(q_full, 0);
+      for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1);
+      for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
+    }
+  } else if (warp == 9) {
+    // ========================================================= MMA issuer
+    if (lane == 0 && nmax > 0) {
+      constexpr uint32_t idesc_qk = tc::idesc_f16(kBF16, BM, BN, false, false);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(kBF16, BM, D, false, true);
+      const uint32_t sbase = smem_u32(smem);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qa = sbase + C::Q_OFF + t * TILE;
+        const uint32_t kb = sbase + C::K_OFF + (j & 1) * TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+          tc::mma_ss(tmem + t * BN, tc::smem_desc_sw128(qa + off, 16, 1024),
+                     tc::smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+        }
+        tc::commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = sbase + C::V_OFF + (j & 1) * TILE;
+        const uint32_t ptm = tmem + t * BN;              // P_t over the S_t columns
+        const uint32_t otm = tmem + 2 * BN + t * D;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          tc::mma_ts(otm, ptm + kk * 8, tc::smem_desc_sw128(vb + kk * 16 * 128, HALF, 1024),
+                     idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_full, 0);
+      // prologue: S0(0), S1(0)
+      if (ok) ok = mbar_wait(&k_full[0], 0);
+      if (ok) {
+        tc::fence_after_sync();
+        if (nkv[0] > 0) issue_s(0, 0);
+        if (nkv[1] > 0) issue_s(1, 0);
+        tc::commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nmax && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        const bool next_k = j + 1 < nmax;
+        bool k_ready = false;
+        if (j < nkv[0]) {
+          if (!mbar_wait(&p_full[0], j & 1)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_pv(0, j);
+          if (j + 1 < nkv[0]) {
+            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            k_ready = true;
+            issue_s(0, j + 1);
+          }
+        }
+        if (j < nkv[1]) {
+          if (!mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_pv(1, j);
+          if (j + 1 < nkv[1]) {
+            if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            k_ready = true;
+            issue_s(1, j + 1);
+          }
+        }
+        if (next_k) {
+          if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+          tc::commit(&k_empty[(j + 1) & 1]);
+        }
+        tc::commit(&v_empty[st]);
+      }
+      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: all MMAs issued by this thread have completed.
+      tc::commit(drain);
+      mbar_wait(drain, 0);
+    }
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+    // ========================================================= softmax warpgroups
+    const int t = warp >> 2;            // query tile of this warpgroup
+    const int qw = warp & 3;            // lane quarter of tensor memory
+    const int row = qw * 32 + lane;     // row within the tile
+    const int r = m0[t] + row;          // query row
+    const uint32_t lane_off = static_cast<uint32_t>(qw * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * BN;
+    const uint32_t tO = tmem + lane_off + 2 * BN + t * D;
+    const float sl = p.scale_log2;
+    float m_run = NEG_INF, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv[t] && ok; ++j) {
+      const bool got = mbar_wait(&s_full[t], j & 1);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      tc::fence_after_sync();
+      float x[BN];
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 32; ++c4) {
+        uint32_t u[32];
+        tc::ld32(tS + c4 * 32, u);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = __uint_as_float(u[i]);
+      }
+      const int c0 = j * BN;
+      const bool need_mask = (p.causal && c0 + BN - 1 > m0[t]) || c0 + BN > p.M;
+      float mx = NEG_INF;
+      if (need_mask) {
+        const int lim = p.causal ? min(r + 1, p.M) : p.M;  // valid keys: c < lim
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          x[i] = (c0 + i < lim) ? x[i] * sl : NEG_INF;
+          mx = fmaxf(mx, x[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          x[i] *= sl;
+          mx = fmaxf(mx, x[i]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new > m_run + kRescaleThreshold;  // also true while m_run = -inf
+      const float m_use = need ? m_new : m_run;
+      const float mu = m_use == NEG_INF ? 0.f : m_use;
+      const float corr = need ? ex2(m_run - mu) : 1.f;
+      float sum = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < BN / 64; ++c4) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = ex2(x[c4 * 64 + 2 * i] - mu);
+          const float b = ex2(x[c4 * 64 + 2 * i + 1] - mu);
+          sum += a + b;
+          pk[i] = pack2<T>(a, b);
+        }
+        tc::st32(tS + c4 * 32, pk);
+      }
+      l_run = l_run * corr + sum;
+      m_run = m_use;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_t must hold P V of tile j-1 before it is rescaled.
+        const bool got_o = mbar_wait(&o_done[t], (j - 1) & 1);
+        if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c4 = 0; c4 < D / 32; ++c4) {
+          uint32_t u[32];
+          tc::ld32(tO + c4 * 32, u);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+          tc::st32(tO + c4 * 32, u);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&p_full[t]);
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
+    } else if (nkv[t] > 0) {
+      const bool got = mbar_wait(&o_done[t], (nkv[t] - 1) & 1);
+      if (__all_sync(0xffffffffu, got)) {
+        tc::fence_after_sync();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + (static_cast<size_t>(bh) * p.N + r) * D;
+#pragma unroll
+        for (int c4 = 0; c4 < D / 32; ++c4) {
+          uint32_t u[32];
+          tc::ld32(tO + c4 * 32, u);
+          tc::wait_ld();
+          if (r < p.N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 v;
+              v.x = pack2<T>(__uint_as_float(u[i + 0]) * inv, __uint_as_float(u[i + 1]) * inv);
+              v.y = pack2<T>(__uint_as_float(u[i + 2]) * inv, __uint_as_float(u[i + 3]) * inv);
+              v.z = pack2<T>(__uint_as_float(u[i + 4]) * inv, __uint_as_float(u[i + 5]) * inv);
+              v.w = pack2<T>(__uint_as_float(u[i + 6]) * inv, __uint_as_float(u[i + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + c4 * 32 + i) = v;
+            }
+          }
+        }
+      } else if (lane == 0) {
+        atomicOr(p.err, kErrWaitTimeout);
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 9) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc<512>(tmem);
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o, int B, int H,
+                            int N, int M, int causal, float scale, cudaStream_t st) {
+  using C = PCfg<D>;
+  auto kern = fa_prefill_kernel<T, D>;
+  cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
+  if (e != cudaSuccess) return e;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const long long BH = static_cast<long long>(B) * H;
+  CUtensorMap qm, km, vm;
+  e = encode_tma_3d_b16(&qm, q, bf16, D, N, BH, 64, 128);
+  if (e != cudaSuccess) return e;
+  e = encode_tma_3d_b16(&km, k, bf16, D, M, BH, 64, 128);
+  if (e != cudaSuccess) return e;
+  e = encode_tma_3d_b16(&vm, v, bf16, D, M, BH, 64, 128);
+  if (e != cudaSuccess) return e;
+  PParams p;
+  p.out = o;
+  p.N = N;
+  p.M = M;
+  p.BH = static_cast<int>(BH);
+  p.causal = causal;
+  p.scale_log2 = scale * kLog2e;
+  p.err = device_error_word();
+  if (!p.err) return cudaErrorInitializationError;
+  dim3 grid((N + 255) / 256, static_cast<unsigned>(BH));
+  kern<<<grid, C::NTHREADS, C::SMEM, st>>>(qm, km, vm, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o, int B, int H,
+                           int N, int M, int d, int causal, float scale, bool is_bf16,
+                           cudaStream_t stream) {
+  if (!(d == 64 || d == 128)) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15)
+    return cudaErrorInvalidValue;
+  if (static_cast<long long>(B) * H > 65535) return cudaErrorInvalidValue;
+  if (is_bf16) {
+    if (d == 128) return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, causal, scale, stream);
+    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, causal, scale, stream);
+  }
+  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, causal, scale, stream);
+  return launch_d<half, 64>(q, k, v, o, B, H, N, M, causal, scale, stream);
 }
 
 }  // namespace prefill

@@ -44,3 +44,50 @@ def test_fp32_shapes(causal, N, M, d):
     ref = O.flash_attention(q, k, v, causal)
     out = flash_engine.flash_attention(cuda(q), cuda(k), cuda(v), causal)
     assert_fp32_close(host(out), ref)
+
+
+def _bf16_case(B, H, N, M, d, causal, seed, dtype=torch.bfloat16):
+    import flash_engine
+    rng = np.random.default_rng(seed)
+    q = O.bf16_round(rng.standard_normal((B, H, N, d), dtype=np.float32))
+    k = O.bf16_round(rng.standard_normal((B, H, M, d), dtype=np.float32))
+    v = O.bf16_round(rng.standard_normal((B, H, M, d), dtype=np.float32))
+    if dtype == torch.float16:
+        q, k, v = (x.astype(np.float16).astype(np.float32) for x in (q, k, v))
+    ref = O.flash_attention_sliced(q, k, v, causal)
+    out = flash_engine.flash_attention(cuda(q, dtype), cuda(k, dtype), cuda(v, dtype), causal)
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    return host(out), ref
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("N,M", [(128, 128), (256, 256), (300, 300), (1, 1), (77, 200),
+                                 (200, 77), (512, 384)])
+def test_bf16_tcgen05_shapes(d, causal, N, M):
+    out, ref = _bf16_case(1, 2, N, M, d, causal, N * 7 + M + d)
+    assert_bf16_close(out, ref)
+
+
+def test_fp16_tcgen05():
+    out, ref = _bf16_case(2, 2, 384, 384, 128, True, 3, torch.float16)
+    assert_bf16_close(out, ref, atol=5e-3)
+
+
+def test_bf16_config2_shape_slice():
+    """BASELINE config 2 shape (causal, seq 4096, d 128) on 2 heads: the oracle runs
+    per (b, h) slice."""
+    out, ref = _bf16_case(1, 2, 4096, 4096, 128, True, 42)
+    assert_bf16_close(out, ref)
+
+
+def test_bf16_reference_scale_inputs(golden):
+    """The reference test recipe (N(0,1) * 0.1 inputs), bf16-rounded."""
+    import flash_engine
+    g = golden("attn_d64_causal")
+    q, k, v = (O.bf16_round(g[x]) for x in ("q", "k", "v"))
+    ref = O.flash_attention(q, k, v, True)
+    out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
+                                       cuda(v, torch.bfloat16), True)
+    assert_bf16_close(host(out), ref)
