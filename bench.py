@@ -413,13 +413,101 @@ def bench_decode_reference(a, ws, rank):
     }
 
 
+# --------------------------------------------------------------------------- prefill workload
+CFG2 = dict(batch=4, heads=32, seq=4096, head_dim=128, causal=True)
+
+
+def prefill_flops(B, H, N, d, causal=True):
+    """4*B*H*N^2*d, halved for causal: the reference's convention
+    (benchmarks/bench_attention.cu:48-49)."""
+    f = 4.0 * B * H * N * N * d
+    return f / 2 if causal else f
+
+
+def bench_prefill_ours(a, ws, rank, local, init_pg=True, steps=None, warmup=None):
+    import torch
+    import flash_engine
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if init_pg:
+        _init_pg(ws, "nccl")
+    c = CFG2
+    B, H, N, d = c["batch"], c["heads"], c["seq"], c["head_dim"]
+    if H % ws:
+        raise SystemExit(f"--gpus {ws} must divide the {H} heads")
+    h_l = H // ws
+    steps = a.steps if steps is None else steps
+    warmup = a.warmup if warmup is None else warmup
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + a.seed * 31 + rank)
+    q, k, v = (torch.randn((B, h_l, N, d), generator=g, device=dev, dtype=torch.float32)
+               .to(torch.bfloat16) for _ in range(3))
+    out = torch.empty_like(q)
+
+    def step():
+        return flash_engine.flash_attention(q, k, v, True)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(ws, dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    _barrier(ws, dev)
+    sampler.stop()
+    assert flash_engine.device_errors() == 0
+    ms_rank = e0.elapsed_time(e1) / steps
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    flops_rank = prefill_flops(B, h_l, N, d)
+    total = prefill_flops(B, H, N, d)
+    tflops = total / (ms * 1e-3) / 1e12
+    achieved = flops_rank / (ms_rank * 1e-3) / 1e12
+    _, peak, src = _peaks()
+    return {
+        "metric": "FA2 prefill TFLOP/s (config 2: bf16 causal [4, 32, 4096, 128])",
+        "value": round(tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "flops_per_step": total,
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_source": src + " bf16 burst",
+                     "kernel": "fa_prefill_kernel<bf16,128>"},
+        "clocks": sampler.summary(t0, t1),
+        "gpu_launches": steps,
+    }
+
+
 def main():
     a = _args()
     ws, rank, local = _dist()
-    if a.workload != "decode":
-        raise SystemExit("prefill workload: see --workload decode (prefill bench pending)")
     if a.impl == "reference":
         res = bench_decode_reference(a, ws, rank)
+    elif a.workload == "prefill":
+        pr = bench_prefill_ours(a, ws, rank, local)
+        res = None
+        if rank == 0:
+            res = dict(pr)
+            res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
+                        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 Q/K/V)",
+                        "config": {"workload": "fa2_prefill_config2", "batch": 4, "heads": 32,
+                                   "seq_len": 4096, "head_dim": 128, "causal": True,
+                                   "parallelism": f"head shard x{ws}",
+                                   "l2": "inputs 384 MiB > L2"}})
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
     else:
         res = bench_decode_ours(a, ws, rank, local)
     if res is not None and rank == 0:
