@@ -1,0 +1,104 @@
+"""Worker bodies for the multi-process (gloo, CPU) tests of flash_engine.sharding.
+Run by torch.multiprocessing with the spawn start method."""
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+for p in (ROOT, os.path.join(ROOT, "flash-kernel-engine_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def _init(rank, world, port, timeout_s=60):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+    return dist
+
+
+def _problem():
+    from oracle import attention_oracle as O
+    lens = [0, 7, 64, 250, 1000, 1017]
+    return O.make_paged_problem(12, len(lens), 16, 4, 64, lens, bf16=False)
+
+
+def kv_range_worker(rank, world, port, result_path):
+    import torch
+    from flash_engine import sharding
+    from oracle import attention_oracle as O
+    dist = _init(rank, world, port)
+    p = _problem()
+    M = int(max(p["context_lens"]))
+    tb, te = sharding.kv_range_bounds(M, world, rank, 16)
+    o, m, l = O.kv_range_partials(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                  p["context_lens"], tb, te)
+    S, H, d = p["q"].shape
+    lo = torch.from_numpy(o.reshape(S * H, d))
+    ls = torch.from_numpy(np.stack([m.reshape(-1), l.reshape(-1)], 1))
+
+    def merge(go, gs, w):
+        outs = [go[i].numpy() for i in range(w)]
+        ms = [gs[i, :, 0].numpy() for i in range(w)]
+        ls_ = [gs[i, :, 1].numpy() for i in range(w)]
+        return O.lse_merge(outs, ms, ls_).reshape(S, H, d)
+
+    out = sharding.allgather_merge(lo, ls, merge)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    err = float(np.abs(out - ref).max())
+    dist.barrier()
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((tb, te, err)))
+
+
+def head_shard_worker(rank, world, port, result_path):
+    import torch
+    from flash_engine import sharding
+    from oracle import attention_oracle as O
+    dist = _init(rank, world, port)
+    p = _problem()
+    S, H, d = p["q"].shape
+    Hkv = p["k_cache"].shape[1]
+    kv_lo, kv_hi, q_lo, q_hi = sharding.head_shard_bounds(H, Hkv, world, rank)
+    part = O.paged_attention_gqa(p["q"][:, q_lo:q_hi], p["k_cache"][:, kv_lo:kv_hi],
+                                 p["v_cache"][:, kv_lo:kv_hi], p["block_tables"],
+                                 p["context_lens"])
+    t = torch.from_numpy(np.ascontiguousarray(part))
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    full = torch.cat(parts, dim=1).numpy()
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    err = float(np.abs(full - ref).max())
+    dist.barrier()
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((q_lo, q_hi, err)))
+
+
+def dropout_worker(rank, world, port, result_path):
+    """Rank 1 leaves before the exchange (between steps); rank 0 must get an error
+    from its collective within the short process-group timeout, not hang."""
+    import time
+
+    import torch
+    from flash_engine import sharding
+    dist = _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        os._exit(0)  # leaves without joining the all-gather
+    t0 = time.time()
+    status = "no-error"
+    try:
+        sharding.allgather_merge(torch.zeros(4, 8), torch.zeros(4, 2),
+                                 lambda go, gs, w: go.sum(0))
+    except Exception as e:  # noqa: BLE001 - any collective error is the expected outcome
+        status = type(e).__name__
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((status, time.time() - t0)))
+    os._exit(0)
