@@ -1,26 +1,31 @@
 #!/usr/bin/env python
-"""Benchmark of the inference-attention hot path on B200.
+"""Benchmark of the inference-attention hot path on B200 (one process per GPU).
 
-Default workload: paged decode, bf16, batch 64, 32 query /
-8 KV heads, head_dim 128, block size 16, context lengths uniform in [512, 4096]
-(seed 0), physical blocks a random permutation of the pool. One step = one
-``flash_engine.paged_attention`` call (split-KV kernel + log-sum-exp merge) over
-the whole batch. With N GPUs (torchrun, one rank per GPU) the KV heads are
+Headline (``value``): BASELINE config 3, paged decode bf16 -- batch 64, 32 query /
+8 KV heads, head_dim 128, block size 16, context lengths U[512, 4096] (seed 0),
+physical blocks a random permutation of the pool. One step = one
+``flash_engine.paged_attention`` call (split-KV kernel + log-sum-exp merge) over the
+whole batch, replayed from a CUDA graph. With N GPUs (torchrun) the KV heads are
 sharded: rank r owns KV heads [r*8/N, (r+1)*8/N) and their query heads; no
-communication is needed (strong scaling, total work fixed).
+communication (strong scaling). Metric: KV GB/s = algorithmic bytes per step (K and
+V rows of every context token and KV head, q, out, block-table entries, context
+lengths) / step time, whole job; ``roofline`` against the measured HBM copy peak.
 
-Metric: paged-decode KV bandwidth in GB/s = algorithmic bytes per step (K and V
-rows of every context token of every KV head, plus q, out, block-table entries and
-context lengths) / step time, whole job. ``--workload prefill`` measures BASELINE
-config 2 (FA2 bf16 causal [4, 32, 4096, 128], heads sharded over ranks) in TFLOP/s.
-
-``--impl reference`` times the reference's CPU implementation of the same path
-(the NumPy port in oracle/, all host threads) on a bounded sample per step.
+``secondary`` reports the other BASELINE configs measured in the same run:
+  config 2 -- FA2 prefill bf16 causal [4, 32, 4096, 128], heads sharded (TFLOP/s);
+  config 4 -- split-KV decode, 131072-token context, KV range sharded over the
+              ranks with an NCCL all-gather of the (O, m, l) partials (KV GB/s);
+  config 5 -- serving-mix paged decode, 256 seqs, 64q/8kv, lognormal contexts,
+              KV-head sharded (KV GB/s).
+``--workload`` makes any of them the headline instead. ``--impl reference`` times the
+reference's CPU implementation of the path (the NumPy port in oracle/, all host
+threads) on a bounded sample per step.
 """
 
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -28,6 +33,7 @@ import statistics
 import sys
 import threading
 import time
+import traceback
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "flash-kernel-engine_b200")
@@ -38,15 +44,17 @@ for _p in (ROOT, PKG):
 import numpy as np  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
+WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32")
 
 
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=WORKLOADS, default="decode")
+    ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args()
@@ -56,18 +64,30 @@ def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 def _traffic(name):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
     try:
         with open(os.path.join(ROOT, "profiles", name)) as f:
-            return json.load(f)
+            return json.load(f).get("dram_bytes_per_launch")
     except Exception:
         return None
+
+
+def _cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
 
 
 # --------------------------------------------------------------------------- clocks
@@ -75,10 +95,9 @@ class ClockSampler:
     """Samples SM clock and throttle reasons through NVML (read-only) every 5 ms."""
 
     REASONS = {
-        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
-        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
-        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
-        0x100: "display_clock_setting",
+        0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
     def __init__(self, device_index: int):
@@ -110,6 +129,7 @@ class ClockSampler:
         if self.ok:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
+        return self
 
     def stop(self):
         if self.ok:
@@ -127,25 +147,15 @@ class ClockSampler:
         bits = 0
         for s in inside:
             bits |= s[2]
-        reasons = [n for b, n in self.REASONS.items() if bits & b and b != 0x1]
+        reasons = [n for b, n in self.REASONS.items() if bits & b]
         return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons,
                 "samples": len(inside), "window": window}
 
 
 # --------------------------------------------------------------------------- distributed
 def _dist():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
-
-
-def _init_pg(ws, backend):
-    if ws > 1:
-        import datetime
-        import torch.distributed as dist
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
 def _max_over_ranks(x, ws, device):
@@ -158,49 +168,77 @@ def _max_over_ranks(x, ws, device):
     return float(t.item())
 
 
-def _barrier(ws, device=None):
+def _barrier(ws, device):
     if ws > 1:
         import torch.distributed as dist
-        if device is not None:
-            dist.barrier(device_ids=[device.index])
-        else:
-            dist.barrier()
+        dist.barrier(device_ids=[device.index])
 
 
-# --------------------------------------------------------------------------- decode workload
-CFG3 = dict(num_seqs=64, num_heads=32, num_kv_heads=8, head_dim=128, block_size=16)
+def _time_steps(step, steps, warmup, ws, dev):
+    """Warm up, then time `steps` back-to-back calls with CUDA events on the current
+    stream between barriers; returns (ms_per_step on this rank, t0, t1)."""
+    import torch
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    _barrier(ws, dev)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(st)
+    for i in range(steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    _barrier(ws, dev)
+    return e0.elapsed_time(e1) / steps, t0, t1
+
+
+# --------------------------------------------------------------------------- paged decode
+CFG3 = dict(name="paged_decode_config3", num_seqs=64, num_heads=32, num_kv_heads=8,
+            head_dim=128, block_size=16,
+            metric="paged decode KV GB/s (config 3: B64, 32q/8kv, d128, bs16, ctx U[512,4096])")
+CFG5 = dict(name="paged_decode_config5_serving", num_seqs=256, num_heads=64, num_kv_heads=8,
+            head_dim=128, block_size=16,
+            metric="serving-mix paged decode KV GB/s (config 5: B256, 64q/8kv, d128, bs16, "
+                   "ctx lognormal(med 1024, sigma 1) in [16, 32768])")
+
+
+def _lens(cfg, seed):
+    from oracle import attention_oracle as O
+    if cfg is CFG5:
+        return O.config5_context_lens(seed)
+    return O.config3_context_lens(seed)
 
 
 def decode_bytes(lens, Hkv, H, d, bs, elt=2):
     """Algorithmic bytes of one decode call: K+V rows of every context token of
     every KV head, plus q and out, block-table entries and context lengths."""
-    tokens = int(np.sum(np.maximum(lens, 0)))
-    pages = int(np.sum((np.maximum(lens, 0) + bs - 1) // bs))
+    lens = np.maximum(np.asarray(lens), 0)
+    tokens = int(lens.sum())
+    pages = int(((lens + bs - 1) // bs).sum())
     S = len(lens)
     return tokens * Hkv * d * 2 * elt + 2 * S * H * d * elt + pages * 4 + S * 4
 
 
-def bench_decode_ours(a, ws, rank, local):
+def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     import torch
     import flash_engine
-    from oracle.attention_oracle import config3_context_lens
 
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    _init_pg(ws, "nccl")
-    c = CFG3
-    S, H, Hkv, d, bs = c["num_seqs"], c["num_heads"], c["num_kv_heads"], c["head_dim"], c["block_size"]
+    S, H, Hkv, d, bs = (cfg[k] for k in ("num_seqs", "num_heads", "num_kv_heads", "head_dim",
+                                         "block_size"))
     if Hkv % ws:
-        raise SystemExit(f"--gpus {ws} must divide the {Hkv} KV heads")
+        raise ValueError(f"{ws} ranks cannot split {Hkv} KV heads")
     hkv_l, h_l = Hkv // ws, H // ws
-    lens = config3_context_lens(a.seed)
+    lens = _lens(cfg, a.seed)
     nblk = (lens + bs - 1) // bs
     pool = int(nblk.sum())
-    step_bytes_rank = decode_bytes(lens, hkv_l, h_l, d, bs)
-    # Disjoint block sets rotated between steps so that consecutive steps never
-    # hit L2 (>= 4 x L2 of distinct KV bytes in flight over the rotation).
-    kv_bytes_set = pool * hkv_l * bs * d * 2 * 2
-    R = max(1, math.ceil(4 * L2_BYTES / kv_bytes_set))
+    # Disjoint block sets rotated between steps: >= 4 x L2 of distinct KV over a cycle.
+    kv_set = pool * hkv_l * bs * d * 2 * 2
+    R = max(1, math.ceil(4 * L2_BYTES / kv_set))
     rng = np.random.default_rng(a.seed + 1)
     perm = rng.permutation(pool * R).astype(np.int32)
     maxb = int(nblk.max())
@@ -214,142 +252,109 @@ def bench_decode_ours(a, ws, rank, local):
         bts.append(torch.from_numpy(bt).to(dev))
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + a.seed * 17 + rank)
-    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    q = torch.randn((S, h_l, d), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn((S, h_l, d), generator=g, device=dev).to(torch.bfloat16)
     lens_t = torch.from_numpy(lens).to(dev)
     out = torch.empty_like(q)
     max_ctx = int(lens.max())
     splits = flash_engine.paged_attention_splits(S, h_l, hkv_l, d, bs, max_ctx)
-    ws_out = torch.empty(S * h_l * splits * d, dtype=torch.float32, device=dev)
-    ws_st = torch.empty(S * h_l * splits * 2, dtype=torch.float32, device=dev)
+    ws_o = torch.empty(S * h_l * splits * d, dtype=torch.float32, device=dev)
+    ws_s = torch.empty(S * h_l * splits * 2, dtype=torch.float32, device=dev)
+
+    def call(i):
+        flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, max_context_len=max_ctx,
+                                     num_splits=splits, out=out, workspace=(ws_o, ws_s))
+
+    # One CUDA graph per block set: a decode step is a graph replay, as in a serving loop.
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    graphs = []
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        for r in range(R):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap):
+                call(r)
+            graphs.append(gr)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
 
     def step(i):
-        flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, max_context_len=max_ctx,
-                                     num_splits=splits, out=out, workspace=(ws_out, ws_st))
+        graphs[i % R].replay()
 
-    sampler = ClockSampler(local)
-    sampler.start()
-    for i in range(a.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    assert flash_engine.device_errors() == 0
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _barrier(ws, dev)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e0.record(st)
-    for i in range(a.steps):
-        step(i)
-    e1.record(st)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    _barrier(ws, dev)
+    sampler = ClockSampler(local).start()
+    ms_rank, t0, t1 = _time_steps(step, steps, warmup, ws, dev)
     sampler.stop()
-    ms_rank = e0.elapsed_time(e1) / a.steps
-    ms = _max_over_ranks(ms_rank, ws, dev)
     assert flash_engine.device_errors() == 0
-    total_bytes = decode_bytes(lens, Hkv, H, d, bs)
-    value = total_bytes / (ms * 1e-3) / 1e9
-    achieved = step_bytes_rank / (ms_rank * 1e-3) / 1e9
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    total = decode_bytes(lens, Hkv, H, d, bs)
+    rank_bytes = decode_bytes(lens, hkv_l, h_l, d, bs)
 
-    # ---- end to end through the public API: per-step inputs (q, block table,
-    # context lengths) from pinned host memory, the output back to pinned host.
+    # End to end through the public API: the step's q, block table and context lengths
+    # from pinned host memory, the output back to pinned host memory, wall clock.
     q_h = q.cpu().pin_memory()
     bt_h = [b.cpu().pin_memory() for b in bts]
     lens_h = lens_t.cpu().pin_memory()
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d, lens_d = torch.empty_like(q), torch.empty_like(lens_t)
-    bt_d = torch.empty_like(bts[0])
+    q_d, lens_d, bt_d = torch.empty_like(q), torch.empty_like(lens_t), torch.empty_like(bts[0])
 
     def e2e_step(i):
         q_d.copy_(q_h, non_blocking=True)
         bt_d.copy_(bt_h[i % R], non_blocking=True)
         lens_d.copy_(lens_h, non_blocking=True)
         o = flash_engine.paged_attention(q_d, kc, vc, bt_d, lens_d, bs, max_context_len=max_ctx,
-                                         num_splits=splits, workspace=(ws_out, ws_st))
+                                         num_splits=splits, workspace=(ws_o, ws_s))
         out_h.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
-    for i in range(min(a.warmup, 5)):
+    for i in range(3):
         e2e_step(i)
     _barrier(ws, dev)
-    n_e2e = max(1, min(a.steps, 200))
+    n_e2e = max(1, min(steps, 200))
     te0 = time.perf_counter()
     for i in range(n_e2e):
         e2e_step(i)
     te1 = time.perf_counter()
     e2e_ms = _max_over_ranks((te1 - te0) * 1e3 / n_e2e, ws, dev)
-    h2d = q_h.numel() * 2 + bt_h[0].numel() * 4 + lens_h.numel() * 4
-    d2h = out_h.numel() * 2
+    del graphs
 
-    peak_hbm, _, peak_src = _peaks()
-    prof = _traffic("paged_decode_config3_traffic.json")
-    traffic = None
-    if prof and ws == 1:
-        traffic = prof.get("dram_bytes_per_launch")
-
+    peak_hbm, _, _, src = _peaks()
     res = {
-        "metric": "paged decode KV GB/s (config 3: B64, 32q/8kv, d128, bs16, ctx U[512,4096])",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": ws,
-        "steps": a.steps,
-        "warmup": a.warmup,
+        "metric": cfg["metric"], "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
         "ms_per_step": round(ms, 5),
-        "higher_is_better": True,
-        "scaling": "strong",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) bf16 K/V/q; lens U[512,4096] seed %d)" % a.seed,
-        "config": {
-            "workload": "paged_decode_config3",
-            "num_seqs": S, "num_heads": H, "num_kv_heads": Hkv, "head_dim": d,
-            "block_size": bs, "total_context_tokens": int(lens.sum()),
-            "bytes_per_step": total_bytes, "num_splits": splits,
-            "parallelism": f"kv-head shard x{ws}",
-            "l2": f"{R} disjoint block sets rotated per step ({R * kv_bytes_set / 2**20:.0f} MiB)",
-        },
-        "roofline": {
-            "bound": "hbm", "achieved": round(achieved, 2), "peak": peak_hbm, "unit": "GB/s",
-            "frac": round(achieved / peak_hbm, 4), "peak_source": peak_src,
-            "traffic": traffic,
-            "kernel": "paged_decode_kernel + merge_kernel (one step)",
-        },
-        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": 2 * a.steps,
+        "config": {"workload": cfg["name"], "num_seqs": S, "num_heads": H, "num_kv_heads": Hkv,
+                   "head_dim": d, "block_size": bs, "total_context_tokens": int(lens.sum()),
+                   "bytes_per_step": total, "num_splits": splits,
+                   "parallelism": f"kv-head shard x{ws}",
+                   "l2": f"{R} disjoint block sets rotated per step "
+                         f"({R * kv_set / 2**20:.0f} MiB per rank)"},
+        "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (ms_rank * 1e-3) / 1e9, 2),
+                     "peak": peak_hbm, "unit": "GB/s",
+                     "frac": round(rank_bytes / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
+                     "peak_source": src, "kernel": "paged_decode_kernel + merge_kernel",
+                     "traffic": _traffic("paged_decode_config3_traffic.json")
+                     if cfg is CFG3 and ws == 1 else None},
+        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 2)},
+        "gpu_launches": 2 * steps,
         "clocks": sampler.summary(t0, t1),
     }
-    if rank == 0 and ws == 1 and not a.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_decode_baseline(lens, a.seed, budget_s=15.0)
-    if ws > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
-    return res if rank == 0 else None
+    if with_cpu and rank == 0 and ws == 1:
+        res["cpu_baseline"] = cpu_paged_baseline(cfg, lens, a.seed, budget_s=12.0)
+    return res
 
 
-def _cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
-
-
-def cpu_decode_baseline(lens, seed, budget_s=15.0, steps=1):
-    """The NumPy port of the reference's paged_attention (per KV-head group), timed
-    on the host over a bounded prefix of config 3's sequences."""
+def cpu_paged_baseline(cfg, lens, seed, budget_s=12.0, steps=1):
+    """The NumPy port of the reference's paged_attention (per KV-head group), timed on
+    the host over a bounded prefix of the workload's sequences."""
     from oracle import attention_oracle as O
-    c = CFG3
-    # size the sample to the budget: time one sequence first
-    p1 = O.make_paged_problem(seed, 1, c["num_heads"], c["num_kv_heads"], c["head_dim"],
-                              lens[:1])
+    H, Hkv, d, bs = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"], cfg["block_size"]
+    p1 = O.make_paged_problem(seed, 1, H, Hkv, d, lens[:1])
     t = time.perf_counter()
     O.paged_attention_gqa(p1["q"], p1["k_cache"], p1["v_cache"], p1["block_tables"],
                           p1["context_lens"])
@@ -358,30 +363,176 @@ def cpu_decode_baseline(lens, seed, budget_s=15.0, steps=1):
     while n < len(lens) and per_tok * int(lens[:n + 1].sum()) * steps < budget_s:
         n += 1
     sub = lens[:n]
-    p = O.make_paged_problem(seed, n, c["num_heads"], c["num_kv_heads"], c["head_dim"], sub)
+    p = O.make_paged_problem(seed, n, H, Hkv, d, sub)
     t = time.perf_counter()
     for _ in range(steps):
         O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
                               p["context_lens"])
     dt = (time.perf_counter() - t) / steps
-    b = decode_bytes(sub, c["num_kv_heads"], c["num_heads"], c["head_dim"], c["block_size"], elt=2)
+    b = decode_bytes(sub, Hkv, H, d, bs)
     return {"value": round(b / dt / 1e9, 4), "unit": "GB/s", "cores": _cpu_threads(),
             "kind": "port",
-            "sample": f"first {n} of {len(lens)} config-3 sequences ({int(sub.sum())} tokens), "
-                      f"{dt:.2f} s per pass; bytes counted as bf16 like the GPU metric"}
+            "sample": f"first {n} of {len(lens)} sequences of {cfg['name']} "
+                      f"({int(sub.sum())} tokens), {dt:.2f} s per pass; bytes counted as bf16"}
 
 
-def bench_decode_reference(a, ws, rank):
-    """--impl reference: the reference's CPU implementation (NumPy port) only."""
+# --------------------------------------------------------------------------- split-KV (config 4)
+CFG4 = dict(name="splitkv_decode_config4", batch=4, num_heads=32, num_kv_heads=8, head_dim=128,
+            block_size=16, context=131072,
+            metric="split-KV decode KV GB/s (config 4: B4, 32q/8kv, d128, ctx 131072, bs16)")
+
+
+def bench_splitkv(a, ws, rank, local, steps, warmup):
+    import torch
+    import flash_engine
+    from flash_engine import sharding
+
+    dev = torch.device("cuda", local)
+    c = CFG4
+    B, H, Hkv, d, bs, M = (c[k] for k in ("batch", "num_heads", "num_kv_heads", "head_dim",
+                                          "block_size", "context"))
+    tb, te = sharding.kv_range_bounds(M, ws, rank, bs)
+    nloc = (te - tb + bs - 1) // bs           # blocks this rank holds per sequence
+    maxb = (M + bs - 1) // bs
+    pool = B * nloc
+    rng = np.random.default_rng(a.seed + 7)
+    perm = rng.permutation(pool).astype(np.int32)
+    bt = np.zeros((B, maxb), np.int32)
+    for s in range(B):
+        bt[s, tb // bs: tb // bs + nloc] = perm[s * nloc:(s + 1) * nloc]
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + rank)
+    kc = torch.randn((pool, Hkv, bs, d), generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn((pool, Hkv, bs, d), generator=g, device=dev).to(torch.bfloat16)
+    q_all = torch.randn((B, H, d), generator=g, device=dev).to(torch.bfloat16)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.broadcast(q_all, 0)        # every rank decodes the same query tokens
+    bt_t = torch.from_numpy(bt).to(dev)
+    lens_t = torch.full((B,), M, dtype=torch.int32, device=dev)
+    splits = max(2, math.ceil(2 * 148 * 2 / (B * Hkv)))   # enough pieces to fill the GPU
+
+    def call(i, qq=q_all, bb=bt_t, ll=lens_t):
+        if ws == 1:
+            return flash_engine.paged_attention(qq, kc, vc, bb, ll, bs, max_context_len=M,
+                                                num_splits=splits, version="v2")
+        return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, num_splits=splits)
+
+    sampler = ClockSampler(local).start()
+    ms_rank, t0, t1 = _time_steps(call, steps, warmup, ws, dev)
+    sampler.stop()
+    assert flash_engine.device_errors() == 0
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    kv_total = B * M * Hkv * d * 2 * 2
+    kv_rank = B * (te - tb) * Hkv * d * 2 * 2
+    # end to end: q, block table and lengths from pinned host, output back to host
+    q_h, bt_h, l_h = q_all.cpu().pin_memory(), bt_t.cpu().pin_memory(), lens_t.cpu().pin_memory()
+    out_h = torch.empty(q_all.shape, dtype=q_all.dtype).pin_memory()
+    q_d, bt_d, l_d = torch.empty_like(q_all), torch.empty_like(bt_t), torch.empty_like(lens_t)
+
+    def e2e(i):
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        l_d.copy_(l_h, non_blocking=True)
+        out_h.copy_(call(i, q_d, bt_d, l_d), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(3):
+        e2e(i)
+    _barrier(ws, dev)
+    n = max(1, min(steps, 100))
+    te0 = time.perf_counter()
+    for i in range(n):
+        e2e(i)
+    e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n, ws, dev)
+    peak_hbm, _, _, src = _peaks()
+    return {
+        "metric": c["metric"], "value": round(kv_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "ms_per_step": round(ms, 5),
+        "config": {"workload": c["name"], "batch": B, "num_heads": H, "num_kv_heads": Hkv,
+                   "head_dim": d, "context": M, "block_size": bs, "num_splits_local": splits,
+                   "parallelism": f"kv-range shard x{ws} + all-gather of (O,m,l) partials",
+                   "l2": f"{kv_rank / 2**20:.0f} MiB of KV per rank"},
+        "roofline": {"bound": "hbm", "achieved": round(kv_rank / (ms_rank * 1e-3) / 1e9, 2),
+                     "peak": peak_hbm, "unit": "GB/s",
+                     "frac": round(kv_rank / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
+                     "peak_source": src},
+        "e2e": {"value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h.numel() * 4 + l_h.numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 2)},
+        "clocks": sampler.summary(t0, t1),
+    }
+
+
+# --------------------------------------------------------------------------- prefill (config 2)
+def prefill_flops(B, H, N, d, causal=True):
+    """4*B*H*N^2*d, halved for causal (the reference's convention,
+    benchmarks/bench_attention.cu:48-49)."""
+    f = 4.0 * B * H * N * N * d
+    return f / 2 if causal else f
+
+
+def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
+    import torch
+    import flash_engine
+
+    dev = torch.device("cuda", local)
+    if fp32:   # config 1: fp32, non-causal, [1, 8, 512, 64]
+        B, H, N, d, causal, dt = 1, 8, 512, 64, False, torch.float32
+        name = "fa2_prefill_fp32_config1"
+        metric = "FA2 forward fp32 TFLOP/s (config 1: [1, 8, 512, 64], non-causal)"
+    else:
+        B, H, N, d, causal, dt = 4, 32, 4096, 128, True, torch.bfloat16
+        name = "fa2_prefill_config2"
+        metric = "FA2 prefill TFLOP/s (config 2: bf16 causal [4, 32, 4096, 128])"
+    if H % ws:
+        raise ValueError(f"{ws} ranks cannot split {H} heads")
+    h_l = H // ws
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + a.seed * 31 + rank)
+    q, k, v = (torch.randn((B, h_l, N, d), generator=g, device=dev).to(dt) for _ in range(3))
+
+    def step(i):
+        return flash_engine.flash_attention(q, k, v, causal)
+
+    sampler = ClockSampler(local).start()
+    ms_rank, t0, t1 = _time_steps(step, steps, warmup, ws, dev)
+    sampler.stop()
+    assert flash_engine.device_errors() == 0
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    total = prefill_flops(B, H, N, d, causal)
+    rank_flops = prefill_flops(B, h_l, N, d, causal)
+    achieved = rank_flops / (ms_rank * 1e-3) / 1e12
+    _, peak, peak_sus, src = _peaks()
+    return {
+        "metric": metric, "value": round(total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "ms_per_step": round(ms, 4),
+        "config": {"workload": name, "batch": B, "heads": H, "seq_len": N, "head_dim": d,
+                   "causal": causal, "parallelism": f"head shard x{ws}",
+                   "flops_per_step": total},
+        "roofline": {"bound": "tensor" if not fp32 else "fma",
+                     "achieved": round(achieved, 3), "peak": None if fp32 else peak,
+                     "unit": "TFLOP/s", "frac": None if fp32 else round(achieved / peak, 4),
+                     "frac_of_sustained": None if fp32 else round(achieved / peak_sus, 4),
+                     "peak_source": src + ("" if fp32 else " bf16 burst"),
+                     "kernel": "fa2_fp32_kernel (FMA pipes)" if fp32 else "fa_prefill_kernel"},
+        "clocks": sampler.summary(t0, t1),
+        "gpu_launches": steps,
+    }
+
+
+# --------------------------------------------------------------------------- reference arm
+def bench_reference(a, ws, rank):
+    """--impl reference: the reference's CPU implementation (its NumPy paged_attention,
+    ported to oracle/) on the host cores, over a bounded prefix of config 3."""
     if rank != 0:
         return None
-    from oracle.attention_oracle import config3_context_lens
-    lens = config3_context_lens(a.seed)
-    total_budget = 120.0
-    per_step = max(0.05, total_budget / max(1, a.steps + a.warmup))
     from oracle import attention_oracle as O
     c = CFG3
-    p1 = O.make_paged_problem(a.seed, 1, c["num_heads"], c["num_kv_heads"], c["head_dim"], lens[:1])
+    lens = _lens(c, a.seed)
+    per_step = max(0.05, 120.0 / max(1, a.steps + a.warmup))
+    H, Hkv, d, bs = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["block_size"]
+    p1 = O.make_paged_problem(a.seed, 1, H, Hkv, d, lens[:1])
     t = time.perf_counter()
     O.paged_attention_gqa(p1["q"], p1["k_cache"], p1["v_cache"], p1["block_tables"],
                           p1["context_lens"])
@@ -390,7 +541,7 @@ def bench_decode_reference(a, ws, rank):
     while n < len(lens) and per_tok * int(lens[:n + 1].sum()) < per_step:
         n += 1
     sub = lens[:n]
-    p = O.make_paged_problem(a.seed, n, c["num_heads"], c["num_kv_heads"], c["head_dim"], sub)
+    p = O.make_paged_problem(a.seed, n, H, Hkv, d, sub)
     args = (p["q"], p["k_cache"], p["v_cache"], p["block_tables"], p["context_lens"])
     for _ in range(a.warmup):
         O.paged_attention_gqa(*args)
@@ -398,119 +549,75 @@ def bench_decode_reference(a, ws, rank):
     for _ in range(a.steps):
         O.paged_attention_gqa(*args)
     dt = (time.perf_counter() - t) / max(1, a.steps)
-    b = decode_bytes(sub, c["num_kv_heads"], c["num_heads"], c["head_dim"], c["block_size"])
-    v = round(b / dt / 1e9, 4)
+    v = round(decode_bytes(sub, Hkv, H, d, bs) / dt / 1e9, 4)
     return {
-        "impl": "reference",
-        "metric": "paged decode KV GB/s (config 3: B64, 32q/8kv, d128, bs16, ctx U[512,4096])",
-        "value": v, "unit": "GB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)", "data": "synthetic",
-        "config": {"workload": "paged_decode_config3", "sample_seqs": n},
+        "impl": "reference", "metric": c["metric"], "value": v, "unit": "GB/s", "n_gpus": ws,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (bf16-rounded inputs)", "data": "synthetic",
+        "config": {"workload": c["name"], "sample_seqs": n},
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": _cpu_threads(), "kind": "port",
                          "sample": f"first {n} of 64 config-3 sequences per step"},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
-# --------------------------------------------------------------------------- prefill workload
-CFG2 = dict(batch=4, heads=32, seq=4096, head_dim=128, causal=True)
-
-
-def prefill_flops(B, H, N, d, causal=True):
-    """4*B*H*N^2*d, halved for causal: the reference's convention
-    (benchmarks/bench_attention.cu:48-49)."""
-    f = 4.0 * B * H * N * N * d
-    return f / 2 if causal else f
-
-
-def bench_prefill_ours(a, ws, rank, local, init_pg=True, steps=None, warmup=None):
-    import torch
-    import flash_engine
-
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if init_pg:
-        _init_pg(ws, "nccl")
-    c = CFG2
-    B, H, N, d = c["batch"], c["heads"], c["seq"], c["head_dim"]
-    if H % ws:
-        raise SystemExit(f"--gpus {ws} must divide the {H} heads")
-    h_l = H // ws
-    steps = a.steps if steps is None else steps
-    warmup = a.warmup if warmup is None else warmup
-    g = torch.Generator(device=dev)
-    g.manual_seed(2000 + a.seed * 31 + rank)
-    q, k, v = (torch.randn((B, h_l, N, d), generator=g, device=dev, dtype=torch.float32)
-               .to(torch.bfloat16) for _ in range(3))
-    out = torch.empty_like(q)
-
-    def step():
-        return flash_engine.flash_attention(q, k, v, True)
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    assert flash_engine.device_errors() == 0
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _barrier(ws, dev)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e0.record(st)
-    for _ in range(steps):
-        step()
-    e1.record(st)
-    torch.cuda.synchronize()
-    t1 = time.perf_counter()
-    _barrier(ws, dev)
-    sampler.stop()
-    assert flash_engine.device_errors() == 0
-    ms_rank = e0.elapsed_time(e1) / steps
-    ms = _max_over_ranks(ms_rank, ws, dev)
-    flops_rank = prefill_flops(B, h_l, N, d)
-    total = prefill_flops(B, H, N, d)
-    tflops = total / (ms * 1e-3) / 1e12
-    achieved = flops_rank / (ms_rank * 1e-3) / 1e12
-    _, peak, src = _peaks()
-    return {
-        "metric": "FA2 prefill TFLOP/s (config 2: bf16 causal [4, 32, 4096, 128])",
-        "value": round(tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
-        "flops_per_step": total,
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                     "peak_source": src + " bf16 burst",
-                     "kernel": "fa_prefill_kernel<bf16,128>"},
-        "clocks": sampler.summary(t0, t1),
-        "gpu_launches": steps,
-    }
+# --------------------------------------------------------------------------- main
+def run_workload(name, a, ws, rank, local, primary):
+    steps = a.steps if primary else min(a.steps, 30)
+    warmup = a.warmup if primary else min(a.warmup, 3)
+    if name == "decode":
+        return bench_paged(a, ws, rank, local, CFG3, primary and not a.no_cpu_baseline, steps,
+                           warmup)
+    if name == "serving":
+        return bench_paged(a, ws, rank, local, CFG5, primary and not a.no_cpu_baseline, steps,
+                           warmup)
+    if name == "splitkv":
+        return bench_splitkv(a, ws, rank, local, steps, warmup)
+    if name == "prefill":
+        return bench_prefill(a, ws, rank, local, steps, warmup)
+    return bench_prefill(a, ws, rank, local, steps, warmup, fp32=True)
 
 
 def main():
     a = _args()
     ws, rank, local = _dist()
     if a.impl == "reference":
-        res = bench_decode_reference(a, ws, rank)
-    elif a.workload == "prefill":
-        pr = bench_prefill_ours(a, ws, rank, local)
-        res = None
-        if rank == 0:
-            res = dict(pr)
-            res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
-                        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 Q/K/V)",
-                        "config": {"workload": "fa2_prefill_config2", "batch": 4, "heads": 32,
-                                   "seq_len": 4096, "head_dim": 128, "causal": True,
-                                   "parallelism": f"head shard x{ws}",
-                                   "l2": "inputs 384 MiB > L2"}})
-        if ws > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-    else:
-        res = bench_decode_ours(a, ws, rank, local)
-    if res is not None and rank == 0:
+        res = bench_reference(a, ws, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    import torch
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    res = run_workload(a.workload, a, ws, rank, local, True)
+    res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) bf16 inputs; BASELINE config shapes)"})
+    if a.workload == "prefill_fp32":
+        res["dtype"] = "f32"
+    if not a.no_secondary:
+        sec = {}
+        for name in ("prefill", "splitkv", "serving"):
+            if name == a.workload:
+                continue
+            try:
+                r = run_workload(name, a, ws, rank, local, False)
+                sec[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step",
+                                               "roofline", "config", "e2e") if k in r}
+            except Exception as e:  # recorded, never silently dropped
+                sec[name] = {"error": f"{type(e).__name__}: {e}"}
+                if rank == 0:
+                    traceback.print_exc()
+        res["secondary"] = sec
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
         print(json.dumps(res), flush=True)
 
 
