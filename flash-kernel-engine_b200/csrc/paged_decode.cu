@@ -22,7 +22,7 @@
 //    place work.
 //  * One producer warp streams each (block, KV head) page of K and V into shared
 //    memory with 2-D TMA bulk-tensor loads (128-byte swizzle, L2 evict-first, no
-//    multicast), completing on mbarriers. Block-table entries are fetched 32 at a
+//    cluster sharing), completing on mbarriers. Block-table entries are fetched 32 at a
 //    time, one 32-page group ahead of the loads they feed.
 //  * NCW consumer warps, each with a private ring of DEPTH stages (page gi of the
 //    CTA belongs to warp gi % NCW). Per 16 tokens a warp computes S^T = K Q^T with

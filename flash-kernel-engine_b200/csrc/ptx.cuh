@@ -86,7 +86,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
-// 2-D tiled bulk-tensor load (no multicast) completing on an mbarrier.
+// 2-D tiled bulk-tensor load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, int y,
                                             uint64_t* bar, uint64_t policy) {
   asm volatile(
@@ -95,7 +95,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, i
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
-// 3-D tiled bulk-tensor load (no multicast).
+// 3-D tiled bulk-tensor load into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x, int y, int z,
                                             uint64_t* bar, uint64_t policy) {
   asm volatile(

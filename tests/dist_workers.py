@@ -102,3 +102,37 @@ def dropout_worker(rank, world, port, result_path):
     with open(f"{result_path}.{rank}", "w") as f:
         f.write(repr((status, time.time() - t0)))
     os._exit(0)
+
+
+def nccl_kv_range_worker(rank, world, port, result_path):
+    """KV-range-sharded paged decode on `world` GPUs over NCCL (each rank holds the
+    blocks of its own window), checked against the oracle's single-pass result."""
+    import torch
+    import torch.distributed as dist
+    import flash_engine
+    from flash_engine import sharding
+    from oracle import attention_oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    lens = [0, 5, 16, 300, 1500, 2047]
+    p = O.make_paged_problem(21, len(lens), 32, 8, 128, lens)
+    M = int(max(lens))
+    dev = torch.device("cuda", rank)
+    q, kc, vc = (torch.from_numpy(p[x]).to(dev).to(torch.bfloat16)
+                 for x in ("q", "k_cache", "v_cache"))
+    bt = torch.from_numpy(p["block_tables"]).to(dev)
+    cl = torch.from_numpy(p["context_lens"]).to(dev)
+    out = sharding.paged_decode_kv_range(q, kc, vc, bt, cl, M, 16, num_splits=4)
+    errs = flash_engine.device_errors()
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    err = float(np.abs(out.float().cpu().numpy() - ref).max())
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((err, errs)))

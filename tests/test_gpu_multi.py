@@ -1,0 +1,20 @@
+"""KV-range sharding over NCCL on 2 GPUs (skipped with fewer GPUs): the partials of
+each rank's token window are all-gathered and merged; every rank must reproduce the
+single-pass attention of the oracle."""
+import pytest
+import torch
+
+import dist_workers
+from test_sharding_gloo import _run
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_kv_range_nccl_two_gpus(tmp_path):
+    res = _run(dist_workers.nccl_kv_range_worker, 2, tmp_path, join_timeout=180)
+    assert all(r is not None for r in res), res
+    for err, dev_errors in res:
+        assert dev_errors == 0
+        assert err <= 2e-2
