@@ -258,13 +258,12 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     lens_t = torch.from_numpy(lens).to(dev)
     out = torch.empty_like(q)
     max_ctx = int(lens.max())
-    splits = flash_engine.paged_attention_splits(S, h_l, hkv_l, d, bs, max_ctx)
-    ws_o = torch.empty(S * h_l * splits * d, dtype=torch.float32, device=dev)
-    ws_s = torch.empty(S * h_l * splits * 2, dtype=torch.float32, device=dev)
+    wsp = torch.empty(flash_engine.paged_attention_workspace_floats(h_l, hkv_l, d, bs),
+                      dtype=torch.float32, device=dev)
 
     def call(i):
         flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, max_context_len=max_ctx,
-                                     num_splits=splits, out=out, workspace=(ws_o, ws_s))
+                                     out=out, workspace=wsp)
 
     # One CUDA graph per block set: a decode step is a graph replay, as in a serving loop.
     for i in range(3):
@@ -306,7 +305,7 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
         bt_d.copy_(bt_h[i % R], non_blocking=True)
         lens_d.copy_(lens_h, non_blocking=True)
         o = flash_engine.paged_attention(q_d, kc, vc, bt_d, lens_d, bs, max_context_len=max_ctx,
-                                         num_splits=splits, workspace=(ws_o, ws_s))
+                                         workspace=wsp)
         out_h.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -327,7 +326,7 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
         "ms_per_step": round(ms, 5),
         "config": {"workload": cfg["name"], "num_seqs": S, "num_heads": H, "num_kv_heads": Hkv,
                    "head_dim": d, "block_size": bs, "total_context_tokens": int(lens.sum()),
-                   "bytes_per_step": total, "num_splits": splits,
+                   "bytes_per_step": total, "workspace_floats": int(wsp.numel()),
                    "parallelism": f"kv-head shard x{ws}",
                    "l2": f"{R} disjoint block sets rotated per step "
                          f"({R * kv_set / 2**20:.0f} MiB per rank)"},
@@ -410,13 +409,14 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
         dist.broadcast(q_all, 0)        # every rank decodes the same query tokens
     bt_t = torch.from_numpy(bt).to(dev)
     lens_t = torch.full((B,), M, dtype=torch.int32, device=dev)
-    splits = max(2, math.ceil(2 * 148 * 2 / (B * Hkv)))   # enough pieces to fill the GPU
+    wsp = torch.empty(flash_engine.paged_attention_workspace_floats(H, Hkv, d, bs),
+                      dtype=torch.float32, device=dev)
 
     def call(i, qq=q_all, bb=bt_t, ll=lens_t):
         if ws == 1:
             return flash_engine.paged_attention(qq, kc, vc, bb, ll, bs, max_context_len=M,
-                                                num_splits=splits, version="v2")
-        return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, num_splits=splits)
+                                                version="v2", workspace=wsp)
+        return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
 
     sampler = ClockSampler(local).start()
     ms_rank, t0, t1 = _time_steps(call, steps, warmup, ws, dev)
@@ -450,7 +450,7 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
         "metric": c["metric"], "value": round(kv_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
         "ms_per_step": round(ms, 5),
         "config": {"workload": c["name"], "batch": B, "num_heads": H, "num_kv_heads": Hkv,
-                   "head_dim": d, "context": M, "block_size": bs, "num_splits_local": splits,
+                   "head_dim": d, "context": M, "block_size": bs,
                    "parallelism": f"kv-range shard x{ws} + all-gather of (O,m,l) partials",
                    "l2": f"{kv_rank / 2**20:.0f} MiB of KV per rank"},
         "roofline": {"bound": "hbm", "achieved": round(kv_rank / (ms_rank * 1e-3) / 1e9, 2),

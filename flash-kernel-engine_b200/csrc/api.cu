@@ -61,29 +61,42 @@ int paged_check(const PagedArgs& a, bool tensor_core) {
 // How the tensor-core decode cuts and finishes the work.
 struct DecodePlan {
   int tok_begin = 0, tok_end = INT_MAX;
-  bool flat = false;          // stream-K chunking with partials (needs scratch)
-  int pps = INT_MAX / 2;      // unit mode: pages per segment; flat: minimum chunk
-  int max_splits = 1;         // partial slots per (seq, head)
-  bool direct_final = true;   // single-slot rows write the final output
+  bool flat = false;          // stream-K chunking with fixup partials (needs workspace)
+  bool direct_final = true;   // whole rows: normalised output (else merged partials)
   int merge_dtype = -1;       // -1: no merge; else MergeParams::out_dtype
   float* merged_out = nullptr;
   float* merged_stats = nullptr;
 };
 
+inline int decode_nt(int H, int Hkv) { return (H / Hkv) <= 8 ? 1 : 2; }
+
+long long workspace_floats_for(int H, int Hkv, int d, int bs) {
+  if (H <= 0 || Hkv <= 0 || H % Hkv) return -1;
+  return fe::paged::fixup_floats(d, bs, decode_nt(H, Hkv));
+}
+
 // Runs the tensor-core decode (and, if planned, the log-sum-exp merge) over all
-// sequences, in chunks of kMaxSeqsPerLaunch sequences.
+// sequences, in chunks of kMaxSeqsPerLaunch sequences. `ws` holds the fixup slots
+// of flat mode (fixup_floats of them).
 template <typename T>
-int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float* part_ml,
-                 cudaStream_t st) {
-  const int G = a.H / a.Hkv;
-  const int nt = G <= 8 ? 1 : 2;
+int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream_t st) {
+  const int nt = decode_nt(a.H, a.Hkv);
   const int hpc = 8 * nt;
-  const int head_chunks = (G + hpc - 1) / hpc;
+  const int head_chunks = (a.H / a.Hkv + hpc - 1) / hpc;
   const long long kv_rows = a.num_blocks > 0
                                 ? static_cast<long long>(a.num_blocks) * a.Hkv * a.bs
                                 : static_cast<long long>(INT_MAX);
   unsigned* err = fe::device_error_word();
   if (!err) return static_cast<int>(cudaErrorInitializationError);
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  if (pl.flat) {
+    const long long nf = workspace_floats_for(a.H, a.Hkv, a.d, a.bs);
+    if (nf <= 0 || !ws) return kErr;
+    const long long slot_rows = nf / (a.d + 2);
+    part_o = ws;
+    part_ml = ws + slot_rows * a.d;
+  }
   for (int s0 = 0; s0 < a.S; s0 += kMaxSeqsPerLaunch) {
     const int n = a.S - s0 < kMaxSeqsPerLaunch ? a.S - s0 : kMaxSeqsPerLaunch;
     const size_t row0 = static_cast<size_t>(s0) * a.H;
@@ -92,8 +105,10 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float*
     p.out = a.out ? static_cast<T*>(a.out) + row0 * a.d : nullptr;
     p.block_tables = a.bt + static_cast<size_t>(s0) * a.maxb;
     p.context_lens = a.lens + s0;
-    p.part_o = part_o ? part_o + row0 * pl.max_splits * a.d : nullptr;
-    p.part_ml = part_ml ? part_ml + row0 * pl.max_splits * 2 : nullptr;
+    p.part_o = part_o;
+    p.part_ml = part_ml;
+    p.merged_o = pl.merged_out ? pl.merged_out + row0 * a.d : nullptr;
+    p.merged_ml = pl.merged_stats ? pl.merged_stats + row0 * 2 : nullptr;
     p.num_seqs = n;
     p.num_heads = a.H;
     p.num_kv_heads = a.Hkv;
@@ -102,8 +117,7 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float*
     p.head_chunks = head_chunks;
     p.tok_begin = pl.tok_begin;
     p.tok_end = pl.tok_end;
-    p.pages_per_split = pl.pps;
-    p.max_splits = pl.max_splits;
+    p.pages_per_split = pl.flat ? 1 : INT_MAX / 2;
     p.flat = pl.flat ? 1 : 0;
     p.direct_final = pl.direct_final ? 1 : 0;
     p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;
@@ -113,11 +127,11 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float*
     if (e != cudaSuccess) return static_cast<int>(e);
     if (pl.merge_dtype < 0) continue;
     fe::paged::MergeParams mp{};
-    mp.part_out = p.part_o;
-    mp.part_stats = p.part_ml;
+    mp.part_out = part_o;
+    mp.part_stats = part_ml;
     mp.rows = n * a.H;
     mp.ranks = 1;
-    mp.parts_per_rank = pl.max_splits;
+    mp.parts_per_rank = 1;
     mp.context_lens = p.context_lens;
     mp.num_seqs = n;
     mp.heads = a.H;
@@ -129,11 +143,10 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float*
     mp.tok_end = pl.tok_end;
     mp.block_size = a.bs;
     mp.decode_ctas = grid;
-    mp.chunk_min = pl.pps;
-    mp.skip_single = pl.direct_final ? 1 : 0;
+    mp.chunk_min = 1;
     if (pl.merge_dtype == 2) {
-      mp.out = pl.merged_out + row0 * a.d;
-      mp.out_stats = pl.merged_stats + row0 * 2;
+      mp.out = p.merged_o;
+      mp.out_stats = p.merged_ml;
     } else {
       mp.out = p.out;
     }
@@ -144,29 +157,6 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* part_o, float*
   return 0;
 }
 
-int default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
-  (void)d;
-  const int G = H / (Hkv > 0 ? Hkv : 1);
-  const int head_chunks = (G + (G <= 8 ? 8 : 16) - 1) / (G <= 8 ? 8 : 16);
-  const int max_pages = max_ctx > 0 ? (max_ctx + bs - 1) / bs : 1;
-  const long long groups = static_cast<long long>(S > 0 ? S : 1) * Hkv * head_chunks;
-  // Enough partial slots for a sequence to be spread over ~2x as many CTAs as its
-  // share of the GPU (2 persistent CTAs per SM), plus the two chunk-boundary pieces.
-  const long long ctas = 2LL * fe::sm_count();
-  long long splits = (2 * ctas + groups - 1) / groups + 2;
-  if (splits > max_pages + 1) splits = max_pages + 1;
-  if (splits < 2) splits = 2;
-  if (splits > 64) splits = 64;
-  return static_cast<int>(splits);
-}
-
-// Flat-mode minimum chunk so that a sequence of up to max_pages pages touches at
-// most `splits` chunks.
-inline int flat_chunk_min(int max_pages, int splits) {
-  if (max_pages < 1) max_pages = 1;
-  return (max_pages + splits - 2) / (splits - 1);
-}
-
 template <typename T>
 int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
   const int rc = paged_check(a, true);
@@ -175,24 +165,21 @@ int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
   // Unit mode, one segment per sequence whatever its length: every segment
   // writes its final rows, no scratch.
   DecodePlan pl;
-  return paged_tc_run<T>(a, pl, nullptr, nullptr, st);
+  return paged_tc_run<T>(a, pl, nullptr, st);
 }
 
 template <typename T>
-int paged_v2_tc(const PagedArgs& a, float* sout, float* sstats, int splits, cudaStream_t st) {
+int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st) {
   const int rc = paged_check(a, true);
   if (rc) return rc;
-  if (splits < 1 || !sout || !sstats) return kErr;
+  const long long need = workspace_floats_for(a.H, a.Hkv, a.d, a.bs);
+  if (need <= 0 || !ws || static_cast<long long>(ws_floats) < need) return kErr;
   if (a.S == 0) return 0;
-  if (splits == 1) return paged_v1_tc<T>(a, st);
-  const int max_pages = a.max_ctx > 0 ? (a.max_ctx + a.bs - 1) / a.bs : 1;
   DecodePlan pl;
   pl.flat = true;
-  pl.pps = flat_chunk_min(max_pages, splits);
-  pl.max_splits = splits;
   pl.direct_final = true;
   pl.merge_dtype = std::is_same<T, __nv_bfloat16>::value ? 1 : 3;
-  return paged_tc_run<T>(a, pl, sout, sstats, st);
+  return paged_tc_run<T>(a, pl, ws, st);
 }
 
 }  // namespace
@@ -273,14 +260,14 @@ int fe_paged_attention_v1_bf16(const void* q, const void* kc, const void* vc, vo
 int fe_paged_attention_v2_bf16(const void* q, const void* kc, const void* vc, void* out,
                                const int* bt, const int* lens, int S, int H, int Hkv, int d,
                                int bs, int max_ctx, int maxb, int num_blocks, float scale,
-                               float* sout, float* sstats, int splits, void* stream) {
+                               float* workspace, size_t workspace_floats, void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
-  return paged_v2_tc<__nv_bfloat16>(a, sout, sstats, splits, as_stream(stream));
+  return paged_v2_tc<__nv_bfloat16>(a, workspace, workspace_floats, as_stream(stream));
 }
 
-int fe_paged_attention_v2_default_splits(int S, int H, int Hkv, int d, int bs, int max_ctx) {
-  if (H <= 0 || Hkv <= 0 || bs <= 0) return 1;
-  return default_splits(S, H, Hkv, d, bs, max_ctx);
+size_t fe_paged_attention_v2_workspace_floats(int H, int Hkv, int d, int bs) {
+  const long long n = workspace_floats_for(H, Hkv, d, bs);
+  return n > 0 ? static_cast<size_t>(n) : 0;
 }
 
 // ---- no-alloc split-KV decode ------------------------------------------------
@@ -312,10 +299,10 @@ static int noalloc_scratch_ptr(float** out) {
 int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* kc, const void* vc, void* out,
                                        const int* bt, const int* lens, int S, int H, int Hkv,
                                        int d, int bs, int max_ctx, int maxb, int num_blocks,
-                                       float scale, int splits, void* stream) {
-  if (S < 0 || H <= 0 || d <= 0 || splits < 1) return kErr;
-  const long long need = static_cast<long long>(S) * H * splits * (d + 2);
-  if (need > FE_NOALLOC_SCRATCH_FLOATS) return kErr;
+                                       float scale, void* stream) {
+  if (S < 0 || H <= 0 || Hkv <= 0 || d <= 0) return kErr;
+  const long long need = workspace_floats_for(H, Hkv, d, bs);
+  if (need <= 0 || need > FE_NOALLOC_SCRATCH_FLOATS) return kErr;
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
   const int rc = paged_check(a, true);
   if (rc) return rc;
@@ -323,9 +310,7 @@ int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* kc, const void
   float* base = nullptr;
   const int e = noalloc_scratch_ptr(&base);
   if (e) return e;
-  float* sout = base;
-  float* sstats = base + static_cast<size_t>(S) * H * splits * d;
-  return paged_v2_tc<__nv_bfloat16>(a, sout, sstats, splits, as_stream(stream));
+  return paged_v2_tc<__nv_bfloat16>(a, base, FE_NOALLOC_SCRATCH_FLOATS, as_stream(stream));
 }
 
 int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* v, float* out,
@@ -350,29 +335,25 @@ int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* 
 
 int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc, const int* bt,
                                   const int* lens, int S, int H, int Hkv, int d, int bs, int maxb,
-                                  int num_blocks, float scale, int tb, int te, int splits,
-                                  float* sout, float* sstats, float* mout, float* mstats,
+                                  int num_blocks, float scale, int tb, int te, float* workspace,
+                                  size_t workspace_floats, float* mout, float* mstats,
                                   void* stream) {
   PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
   int rc = paged_check(a, true);
   if (rc) return rc;
-  if (splits < 1 || tb < 0 || te < tb || !sout || !sstats || !mout || !mstats || tb % bs != 0)
-    return kErr;
+  const long long need = workspace_floats_for(H, Hkv, d, bs);
+  if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
+  if (tb < 0 || te < tb || !mout || !mstats || tb % bs != 0) return kErr;
   if (S == 0) return 0;
-  const int range_pages = (te - tb + bs - 1) / bs;
   DecodePlan pl;
   pl.tok_begin = tb;
   pl.tok_end = te;
+  pl.flat = true;
   pl.direct_final = false;
-  pl.max_splits = splits;
   pl.merge_dtype = 2;
   pl.merged_out = mout;
   pl.merged_stats = mstats;
-  if (splits >= 2) {
-    pl.flat = true;
-    pl.pps = flat_chunk_min(range_pages, splits);
-  }
-  return paged_tc_run<__nv_bfloat16>(a, pl, sout, sstats, as_stream(stream));
+  return paged_tc_run<__nv_bfloat16>(a, pl, workspace, as_stream(stream));
 }
 
 int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,
@@ -461,11 +442,11 @@ cudaError_t launch_paged_attention_v1_bf16(const __nv_bfloat16* q, const __nv_bf
 cudaError_t launch_paged_attention_v2_bf16(const __nv_bfloat16* q, const __nv_bfloat16* kc,
                                            const __nv_bfloat16* vc, __nv_bfloat16* out,
                                            const int* bt, const int* lens,
-                                           const PagedAttentionConfig& c, float* sout,
-                                           float* sstats, int splits, cudaStream_t s) {
+                                           const PagedAttentionConfig& c, float* workspace,
+                                           size_t workspace_floats, cudaStream_t s) {
   return static_cast<cudaError_t>(fe_paged_attention_v2_bf16(
       q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
-      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, sout, sstats, splits, s));
+      c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, workspace, workspace_floats, s));
 }
 
 }  // namespace paged_attention

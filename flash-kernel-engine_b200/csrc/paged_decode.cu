@@ -14,9 +14,12 @@
 //        dealt round-robin to the CTAs;
 //      - flat mode (split-KV with partials): the (KV-head group, sequence, page)
 //        space is cut into gridDim.x equal contiguous chunks (stream-K style), one
-//        per CTA, so every CTA streams the same number of pages. A sequence cut by
-//        a chunk boundary leaves one fp32 partial per chunk; merge_kernel combines
-//        them. A sequence inside one chunk is finalised directly.
+//        per CTA, so every CTA streams the same number of pages whatever the
+//        context-length mix. A sequence inside one chunk is finalised directly. Only
+//        the first and the last segment of a chunk can be pieces of a longer
+//        sequence, so each CTA owns two fp32 partial slots of a small fixup buffer
+//        (slot 0: its first segment, slot 1: its last); merge_kernel combines the
+//        pieces of every sequence that crosses a chunk boundary.
 //    Both modes read context_lens and build the page prefix with a block-wide scan
 //    in every CTA, so no host synchronisation or scratch is needed to skip or
 //    place work.
@@ -160,8 +163,8 @@ struct Seg {
   int seq, kvh, hc;
   int p0, p1;     // absolute pages [p0, p1)
   int lo, hi;     // valid tokens [lo, hi)
-  int slot;       // partial slot of this segment
-  int nslots;     // segments of this (sequence, head group); 1 = write final output
+  int slot;       // flat mode: 0 = first segment of the CTA's chunk, 1 = a later one
+  int nslots;     // chunks (segments) of this (sequence, head group); 1 = finalise here
 };
 
 // Walks the segments of one CTA. Producer and consumers run identical copies.
@@ -175,6 +178,7 @@ struct SegIter {
   // flat mode
   long long P, Pend, chunk;
   int Ptot;
+  bool first_seg;
 
   __device__ __forceinline__ bool next(Seg& g) {
     if (!flat) {
@@ -215,7 +219,8 @@ struct SegIter {
     g.hi = w.hi;
     const int cfirst = static_cast<int>(gstart / chunk);
     g.nslots = static_cast<int>(gend / chunk) - cfirst + 1;
-    g.slot = static_cast<int>(blockIdx.x) - cfirst;
+    g.slot = first_seg ? 0 : 1;
+    first_seg = false;
     P += n;
     return true;
   }
@@ -306,6 +311,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     it.chunk = flat_chunk(total_pages, gridDim.x, p.pages_per_split);
     it.P = min(total_pages, static_cast<long long>(blockIdx.x) * it.chunk);
     it.Pend = min(total_pages, it.P + it.chunk);
+    it.first_seg = true;
     it.u = it.total_units = 0;
   } else {
     block_prefix<NTH>(pre, S, warp_tot, [&](int i) {
@@ -317,6 +323,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     it.P = it.Pend = 0;
     it.chunk = 1;
     it.Ptot = 0;
+    it.first_seg = true;
   }
 
   if (warp == NCW) {
@@ -611,12 +618,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     __syncwarp();
     named_bar(1, NCW * 32);
 
-    const bool final_out = direct_final && sg.nslots == 1;
-    // A sequence longer than max_context_len would need more partial slots than the
-    // scratch holds; such a segment is dropped and flagged.
-    const bool slot_ok = final_out || (sg.slot >= 0 && sg.slot < p.max_splits);
-    if (!slot_ok && tid == 0) atomicOr(p.err, kErrBadBlock);
-    for (int idx = tid; idx < HPC * D && slot_ok; idx += NCW * 32) {
+    // A segment that is the whole (sequence, head group) is finished here: as the
+    // normalised output row, or (partials mode) as that row's merged partial.
+    // Pieces of longer sequences go to this CTA's fixup slot.
+    const bool whole = sg.nslots == 1;
+    for (int idx = tid; idx < HPC * D; idx += NCW * 32) {
       const int hl = idx / D, dim = idx - hl * D;
       const int gh = sg.hc * HPC + hl;
       if (gh >= G) continue;
@@ -632,14 +638,20 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         O += comb_o[(w * HPC + hl) * CSTRIDE + dim] * wt;
       }
       const size_t row = static_cast<size_t>(sg.seq) * p.num_heads + sg.kvh * G + gh;
-      if (final_out) {
+      if (whole && direct_final) {
         reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(L > 0.f ? O / L : 0.f);
-      } else {
-        const size_t part = row * p.max_splits + sg.slot;
-        p.part_o[part * D + dim] = O;
+      } else if (whole) {
+        p.merged_o[row * D + dim] = O;
         if (dim == 0) {
-          p.part_ml[part * 2 + 0] = M;
-          p.part_ml[part * 2 + 1] = L;
+          p.merged_ml[row * 2 + 0] = L > 0.f ? M : NEG_INF;
+          p.merged_ml[row * 2 + 1] = L;
+        }
+      } else {
+        const size_t fix = (static_cast<size_t>(blockIdx.x) * 2 + sg.slot) * HPC + hl;
+        p.part_o[fix * D + dim] = O;
+        if (dim == 0) {
+          p.part_ml[fix * 2 + 0] = M;
+          p.part_ml[fix * 2 + 1] = L;
         }
       }
     }
@@ -653,10 +665,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
 
 // ---------------------------------------------------------------------------
 // Log-sum-exp merge of split partials. One warp per output row.
-//   ctx mode (context_lens != nullptr): row = seq * H + h; its valid slots follow
-//     from the decode kernel's flat chunking (same prefix, same chunk length);
-//     rows with one slot were finalised by the decode kernel (skip_single), rows
-//     with none are empty (zeros / (-inf, 0)).
+//   ctx mode (context_lens != nullptr): row = seq * H + h; its parts are the fixup
+//     slots of the chunks its (sequence, head group) crosses, found from the decode
+//     kernel's flat chunking (same prefix, same chunk length). Rows inside one
+//     chunk were finalised by the decode kernel; rows with no pages are written
+//     here as zeros / (0, -inf, 0).
 //   all mode: every (rank, part) slot is a partial (possibly empty: l = 0).
 template <int DMAX, int ROWS>
 __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
@@ -680,34 +693,45 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
     const int row = blockIdx.x * ROWS + rr;
     if (row >= mp.rows) break;
     int nparts, ranks;
+    // ctx mode: parts are the fixup slots of the chunks c_first..c_last the
+    // (sequence, head group) of this row crosses.
+    long long cfirst = 0, gstart = 0;
+    int hl = 0;
     if (mp.context_lens) {
       const int seq = row / mp.heads, h = row - seq * mp.heads;
       const int G = mp.heads / mp.kv_heads;
-      const int kvh = h / G, hc = (h - kvh * G) / mp.heads_per_chunk;
+      const int kvh = h / G, gh = h - kvh * G, hc = gh / mp.heads_per_chunk;
+      hl = gh - hc * mp.heads_per_chunk;
       const int y = kvh * mp.head_chunks + hc;
       const int np = pre[seq + 1] - pre[seq];
       if (np == 0) {
         nparts = 0;
       } else {
-        const long long gstart = static_cast<long long>(y) * Ptot + pre[seq];
-        nparts = static_cast<int>((gstart + np - 1) / chunk - gstart / chunk + 1);
+        gstart = static_cast<long long>(y) * Ptot + pre[seq];
+        cfirst = gstart / chunk;
+        nparts = static_cast<int>((gstart + np - 1) / chunk - cfirst + 1);
       }
-      if (mp.skip_single && nparts == 1) continue;
-      if (nparts > mp.parts_per_rank) nparts = mp.parts_per_rank;
+      if (nparts == 1) continue;  // finalised by the decode kernel
       ranks = 1;
     } else {
       nparts = mp.parts_per_rank;
       ranks = mp.ranks;
     }
-    // Stats of every (rank, part) slot of the row, 32 slots per pass; the O rows of
-    // a pass are loaded together so each pass costs about two memory round trips.
+    auto slot_of = [&](int j) -> size_t {
+      if (mp.context_lens) {
+        const long long c = cfirst + j;
+        const int k = (j == 0 && gstart != c * chunk) ? 1 : 0;
+        return (static_cast<size_t>(c) * 2 + k) * mp.heads_per_chunk + hl;
+      }
+      const int rk = j / nparts, pj = j - rk * nparts;
+      return (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + pj;
+    };
+    // Stats of every part of the row, 32 parts per pass; the O rows of a pass are
+    // loaded together so each pass costs about two memory round trips.
     const int total = ranks * nparts;
-    const size_t rstride = static_cast<size_t>(mp.rows) * mp.parts_per_rank;
-    const size_t rbase = static_cast<size_t>(row) * mp.parts_per_rank;
     float M = NEG_INF;
     for (int j = lane; j < total; j += 32) {
-      const int rk = j / nparts, pj = j - rk * nparts;
-      const size_t slot = rk * rstride + rbase + pj;
+      const size_t slot = slot_of(j);
       const float l = mp.part_stats[slot * 2 + 1];
       if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
     }
@@ -721,8 +745,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
       float wt = 0.f, l = 0.f;
       size_t myslot = 0;
       if (j < total) {
-        const int rk = j / nparts, pj = j - rk * nparts;
-        myslot = rk * rstride + rbase + pj;
+        myslot = slot_of(j);
         l = mp.part_stats[myslot * 2 + 1];
         if (l > 0.f) wt = ex2(mp.part_stats[myslot * 2] - M);
       }
@@ -824,6 +847,32 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
   FE_CASE(64, 32, 2)
 #undef FE_CASE
   return cudaErrorInvalidValue;
+}
+
+template <typename T, int D, int BS, int NT>
+static long long grid_max_cfg() {
+  constexpr int NCW = 4;
+  constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
+  constexpr int NSTAGE = NCW * DEPTH;
+  using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
+  auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE>;
+  const int smem = C::smem_bytes(1);
+  if (ensure_smem_optin(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return -1;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NTHREADS, smem) != cudaSuccess)
+    return -1;
+  return static_cast<long long>(sm_count()) * (occ > 0 ? occ : 1);
+}
+
+long long fixup_floats(int head_dim, int block_size, int nt) {
+  long long g = -1;
+#define FE_CASE(D_, BS_, NT_)                                                           \
+  if (head_dim == D_ && block_size == BS_ && nt == NT_) g = grid_max_cfg<__nv_bfloat16, D_, BS_, NT_>();
+  FE_CASE(128, 16, 1) FE_CASE(128, 16, 2) FE_CASE(64, 16, 1) FE_CASE(64, 16, 2)
+  FE_CASE(128, 32, 1) FE_CASE(128, 32, 2) FE_CASE(64, 32, 1) FE_CASE(64, 32, 2)
+#undef FE_CASE
+  if (g < 0) return -1;
+  return g * 2 * (8LL * nt) * (head_dim + 2);
 }
 
 template cudaError_t launch_decode<__nv_bfloat16>(const Params&, int, int, const void*, const void*,

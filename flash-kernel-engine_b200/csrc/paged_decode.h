@@ -13,16 +13,18 @@ struct Params {
   void* out;               // [S, H, D] (T), written for single-split sequences
   const int* block_tables; // [S, max_blocks_per_seq]
   const int* context_lens; // [S]
-  float* part_o;           // [S, H, max_splits, D] fp32 partial O (unnormalised)
-  float* part_ml;          // [S, H, max_splits, 2] (m in log2 units, l)
+  float* part_o;           // fixup slots [grid][2][8*NT][D] fp32 partial O (unnormalised)
+  float* part_ml;          // fixup slots [grid][2][8*NT][2] (m in log2 units, l)
+  float* merged_o;         // partials mode: [S, H, D] merged partial of whole rows
+  float* merged_ml;        // partials mode: [S, H, 2]
   int num_seqs, num_heads, num_kv_heads, max_blocks_per_seq;
   int num_phys_blocks;     // 0 = unknown (no range check)
   int head_chunks;         // ceil(G / (8 * NT))
   int tok_begin, tok_end;  // token window [tok_begin, tok_end) of every sequence
   int pages_per_split;     // unit mode: pages per segment; flat mode: minimum chunk
-  int max_splits;          // partial slots per (seq, head)
   int flat;                // 1: flat (stream-K) chunking, 0: unit mode
-  int direct_final;        // 1: sequences with one split write `out` directly
+  int direct_final;        // 1: whole rows are written normalised to `out`;
+                           // 0: as merged partials to merged_o / merged_ml
   float scale_log2;        // softmax scale * log2(e)
   unsigned* err;           // device error word
   long long dbg_kv_rows;   // rows of the K/V tensor maps (bounds checks in debug builds)
@@ -37,10 +39,10 @@ struct MergeParams {
   // ctx mode (context_lens != nullptr): the valid slots of a row follow from the
   // decode kernel's flat chunking, rebuilt from the same inputs
   const int* context_lens;
-  int num_seqs, heads, kv_heads, heads_per_chunk, head_chunks, groups;
+  int num_seqs, heads, kv_heads, heads_per_chunk, head_chunks, groups;  // heads_per_chunk
+                                                                         // = 8*NT (fixup rows)
   int tok_begin, tok_end, block_size;
   int decode_ctas, chunk_min;
-  int skip_single;         // rows with one slot were finalised by the decode kernel
   void* out;
   float* out_stats;
   int out_dtype;           // 0 f32 final, 1 bf16 final, 2 merged partial, 3 fp16 final
@@ -61,6 +63,10 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
                           cudaStream_t stream);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
+
+// Floats of fixup scratch (O and stats together) the flat-mode decode needs for
+// this shape, or -1 if the shape is unsupported.
+long long fixup_floats(int head_dim, int block_size, int nt);
 
 }  // namespace paged
 }  // namespace fe

@@ -14,7 +14,7 @@ from .ops import (  # noqa: F401
     merge_partials,
     naive_attention,
     paged_attention,
-    paged_attention_splits,
+    paged_attention_workspace_floats,
     paged_decode_partials,
 )
 
@@ -27,7 +27,7 @@ __all__ = [
     "naive_attention",
     "paged_decode_partials",
     "merge_partials",
-    "paged_attention_splits",
+    "paged_attention_workspace_floats",
     "device_errors",
     "get_version",
 ]

@@ -109,27 +109,38 @@ def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, blo
     return S, H, Hkv, d, nb, block_tables.shape[1]
 
 
-def paged_attention_splits(num_seqs, num_heads, num_kv_heads, head_dim, block_size,
-                           max_context_len) -> int:
-    """Default split count of the split-KV (v2) bf16 kernel."""
-    return int(_lib_c.fe_paged_attention_v2_default_splits(
-        num_seqs, num_heads, num_kv_heads, head_dim, block_size, max_context_len))
+def paged_attention_workspace_floats(num_heads, num_kv_heads, head_dim, block_size=16) -> int:
+    """Float32 elements of workspace the split-KV (v2) bf16 decode needs on the current
+    device for this head configuration (independent of batch and context lengths)."""
+    n = int(_lib_c.fe_paged_attention_v2_workspace_floats(num_heads, num_kv_heads, head_dim,
+                                                          block_size))
+    if n == 0:
+        raise ValueError("unsupported head configuration for the bf16 decode")
+    return n
+
+
+def _workspace(query, H, Hkv, d, bs, workspace):
+    n = paged_attention_workspace_floats(H, Hkv, d, bs)
+    if workspace is None:
+        return torch.empty(n, dtype=torch.float32, device=query.device), n
+    if workspace.dtype != torch.float32 or workspace.numel() < n or not workspace.is_cuda:
+        raise ValueError(f"workspace must be a CUDA float32 tensor of >= {n} elements")
+    return workspace, workspace.numel()
 
 
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
                     block_size: int = 16, scale: float | None = None, *,
-                    max_context_len: int | None = None, num_splits: int | None = None,
-                    out=None, workspace=None, version: str = "auto"):
+                    max_context_len: int | None = None, out=None, workspace=None,
+                    version: str = "auto"):
     """Paged-KV decode attention (one query token per sequence).
 
     query [S, H, d]; key_cache/value_cache [num_blocks, Hkv, block_size, d];
     block_tables [S, max_blocks] int32; context_lens [S] int32. Returns [S, H, d].
 
-    ``max_context_len`` sizes the split-KV work split (default: max_blocks *
-    block_size, which needs no device sync); ``version`` "v1" forces the
-    single-pass kernel, "v2" the split-KV kernel with scratch (bf16 only).
-    ``workspace`` optionally passes a preallocated (scratch_out, scratch_stats)
-    pair sized [S*H*splits*d] and [S*H*splits*2] float32.
+    bf16 caches use the split-KV kernel (``version`` "auto"/"v2"), whose ``workspace``
+    (float32, ``paged_attention_workspace_floats(...)`` elements) is allocated here
+    if not given, or the single-pass kernel (``version="v1"``, no workspace).
+    fp16 and fp32 caches use the single-pass kernels.
     """
     _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
@@ -152,45 +163,27 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
                 _lib.check(_lib_c.fe_paged_attention_v1_bf16(*args_head, _stream()),
                            "paged_attention")
             else:
-                splits = num_splits or paged_attention_splits(S, H, Hkv, d, block_size,
-                                                              int(max_context_len))
-                if workspace is None:
-                    so = torch.empty(max(1, S * H * splits * d), dtype=torch.float32,
-                                     device=query.device)
-                    ss = torch.empty(max(1, S * H * splits * 2), dtype=torch.float32,
-                                     device=query.device)
-                else:
-                    so, ss = workspace
-                    if so.numel() < S * H * splits * d or ss.numel() < S * H * splits * 2:
-                        raise ValueError("workspace too small for the split count")
-                _lib.check(_lib_c.fe_paged_attention_v2_bf16(*args_head, _ptr(so), _ptr(ss),
-                                                             splits, _stream()),
-                           "paged_attention")
+                ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+                _lib.check(_lib_c.fe_paged_attention_v2_bf16(*args_head, _ptr(ws), n,
+                                                             _stream()), "paged_attention")
         else:
             raise TypeError(f"unsupported dtype {query.dtype}")
     return out
 
 
 def paged_decode_partials(query, key_cache, value_cache, block_tables, context_lens,
-                          token_begin: int, token_end: int, num_splits: int,
-                          block_size: int = 16, scale: float | None = None, workspace=None,
-                          out=None, out_stats=None):
+                          token_begin: int, token_end: int, block_size: int = 16,
+                          scale: float | None = None, workspace=None, out=None, out_stats=None):
     """Partial attention of every (sequence, query head) over the token window
     [token_begin, token_end) (bf16 cache; token_begin a multiple of block_size).
 
     Returns (O [S, H, d] f32 unnormalised, stats [S, H, 2] f32 = (m log2, l)); an
-    empty window gives (0, (-inf, 0)). ``num_splits`` pieces of the window run in
-    parallel and are merged on the device; ``workspace`` optionally passes their
-    (scratch_out, scratch_stats) buffers [S*H*splits*d], [S*H*splits*2]."""
+    empty window gives (0, (-inf, 0)). ``workspace`` as for ``paged_attention``."""
     _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
                                            context_lens, block_size)
     dev = query.device
-    if workspace is None:
-        so = torch.empty(max(1, S * H * num_splits * d), dtype=torch.float32, device=dev)
-        ss = torch.empty(max(1, S * H * num_splits * 2), dtype=torch.float32, device=dev)
-    else:
-        so, ss = workspace
+    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
     if out is None:
         out = torch.empty((S, H, d), dtype=torch.float32, device=dev)
     if out_stats is None:
@@ -199,8 +192,8 @@ def paged_decode_partials(query, key_cache, value_cache, block_tables, context_l
         _lib.check(_lib_c.fe_paged_decode_partials_bf16(
             _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
             _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
-            int(token_begin), int(token_end), int(num_splits), _ptr(so), _ptr(ss), _ptr(out),
-            _ptr(out_stats), _stream()), "paged_decode_partials")
+            int(token_begin), int(token_end), _ptr(ws), n, _ptr(out), _ptr(out_stats),
+            _stream()), "paged_decode_partials")
     return out, out_stats
 
 

@@ -76,7 +76,7 @@ def allgather_merge(local_out: torch.Tensor, local_stats: torch.Tensor, merge, g
 
 def paged_decode_kv_range(query, key_cache, value_cache, block_tables, context_lens,
                           max_context_len: int, block_size: int = 16, scale=None,
-                          num_splits: int = 8, group=None, out_dtype: str = "bf16"):
+                          group=None, out_dtype: str = "bf16", workspace=None):
     """KV-range-sharded paged decode (bf16 cache) on this rank's GPU.
 
     ``key_cache`` / ``value_cache`` hold this rank's blocks; ``block_tables`` maps the
@@ -88,7 +88,7 @@ def paged_decode_kv_range(query, key_cache, value_cache, block_tables, context_l
     rank = dist.get_rank(group)
     tb, te = kv_range_bounds(max_context_len, world, rank, block_size)
     o, st = ops.paged_decode_partials(query, key_cache, value_cache, block_tables,
-                                      context_lens, tb, te, num_splits, block_size, scale)
+                                      context_lens, tb, te, block_size, scale, workspace)
     S, H, d = query.shape
 
     def merge(go, gs, w):

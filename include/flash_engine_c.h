@@ -17,9 +17,9 @@
  *   dense attention  Q,O [B, H, N, d]; K,V [B, H, M, d]
  *   paged decode     q,out [S, H, d]; k_cache,v_cache [num_blocks, Hkv, block_size, d];
  *                    block_tables [S, max_blocks_per_seq] int32; context_lens [S] int32
- *   split-KV scratch scratch_out [S, H, num_splits, d] f32; scratch_stats
- *                    [S, H, num_splits, 2] f32 = (m, l) with m in log2 units of the
- *                    scaled score, l = sum 2^(s*log2e - m)
+ *   dense split-KV   scratch_out [B, H, num_splits, d] f32; scratch_stats
+ *   scratch          [B, H, num_splits, 2] f32 = (m, l), m in log2 units of the
+ *                    scaled score, l = sum 2^(s*scale*log2e - m)
  *
  * bf16 / fp16 buffers are passed as `const void*` (__nv_bfloat16 / half in C++).
  */
@@ -115,23 +115,27 @@ int fe_paged_attention_v1_bf16(const void* q, const void* k_cache, const void* v
                                int block_size, int max_context_len, int max_blocks_per_seq,
                                int num_blocks, float scale, void* stream);
 
-/* bf16 cache, split-KV with caller-owned scratch (the v2 form of vLLM's paged
- * attention; the reference has only v1). num_splits >= 1 (see
- * fe_paged_attention_v2_default_splits for a choice sized to the GPU); each
- * sequence's pages are cut into pieces of ceil(ceil(max_context_len/block_size) /
- * num_splits) pages and a sequence needing one piece is finalised directly.
- * Scratch sizes: scratch_out
- * num_seqs*num_heads*num_splits*head_dim floats, scratch_stats
- * num_seqs*num_heads*num_splits*2 floats. */
+/* bf16 cache, split-KV with a caller-owned workspace (the v2 form of vLLM's paged
+ * attention; the reference has only v1). The (KV head, sequence, page) space is cut
+ * into equal chunks, one per persistent CTA, whatever the context-length mix; a
+ * sequence crossing chunk boundaries leaves fp32 partials in the workspace that a
+ * log-sum-exp merge combines. workspace must hold
+ * fe_paged_attention_v2_workspace_floats(num_heads, num_kv_heads, head_dim,
+ * block_size) floats (about 2.5 MB at d = 128; independent of the batch and of the
+ * context lengths). max_context_len is not used. */
 int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
                                int block_size, int max_context_len, int max_blocks_per_seq,
-                               int num_blocks, float scale, float* scratch_out,
-                               float* scratch_stats, int num_splits, void* stream);
+                               int num_blocks, float scale, float* workspace,
+                               size_t workspace_floats, void* stream);
 
-/* Maximum scratch of fe_paged_attention_v2_bf16_noalloc, in floats (16 MiB): the call
- * needs num_seqs * num_heads * num_splits * (head_dim + 2) floats of it. */
+/* Workspace floats fe_paged_attention_v2_bf16 and fe_paged_decode_partials_bf16 need
+ * on the current device for this head configuration; 0 if the shape is not supported. */
+size_t fe_paged_attention_v2_workspace_floats(int num_heads, int num_kv_heads, int head_dim,
+                                              int block_size);
+
+/* Maximum scratch of fe_paged_attention_v2_bf16_noalloc, in floats (16 MiB). */
 #define FE_NOALLOC_SCRATCH_FLOATS (4 * 1024 * 1024)
 
 /* The split-KV bf16 decode of fe_paged_attention_v2_bf16 for callers that cannot
@@ -141,8 +145,9 @@ int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v
  * a fixed 16 MiB array inside this library (FE_NOALLOC_SCRATCH_FLOATS), which
  * every GPU that loads the library holds until the process exits; nothing is
  * allocated or freed by this call. It has no counterpart in the reference.
- *   - Returns cudaErrorInvalidValue (1), before touching the GPU, when
- *     num_seqs * num_heads * num_splits * (head_dim + 2) > FE_NOALLOC_SCRATCH_FLOATS.
+ *   - Returns cudaErrorInvalidValue (1), before touching the GPU, when the
+ *     configuration needs more than FE_NOALLOC_SCRATCH_FLOATS floats
+ *     (fe_paged_attention_v2_workspace_floats).
  *   - The first call on a device looks up the array's device address on the
  *     current device; make that first call before any stream capture.
  *   - All calls share the one array: calls that can overlap on the GPU (other
@@ -154,12 +159,7 @@ int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* k_cache, const
                                        const int* context_lens, int num_seqs, int num_heads,
                                        int num_kv_heads, int head_dim, int block_size,
                                        int max_context_len, int max_blocks_per_seq,
-                                       int num_blocks, float scale, int num_splits,
-                                       void* stream);
-
-/* Split count fe_paged_attention_v2_bf16 uses when passed num_splits <= 0. */
-int fe_paged_attention_v2_default_splits(int num_seqs, int num_heads, int num_kv_heads,
-                                         int head_dim, int block_size, int max_context_len);
+                                       int num_blocks, float scale, void* stream);
 
 /* ---------------------------------------------------------------- split-KV decoding
  * Dense [B, H, M, d] fp32 flash decoding with caller-owned scratch. Replaces
@@ -172,12 +172,12 @@ int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* 
                                    int seq_kv, int head_dim, int num_splits, float scale,
                                    void* stream);
 
-/* Paged, GQA split-KV partial over the logical token window [token_begin, token_end)
- * of every sequence (clipped to its context length), bf16 cache: the window is cut
- * into num_splits page-aligned pieces written to scratch_out / scratch_stats
- * (layouts above), which are then merged into ONE partial per (sequence, query
- * head): merged_out [S, H, d] f32 (unnormalised O) and merged_stats [S, H, 2]
- * (m in log2 units, l); a sequence whose window is empty gets (0, -inf, 0).
+/* Paged, GQA partial attention over the logical token window [token_begin,
+ * token_end) of every sequence (clipped to its context length), bf16 cache: ONE
+ * merged partial per (sequence, query head) in merged_out [S, H, d] f32
+ * (unnormalised O) and merged_stats [S, H, 2] (m in log2 units of the scaled score,
+ * l = sum 2^(s*scale*log2e - m)); a sequence whose window is empty gets (0, -inf, 0).
+ * The work is spread like fe_paged_attention_v2_bf16 and needs the same workspace.
  * token_begin must be a multiple of block_size. Used for KV-range sharding across
  * GPUs: each GPU runs its own window, the merged partials are all-gathered and
  * fe_merge_partials combines them. New (the reference has no paged split-KV). */
@@ -185,8 +185,8 @@ int fe_paged_decode_partials_bf16(const void* q, const void* k_cache, const void
                                   const int* block_tables, const int* context_lens, int num_seqs,
                                   int num_heads, int num_kv_heads, int head_dim, int block_size,
                                   int max_blocks_per_seq, int num_blocks, float scale,
-                                  int token_begin, int token_end, int num_splits,
-                                  float* scratch_out, float* scratch_stats, float* merged_out,
+                                  int token_begin, int token_end, float* workspace,
+                                  size_t workspace_floats, float* merged_out,
                                   float* merged_stats, void* stream);
 
 /* Log-sum-exp combine of partials -- the stage-2 reduction of

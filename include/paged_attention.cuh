@@ -51,15 +51,16 @@ cudaError_t launch_paged_attention_v1_bf16(const __nv_bfloat16* d_query,
                                            const PagedAttentionConfig& config,
                                            cudaStream_t stream = nullptr);
 
-// New: bf16 cache, split-KV with caller-owned scratch (sizes in flash_engine_c.h).
+// New: bf16 cache, split-KV with a caller-owned workspace of
+// fe_paged_attention_v2_workspace_floats(...) floats (see flash_engine_c.h).
 cudaError_t launch_paged_attention_v2_bf16(const __nv_bfloat16* d_query,
                                            const __nv_bfloat16* d_key_cache,
                                            const __nv_bfloat16* d_value_cache,
                                            __nv_bfloat16* d_output, const int* d_block_tables,
                                            const int* d_context_lens,
                                            const PagedAttentionConfig& config,
-                                           float* d_scratch_out, float* d_scratch_stats,
-                                           int num_splits, cudaStream_t stream = nullptr);
+                                           float* d_workspace, size_t workspace_floats,
+                                           cudaStream_t stream = nullptr);
 
 }  // namespace paged_attention
 }  // namespace flash_engine

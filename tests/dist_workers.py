@@ -127,7 +127,7 @@ def nccl_kv_range_worker(rank, world, port, result_path):
                  for x in ("q", "k_cache", "v_cache"))
     bt = torch.from_numpy(p["block_tables"]).to(dev)
     cl = torch.from_numpy(p["context_lens"]).to(dev)
-    out = sharding.paged_decode_kv_range(q, kc, vc, bt, cl, M, 16, num_splits=4)
+    out = sharding.paged_decode_kv_range(q, kc, vc, bt, cl, M, 16)
     errs = flash_engine.device_errors()
     ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
                                 p["context_lens"])

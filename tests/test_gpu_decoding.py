@@ -49,7 +49,7 @@ def test_kv_range_partials_merge(ranks):
     per = -(-per // bs) * bs
     outs, stats = [], []
     for r in range(ranks):
-        o, s = flash_engine.paged_decode_partials(q, kc, vc, bt, cl, r * per, (r + 1) * per, 4)
+        o, s = flash_engine.paged_decode_partials(q, kc, vc, bt, cl, r * per, (r + 1) * per)
         outs.append(o)
         stats.append(s)
     go = torch.stack(outs)  # [ranks, S, H, d]
@@ -67,7 +67,7 @@ def test_partials_match_oracle_partials():
     o, s = flash_engine.paged_decode_partials(*(cuda(p[x], torch.bfloat16)
                                                 for x in ("q", "k_cache", "v_cache")),
                                               cuda(p["block_tables"]), cuda(p["context_lens"]),
-                                              32, 96, 2)
+                                              32, 96)
     O_ref, m_ref, l_ref = O.kv_range_partials(p["q"], p["k_cache"], p["v_cache"],
                                               p["block_tables"], p["context_lens"], 32, 96)
     o, s = host(o), host(s)

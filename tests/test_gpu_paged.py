@@ -10,15 +10,14 @@ from oracle import attention_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _run(p, dtype, version="auto", bs=16, num_splits=None, num_blocks_check=True):
+def _run(p, dtype, version="auto", bs=16):
     import flash_engine
     q = cuda(p["q"], dtype)
     kc = cuda(p["k_cache"], dtype)
     vc = cuda(p["v_cache"], dtype)
     bt = cuda(p["block_tables"])
     lens = cuda(p["context_lens"])
-    out = flash_engine.paged_attention(q, kc, vc, bt, lens, bs, version=version,
-                                       num_splits=num_splits)
+    out = flash_engine.paged_attention(q, kc, vc, bt, lens, bs, version=version)
     torch.cuda.synchronize()
     assert flash_engine.device_errors() == 0
     return host(out)
@@ -57,7 +56,7 @@ def test_paged_bf16_random(d, bs, H, Hkv, version):
                              extra_blocks=5)
     ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
                                 p["context_lens"], bs)
-    out = _run(p, torch.bfloat16, version, bs=bs, num_splits=3 if version == "v2" else None)
+    out = _run(p, torch.bfloat16, version, bs=bs)
     assert_bf16_close(out, ref)
 
 
@@ -98,7 +97,7 @@ def test_block_table_gather_is_bit_exact(version):
         j = sel[s]
         kc[p["block_tables"][s, j // bs], :, j % bs, 0] = 64.0
     p2 = dict(p, q=q, k_cache=kc)
-    out = _run(p2, torch.bfloat16, version, num_splits=4 if version == "v2" else None)
+    out = _run(p2, torch.bfloat16, version)
     for s in range(S):
         j = sel[s]
         vrow = p["v_cache"][p["block_tables"][s, j // bs], :, j % bs, :]  # [Hkv, d]
@@ -133,10 +132,10 @@ def test_config3_shape_parity():
     assert_bf16_close(out, ref)
 
 
-def test_config3_full_batch_split_sweep():
+def test_config3_full_batch():
     """All 64 sequences of BASELINE config 3 (seed 0) against the oracle, through the
-    single-pass kernel and the split-KV kernel at several split counts (the flat
-    chunking then cuts sequences at different places)."""
+    single-pass kernel and the split-KV kernel (whose flat chunking cuts sequences
+    at arbitrary pages)."""
     import flash_engine
     lens = O.config3_context_lens(0)
     p = O.make_paged_problem(0, 64, 32, 8, 128, lens)
@@ -144,8 +143,24 @@ def test_config3_full_batch_split_sweep():
                                 p["context_lens"])
     q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
     bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
-    for version, splits in [("v1", None), ("v2", 2), ("v2", 3), ("v2", 9), ("v2", 64)]:
-        out = flash_engine.paged_attention(q, kc, vc, bt, cl, 16, version=version,
-                                           num_splits=splits, max_context_len=int(lens.max()))
+    for version in ("v1", "v2"):
+        out = flash_engine.paged_attention(q, kc, vc, bt, cl, 16, version=version)
         assert flash_engine.device_errors() == 0
         assert_bf16_close(host(out), ref)
+
+
+def test_serving_mix_long_tail():
+    """Config-5-like lognormal context lengths (a few very long sequences among many
+    short ones): the flat chunking spreads the long ones over many CTAs."""
+    import flash_engine
+    lens = O.config5_context_lens(3)[:48]
+    lens[5] = 20000
+    p = O.make_paged_problem(5, len(lens), 64, 8, 128, lens)
+    sel = [0, 5, 17, 47]
+    ref = O.paged_attention_gqa(p["q"][sel], p["k_cache"], p["v_cache"],
+                                p["block_tables"][sel], p["context_lens"][sel])
+    q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+    out = flash_engine.paged_attention(q, kc, vc, cuda(p["block_tables"]),
+                                       cuda(p["context_lens"]), 16)
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out)[sel], ref)

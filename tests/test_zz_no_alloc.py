@@ -30,12 +30,12 @@ def _inputs(seed, lens, H=32, Hkv=8, d=128):
                 max_ctx=int(max(lens)), ref=p)
 
 
-def _noalloc(lib, x, splits, out):
+def _noalloc(lib, x, out, d=None):
     S = x["q"].shape[0]
     return lib.fe_paged_attention_v2_bf16_noalloc(
         x["q"].data_ptr(), x["kc"].data_ptr(), x["vc"].data_ptr(), out.data_ptr(),
-        x["bt"].data_ptr(), x["lens"].data_ptr(), S, x["H"], x["Hkv"], x["d"], 16,
-        x["max_ctx"], x["bt"].shape[1], x["kc"].shape[0], 0.0, splits,
+        x["bt"].data_ptr(), x["lens"].data_ptr(), S, x["H"], x["Hkv"], d or x["d"], 16,
+        x["max_ctx"], x["bt"].shape[1], x["kc"].shape[0], 0.0,
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
@@ -43,14 +43,13 @@ def test_noalloc_matches_scratch_entry_on_two_calls():
     import flash_engine
     from flash_engine import _lib
     lib = _lib.lib
-    problems = [(_inputs(21, [0, 1, 300, 4000, 2049, 16]), 6),
-                (_inputs(22, [700, 33, 1, 1500], H=64, Hkv=8, d=64), 3)]
-    for x, splits in problems:
+    problems = [_inputs(21, [0, 1, 300, 4000, 2049, 16]),
+                _inputs(22, [700, 33, 1, 1500], H=64, Hkv=4, d=64)]
+    for x in problems:
         ref = flash_engine.paged_attention(x["q"], x["kc"], x["vc"], x["bt"], x["lens"], 16,
-                                           max_context_len=x["max_ctx"], num_splits=splits,
                                            version="v2")
         out = torch.full_like(x["q"], float("nan"))
-        assert _noalloc(lib, x, splits, out) == 0
+        assert _noalloc(lib, x, out) == 0
         torch.cuda.synchronize()
         assert flash_engine.device_errors() == 0
         assert_bf16_close(host(out), host(ref))
@@ -61,15 +60,19 @@ def test_noalloc_matches_scratch_entry_on_two_calls():
         assert_bf16_close(host(out), oracle)
 
 
-def test_noalloc_rejects_oversize_scratch():
+def test_noalloc_limit_and_rejection():
+    """The library-owned scratch covers every supported head configuration on this
+    GPU; shapes the kernel does not support are refused before any GPU work."""
     from flash_engine import _lib
     lib = _lib.lib
+    limit = 4 * 1024 * 1024  # FE_NOALLOC_SCRATCH_FLOATS
+    for H, Hkv in ((32, 8), (64, 8), (64, 4), (16, 1)):
+        for d in (64, 128):
+            need = lib.fe_paged_attention_v2_workspace_floats(H, Hkv, d, 16)
+            assert 0 < need <= limit, (H, Hkv, d, need)
     x = _inputs(23, [64, 64])
     out = torch.empty_like(x["q"])
-    limit = 4 * 1024 * 1024  # FE_NOALLOC_SCRATCH_FLOATS
-    S, H, d = 2, 32, 128
-    too_many = limit // (S * H * (d + 2)) + 1
-    assert _noalloc(lib, x, too_many, out) == 1
-    assert _noalloc(lib, x, too_many - 1, out) == 0
+    assert _noalloc(lib, x, out, d=96) == 1
+    assert _noalloc(lib, x, out) == 0
     torch.cuda.synchronize()
     assert np.isfinite(host(out)).all()
