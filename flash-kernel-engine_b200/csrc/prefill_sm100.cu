@@ -39,6 +39,11 @@ namespace prefill {
 
 constexpr float NEG_INF = -__builtin_huge_valf();
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
+// One exponential pair in every kPolyEvery goes to the FMA-pipe polynomial (0: none).
+#ifndef FE_PREFILL_POLY_EVERY
+#define FE_PREFILL_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = FE_PREFILL_POLY_EVERY;
 
 template <int D>
 struct PCfg {
@@ -76,6 +81,31 @@ __device__ __forceinline__ float ex2_poly(float x) {
   q = fmaf(q, f, 0.693261f);
   q = fmaf(q, f, 0.99992806f);
   return __int_as_float(__float_as_int(q) + (n << 23));
+}
+
+// Paired fp32 arithmetic of sm_100 (two lanes per instruction) and the 3-input max.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 template <typename T>
@@ -303,43 +333,57 @@ __global__ void __launch_bounds__(384, 1)
         for (int i = 0; i < BN; ++i)
           if (c0 + i >= lim) u[i] = __float_as_uint(NEG_INF);
       }
-      // Row max with 8 independent chains (sl > 0, so max(s) * sl = max(s * sl)).
+      // Row max: 3-input max over pairs, 8 independent chains (sl > 0, so
+      // max(s) * sl = max(s * sl)).
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(u[i]);
 #pragma unroll
-      for (int i = 8; i < BN; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(u[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl;
+      for (int i = 8; i < BN; i += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          m8[k] = max3(m8[k], __uint_as_float(u[i + 2 * k]), __uint_as_float(u[i + 2 * k + 1]));
+      const float mx = max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]),
+                            fmaxf(m8[6], m8[7])) * sl;
       const float m_new = fmaxf(m_run, mx);
       const bool need = m_new > m_run + kRescaleThreshold;  // also true while m_run = -inf
       const float m_use = need ? m_new : m_run;
       const float mu = m_use == NEG_INF ? 0.f : m_use;
       const float corr = need ? ex2(m_run - mu) : 1.f;
-      // p = 2^(s*sl - m): one FFMA each, then the MUFU ex2 for 3 of every 4 pairs and
-      // a polynomial on the FMA pipe for the 4th (splits the work over both pipes).
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // p = 2^(s*sl - m): one FFMA each, then the MUFU ex2, except one pair in every
+      // kPolyEvery that uses a polynomial on the FMA pipe (splits the work over both).
+      uint64_t acc2[4] = {0, 0, 0, 0};  // paired partial sums (0 bits = 0.0f, 0.0f)
+      const uint64_t sl2 = f2(sl, sl), nmu2 = f2(-mu, -mu);
 #pragma unroll
       for (int c4 = 0; c4 < BN / 64; ++c4) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float xa = fmaf(__uint_as_float(u[c4 * 64 + 2 * i]), sl, -mu);
-          const float xb = fmaf(__uint_as_float(u[c4 * 64 + 2 * i + 1]), sl, -mu);
+          const uint64_t x2 = fma2(f2(__uint_as_float(u[c4 * 64 + 2 * i]),
+                                      __uint_as_float(u[c4 * 64 + 2 * i + 1])),
+                                   sl2, nmu2);
+          float xa, xb;
+          f2_split(x2, xa, xb);
           float a, b;
-          if ((i & 3) == 3) {
+          if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
             a = ex2_poly(xa);
             b = ex2_poly(xb);
           } else {
             a = ex2(xa);
             b = ex2(xb);
           }
-          sum4[i & 3] += a + b;
+          acc2[i & 3] = add2(acc2[i & 3], f2(a, b));
           pk[i] = pack2<T>(a, b);
         }
         tc::st32(tS + c4 * 32, pk);
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float lo, hi;
+        f2_split(acc2[k], lo, hi);
+        sum += lo + hi;
+      }
       l_run = l_run * corr + sum;
       m_run = m_use;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
