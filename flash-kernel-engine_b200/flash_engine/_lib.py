@@ -46,11 +46,17 @@ _SIGS = {
     "fe_paged_decode_partials_bf16": ([_P] * 5 + [_I] * 7 + [_F, _I, _I, _P, ctypes.c_size_t,
                                                               _P, _P, _P], _I),
     "fe_merge_partials": ([_P, _P, _I, _I, _I, _I, _P, _P, _I, _P], _I),
+    "fe_graph_capture": ([None, _P, _P, ctypes.POINTER(ctypes.c_void_p)], _I),
+    "fe_graph_launch": ([_P, _P], _I),
+    "fe_graph_destroy": ([_P], None),
 }
+
+# void record(void* stream, void* user): the step recorded by fe_graph_capture
+RECORD_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_void_p)
 
 for _name, (_args, _res) in _SIGS.items():
     _fn = getattr(lib, _name)
-    _fn.argtypes = _args
+    _fn.argtypes = [RECORD_FN if a is None else a for a in _args]
     _fn.restype = _res
 
 EXPORTED = tuple(_SIGS)

@@ -1,10 +1,11 @@
 // Umbrella header of the B200 inference-attention library -- drop-in for the
-// hot-path part of the reference's include/flash_engine.h:1-31. Only the
-// attention headers are included; the reference's other kernels (RMSNorm,
-// activations, RoPE, speculative decoding, quantized GEMM, cross-entropy,
-// memory pool, graph runner) are not part of this library.
+// hot-path part of the reference's include/flash_engine.h:1-31: the attention
+// headers and the CUDA graph runner used to capture decode steps. The reference's
+// other kernels (RMSNorm, activations, speculative decoding, quantized GEMM,
+// cross-entropy) and its memory pool are not part of this library.
 #pragma once
 
+#include "cuda_graph_runner.h"
 #include "cuda_utils.cuh"
 #include "flash_attention.cuh"
 #include "flash_decoding.cuh"

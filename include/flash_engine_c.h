@@ -206,6 +206,17 @@ int fe_merge_partials(const float* part_out, const float* part_stats, int rows, 
                       int parts_per_rank, int head_dim, void* out, float* out_stats,
                       int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------- CUDA graphs
+ * Capture-once / replay-per-step of a decode step (kernels, merges and -- when the
+ * recorded function issues them -- NCCL collectives). Wraps the CUDAGraphRunner of
+ * include/cuda_graph_runner.h, the C++ class of the reference's
+ * include/cuda_graph_runner.h:10-35 / src/cuda_graph_runner.cu:14-55.
+ * `record(stream, user)` enqueues the step on `stream` during capture. */
+typedef void (*fe_record_fn)(void* stream, void* user);
+int fe_graph_capture(fe_record_fn record, void* user, void* stream, void** graph_out);
+int fe_graph_launch(void* graph, void* stream);
+void fe_graph_destroy(void* graph);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -136,3 +136,41 @@ def nccl_kv_range_worker(rank, world, port, result_path):
     dist.destroy_process_group()
     with open(f"{result_path}.{rank}", "w") as f:
         f.write(repr((err, errs)))
+
+
+def nccl_graph_worker(rank, world, port, result_path):
+    """The KV-range-sharded decode step, NCCL all-gather included, captured once in
+    a CUDA graph and replayed on new query tokens."""
+    import torch
+    import torch.distributed as dist
+    from flash_engine import graph, sharding
+    from oracle import attention_oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    lens = [9, 300, 1024, 2000]
+    p = O.make_paged_problem(51, len(lens), 32, 8, 128, lens)
+    dev = torch.device("cuda", rank)
+    q, kc, vc = (torch.from_numpy(p[x]).to(dev).to(torch.bfloat16)
+                 for x in ("q", "k_cache", "v_cache"))
+    bt = torch.from_numpy(p["block_tables"]).to(dev)
+    cl = torch.from_numpy(p["context_lens"]).to(dev)
+    g = graph.DecodeGraph(lambda: sharding.paged_decode_kv_range(q, kc, vc, bt, cl, 2000, 16))
+    errs = []
+    for seed in (52, 53):
+        q2 = O.make_paged_problem(seed, len(lens), 32, 8, 128, lens)["q"]
+        q.copy_(torch.from_numpy(q2).to(dev).to(torch.bfloat16))
+        out = g.replay()
+        torch.cuda.synchronize()
+        ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        errs.append(float(np.abs(out.float().cpu().numpy() - ref).max()))
+    del g
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr(max(errs)))

@@ -18,3 +18,11 @@ def test_kv_range_nccl_two_gpus(tmp_path):
     for err, dev_errors in res:
         assert dev_errors == 0
         assert err <= 2e-2
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_graph_captured_kv_range_step_two_gpus(tmp_path):
+    res = _run(dist_workers.nccl_graph_worker, 2, tmp_path, join_timeout=180)
+    assert all(r is not None for r in res), res
+    assert all(e <= 2e-2 for e in res)
