@@ -39,6 +39,7 @@ struct PagedArgs {
   const int* lens;
   int S, H, Hkv, d, bs, max_ctx, maxb, num_blocks;
   float scale;
+  int kv_layout = fe::paged::kKvFlat;
 };
 
 int paged_check(const PagedArgs& a, bool tensor_core) {
@@ -47,6 +48,8 @@ int paged_check(const PagedArgs& a, bool tensor_core) {
     return kErr;
   if (tensor_core) {
     if (!(a.d == 64 || a.d == 128) || !(a.bs == 16 || a.bs == 32)) return kErr;
+    if (a.kv_layout == fe::paged::kKvVllm && a.bs != 16) return kErr;
+    if (a.kv_layout != fe::paged::kKvFlat && a.kv_layout != fe::paged::kKvVllm) return kErr;
     if (!aligned(a.kc, 16) || !aligned(a.vc, 16) || !aligned(a.q, 4) || !aligned(a.out, 2))
       return kErr;
     if (a.num_blocks > 0 &&
@@ -123,7 +126,8 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;
     p.err = err;
     int grid = 0;
-    cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, &grid, st);
+    cudaError_t e =
+        fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, a.kv_layout, &grid, st);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (pl.merge_dtype < 0) continue;
     fe::paged::MergeParams mp{};
@@ -246,7 +250,26 @@ int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, vo
                                int bs, int max_ctx, int maxb, int num_blocks, float scale,
                                void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
+  a.kv_layout = fe::paged::kKvVllm;  // the layout include/paged_attention.cuh:29-30 declares
   return paged_v1_tc<half>(a, as_stream(stream));
+}
+
+int fe_paged_attention_ex(const void* q, const void* kc, const void* vc, void* out,
+                          const int* bt, const int* lens, int S, int H, int Hkv, int d, int bs,
+                          int maxb, int num_blocks, float scale, int dtype, int kv_layout,
+                          float* workspace, size_t workspace_floats, void* stream) {
+  PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
+  a.kv_layout = kv_layout;
+  cudaStream_t st = as_stream(stream);
+  if (dtype == 0) {
+    return workspace ? paged_v2_tc<__nv_bfloat16>(a, workspace, workspace_floats, st)
+                     : paged_v1_tc<__nv_bfloat16>(a, st);
+  }
+  if (dtype == 1) {
+    return workspace ? paged_v2_tc<half>(a, workspace, workspace_floats, st)
+                     : paged_v1_tc<half>(a, st);
+  }
+  return kErr;
 }
 
 int fe_paged_attention_v1_bf16(const void* q, const void* kc, const void* vc, void* out,

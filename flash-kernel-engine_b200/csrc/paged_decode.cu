@@ -24,9 +24,12 @@
 //    in every CTA, so no host synchronisation or scratch is needed to skip or
 //    place work.
 //  * One producer warp streams each (block, KV head) page of K and V into shared
-//    memory with 2-D TMA bulk-tensor loads (128-byte swizzle, L2 evict-first, no
-//    cluster sharing), completing on mbarriers. Block-table entries are fetched 32 at a
-//    time, one 32-page group ahead of the loads they feed.
+//    memory, completing on mbarriers. Flat cache layout: 2-D TMA bulk-tensor loads
+//    with 128-byte swizzle. vLLM layout (K [blocks, Hkv, d/8, 16, 8], V [blocks,
+//    Hkv, d, 16]): one contiguous bulk copy per page of K and of V; that layout is
+//    already conflict-free for ldmatrix (K chunks of 8 tokens are 128 contiguous
+//    bytes, V is stored as V^T rows). L2 evict-first; single-CTA destinations.
+//    Block-table entries are fetched 32 at a time, one 32-page group ahead.
 //  * NCW consumer warps, each with a private ring of DEPTH stages (page gi of the
 //    CTA belongs to warp gi % NCW). Per 16 tokens a warp computes S^T = K Q^T with
 //    mma.m16n8k16 (tokens x query heads: all G query heads of the group share
@@ -254,7 +257,7 @@ struct Cfg {
   static int smem_bytes(int num_seqs) { return FIXED_SMEM + (num_seqs + 1) * 4; }
 };
 
-template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
+template <typename T, int D, int BS, int NT, int NCW, int NSTAGE, int KVL>
 __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
 
   if (warp == NCW) {
     // ===================================================== producer warp
-    if (lane == 0) {
+    if (lane == 0 && KVL == kKvFlat) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
@@ -389,10 +392,16 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
 #ifdef FE_DEBUG_CHECKS
               if (static_cast<long long>(y) + BS > p.dbg_kv_rows) atomicOr(p.err, 1u << 8);
 #endif
+              if constexpr (KVL == kKvFlat) {
 #pragma unroll
-              for (int h = 0; h < HALVES; ++h) {
-                tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
-                tma_load_2d(vs + h * BS * 128, &vmap, h * 64, y, &full[s], pol);
+                for (int h = 0; h < HALVES; ++h) {
+                  tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
+                  tma_load_2d(vs + h * BS * 128, &vmap, h * 64, y, &full[s], pol);
+                }
+              } else {
+                const size_t off = static_cast<size_t>(y) * D * 2;  // page = BS*D elements
+                bulk_load(ks, static_cast<const uint8_t*>(p.k_cache) + off, TILE, &full[s], pol);
+                bulk_load(vs, static_cast<const uint8_t*>(p.v_cache) + off, TILE, &full[s], pol);
               }
             } else {
               mbar_arrive(&full[s]);  // nothing to load; consumers skip the page
@@ -498,10 +507,20 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
           // Rows outside the window may hold anything (NaN included); P is 0 there
           // but 0 * NaN is not, so clear those V rows before the PV product.
           uint8_t* vrow = smem + s * STAGE + TILE;
-          for (int idx = lane; idx < BS * HALVES * 8; idx += 32) {
-            const int row = (idx >> 3) % BS, h = idx / (8 * BS), ch = idx & 7;
-            if (row < vlo || row >= vhi)
-              *reinterpret_cast<uint4*>(vrow + h * BS * 128 + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+          if constexpr (KVL == kKvFlat) {
+            for (int idx = lane; idx < BS * HALVES * 8; idx += 32) {
+              const int row = (idx >> 3) % BS, h = idx / (8 * BS), ch = idx & 7;
+              if (row < vlo || row >= vhi)
+                *reinterpret_cast<uint4*>(vrow + h * BS * 128 + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+            }
+          } else {
+            // V^T rows: one BS-token row per head dimension
+            for (int dim = lane; dim < D; dim += 32) {
+              uint16_t* vr = reinterpret_cast<uint16_t*>(vrow) + dim * BS;
+#pragma unroll
+              for (int tk = 0; tk < BS; ++tk)
+                if (tk < vlo || tk >= vhi) vr[tk] = 0;
+            }
           }
           __syncwarp();
           zeroed = true;
@@ -520,7 +539,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
             for (int kk = 0; kk < D / 16; ++kk) {
               const int ch = 2 * kk + (mq >> 1);
               const uint32_t addr =
-                  ks + (ch >> 3) * (BS * 128) + tok * 128 + ((((ch & 7) ^ (tok & 7))) << 4);
+                  KVL == kKvFlat
+                      ? ks + (ch >> 3) * (BS * 128) + tok * 128 + ((((ch & 7) ^ (tok & 7))) << 4)
+                      : ks + (ch * BS + tok) * 16;
               uint32_t a[4];
               ldsm_x4(addr, a[0], a[1], a[2], a[3]);
 #pragma unroll
@@ -562,17 +583,24 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
             pb[nt][0] = movmatrix_t(E::pack(p0, p1));
             pb[nt][1] = movmatrix_t(E::pack(p2, p3));
           }
-          // O^T += V^T P^T : A = V^T via ldmatrix.trans
+          // O^T += V^T P^T : A = V^T, via ldmatrix.trans of the swizzled V tile (flat)
+          // or plain ldmatrix of the V^T rows (vLLM layout)
           {
             const int mq = lane >> 3;
-            const int tok = t * 16 + (lane & 7) + 8 * (mq >> 1);
 #pragma unroll
             for (int mt = 0; mt < D / 16; ++mt) {
-              const int ch = 2 * mt + (mq & 1);
-              const uint32_t addr =
-                  vs + (ch >> 3) * (BS * 128) + tok * 128 + ((((ch & 7) ^ (tok & 7))) << 4);
               uint32_t a[4];
-              ldsm_x4_t(addr, a[0], a[1], a[2], a[3]);
+              if constexpr (KVL == kKvFlat) {
+                const int tok = t * 16 + (lane & 7) + 8 * (mq >> 1);
+                const int ch = 2 * mt + (mq & 1);
+                const uint32_t addr =
+                    vs + (ch >> 3) * (BS * 128) + tok * 128 + ((((ch & 7) ^ (tok & 7))) << 4);
+                ldsm_x4_t(addr, a[0], a[1], a[2], a[3]);
+              } else {
+                const int dim = mt * 16 + (lane & 7) + 8 * (mq & 1);
+                const int tok = t * 16 + 8 * (mq >> 1);
+                ldsm_x4(vs + (dim * BS + tok) * 2, a[0], a[1], a[2], a[3]);
+              }
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) E::mma(o[nt][mt], a, pb[nt][0], pb[nt][1]);
             }
@@ -800,7 +828,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
 // ---------------------------------------------------------------------------
 // host launch
 
-template <typename T, int D, int BS, int NT>
+template <typename T, int D, int BS, int NT, int KVL>
 static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, long long kv_rows,
                               int* grid_out, cudaStream_t stream) {
   constexpr int NCW = 4;
@@ -808,16 +836,18 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
   constexpr int NSTAGE = NCW * DEPTH;
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
-  auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE>;
+  auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE, KVL>;
   const int smem = C::smem_bytes(p.num_seqs);
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
-  CUtensorMap km, vm;
-  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  e = encode_tma_2d_b16(&km, kc, bf16, D, kv_rows, D, 64, BS);
-  if (e != cudaSuccess) return e;
-  e = encode_tma_2d_b16(&vm, vc, bf16, D, kv_rows, D, 64, BS);
-  if (e != cudaSuccess) return e;
+  CUtensorMap km = {}, vm = {};
+  if (KVL == kKvFlat) {
+    const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+    e = encode_tma_2d_b16(&km, kc, bf16, D, kv_rows, D, 64, BS);
+    if (e != cudaSuccess) return e;
+    e = encode_tma_2d_b16(&vm, vc, bf16, D, kv_rows, D, 64, BS);
+    if (e != cudaSuccess) return e;
+  }
   int occ = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NTHREADS, smem);
   if (e != cudaSuccess) return e;
@@ -826,25 +856,31 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   if (grid_out) *grid_out = grid;
   Params pp = p;
   pp.dbg_kv_rows = kv_rows;
+  pp.k_cache = kc;
+  pp.v_cache = vc;
   kern<<<grid, C::NTHREADS, smem, stream>>>(km, vm, pp);
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* kc,
-                          const void* vc, long long kv_rows, int nt, int* grid_out,
+                          const void* vc, long long kv_rows, int nt, int kv_layout, int* grid_out,
                           cudaStream_t stream) {
-#define FE_CASE(D_, BS_, NT_)                                                     \
-  if (head_dim == D_ && block_size == BS_ && nt == NT_)                           \
-    return launch_cfg<T, D_, BS_, NT_>(p, kc, vc, kv_rows, grid_out, stream);
-  FE_CASE(128, 16, 1)
-  FE_CASE(128, 16, 2)
-  FE_CASE(64, 16, 1)
-  FE_CASE(64, 16, 2)
-  FE_CASE(128, 32, 1)
-  FE_CASE(128, 32, 2)
-  FE_CASE(64, 32, 1)
-  FE_CASE(64, 32, 2)
+#define FE_CASE(D_, BS_, NT_, L_)                                                   \
+  if (head_dim == D_ && block_size == BS_ && nt == NT_ && kv_layout == L_)          \
+    return launch_cfg<T, D_, BS_, NT_, L_>(p, kc, vc, kv_rows, grid_out, stream);
+  FE_CASE(128, 16, 1, kKvFlat)
+  FE_CASE(128, 16, 2, kKvFlat)
+  FE_CASE(64, 16, 1, kKvFlat)
+  FE_CASE(64, 16, 2, kKvFlat)
+  FE_CASE(128, 32, 1, kKvFlat)
+  FE_CASE(128, 32, 2, kKvFlat)
+  FE_CASE(64, 32, 1, kKvFlat)
+  FE_CASE(64, 32, 2, kKvFlat)
+  FE_CASE(128, 16, 1, kKvVllm)
+  FE_CASE(128, 16, 2, kKvVllm)
+  FE_CASE(64, 16, 1, kKvVllm)
+  FE_CASE(64, 16, 2, kKvVllm)
 #undef FE_CASE
   return cudaErrorInvalidValue;
 }
@@ -855,7 +891,7 @@ static long long grid_max_cfg() {
   constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
   constexpr int NSTAGE = NCW * DEPTH;
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
-  auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE>;
+  auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE, kKvFlat>;
   const int smem = C::smem_bytes(1);
   if (ensure_smem_optin(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return -1;
   int occ = 0;
@@ -876,9 +912,9 @@ long long fixup_floats(int head_dim, int block_size, int nt) {
 }
 
 template cudaError_t launch_decode<__nv_bfloat16>(const Params&, int, int, const void*, const void*,
-                                                  long long, int, int*, cudaStream_t);
+                                                  long long, int, int, int*, cudaStream_t);
 template cudaError_t launch_decode<half>(const Params&, int, int, const void*, const void*,
-                                         long long, int, int*, cudaStream_t);
+                                         long long, int, int, int*, cudaStream_t);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream) {
   if (mp.rows <= 0) return cudaSuccess;

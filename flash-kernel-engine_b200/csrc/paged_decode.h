@@ -8,8 +8,16 @@
 namespace fe {
 namespace paged {
 
+// KV-cache layouts of the tensor-core decode.
+enum KvLayout : int {
+  kKvFlat = 0,  // K and V [num_blocks, Hkv, BS, D] (the reference's fp32 layout)
+  kKvVllm = 1,  // vLLM: K [num_blocks, Hkv, D/8, BS, 8], V [num_blocks, Hkv, D, BS]
+};
+
 struct Params {
   const void* q;           // [S, H, D] (T)
+  const void* k_cache;     // used by the bulk-copy (vLLM layout) path
+  const void* v_cache;
   void* out;               // [S, H, D] (T), written for single-split sequences
   const int* block_tables; // [S, max_blocks_per_seq]
   const int* context_lens; // [S]
@@ -59,8 +67,8 @@ inline int pages_per_split_for(int max_pages, int splits) {
 // ctx-mode merge to rebuild the flat chunking).
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* k_cache,
-                          const void* v_cache, long long kv_rows, int nt, int* grid_out,
-                          cudaStream_t stream);
+                          const void* v_cache, long long kv_rows, int nt, int kv_layout,
+                          int* grid_out, cudaStream_t stream);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
 

@@ -104,6 +104,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int x, i
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Contiguous bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completing on an mbarrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA / tensor core) accesses of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -95,11 +95,22 @@ def naive_attention(q, k, v, is_causal: bool = False, scale: float | None = None
 
 
 # --------------------------------------------------------------------------- paged
-def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, block_size):
+def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, block_size,
+                  kv_layout="flat"):
     S, H, d = query.shape
-    nb, Hkv, bs, d2 = key_cache.shape
-    if bs != block_size or d2 != d or value_cache.shape != key_cache.shape:
-        raise ValueError("cache must be [num_blocks, Hkv, block_size, d] matching query")
+    if kv_layout == "flat":
+        nb, Hkv, bs, d2 = key_cache.shape
+        ok = bs == block_size and d2 == d and value_cache.shape == key_cache.shape
+    elif kv_layout == "vllm":
+        nb, Hkv, dx, bs, x = key_cache.shape
+        ok = (bs == block_size and dx * x == d and x == 8
+              and tuple(value_cache.shape) == (nb, Hkv, d, bs))
+    else:
+        raise ValueError("kv_layout must be 'flat' or 'vllm'")
+    if not ok:
+        raise ValueError("cache shape does not match the layout: flat K/V [num_blocks, Hkv, "
+                         "block_size, d]; vllm K [num_blocks, Hkv, d/8, block_size, 8], "
+                         "V [num_blocks, Hkv, d, block_size]")
     if H % Hkv:
         raise ValueError("num_heads must be a multiple of num_kv_heads")
     if block_tables.dtype != torch.int32 or context_lens.dtype != torch.int32:
@@ -131,41 +142,46 @@ def _workspace(query, H, Hkv, d, bs, workspace):
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
                     block_size: int = 16, scale: float | None = None, *,
                     max_context_len: int | None = None, out=None, workspace=None,
-                    version: str = "auto"):
+                    version: str = "auto", kv_layout: str = "flat"):
     """Paged-KV decode attention (one query token per sequence).
 
-    query [S, H, d]; key_cache/value_cache [num_blocks, Hkv, block_size, d];
-    block_tables [S, max_blocks] int32; context_lens [S] int32. Returns [S, H, d].
-
-    bf16 caches use the split-KV kernel (``version`` "auto"/"v2"), whose ``workspace``
-    (float32, ``paged_attention_workspace_floats(...)`` elements) is allocated here
-    if not given, or the single-pass kernel (``version="v1"``, no workspace).
-    fp16 and fp32 caches use the single-pass kernels.
+    query [S, H, d]; block_tables [S, max_blocks] int32; context_lens [S] int32.
+    Returns [S, H, d]. Cache layouts (``kv_layout``):
+      "flat" -- K and V [num_blocks, Hkv, block_size, d] (the reference's fp32 layout);
+      "vllm" -- K [num_blocks, Hkv, d/8, block_size, 8], V [num_blocks, Hkv, d,
+                block_size] (vLLM's x-packed layout; bf16/fp16, block_size 16).
+    bf16 / fp16 use the split-KV kernel (``version`` "auto"/"v2") with a float32
+    ``workspace`` of ``paged_attention_workspace_floats(...)`` elements (allocated here
+    if not given), or the single-pass kernel (``version="v1"``, no workspace). fp32
+    caches use the single-pass fp32 kernel.
     """
     _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
-                                           context_lens, block_size)
+                                           context_lens, block_size, kv_layout)
     if out is None:
         out = torch.empty_like(query)
     sc = _scale_arg(scale, d)
     if max_context_len is None:
         max_context_len = maxb * block_size
-    args_head = (_ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out),
-                 _ptr(block_tables), _ptr(context_lens), S, H, Hkv, d, block_size,
-                 int(max_context_len), maxb, nb, sc)
     with torch.cuda.device(query.device):
         if query.dtype == torch.float32:
-            _lib.check(_lib_c.fe_paged_attention_v1_fp32(*args_head, _stream()), "paged_attention")
-        elif query.dtype == torch.float16:
-            _lib.check(_lib_c.fe_paged_attention_v1_fp16(*args_head, _stream()), "paged_attention")
-        elif query.dtype == torch.bfloat16:
+            if kv_layout != "flat":
+                raise ValueError("the fp32 decode takes the flat cache layout")
+            _lib.check(_lib_c.fe_paged_attention_v1_fp32(
+                _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out), _ptr(block_tables),
+                _ptr(context_lens), S, H, Hkv, d, block_size, int(max_context_len), maxb, nb, sc,
+                _stream()), "paged_attention")
+        elif query.dtype in (torch.bfloat16, torch.float16):
+            dt = 0 if query.dtype == torch.bfloat16 else 1
+            lay = 0 if kv_layout == "flat" else 1
             if version == "v1":
-                _lib.check(_lib_c.fe_paged_attention_v1_bf16(*args_head, _stream()),
-                           "paged_attention")
+                ws, n = None, 0
             else:
                 ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
-                _lib.check(_lib_c.fe_paged_attention_v2_bf16(*args_head, _ptr(ws), n,
-                                                             _stream()), "paged_attention")
+            _lib.check(_lib_c.fe_paged_attention_ex(
+                _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out), _ptr(block_tables),
+                _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, sc, dt, lay,
+                _ptr(ws) if ws is not None else None, n, _stream()), "paged_attention")
         else:
             raise TypeError(f"unsupported dtype {query.dtype}")
     return out

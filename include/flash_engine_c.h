@@ -95,15 +95,29 @@ int fe_paged_attention_v1_fp32(const float* q, const float* k_cache, const float
                                int block_size, int max_context_len, int max_blocks_per_seq,
                                int num_blocks, float scale, void* stream);
 
-/* fp16 cache in the same [num_blocks, Hkv, block_size, d] layout as the fp32 entry.
- * Replaces the launch_paged_attention_v1_fp16 stub (include/paged_attention.cuh:27-36,
- * src/paged_attention.cu:218-230, which launches nothing). block_size 16 or 32,
+/* fp16 cache in the layout the reference's header declares for this entry
+ * (include/paged_attention.cuh:27-36, vLLM's x-packed layout, x = 8 halves):
+ * K [num_blocks, Hkv, head_dim/8, block_size, 8], V [num_blocks, Hkv, head_dim,
+ * block_size]. Replaces the launch_paged_attention_v1_fp16 stub
+ * (src/paged_attention.cu:218-230, which launches nothing). block_size 16,
  * head_dim 64 or 128. */
 int fe_paged_attention_v1_fp16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
                                int block_size, int max_context_len, int max_blocks_per_seq,
                                int num_blocks, float scale, void* stream);
+
+/* General tensor-core paged decode: dtype 0 = bf16, 1 = fp16; kv_layout 0 = flat
+ * [num_blocks, Hkv, block_size, d] (K and V), 1 = vLLM x-packed (K [num_blocks, Hkv,
+ * d/8, block_size, 8], V [num_blocks, Hkv, d, block_size]; block_size 16). With a
+ * workspace (fe_paged_attention_v2_workspace_floats floats) it runs the split-KV
+ * path, without one (NULL) the single-pass path. New. */
+int fe_paged_attention_ex(const void* q, const void* k_cache, const void* v_cache, void* out,
+                          const int* block_tables, const int* context_lens, int num_seqs,
+                          int num_heads, int num_kv_heads, int head_dim, int block_size,
+                          int max_blocks_per_seq, int num_blocks, float scale, int dtype,
+                          int kv_layout, float* workspace, size_t workspace_floats,
+                          void* stream);
 
 /* bf16 cache, single pass, no scratch: one unit of work per (sequence, KV head),
  * its pages spread over the CTA's consumer warps and merged in shared memory.

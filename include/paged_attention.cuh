@@ -1,7 +1,9 @@
 // Paged-KV decode -- drop-in for the reference's include/paged_attention.cuh
 // (namespaces, PagedAttentionConfig and v1 launcher signatures as in :7-48).
-// Cache layout for every dtype: [num_blocks, num_kv_heads, block_size, head_dim]
-// (the layout the reference's fp32 kernel implements, src/paged_attention.cu:73).
+// Cache layouts as the reference declares them: fp32 (and the new bf16 entries)
+// [num_blocks, num_kv_heads, block_size, head_dim]; fp16 vLLM x-packed
+// K [num_blocks, num_kv_heads, head_dim/8, block_size, 8], V [num_blocks,
+// num_kv_heads, head_dim, block_size].
 #pragma once
 
 #include <cmath>
@@ -29,7 +31,7 @@ struct PagedAttentionConfig {
         scale(1.0f / std::sqrt(static_cast<float>(dim))) {}
 };
 
-// fp16 cache (the reference's entry is a stub that launches nothing).
+// fp16 cache, vLLM layout (the reference's entry is a stub that launches nothing).
 cudaError_t launch_paged_attention_v1_fp16(const half* d_query, const half* d_key_cache,
                                            const half* d_value_cache, half* d_output,
                                            const int* d_block_tables, const int* d_context_lens,

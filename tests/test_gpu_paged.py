@@ -164,3 +164,49 @@ def test_serving_mix_long_tail():
                                        cuda(p["context_lens"]), 16)
     assert flash_engine.device_errors() == 0
     assert_bf16_close(host(out)[sel], ref)
+
+
+def _to_vllm(kc, vc):
+    """[nb, Hkv, bs, d] -> vLLM K [nb, Hkv, d/8, bs, 8] and V [nb, Hkv, d, bs]."""
+    nb, hkv, bs, d = kc.shape
+    kx = np.ascontiguousarray(kc.reshape(nb, hkv, bs, d // 8, 8).transpose(0, 1, 3, 2, 4))
+    vx = np.ascontiguousarray(vc.transpose(0, 1, 3, 2))
+    return kx, vx
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("version", ["v1", "v2"])
+@pytest.mark.parametrize("H,Hkv,d", [(32, 8, 128), (64, 4, 64), (8, 8, 128)])
+def test_paged_vllm_layout(dtype, version, H, Hkv, d):
+    import flash_engine
+    lens = [0, 1, 15, 16, 17, 250, 1500]
+    p = O.make_paged_problem(61 + H + d, len(lens), H, Hkv, d, lens, extra_blocks=3)
+    kc, vc = p["k_cache"], p["v_cache"]
+    if dtype == torch.float16:
+        kc, vc = kc.astype(np.float16).astype(np.float32), vc.astype(np.float16).astype(np.float32)
+    ref = O.paged_attention_gqa(p["q"], kc, vc, p["block_tables"], p["context_lens"])
+    kx, vx = _to_vllm(kc, vc)
+    out = flash_engine.paged_attention(cuda(p["q"], dtype), cuda(kx, dtype), cuda(vx, dtype),
+                                       cuda(p["block_tables"]), cuda(p["context_lens"]), 16,
+                                       version=version, kv_layout="vllm")
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out), ref, atol=2e-2 if dtype == torch.bfloat16 else 5e-3)
+
+
+def test_fp16_reference_entry_takes_vllm_layout(golden):
+    """fe_paged_attention_v1_fp16 follows the layout the reference's header declares
+    for it; the constant known-answer case gives 0.25."""
+    from flash_engine import _lib
+    g = golden("paged_kat")
+    kx, vx = _to_vllm(g["k_cache"], g["v_cache"])
+    q, kc, vc = cuda(g["q"], torch.float16), cuda(kx, torch.float16), cuda(vx, torch.float16)
+    out = torch.empty_like(q)
+    bt, cl = cuda(g["block_tables"]), cuda(g["context_lens"])
+    S, H, d = g["q"].shape
+    rc = _lib.lib.fe_paged_attention_v1_fp16(q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                             out.data_ptr(), bt.data_ptr(), cl.data_ptr(), S, H,
+                                             H, d, 16, 64, bt.shape[1], 0, 0.0,
+                                             torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host(out), np.full((S, H, d), 0.25, np.float32))
