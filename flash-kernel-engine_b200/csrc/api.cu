@@ -40,6 +40,9 @@ struct PagedArgs {
   int S, H, Hkv, d, bs, max_ctx, maxb, num_blocks;
   float scale;
   int kv_layout = fe::paged::kKvFlat;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_max_pos = 0;
 };
 
 int paged_check(const PagedArgs& a, bool tensor_core) {
@@ -124,6 +127,9 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.flat = pl.flat ? 1 : 0;
     p.direct_final = pl.direct_final ? 1 : 0;
     p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;
+    p.rope_cos = a.rope_cos;
+    p.rope_sin = a.rope_sin;
+    p.rope_max_pos = a.rope_max_pos;
     p.err = err;
     int grid = 0;
     cudaError_t e =
@@ -257,9 +263,15 @@ int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, vo
 int fe_paged_attention_ex(const void* q, const void* kc, const void* vc, void* out,
                           const int* bt, const int* lens, int S, int H, int Hkv, int d, int bs,
                           int maxb, int num_blocks, float scale, int dtype, int kv_layout,
+                          const float* rope_cos, const float* rope_sin, int rope_max_pos,
                           float* workspace, size_t workspace_floats, void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
   a.kv_layout = kv_layout;
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return kErr;
+  if (rope_cos && rope_max_pos < 1) return kErr;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.rope_max_pos = rope_max_pos;
   cudaStream_t st = as_stream(stream);
   if (dtype == 0) {
     return workspace ? paged_v2_tc<__nv_bfloat16>(a, workspace, workspace_floats, st)

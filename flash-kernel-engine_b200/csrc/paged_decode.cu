@@ -443,7 +443,21 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
 
   uint32_t qf[NT][D / 16][2];
   uint32_t qn[NT][D / 16][2];
+  // q fragments (B operand of S^T = K Q^T): register j of k-step ks holds the
+  // dimension pair (2i, 2i+1) with i = ks*8 + 4j + c, so the optional rotary
+  // embedding (src/fused_rope.cu:33-43 arithmetic: x0 c - x1 s, x0 s + x1 c) is
+  // applied pair by pair in fp32 before the repack.
   auto load_q = [&](uint32_t (&dst)[NT][D / 16][2], const Seg& sg) {
+    const bool rope = p.rope_cos != nullptr;
+    int pos = 0;
+    if (rope) {
+      pos = __ldg(p.context_lens + sg.seq) - 1;
+      if (pos < 0) pos = 0;
+      if (pos >= p.rope_max_pos) {
+        if (lane == 0) atomicOr(p.err, kErrBadBlock);
+        pos = p.rope_max_pos - 1;
+      }
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int gh = sg.hc * HPC + nt * 8 + g;
@@ -452,8 +466,20 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
           qbase + (static_cast<size_t>(sg.seq) * p.num_heads + sg.kvh * G + (v ? gh : 0)) * D;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
-        dst[nt][ks][0] = v ? __ldg(reinterpret_cast<const unsigned*>(qp + ks * 16 + 2 * c)) : 0u;
-        dst[nt][ks][1] = v ? __ldg(reinterpret_cast<const unsigned*>(qp + ks * 16 + 8 + 2 * c)) : 0u;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t w = v ? __ldg(reinterpret_cast<const unsigned*>(qp + ks * 16 + 8 * j + 2 * c))
+                         : 0u;
+          if (rope && v) {
+            const int i = ks * 8 + 4 * j + c;
+            const float cs = __ldg(p.rope_cos + static_cast<size_t>(pos) * (D / 2) + i);
+            const float sn = __ldg(p.rope_sin + static_cast<size_t>(pos) * (D / 2) + i);
+            const T* e = reinterpret_cast<const T*>(&w);
+            const float x0 = static_cast<float>(e[0]), x1 = static_cast<float>(e[1]);
+            w = E::pack(x0 * cs - x1 * sn, x0 * sn + x1 * cs);
+          }
+          dst[nt][ks][j] = w;
+        }
       }
     }
   };

@@ -34,6 +34,11 @@ struct Params {
   int direct_final;        // 1: whole rows are written normalised to `out`;
                            // 0: as merged partials to merged_o / merged_ml
   float scale_log2;        // softmax scale * log2(e)
+  // Optional rotary embedding of the query token (position context_len - 1): pair
+  // (2i, 2i+1) is rotated by cos/sin[pos][i] of [rope_max_pos, D/2] fp32 tables.
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_max_pos;
   unsigned* err;           // device error word
   long long dbg_kv_rows;   // rows of the K/V tensor maps (bounds checks in debug builds)
 };

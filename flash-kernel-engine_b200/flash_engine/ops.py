@@ -142,7 +142,7 @@ def _workspace(query, H, Hkv, d, bs, workspace):
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
                     block_size: int = 16, scale: float | None = None, *,
                     max_context_len: int | None = None, out=None, workspace=None,
-                    version: str = "auto", kv_layout: str = "flat"):
+                    version: str = "auto", kv_layout: str = "flat", rope=None):
     """Paged-KV decode attention (one query token per sequence).
 
     query [S, H, d]; block_tables [S, max_blocks] int32; context_lens [S] int32.
@@ -154,6 +154,10 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
     ``workspace`` of ``paged_attention_workspace_floats(...)`` elements (allocated here
     if not given), or the single-pass kernel (``version="v1"``, no workspace). fp32
     caches use the single-pass fp32 kernel.
+
+    ``rope=(cos, sin)`` (bf16/fp16): float32 CUDA tables [max_pos, d/2]; each query is
+    rotated at position context_len - 1 inside the kernel (pairs (2i, 2i+1), the
+    arithmetic of the reference's fused RoPE). Cached keys are taken as already rotated.
     """
     _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
@@ -178,9 +182,17 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
                 ws, n = None, 0
             else:
                 ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+            rc, rs, rmax = None, None, 0
+            if rope is not None:
+                rcos, rsin = rope
+                _require_cuda(rcos, rsin)
+                if rcos.dtype != torch.float32 or rcos.shape != rsin.shape or \
+                        rcos.dim() != 2 or rcos.shape[1] != d // 2:
+                    raise ValueError("rope tables must be float32 [max_pos, d/2]")
+                rc, rs, rmax = _ptr(rcos), _ptr(rsin), rcos.shape[0]
             _lib.check(_lib_c.fe_paged_attention_ex(
                 _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out), _ptr(block_tables),
-                _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, sc, dt, lay,
+                _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, sc, dt, lay, rc, rs, rmax,
                 _ptr(ws) if ws is not None else None, n, _stream()), "paged_attention")
         else:
             raise TypeError(f"unsupported dtype {query.dtype}")

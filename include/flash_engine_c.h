@@ -111,12 +111,17 @@ int fe_paged_attention_v1_fp16(const void* q, const void* k_cache, const void* v
  * [num_blocks, Hkv, block_size, d] (K and V), 1 = vLLM x-packed (K [num_blocks, Hkv,
  * d/8, block_size, 8], V [num_blocks, Hkv, d, block_size]; block_size 16). With a
  * workspace (fe_paged_attention_v2_workspace_floats floats) it runs the split-KV
- * path, without one (NULL) the single-pass path. New. */
+ * path, without one (NULL) the single-pass path.
+ * rope_cos / rope_sin (NULL = off): fp32 tables [rope_max_pos, d/2]; the query of
+ * sequence s is rotated at position context_lens[s] - 1 in the kernel prologue,
+ * pairs (2i, 2i+1) as in the reference's src/fused_rope.cu:33-43 (the cached keys are
+ * expected to be rotated already, as a cache-writing step stores them). New. */
 int fe_paged_attention_ex(const void* q, const void* k_cache, const void* v_cache, void* out,
                           const int* block_tables, const int* context_lens, int num_seqs,
                           int num_heads, int num_kv_heads, int head_dim, int block_size,
                           int max_blocks_per_seq, int num_blocks, float scale, int dtype,
-                          int kv_layout, float* workspace, size_t workspace_floats,
+                          int kv_layout, const float* rope_cos, const float* rope_sin,
+                          int rope_max_pos, float* workspace, size_t workspace_floats,
                           void* stream);
 
 /* bf16 cache, single pass, no scratch: one unit of work per (sequence, KV head),

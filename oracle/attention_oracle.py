@@ -320,3 +320,30 @@ def config5_context_lens(seed: int = 0, num_seqs: int = 256):
     rng = np.random.default_rng(seed)
     x = rng.lognormal(mean=math.log(1024.0), sigma=1.0, size=num_seqs)
     return np.clip(np.round(x), 16, 32768).astype(np.int32)
+
+
+# --------------------------------------------------------------------------
+# Rotary position embedding (the arithmetic of src/fused_rope.cu:29-43)
+# --------------------------------------------------------------------------
+
+def rope_tables(max_pos: int, head_dim: int, base: float = 10000.0):
+    """cos/sin tables [max_pos, head_dim/2] (float32) for pair i at position p:
+    angle = p * base^(-2i/head_dim) (RoPEConfig's theta_base, include/fused_rope.cuh:13)."""
+    i = np.arange(head_dim // 2, dtype=np.float64)
+    inv = base ** (-2.0 * i / head_dim)
+    ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def rope_rotate(x, cos, sin, pos):
+    """Rotate adjacent pairs (2i, 2i+1) of x[..., d] by cos/sin[pos, i]:
+    (x0 c - x1 s, x0 s + x1 c) -- src/fused_rope.cu:33-43. `pos` broadcasts over the
+    leading dimensions of x: cos[pos] must broadcast against x[..., 0::2]."""
+    x = np.asarray(x, dtype=np.float64)
+    c = np.asarray(cos, np.float64)[pos]
+    s = np.asarray(sin, np.float64)[pos]
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x0 * s + x1 * c
+    return out

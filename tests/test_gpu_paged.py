@@ -210,3 +210,27 @@ def test_fp16_reference_entry_takes_vllm_layout(golden):
     assert rc == 0
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(out), np.full((S, H, d), 0.25, np.float32))
+
+
+@pytest.mark.parametrize("version", ["v1", "v2"])
+@pytest.mark.parametrize("kv_layout", ["flat", "vllm"])
+def test_paged_decode_fused_query_rope(version, kv_layout):
+    """RoPE of the query token at position context_len - 1, applied in the kernel
+    prologue, against the oracle rotating q first."""
+    import flash_engine
+    lens = [1, 33, 700, 2000]
+    p = O.make_paged_problem(71, len(lens), 32, 8, 128, lens)
+    cos, sin = O.rope_tables(4096, 128)
+    pos = np.maximum(np.asarray(lens) - 1, 0)
+    q_rot = O.bf16_round(O.rope_rotate(p["q"], cos, sin, pos[:, None]).astype(np.float32))
+    ref = O.paged_attention_gqa(q_rot, p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    kc, vc = p["k_cache"], p["v_cache"]
+    if kv_layout == "vllm":
+        kc, vc = _to_vllm(kc, vc)
+    out = flash_engine.paged_attention(cuda(p["q"], torch.bfloat16), cuda(kc, torch.bfloat16),
+                                       cuda(vc, torch.bfloat16), cuda(p["block_tables"]),
+                                       cuda(p["context_lens"]), 16, version=version,
+                                       kv_layout=kv_layout, rope=(cuda(cos), cuda(sin)))
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out), ref)

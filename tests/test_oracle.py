@@ -96,3 +96,19 @@ def test_config_generators():
     used = np.concatenate([p["block_tables"][s, :(int(c) + 15) // 16]
                            for s, c in enumerate(p["context_lens"])])
     assert len(set(used.tolist())) == len(used) == p["k_cache"].shape[0]
+
+
+def test_rope_rotation_is_the_reference_formula():
+    cos, sin = O.rope_tables(64, 8)
+    x = np.arange(16, dtype=np.float32).reshape(2, 8)
+    pos = np.array([3, 40])
+    got = O.rope_rotate(x, cos, sin, pos)
+    for r in range(2):
+        for i in range(4):
+            c, s = float(cos[pos[r], i]), float(sin[pos[r], i])
+            x0, x1 = float(x[r, 2 * i]), float(x[r, 2 * i + 1])
+            assert abs(got[r, 2 * i] - (x0 * c - x1 * s)) < 1e-6
+            assert abs(got[r, 2 * i + 1] - (x0 * s + x1 * c)) < 1e-6
+    # a rotation keeps pair norms
+    assert np.allclose(np.linalg.norm(got.reshape(2, 4, 2), axis=-1),
+                       np.linalg.norm(x.reshape(2, 4, 2), axis=-1))
