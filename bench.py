@@ -258,7 +258,7 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     lens_t = torch.from_numpy(lens).to(dev)
     out = torch.empty_like(q)
     max_ctx = int(lens.max())
-    wsp = torch.empty(flash_engine.paged_attention_workspace_floats(h_l, hkv_l, d, bs),
+    wsp = torch.zeros(flash_engine.paged_attention_workspace_floats(h_l, hkv_l, d, bs),
                       dtype=torch.float32, device=dev)
 
     def call(i):
@@ -333,14 +333,14 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
         "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (ms_rank * 1e-3) / 1e9, 2),
                      "peak": peak_hbm, "unit": "GB/s",
                      "frac": round(rank_bytes / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
-                     "peak_source": src, "kernel": "paged_decode_kernel + merge_kernel",
+                     "peak_source": src, "kernel": "paged_decode_kernel (merge fused)",
                      "traffic": _traffic("paged_decode_config3_traffic.json")
                      if cfg is CFG3 and ws == 1 else None},
         "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
                 "d2h_bytes_per_step": int(out_h.numel() * 2)},
-        "gpu_launches": 2 * steps,
+        "gpu_launches": steps,
         "clocks": sampler.summary(t0, t1),
     }
     if with_cpu and rank == 0 and ws == 1:
@@ -409,7 +409,7 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
         dist.broadcast(q_all, 0)        # every rank decodes the same query tokens
     bt_t = torch.from_numpy(bt).to(dev)
     lens_t = torch.full((B,), M, dtype=torch.int32, device=dev)
-    wsp = torch.empty(flash_engine.paged_attention_workspace_floats(H, Hkv, d, bs),
+    wsp = torch.zeros(flash_engine.paged_attention_workspace_floats(H, Hkv, d, bs),
                       dtype=torch.float32, device=dev)
 
     def call(i, qq=q_all, bb=bt_t, ll=lens_t):
@@ -418,8 +418,15 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
                                                 version="v2", workspace=wsp)
         return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
 
+    # A step (decode, all-gather and merge at N > 1) is one CUDA-graph replay.
+    from flash_engine.graph import DecodeGraph
+    graph = DecodeGraph(lambda: call(0))
+
+    def step(i):
+        graph.replay()
+
     sampler = ClockSampler(local).start()
-    ms_rank, t0, t1 = _time_steps(call, steps, warmup, ws, dev)
+    ms_rank, t0, t1 = _time_steps(step, steps, warmup, ws, dev)
     sampler.stop()
     assert flash_engine.device_errors() == 0
     ms = _max_over_ranks(ms_rank, ws, dev)
@@ -445,6 +452,7 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
     for i in range(n):
         e2e(i)
     e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n, ws, dev)
+    del graph
     peak_hbm, _, _, src = _peaks()
     return {
         "metric": c["metric"], "value": round(kv_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",

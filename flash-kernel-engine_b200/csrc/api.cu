@@ -68,8 +68,7 @@ int paged_check(const PagedArgs& a, bool tensor_core) {
 struct DecodePlan {
   int tok_begin = 0, tok_end = INT_MAX;
   bool flat = false;          // stream-K chunking with fixup partials (needs workspace)
-  bool direct_final = true;   // whole rows: normalised output (else merged partials)
-  int merge_dtype = -1;       // -1: no merge; else MergeParams::out_dtype
+  bool direct_final = true;   // normalised output rows (else merged partials)
   float* merged_out = nullptr;
   float* merged_stats = nullptr;
 };
@@ -78,12 +77,12 @@ inline int decode_nt(int H, int Hkv) { return (H / Hkv) <= 8 ? 1 : 2; }
 
 long long workspace_floats_for(int H, int Hkv, int d, int bs) {
   if (H <= 0 || Hkv <= 0 || H % Hkv) return -1;
-  return fe::paged::fixup_floats(d, bs, decode_nt(H, Hkv));
+  return fe::paged::fixup_layout(d, bs, decode_nt(H, Hkv)).floats;
 }
 
-// Runs the tensor-core decode (and, if planned, the log-sum-exp merge) over all
-// sequences, in chunks of kMaxSeqsPerLaunch sequences. `ws` holds the fixup slots
-// of flat mode (fixup_floats of them).
+// Runs the tensor-core decode over all sequences, in launches of at most
+// kMaxSeqsPerLaunch sequences. In flat mode `ws` holds the arrival counters and
+// fixup slots (fixup_layout); the kernel merges split sequences itself.
 template <typename T>
 int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream_t st) {
   const int nt = decode_nt(a.H, a.Hkv);
@@ -96,12 +95,13 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
   if (!err) return static_cast<int>(cudaErrorInitializationError);
   float* part_o = nullptr;
   float* part_ml = nullptr;
+  int* counters = nullptr;
   if (pl.flat) {
-    const long long nf = workspace_floats_for(a.H, a.Hkv, a.d, a.bs);
-    if (nf <= 0 || !ws) return kErr;
-    const long long slot_rows = nf / (a.d + 2);
-    part_o = ws;
-    part_ml = ws + slot_rows * a.d;
+    const fe::paged::FixupLayout f = fe::paged::fixup_layout(a.d, a.bs, nt);
+    if (f.floats <= 0 || !ws) return kErr;
+    counters = reinterpret_cast<int*>(ws);
+    part_o = ws + fe::paged::kCounterSlots;
+    part_ml = part_o + f.slot_rows * a.d;
   }
   for (int s0 = 0; s0 < a.S; s0 += kMaxSeqsPerLaunch) {
     const int n = a.S - s0 < kMaxSeqsPerLaunch ? a.S - s0 : kMaxSeqsPerLaunch;
@@ -113,6 +113,7 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.context_lens = a.lens + s0;
     p.part_o = part_o;
     p.part_ml = part_ml;
+    p.counters = counters;
     p.merged_o = pl.merged_out ? pl.merged_out + row0 * a.d : nullptr;
     p.merged_ml = pl.merged_stats ? pl.merged_stats + row0 * 2 : nullptr;
     p.num_seqs = n;
@@ -131,37 +132,8 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.rope_sin = a.rope_sin;
     p.rope_max_pos = a.rope_max_pos;
     p.err = err;
-    int grid = 0;
-    cudaError_t e =
-        fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt, a.kv_layout, &grid, st);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    if (pl.merge_dtype < 0) continue;
-    fe::paged::MergeParams mp{};
-    mp.part_out = part_o;
-    mp.part_stats = part_ml;
-    mp.rows = n * a.H;
-    mp.ranks = 1;
-    mp.parts_per_rank = 1;
-    mp.context_lens = p.context_lens;
-    mp.num_seqs = n;
-    mp.heads = a.H;
-    mp.kv_heads = a.Hkv;
-    mp.heads_per_chunk = hpc;
-    mp.head_chunks = head_chunks;
-    mp.groups = a.Hkv * head_chunks;
-    mp.tok_begin = pl.tok_begin;
-    mp.tok_end = pl.tok_end;
-    mp.block_size = a.bs;
-    mp.decode_ctas = grid;
-    mp.chunk_min = 1;
-    if (pl.merge_dtype == 2) {
-      mp.out = p.merged_o;
-      mp.out_stats = p.merged_ml;
-    } else {
-      mp.out = p.out;
-    }
-    mp.out_dtype = pl.merge_dtype;
-    e = fe::paged::launch_merge(mp, a.d, st);
+    const cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt,
+                                                      a.kv_layout, nullptr, st);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   return 0;
@@ -188,7 +160,6 @@ int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st
   DecodePlan pl;
   pl.flat = true;
   pl.direct_final = true;
-  pl.merge_dtype = std::is_same<T, __nv_bfloat16>::value ? 1 : 3;
   return paged_tc_run<T>(a, pl, ws, st);
 }
 
@@ -325,6 +296,10 @@ static int noalloc_scratch_ptr(float** out) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return static_cast<int>(e);
+    // The split-KV arrival counters at the start of the scratch must begin at zero
+    // (every call leaves them so).
+    e = cudaMemset(p, 0, sizeof(int) * fe::paged::kCounterSlots);
+    if (e != cudaSuccess) return static_cast<int>(e);
     ptrs[dev] = static_cast<float*>(p);
   }
   *out = ptrs[dev];
@@ -385,7 +360,6 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
   pl.tok_end = te;
   pl.flat = true;
   pl.direct_final = false;
-  pl.merge_dtype = 2;
   pl.merged_out = mout;
   pl.merged_stats = mstats;
   return paged_tc_run<__nv_bfloat16>(a, pl, workspace, as_stream(stream));

@@ -18,8 +18,12 @@
 //        context-length mix. A sequence inside one chunk is finalised directly. Only
 //        the first and the last segment of a chunk can be pieces of a longer
 //        sequence, so each CTA owns two fp32 partial slots of a small fixup buffer
-//        (slot 0: its first segment, slot 1: its last); merge_kernel combines the
-//        pieces of every sequence that crosses a chunk boundary.
+//        (slot 0: its first segment, slot 1: its last). After its last segment a
+//        CTA bumps the arrival counter of each sequence it holds a piece of
+//        (indexed by the chunk the sequence starts in); the CTA whose piece
+//        arrives last combines all pieces with the log-sum-exp merge and resets
+//        the counter to zero. No second kernel and no waiting; counting at the end
+//        keeps the fence and atomic out of the streaming loop.
 //    Both modes read context_lens and build the page prefix with a block-wide scan
 //    in every CTA, so no host synchronisation or scratch is needed to skip or
 //    place work.
@@ -168,6 +172,8 @@ struct Seg {
   int lo, hi;     // valid tokens [lo, hi)
   int slot;       // flat mode: 0 = first segment of the CTA's chunk, 1 = a later one
   int nslots;     // chunks (segments) of this (sequence, head group); 1 = finalise here
+  int cfirst;     // flat mode: chunk holding the first page of this (sequence, group)
+  int kfirst;     // flat mode: slot of the piece in chunk cfirst (1 if it starts mid-chunk)
 };
 
 // Walks the segments of one CTA. Producer and consumers run identical copies.
@@ -201,6 +207,7 @@ struct SegIter {
       g.hi = w.hi;
       g.slot = split;
       g.nslots = pre[seq + 1] - pre[seq];
+      g.cfirst = g.kfirst = 0;
       return true;
     }
     if (P >= Pend) return false;
@@ -222,6 +229,8 @@ struct SegIter {
     g.hi = w.hi;
     const int cfirst = static_cast<int>(gstart / chunk);
     g.nslots = static_cast<int>(gend / chunk) - cfirst + 1;
+    g.cfirst = cfirst;
+    g.kfirst = gstart != static_cast<long long>(cfirst) * chunk ? 1 : 0;
     g.slot = first_seg ? 0 : 1;
     first_seg = false;
     P += n;
@@ -243,6 +252,122 @@ struct StageOf {
   }
 };
 
+// Log-sum-exp combine of the `total` partials of one output row by one warp
+// (src/flash_decoding.cu:151-223: g = max m_p, L = sum l_p 2^(m_p - g),
+// O = sum O_p 2^(m_p - g)); part j lives at slot slot_of(j) of part_out (D floats)
+// and part_stats (m in log2 units, l); empty parts (l = 0) carry no weight.
+// Returns M = g (-inf if every part is empty), L, and acc[e] = O at dim lane + 32e.
+// Loads bypass L1: the partials may have been written by other CTAs of this grid.
+// Up to BATCH parts take one memory round trip (stats and O rows loaded together);
+// more take one for the stats and one per BATCH parts of O rows.
+template <int PER, int BATCH, typename SlotOf>
+__device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_out,
+                                                 const float* __restrict__ part_stats, int total,
+                                                 int D, SlotOf slot_of, float& M_out, float& L_out,
+                                                 float (&acc)[PER]) {
+  const int lane = threadIdx.x & 31;
+  if (total <= BATCH) {
+    // Few parts: the stats and every O row are loaded at once (one round trip).
+    float m = NEG_INF, l = 0.f;
+    if (lane < total) {
+      const size_t slot = slot_of(lane);
+      m = __ldcg(part_stats + slot * 2);
+      l = __ldcg(part_stats + slot * 2 + 1);
+    }
+    float v[BATCH][PER];
+#pragma unroll
+    for (int k = 0; k < BATCH; ++k) {
+      const float* po = part_out + (k < total ? slot_of(k) : 0) * D;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const int dim = lane + 32 * e;
+        v[k][e] = (k < total && dim < D) ? __ldcg(po + dim) : 0.f;
+      }
+    }
+    float M = l > 0.f ? m : NEG_INF;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w = l > 0.f ? ex2(m - M) : 0.f;
+    float L = l * w;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int k = 0; k < BATCH; ++k) {
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * wk;
+    }
+    M_out = M;
+    L_out = L;
+    return;
+  }
+  float M = NEG_INF;
+  for (int j = lane; j < total; j += 32) {
+    const size_t slot = slot_of(j);
+    const float l = __ldcg(part_stats + slot * 2 + 1);
+    if (l > 0.f) M = fmaxf(M, __ldcg(part_stats + slot * 2));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float L = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+  for (int j0 = 0; j0 < total; j0 += 32) {
+    const int j = j0 + lane;
+    float wt = 0.f, l = 0.f;
+    size_t myslot = 0;
+    if (j < total) {
+      myslot = slot_of(j);
+      l = __ldcg(part_stats + myslot * 2 + 1);
+      if (l > 0.f) wt = ex2(__ldcg(part_stats + myslot * 2) - M);
+    }
+    L += l * wt;
+    const int cnt = min(32, total - j0);
+    for (int k0 = 0; k0 < cnt; k0 += BATCH) {
+      float v[BATCH][PER];
+      float w8[BATCH];
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        const int kk = min(k0 + k, cnt - 1);
+        w8[k] = k0 + k < cnt ? __shfl_sync(0xffffffffu, wt, kk) : 0.f;
+        const size_t sl = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(myslot), kk);
+        const float* po = part_out + sl * D;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const int dim = lane + 32 * e;
+          v[k][e] = (dim < D && w8[k] != 0.f) ? __ldcg(po + dim) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k)
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * w8[k];
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  M_out = M;
+  L_out = L;
+}
+
+#ifdef FE_TIMELINE
+// Per-CTA event times (globaltimer ns) of the last decode launch, for profiling
+// builds only: [0] entry, [1] prefix done, [2] first page issued, [3] first page
+// ready (consumer warp 0), [4] consumers done, [5] producer done issuing,
+// [6] SM id, [7] nanoseconds spent merging split sequences.
+__device__ unsigned long long g_timeline[kCounterSlots][8];
+#define FE_TL(slot) (g_timeline[blockIdx.x][slot] = globaltimer_ns())
+#else
+#define FE_TL(slot) ((void)0)
+#endif
+
+// A piece of a split (sequence, head group) written by this CTA (flat mode).
+struct Pending {
+  int cfirst, kfirst, nslots, seq, kvh, hc, last;
+};
+
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
 struct Cfg {
   static constexpr int HPC = 8 * NT;       // query heads per CTA
@@ -257,8 +382,13 @@ struct Cfg {
   static int smem_bytes(int num_seqs) { return FIXED_SMEM + (num_seqs + 1) * 4; }
 };
 
+// Two CTAs of NCW + 1 warps share an SM only if three warps fit one SM sub-partition's
+// 16K registers: at most 168 registers a thread (NT = 1). NT = 2 keeps one CTA per SM.
+template <int NT>
+constexpr int decode_max_regs() { return NT == 1 ? 168 : 255; }
+
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE, int KVL>
-__global__ void __launch_bounds__((NCW + 1) * 32, 1)
+__global__ void __maxnreg__(decode_max_regs<NT>())
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
@@ -277,12 +407,22 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
   int* stage_valid = reinterpret_cast<int*>(empty + NSTAGE);
   int* pre = stage_valid + NSTAGE;  // [num_seqs + 1]
   __shared__ int warp_tot[NCW + 1];
+  __shared__ Pending pend[2];  // flat mode: pieces written as slot 0 / slot 1
 
   // Let the merge kernel that follows (programmatic dependent launch) start its
   // prologue; it waits for this grid's results before reading them.
   griddep_launch_dependents();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) FE_TL(0);
+#ifdef FE_TIMELINE
+  if (tid == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_timeline[blockIdx.x][6] = smid;
+    g_timeline[blockIdx.x][7] = 0;
+  }
+#endif
   const int S = p.num_seqs;
   const int Hkv = p.num_kv_heads, G = p.num_heads / p.num_kv_heads;
   const int HC = p.head_chunks, Y = Hkv * HC;
@@ -295,6 +435,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
       mbar_init(&empty[s], 1);
     }
     fence_mbar_init();
+    pend[0].nslots = pend[1].nslots = 0;
   }
 
   SegIter it;
@@ -328,6 +469,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     it.Ptot = 0;
     it.first_seg = true;
   }
+  if (tid == 0) FE_TL(1);
 
   if (warp == NCW) {
     // ===================================================== producer warp
@@ -387,6 +529,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
             uint8_t* ks = smem + s * STAGE;
             uint8_t* vs = ks + TILE;
             if (vd) {
+#ifdef FE_TIMELINE
+              if (gi == 0) FE_TL(2);
+#endif
               mbar_arrive_expect_tx(&full[s], STAGE);
               const int y = (ph * Hkv + cur.kvh) * BS;
 #ifdef FE_DEBUG_CHECKS
@@ -422,6 +567,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
       have = have_n;
     }
     // Drain: no bulk copy of this CTA may still be in flight when it exits.
+    if (lane == 0) FE_TL(5);
     if (lane == 0) {
       for (int j = max(0, gi - NSTAGE); j < gi; ++j) {
         const SO so(j);
@@ -484,6 +630,27 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
     }
   };
 
+  // Flat mode never visits a sequence with no pages in its window: its rows are
+  // written here, by one CTA each, as zeros (or empty partials (0, -inf, 0)).
+  if (flat) {
+    for (int s = blockIdx.x; s < S; s += gridDim.x) {
+      if (pre[s + 1] != pre[s]) continue;
+      for (int idx = tid; idx < p.num_heads * D; idx += NCW * 32) {
+        const size_t row = static_cast<size_t>(s) * p.num_heads + idx / D;
+        const int dim = idx % D;
+        if (direct_final) {
+          reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(0.f);
+        } else {
+          p.merged_o[row * D + dim] = 0.f;
+          if (dim == 0) {
+            p.merged_ml[row * 2 + 0] = NEG_INF;
+            p.merged_ml[row * 2 + 1] = 0.f;
+          }
+        }
+      }
+    }
+  }
+
   int gbase = 0;  // pages consumed by this CTA before the current segment
   bool ok = true;
   Seg sg, sn;
@@ -519,6 +686,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
       const SO so(gi);
       const int s = so.s;
       const bool waited = mbar_wait(&full[s], so.round & 1);
+#ifdef FE_TIMELINE
+      if (gi == 0 && lane == 0) FE_TL(3);
+#endif
       if (!__all_sync(0xffffffffu, waited)) {
         if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
         ok = false;
@@ -709,125 +879,109 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1)
         }
       }
     }
+    if (!whole && tid == 0) {
+      // A piece of a longer sequence: counted in after this CTA's last segment.
+      Pending& pd = pend[sg.slot];
+      pd.cfirst = sg.cfirst;
+      pd.kfirst = sg.kfirst;
+      pd.nslots = sg.nslots;
+      pd.seq = sg.seq;
+      pd.kvh = sg.kvh;
+      pd.hc = sg.hc;
+      pd.last = 0;
+    }
     __syncwarp();
     named_bar(2, NCW * 32);
     sg = sn;
     have = have_n;
     if (have) have_n = it.next(sn);
   }
+
+  // Count this CTA's pieces in (at most two: the chunk's first and last segment)
+  // and merge every sequence whose last piece this was. The CTA barrier orders all
+  // threads' partial writes before thread 0's fence and counter update (the
+  // release); thread 0's fence after the update orders the merge's reads after the
+  // other CTAs' releases (the acquire).
+  if (flat) {
+    named_bar(2, NCW * 32);
+    if (tid == 0) {
+      __threadfence();
+      for (int k = 0; k < 2; ++k) {
+        Pending& pd = pend[k];
+        if (pd.nslots <= 1) continue;
+        const int old = atomicAdd(p.counters + pd.cfirst, 1);
+        if (old >= pd.nslots) atomicOr(p.err, kErrWorkspace);
+        pd.last = old == pd.nslots - 1;
+        if (pd.last) atomicExch(p.counters + pd.cfirst, 0);  // zero for the next launch
+      }
+      __threadfence();
+    }
+    named_bar(2, NCW * 32);
+#ifdef FE_TIMELINE
+    const unsigned long long tm0 = globaltimer_ns();
+#endif
+    constexpr int PER = D / 32;
+    for (int k = 0; k < 2; ++k) {
+      const Pending pd = pend[k];
+      if (pd.nslots <= 1 || !pd.last) continue;
+      for (int hl = warp; hl < HPC; hl += NCW) {
+        const int gh = pd.hc * HPC + hl;
+        if (gh >= G) break;
+        float M, L, acc[PER];
+        lse_combine_warp<PER, 8>(
+            p.part_o, p.part_ml, pd.nslots, D,
+            [&](int j) -> size_t {
+              return (static_cast<size_t>(pd.cfirst + j) * 2 + (j == 0 ? pd.kfirst : 0)) * HPC +
+                     hl;
+            },
+            M, L, acc);
+        const size_t row = static_cast<size_t>(pd.seq) * p.num_heads + pd.kvh * G + gh;
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+          const int dim = lane + 32 * e;
+          if (direct_final) {
+            reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(acc[e] * inv);
+          } else {
+            p.merged_o[row * D + dim] = acc[e];
+          }
+        }
+        if (!direct_final && lane == 0) {
+          p.merged_ml[row * 2 + 0] = L > 0.f ? M : NEG_INF;
+          p.merged_ml[row * 2 + 1] = L;
+        }
+      }
+    }
+#ifdef FE_TIMELINE
+    __syncwarp();
+    if (tid == 0) g_timeline[blockIdx.x][7] = globaltimer_ns() - tm0;
+#endif
+  }
+  if (tid == 0) FE_TL(4);
 }
 
 // ---------------------------------------------------------------------------
-// Log-sum-exp merge of split partials. One warp per output row.
-//   ctx mode (context_lens != nullptr): row = seq * H + h; its parts are the fixup
-//     slots of the chunks its (sequence, head group) crosses, found from the decode
-//     kernel's flat chunking (same prefix, same chunk length). Rows inside one
-//     chunk were finalised by the decode kernel; rows with no pages are written
-//     here as zeros / (0, -inf, 0).
-//   all mode: every (rank, part) slot is a partial (possibly empty: l = 0).
+// Log-sum-exp merge of partials laid out [ranks, rows, parts_per_rank] (the
+// all-gathered per-rank partials of KV-range sharding, or the splits of the dense
+// fp32 flash decoding). One warp per output row.
 template <int DMAX, int ROWS>
 __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
   constexpr int PER = DMAX / 32;
-  extern __shared__ int msmem[];
-  __shared__ int warp_tot[8];
   const int D = mp.head_dim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* pre = msmem;
-  long long chunk = 1;
-  int Ptot = 0;
-  if (mp.context_lens) {
-    block_prefix<256>(pre, mp.num_seqs, warp_tot, [&](int i) {
-      return seq_window(__ldg(mp.context_lens + i), mp.tok_begin, mp.tok_end, mp.block_size).np;
-    });
-    Ptot = pre[mp.num_seqs];
-    chunk = flat_chunk(static_cast<long long>(mp.groups) * Ptot, mp.decode_ctas, mp.chunk_min);
-  }
-  griddep_wait();  // the decode grid's partials are complete and visible
+  griddep_wait();  // the producing grid's partials are complete and visible
   for (int rr = warp; rr < ROWS; rr += 8) {
     const int row = blockIdx.x * ROWS + rr;
     if (row >= mp.rows) break;
-    int nparts, ranks;
-    // ctx mode: parts are the fixup slots of the chunks c_first..c_last the
-    // (sequence, head group) of this row crosses.
-    long long cfirst = 0, gstart = 0;
-    int hl = 0;
-    if (mp.context_lens) {
-      const int seq = row / mp.heads, h = row - seq * mp.heads;
-      const int G = mp.heads / mp.kv_heads;
-      const int kvh = h / G, gh = h - kvh * G, hc = gh / mp.heads_per_chunk;
-      hl = gh - hc * mp.heads_per_chunk;
-      const int y = kvh * mp.head_chunks + hc;
-      const int np = pre[seq + 1] - pre[seq];
-      if (np == 0) {
-        nparts = 0;
-      } else {
-        gstart = static_cast<long long>(y) * Ptot + pre[seq];
-        cfirst = gstart / chunk;
-        nparts = static_cast<int>((gstart + np - 1) / chunk - cfirst + 1);
-      }
-      if (nparts == 1) continue;  // finalised by the decode kernel
-      ranks = 1;
-    } else {
-      nparts = mp.parts_per_rank;
-      ranks = mp.ranks;
-    }
-    auto slot_of = [&](int j) -> size_t {
-      if (mp.context_lens) {
-        const long long c = cfirst + j;
-        const int k = (j == 0 && gstart != c * chunk) ? 1 : 0;
-        return (static_cast<size_t>(c) * 2 + k) * mp.heads_per_chunk + hl;
-      }
-      const int rk = j / nparts, pj = j - rk * nparts;
-      return (static_cast<size_t>(rk) * mp.rows + row) * mp.parts_per_rank + pj;
-    };
-    // Stats of every part of the row, 32 parts per pass; the O rows of a pass are
-    // loaded together so each pass costs about two memory round trips.
-    const int total = ranks * nparts;
-    float M = NEG_INF;
-    for (int j = lane; j < total; j += 32) {
-      const size_t slot = slot_of(j);
-      const float l = mp.part_stats[slot * 2 + 1];
-      if (l > 0.f) M = fmaxf(M, mp.part_stats[slot * 2]);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f, acc[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) acc[k] = 0.f;
-    for (int j0 = 0; j0 < total; j0 += 32) {
-      const int j = j0 + lane;
-      float wt = 0.f, l = 0.f;
-      size_t myslot = 0;
-      if (j < total) {
-        myslot = slot_of(j);
-        l = mp.part_stats[myslot * 2 + 1];
-        if (l > 0.f) wt = ex2(mp.part_stats[myslot * 2] - M);
-      }
-      L += l * wt;
-      const int cnt = min(32, total - j0);
-      for (int k0 = 0; k0 < cnt; k0 += 8) {
-        float v[8][PER];
-        float w8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int kk = min(k0 + k, cnt - 1);
-          w8[k] = __shfl_sync(0xffffffffu, wt, kk);
-          const size_t sl = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(myslot), kk);
-          const float* po = mp.part_out + sl * D;
-#pragma unroll
-          for (int e = 0; e < PER; ++e) {
-            const int dim = lane + 32 * e;
-            v[k][e] = (k0 + k < cnt && dim < D && w8[k] != 0.f) ? po[dim] : 0.f;
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-#pragma unroll
-          for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * (k0 + k < cnt ? w8[k] : 0.f);
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const int nparts = mp.parts_per_rank;
+    float M, L, acc[PER];
+    lse_combine_warp<PER, 8>(
+        mp.part_out, mp.part_stats, mp.ranks * nparts, D,
+        [&](int j) -> size_t {
+          const int rk = j / nparts, pj = j - rk * nparts;
+          return (static_cast<size_t>(rk) * mp.rows + row) * nparts + pj;
+        },
+        M, L, acc);
     const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
@@ -878,7 +1032,7 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NTHREADS, smem);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
-  const int grid = sm_count() * occ;
+  const int grid = min(sm_count() * occ, kCounterSlots);
   if (grid_out) *grid_out = grid;
   Params pp = p;
   pp.dbg_kv_rows = kv_rows;
@@ -923,19 +1077,32 @@ static long long grid_max_cfg() {
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NTHREADS, smem) != cudaSuccess)
     return -1;
-  return static_cast<long long>(sm_count()) * (occ > 0 ? occ : 1);
+  const long long g = static_cast<long long>(sm_count()) * (occ > 0 ? occ : 1);
+  return g < kCounterSlots ? g : kCounterSlots;
 }
 
-long long fixup_floats(int head_dim, int block_size, int nt) {
+FixupLayout fixup_layout(int head_dim, int block_size, int nt) {
   long long g = -1;
 #define FE_CASE(D_, BS_, NT_)                                                           \
   if (head_dim == D_ && block_size == BS_ && nt == NT_) g = grid_max_cfg<__nv_bfloat16, D_, BS_, NT_>();
   FE_CASE(128, 16, 1) FE_CASE(128, 16, 2) FE_CASE(64, 16, 1) FE_CASE(64, 16, 2)
   FE_CASE(128, 32, 1) FE_CASE(128, 32, 2) FE_CASE(64, 32, 1) FE_CASE(64, 32, 2)
 #undef FE_CASE
-  if (g < 0) return -1;
-  return g * 2 * (8LL * nt) * (head_dim + 2);
+  FixupLayout f{-1, 0, -1};
+  if (g < 0) return f;
+  f.grid_max = g;
+  f.slot_rows = g * 2 * (8LL * nt);
+  f.floats = kCounterSlots + f.slot_rows * (head_dim + 2);
+  return f;
 }
+
+#ifdef FE_TIMELINE
+extern "C" int fe_debug_timeline(unsigned long long* host, int ctas) {
+  if (ctas > kCounterSlots) ctas = kCounterSlots;
+  return static_cast<int>(
+      cudaMemcpyFromSymbol(host, g_timeline, sizeof(unsigned long long) * 8 * ctas));
+}
+#endif
 
 template cudaError_t launch_decode<__nv_bfloat16>(const Params&, int, int, const void*, const void*,
                                                   long long, int, int, int*, cudaStream_t);
@@ -948,11 +1115,10 @@ cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t strea
   MergeParams m2 = mp;
   m2.head_dim = head_dim;
   if (head_dim < 1) return cudaErrorInvalidValue;
-  const int smem = mp.context_lens ? (mp.num_seqs + 1) * 4 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((mp.rows + ROWS - 1) / ROWS);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -964,10 +1130,6 @@ cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t strea
   else if (head_dim <= 128) kern = merge_kernel<128, ROWS>;
   else if (head_dim <= 256) kern = merge_kernel<256, ROWS>;
   else return cudaErrorInvalidValue;
-  if (smem > 48 * 1024) {
-    cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), smem);
-    if (e != cudaSuccess) return e;
-  }
   return cudaLaunchKernelEx(&cfg, kern, m2);
 }
 

@@ -23,6 +23,8 @@ struct Params {
   const int* context_lens; // [S]
   float* part_o;           // fixup slots [grid][2][8*NT][D] fp32 partial O (unnormalised)
   float* part_ml;          // fixup slots [grid][2][8*NT][2] (m in log2 units, l)
+  int* counters;           // flat mode: [grid] piece-arrival counters; zero before the
+                           // launch, and left zero by it
   float* merged_o;         // partials mode: [S, H, D] merged partial of whole rows
   float* merged_ml;        // partials mode: [S, H, 2]
   int num_seqs, num_heads, num_kv_heads, max_blocks_per_seq;
@@ -44,18 +46,11 @@ struct Params {
 };
 
 struct MergeParams {
-  const float* part_out;
-  const float* part_stats;
+  const float* part_out;   // [ranks, rows, parts_per_rank, D]
+  const float* part_stats; // [ranks, rows, parts_per_rank, 2] (m in log2 units, l)
   int rows;
   int ranks;
-  int parts_per_rank;      // slot stride per (rank, row)
-  // ctx mode (context_lens != nullptr): the valid slots of a row follow from the
-  // decode kernel's flat chunking, rebuilt from the same inputs
-  const int* context_lens;
-  int num_seqs, heads, kv_heads, heads_per_chunk, head_chunks, groups;  // heads_per_chunk
-                                                                         // = 8*NT (fixup rows)
-  int tok_begin, tok_end, block_size;
-  int decode_ctas, chunk_min;
+  int parts_per_rank;
   void* out;
   float* out_stats;
   int out_dtype;           // 0 f32 final, 1 bf16 final, 2 merged partial, 3 fp16 final
@@ -68,8 +63,7 @@ inline int pages_per_split_for(int max_pages, int splits) {
   return (max_pages + splits - 1) / splits;
 }
 
-// Launches the decode kernel; *grid_out receives its CTA count (needed by the
-// ctx-mode merge to rebuild the flat chunking).
+// Launches the decode kernel; *grid_out receives its CTA count.
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* k_cache,
                           const void* v_cache, long long kv_rows, int nt, int kv_layout,
@@ -77,9 +71,17 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
 
-// Floats of fixup scratch (O and stats together) the flat-mode decode needs for
-// this shape, or -1 if the shape is unsupported.
-long long fixup_floats(int head_dim, int block_size, int nt);
+// Flat-mode scratch: kCounterSlots int arrival counters at the start (the same
+// place for every shape, so a workspace shared by several shapes keeps them at
+// zero), then `slot_rows` fixup rows of O (D floats each) and of stats (2 each).
+constexpr int kCounterSlots = 1024;  // also the largest flat-mode grid
+struct FixupLayout {
+  long long grid_max;   // largest CTA count of the decode grid on this device
+  long long slot_rows;  // grid_max * 2 * 8 * NT
+  long long floats;     // kCounterSlots + slot_rows * (D + 2)
+};
+// Layout for this shape, or floats = -1 if the shape is unsupported.
+FixupLayout fixup_layout(int head_dim, int block_size, int nt);
 
 }  // namespace paged
 }  // namespace fe

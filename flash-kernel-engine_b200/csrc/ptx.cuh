@@ -18,6 +18,7 @@ enum : unsigned {
   kErrWaitTimeout = 1u << 0,   // an mbarrier wait exceeded kWaitLimitNs
   kErrBadBlock    = 1u << 1,   // a block-table entry was outside [0, num_blocks)
   kErrTmem        = 1u << 2,   // tensor-memory allocation did not succeed
+  kErrWorkspace   = 1u << 3,   // split-KV arrival counters were not zero at the launch
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

@@ -122,7 +122,12 @@ def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, blo
 
 def paged_attention_workspace_floats(num_heads, num_kv_heads, head_dim, block_size=16) -> int:
     """Float32 elements of workspace the split-KV (v2) bf16 decode needs on the current
-    device for this head configuration (independent of batch and context lengths)."""
+    device for this head configuration (independent of batch and context lengths).
+
+    Allocate it zero-filled (``torch.zeros``): its first 4 KiB hold arrival counters
+    that must be zero when a call starts, and every call leaves them at zero, so one
+    workspace serves any number of calls and head configurations (one stream at a
+    time)."""
     n = int(_lib_c.fe_paged_attention_v2_workspace_floats(num_heads, num_kv_heads, head_dim,
                                                           block_size))
     if n == 0:
@@ -133,7 +138,7 @@ def paged_attention_workspace_floats(num_heads, num_kv_heads, head_dim, block_si
 def _workspace(query, H, Hkv, d, bs, workspace):
     n = paged_attention_workspace_floats(H, Hkv, d, bs)
     if workspace is None:
-        return torch.empty(n, dtype=torch.float32, device=query.device), n
+        return torch.zeros(n, dtype=torch.float32, device=query.device), n
     if workspace.dtype != torch.float32 or workspace.numel() < n or not workspace.is_cuda:
         raise ValueError(f"workspace must be a CUDA float32 tensor of >= {n} elements")
     return workspace, workspace.numel()
@@ -150,10 +155,10 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
       "flat" -- K and V [num_blocks, Hkv, block_size, d] (the reference's fp32 layout);
       "vllm" -- K [num_blocks, Hkv, d/8, block_size, 8], V [num_blocks, Hkv, d,
                 block_size] (vLLM's x-packed layout; bf16/fp16, block_size 16).
-    bf16 / fp16 use the split-KV kernel (``version`` "auto"/"v2") with a float32
-    ``workspace`` of ``paged_attention_workspace_floats(...)`` elements (allocated here
-    if not given), or the single-pass kernel (``version="v1"``, no workspace). fp32
-    caches use the single-pass fp32 kernel.
+    bf16 / fp16 use the split-KV kernel (``version`` "auto"/"v2") with a zero-filled
+    float32 ``workspace`` of ``paged_attention_workspace_floats(...)`` elements
+    (allocated here if not given; reuse one across calls), or the single-pass kernel
+    (``version="v1"``, no workspace). fp32 caches use the single-pass fp32 kernel.
 
     ``rope=(cos, sin)`` (bf16/fp16): float32 CUDA tables [max_pos, d/2]; each query is
     rotated at position context_len - 1 inside the kernel (pairs (2i, 2i+1), the

@@ -42,7 +42,8 @@ int fe_print_device_info(int device_id);
 
 /* Reads and clears the library's device error word on the current device
  * (bit 0: a bounded wait timed out; bit 1: a block-table entry was out of range;
- * bit 2: tensor-memory allocation failed). Synchronises the device. The reference
+ * bit 2: tensor-memory allocation failed; bit 3: a split-KV workspace's arrival
+ * counters were not zero when a call started). Synchronises the device. The reference
  * has no device-side checking; this is new. */
 int fe_get_device_errors(unsigned int* errors_out);
 
@@ -137,11 +138,15 @@ int fe_paged_attention_v1_bf16(const void* q, const void* k_cache, const void* v
 /* bf16 cache, split-KV with a caller-owned workspace (the v2 form of vLLM's paged
  * attention; the reference has only v1). The (KV head, sequence, page) space is cut
  * into equal chunks, one per persistent CTA, whatever the context-length mix; a
- * sequence crossing chunk boundaries leaves fp32 partials in the workspace that a
- * log-sum-exp merge combines. workspace must hold
- * fe_paged_attention_v2_workspace_floats(num_heads, num_kv_heads, head_dim,
- * block_size) floats (about 2.5 MB at d = 128; independent of the batch and of the
- * context lengths). max_context_len is not used. */
+ * sequence crossing chunk boundaries leaves fp32 partials in the workspace, and the
+ * CTA that finishes its last piece combines them (log-sum-exp merge) in the same
+ * kernel. workspace must hold fe_paged_attention_v2_workspace_floats(num_heads,
+ * num_kv_heads, head_dim, block_size) floats (about 2.5 MB at d = 128; independent of
+ * the batch and of the context lengths). Its first 1024 floats (4 KiB) are arrival
+ * counters: zero-fill the workspace once before its first use (cudaMemset); every
+ * call leaves the counters at zero, so the workspace can be reused for any shape.
+ * Calls that share a workspace must not overlap on the GPU. max_context_len is not
+ * used. */
 int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
@@ -171,7 +176,8 @@ size_t fe_paged_attention_v2_workspace_floats(int num_heads, int num_kv_heads, i
  *     current device; make that first call before any stream capture.
  *   - All calls share the one array: calls that can overlap on the GPU (other
  *     streams, other threads) race on it and must be serialised by the caller.
- *     No part of it needs to start at zero; a call writes every slot it reads.
+ *     Its arrival counters are zeroed by the first call on a device, and every
+ *     call leaves them at zero.
  * Other arguments and limits are those of fe_paged_attention_v2_bf16. */
 int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                        void* out, const int* block_tables,

@@ -26,7 +26,7 @@ def test_cpp_graph_runner_replays_decode():
     S, H, d = p["q"].shape
     out = torch.empty_like(t["q"])
     n = flash_engine.paged_attention_workspace_floats(32, 8, 128)
-    ws = torch.empty(n, dtype=torch.float32, device="cuda")
+    ws = torch.zeros(n, dtype=torch.float32, device="cuda")
 
     def record(stream):
         rc = _lib.lib.fe_paged_attention_v2_bf16(

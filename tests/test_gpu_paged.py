@@ -166,6 +166,57 @@ def test_serving_mix_long_tail():
     assert_bf16_close(host(out)[sel], ref)
 
 
+def test_workspace_counters_left_zero_across_shapes():
+    """One zero-filled workspace serves split-KV calls of several head configurations
+    back to back: every call leaves the arrival counters (the first 1024 floats) at
+    zero. The long sequences make the kernel split them and merge the pieces."""
+    import flash_engine
+    shapes = [(32, 8, 128), (64, 8, 128), (8, 1, 64), (16, 2, 128)]
+    n = max(flash_engine.paged_attention_workspace_floats(H, Hkv, d) for H, Hkv, d in shapes)
+    ws = torch.zeros(n, dtype=torch.float32, device="cuda")
+    lens = [3000, 1, 0, 700, 4096, 17]
+    for seed, (H, Hkv, d) in enumerate(shapes):
+        p = O.make_paged_problem(40 + seed, len(lens), H, Hkv, d, lens)
+        ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+        out = flash_engine.paged_attention(q, kc, vc, cuda(p["block_tables"]),
+                                           cuda(p["context_lens"]), 16, workspace=ws)
+        assert flash_engine.device_errors() == 0
+        assert_bf16_close(host(out), ref)
+        assert int(torch.count_nonzero(ws[:1024].view(torch.int32))) == 0
+
+
+def test_single_long_sequence_many_pieces():
+    """One KV head and one 60k-token sequence: its pages are cut over every CTA, so
+    the CTA of the last piece merges a few hundred partials (more than one 32-part
+    pass of the combine)."""
+    import flash_engine
+    lens = [60000, 5]
+    p = O.make_paged_problem(51, 2, 8, 1, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    for version in ("v2", "v1"):
+        out = _run(p, torch.bfloat16, version)
+        assert_bf16_close(out, ref)
+
+
+def test_nonzero_workspace_counters_are_flagged():
+    """A workspace whose counters were not zero-filled is reported through the device
+    error word (bit 3) instead of being trusted silently."""
+    import flash_engine
+    lens = [4096] * 6
+    p = O.make_paged_problem(52, len(lens), 32, 8, 128, lens)
+    q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+    n = flash_engine.paged_attention_workspace_floats(32, 8, 128)
+    ws = torch.zeros(n, dtype=torch.float32, device="cuda")
+    ws[:1024].view(torch.int32).fill_(100000)
+    flash_engine.paged_attention(q, kc, vc, cuda(p["block_tables"]), cuda(p["context_lens"]), 16,
+                                 workspace=ws)
+    assert flash_engine.device_errors() & 8
+    assert flash_engine.device_errors() == 0
+
+
 def _to_vllm(kc, vc):
     """[nb, Hkv, bs, d] -> vLLM K [nb, Hkv, d/8, bs, 8] and V [nb, Hkv, d, bs]."""
     nb, hkv, bs, d = kc.shape
