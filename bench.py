@@ -57,6 +57,9 @@ def _args():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--kv-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="KV-range all-gather at N > 1: the decode kernel's own peer stores "
+                         "(p2p) or NCCL all-gather + merge kernel (nccl)")
     return ap.parse_args()
 
 
@@ -412,10 +415,14 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
     wsp = torch.zeros(flash_engine.paged_attention_workspace_floats(H, Hkv, d, bs),
                       dtype=torch.float32, device=dev)
 
+    ex = sharding.KVRangeExchange(B * H, d) if ws > 1 and a.kv_exchange == "p2p" else None
+
     def call(i, qq=q_all, bb=bt_t, ll=lens_t):
         if ws == 1:
             return flash_engine.paged_attention(qq, kc, vc, bb, ll, bs, max_context_len=M,
                                                 version="v2", workspace=wsp)
+        if ex is not None:
+            return ex.decode(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
         return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
 
     # A step (decode, all-gather and merge at N > 1) is one CUDA-graph replay.
@@ -453,13 +460,18 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
         e2e(i)
     e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n, ws, dev)
     del graph
+    if ex is not None:
+        ex.close()
     peak_hbm, _, _, src = _peaks()
     return {
         "metric": c["metric"], "value": round(kv_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
         "ms_per_step": round(ms, 5),
         "config": {"workload": c["name"], "batch": B, "num_heads": H, "num_kv_heads": Hkv,
                    "head_dim": d, "context": M, "block_size": bs,
-                   "parallelism": f"kv-range shard x{ws} + all-gather of (O,m,l) partials",
+                   "parallelism": f"kv-range shard x{ws} + all-gather of (O,m,l) partials"
+                                  + ("" if ws == 1 else
+                                     " by the decode kernel's peer stores" if ex is not None
+                                     else " by NCCL"),
                    "l2": f"{kv_rank / 2**20:.0f} MiB of KV per rank"},
         "roofline": {"bound": "hbm", "achieved": round(kv_rank / (ms_rank * 1e-3) / 1e9, 2),
                      "peak": peak_hbm, "unit": "GB/s",

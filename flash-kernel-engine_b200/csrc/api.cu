@@ -8,6 +8,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <string.h>
+
 #include <mutex>
 #include <type_traits>
 
@@ -71,6 +73,9 @@ struct DecodePlan {
   bool direct_final = true;   // normalised output rows (else merged partials)
   float* merged_out = nullptr;
   float* merged_stats = nullptr;
+  // exchange mode (partials stored into every rank's exchange buffer)
+  char* xbuf[fe::paged::kMaxRanks] = {};
+  int xworld = 0, xrank = 0, xmax_rows = 0;
 };
 
 inline int decode_nt(int H, int Hkv) { return (H / Hkv) <= 8 ? 1 : 2; }
@@ -132,6 +137,10 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.rope_sin = a.rope_sin;
     p.rope_max_pos = a.rope_max_pos;
     p.err = err;
+    for (int r = 0; r < fe::paged::kMaxRanks; ++r) p.xbuf[r] = pl.xbuf[r];
+    p.xworld = pl.xworld;
+    p.xrank = pl.xrank;
+    p.xmax_rows = pl.xmax_rows;
     const cudaError_t e = fe::paged::launch_decode<T>(p, a.d, a.bs, a.kc, a.vc, kv_rows, nt,
                                                       a.kv_layout, nullptr, st);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -364,6 +373,97 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
   pl.merged_stats = mstats;
   return paged_tc_run<__nv_bfloat16>(a, pl, workspace, as_stream(stream));
 }
+
+int fe_paged_decode_kv_exchange_bf16(const void* q, const void* kc, const void* vc,
+                                     const int* bt, const int* lens, int S, int H, int Hkv, int d,
+                                     int bs, int maxb, int num_blocks, float scale, int tb, int te,
+                                     float* workspace, size_t workspace_floats,
+                                     void* const* xbufs, int world, int rank, int max_rows,
+                                     void* out, int phases, void* stream) {
+  PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
+  int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (world < 1 || world > fe::paged::kMaxRanks || rank < 0 || rank >= world || !xbufs)
+    return kErr;
+  if (phases < 1 || phases > 3 || S > kMaxSeqsPerLaunch) return kErr;
+  if (static_cast<long long>(S) * H > max_rows || tb < 0 || te < tb || tb % bs != 0) return kErr;
+  for (int r = 0; r < world; ++r)
+    if (!xbufs[r] || !aligned(xbufs[r], 256)) return kErr;
+  if (S == 0) return 0;
+  cudaStream_t st = as_stream(stream);
+  if (phases & 1) {
+    const long long need = workspace_floats_for(H, Hkv, d, bs);
+    if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
+    DecodePlan pl;
+    pl.tok_begin = tb;
+    pl.tok_end = te;
+    pl.flat = true;
+    pl.direct_final = false;
+    for (int r = 0; r < world; ++r) pl.xbuf[r] = static_cast<char*>(xbufs[r]);
+    pl.xworld = world;
+    pl.xrank = rank;
+    pl.xmax_rows = max_rows;
+    rc = paged_tc_run<__nv_bfloat16>(a, pl, workspace, st);
+    if (rc) return rc;
+  }
+  if (phases & 2) {
+    if (!out || !aligned(out, 2)) return kErr;
+    unsigned* err = fe::device_error_word();
+    if (!err) return static_cast<int>(cudaErrorInitializationError);
+    fe::paged::XMergeParams xp{};
+    xp.xbuf = static_cast<char*>(xbufs[rank]);
+    xp.world = world;
+    xp.max_rows = max_rows;
+    xp.rows = S * H;
+    xp.head_dim = d;
+    xp.out = out;
+    xp.out_dtype = 1;
+    xp.err = err;
+    return static_cast<int>(fe::paged::launch_xmerge(xp, st));
+  }
+  return 0;
+}
+
+size_t fe_kv_exchange_bytes(int world, int max_rows, int head_dim) {
+  if (world < 1 || world > fe::paged::kMaxRanks || max_rows < 1 || head_dim < 1) return 0;
+  return static_cast<size_t>(fe::paged::x_buffer_bytes(world, max_rows, head_dim));
+}
+
+int fe_kv_exchange_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes < sizeof(fe::paged::XHeader)) return kErr;
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return static_cast<int>(e);
+  }
+  *ptr = p;
+  return 0;
+}
+
+int fe_kv_exchange_free(void* ptr) { return static_cast<int>(cudaFree(ptr)); }
+
+int fe_kv_exchange_ipc_handle(void* ptr, void* handle_out) {
+  if (!ptr || !handle_out) return kErr;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  memcpy(handle_out, &h, sizeof(h));
+  return 0;
+}
+
+int fe_kv_exchange_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return kErr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int fe_kv_exchange_ipc_close(void* ptr) { return static_cast<int>(cudaIpcCloseMemHandle(ptr)); }
 
 int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,
                       int parts_per_rank, int d, void* out, float* out_stats, int out_dtype,

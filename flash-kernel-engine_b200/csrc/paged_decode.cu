@@ -356,8 +356,9 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
 // Per-CTA event times (globaltimer ns) of the last decode launch, for profiling
 // builds only: [0] entry, [1] prefix done, [2] first page issued, [3] first page
 // ready (consumer warp 0), [4] consumers done, [5] producer done issuing,
-// [6] SM id, [7] nanoseconds spent merging split sequences.
-__device__ unsigned long long g_timeline[kCounterSlots][8];
+// [6] SM id, [7] nanoseconds spent merging split sequences, [8..11] exchange-mode
+// end: before the peer-store fence, after it, after the CTA barrier, after the flags.
+__device__ unsigned long long g_timeline[kCounterSlots][12];
 #define FE_TL(slot) (g_timeline[blockIdx.x][slot] = globaltimer_ns())
 #else
 #define FE_TL(slot) ((void)0)
@@ -408,6 +409,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   int* pre = stage_valid + NSTAGE;  // [num_seqs + 1]
   __shared__ int warp_tot[NCW + 1];
   __shared__ Pending pend[2];  // flat mode: pieces written as slot 0 / slot 1
+  __shared__ unsigned xstep_s;
 
   // Let the merge kernel that follows (programmatic dependent launch) start its
   // prologue; it waits for this grid's results before reading them.
@@ -436,6 +438,11 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     }
     fence_mbar_init();
     pend[0].nslots = pend[1].nslots = 0;
+    // exchange mode: the step this launch produces (one read per CTA; the block-wide
+    // prefix below orders it before every use)
+    xstep_s = p.xworld > 0
+                  ? ld_volatile_u32(&reinterpret_cast<const XHeader*>(p.xbuf[p.xrank])->step) + 1u
+                  : 0u;
   }
 
   SegIter it;
@@ -630,6 +637,36 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     }
   };
 
+  // Partials mode: a finished (O, m, l) row goes to merged_o / merged_ml, or, in
+  // exchange mode, to this rank's slot of every rank's exchange buffer (generation
+  // xstep & 1) as words tagged with xstep -- the all-gather of KV-range sharding done
+  // by peer stores.
+  const unsigned xstep = xstep_s;
+  auto emit_partial = [&](size_t row, int dim, float O, float M, float L) {
+    if (p.xworld > 0) {
+      const int par = static_cast<int>(xstep & 1u);
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        if (r >= p.xworld) break;
+        unsigned long long* b =
+            reinterpret_cast<unsigned long long*>(p.xbuf[r] + sizeof(XHeader));
+        st_volatile_u64(b + x_o_word(par, p.xworld, p.xrank, p.xmax_rows, row, D) + dim,
+                        tag_word(O, xstep));
+        if (dim == 0) {
+          unsigned long long* ml = b + x_ml_word(par, p.xworld, p.xrank, p.xmax_rows, row, D);
+          st_volatile_u64(ml, tag_word(M, xstep));
+          st_volatile_u64(ml + 1, tag_word(L, xstep));
+        }
+      }
+    } else {
+      p.merged_o[row * D + dim] = O;
+      if (dim == 0) {
+        p.merged_ml[row * 2 + 0] = M;
+        p.merged_ml[row * 2 + 1] = L;
+      }
+    }
+  };
+
   // Flat mode never visits a sequence with no pages in its window: its rows are
   // written here, by one CTA each, as zeros (or empty partials (0, -inf, 0)).
   if (flat) {
@@ -641,11 +678,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
         if (direct_final) {
           reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(0.f);
         } else {
-          p.merged_o[row * D + dim] = 0.f;
-          if (dim == 0) {
-            p.merged_ml[row * 2 + 0] = NEG_INF;
-            p.merged_ml[row * 2 + 1] = 0.f;
-          }
+          emit_partial(row, dim, 0.f, NEG_INF, 0.f);
         }
       }
     }
@@ -865,11 +898,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
       if (whole && direct_final) {
         reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(L > 0.f ? O / L : 0.f);
       } else if (whole) {
-        p.merged_o[row * D + dim] = O;
-        if (dim == 0) {
-          p.merged_ml[row * 2 + 0] = L > 0.f ? M : NEG_INF;
-          p.merged_ml[row * 2 + 1] = L;
-        }
+        emit_partial(row, dim, O, L > 0.f ? M : NEG_INF, L);
       } else {
         const size_t fix = (static_cast<size_t>(blockIdx.x) * 2 + sg.slot) * HPC + hl;
         p.part_o[fix * D + dim] = O;
@@ -943,12 +972,8 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
           if (direct_final) {
             reinterpret_cast<T*>(p.out)[row * D + dim] = E::cvt(acc[e] * inv);
           } else {
-            p.merged_o[row * D + dim] = acc[e];
+            emit_partial(row, dim, acc[e], L > 0.f ? M : NEG_INF, L);
           }
-        }
-        if (!direct_final && lane == 0) {
-          p.merged_ml[row * 2 + 0] = L > 0.f ? M : NEG_INF;
-          p.merged_ml[row * 2 + 1] = L;
         }
       }
     }
@@ -957,6 +982,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     if (tid == 0) g_timeline[blockIdx.x][7] = globaltimer_ns() - tm0;
 #endif
   }
+
   if (tid == 0) FE_TL(4);
 }
 
@@ -1001,6 +1027,112 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
     if (mp.out_dtype == 2 && lane == 0) {
       mp.out_stats[static_cast<size_t>(row) * 2] = L > 0.f ? M : NEG_INF;
       mp.out_stats[static_cast<size_t>(row) * 2 + 1] = L;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge of one KV-range exchange step: each rank's decode stored its (O, m, l) rows
+// as step-tagged words into slot [rank] of this buffer. One warp per row loads every
+// rank's words of the row at once, re-reads the ones that do not carry this step yet
+// (bounded wait), and combines the world partials (src/flash_decoding.cu:151-223
+// arithmetic). A wait that runs out sets kErrWaitTimeout and the row is written as
+// zeros. The last CTA advances the step count.
+template <int DMAX, int ROWS>
+__global__ void __launch_bounds__(256) xmerge_kernel(const XMergeParams xp) {
+  constexpr int PER = DMAX / 32;
+  XHeader* h = reinterpret_cast<XHeader*>(xp.xbuf);
+  const unsigned step = ld_volatile_u32(&h->step) + 1u;  // the step being merged
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = xp.head_dim, W = xp.world;
+  const int par = static_cast<int>(step & 1u);
+  const unsigned long long* words =
+      reinterpret_cast<const unsigned long long*>(xp.xbuf + sizeof(XHeader));
+  const unsigned long long t0 = globaltimer_ns();
+  // Re-reads *w until its tag is `step`; false once the wait limit has passed.
+  auto settle = [&](const unsigned long long* addr, unsigned long long& w) -> bool {
+    while (static_cast<unsigned>(w >> 32) != step) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      w = ld_volatile_u64(addr);
+    }
+    return true;
+  };
+  for (int rr = warp; rr < ROWS; rr += 8) {
+    const int row = blockIdx.x * ROWS + rr;
+    if (row >= xp.rows) break;
+    // stats of rank `lane`, O words of every rank for this lane's dims: one round trip
+    unsigned long long wm = 0, wl = 0;
+    const unsigned long long* am = nullptr;
+    if (lane < W) {
+      am = words + x_ml_word(par, W, lane, xp.max_rows, row, D);
+      wm = ld_volatile_u64(am);
+      wl = ld_volatile_u64(am + 1);
+    }
+    unsigned long long wo[kMaxRanks][PER];
+#pragma unroll
+    for (int j = 0; j < kMaxRanks; ++j) {
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const int dim = lane + 32 * e;
+        wo[j][e] = (j < W && dim < D)
+                       ? ld_volatile_u64(words + x_o_word(par, W, j, xp.max_rows, row, D) + dim)
+                       : (static_cast<unsigned long long>(step) << 32);
+      }
+    }
+    bool ok = true;
+    if (lane < W) ok = settle(am, wm) && settle(am + 1, wl);
+#pragma unroll
+    for (int j = 0; j < kMaxRanks; ++j) {
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const int dim = lane + 32 * e;
+        if (j < W && dim < D && ok)
+          ok = settle(words + x_o_word(par, W, j, xp.max_rows, row, D) + dim, wo[j][e]);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && lane == 0) atomicOr(xp.err, kErrWaitTimeout);
+    const float m = __uint_as_float(static_cast<unsigned>(wm));
+    const float l = lane < W ? __uint_as_float(static_cast<unsigned>(wl)) : 0.f;
+    float M = l > 0.f ? m : NEG_INF;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float wgt = l > 0.f ? ex2(m - M) : 0.f;
+    float L = l * wgt;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    float acc[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxRanks; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, wgt, j);
+#pragma unroll
+      for (int e = 0; e < PER; ++e)
+        acc[e] += (j < W ? __uint_as_float(static_cast<unsigned>(wo[j][e])) : 0.f) * wj;
+    }
+    const float inv = (ok && L > 0.f) ? 1.f / L : 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const int dim = lane + 32 * e;
+      if (dim >= D) continue;
+      const size_t oi = static_cast<size_t>(row) * D + dim;
+      if (xp.out_dtype == 0) {
+        reinterpret_cast<float*>(xp.out)[oi] = acc[e] * inv;
+      } else if (xp.out_dtype == 1) {
+        reinterpret_cast<__nv_bfloat16*>(xp.out)[oi] = __float2bfloat16_rn(acc[e] * inv);
+      } else {
+        reinterpret_cast<half*>(xp.out)[oi] = __float2half_rn(acc[e] * inv);
+      }
+    }
+  }
+  // The last CTA of this merge advances the step (read by the next decode and merge).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&h->merge_ctas, 1u) == gridDim.x - 1) {
+      atomicExch(&h->merge_ctas, 0u);
+      atomicExch(&h->step, step);
     }
   }
 }
@@ -1096,11 +1228,22 @@ FixupLayout fixup_layout(int head_dim, int block_size, int nt) {
   return f;
 }
 
+cudaError_t launch_xmerge(const XMergeParams& xp, cudaStream_t stream) {
+  if (xp.rows <= 0) return cudaSuccess;
+  if (xp.world < 1 || xp.world > kMaxRanks || xp.head_dim < 1) return cudaErrorInvalidValue;
+  constexpr int ROWS = 8;
+  const dim3 grid((xp.rows + ROWS - 1) / ROWS);
+  if (xp.head_dim <= 64) xmerge_kernel<64, ROWS><<<grid, 256, 0, stream>>>(xp);
+  else if (xp.head_dim <= 128) xmerge_kernel<128, ROWS><<<grid, 256, 0, stream>>>(xp);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
 #ifdef FE_TIMELINE
 extern "C" int fe_debug_timeline(unsigned long long* host, int ctas) {
   if (ctas > kCounterSlots) ctas = kCounterSlots;
   return static_cast<int>(
-      cudaMemcpyFromSymbol(host, g_timeline, sizeof(unsigned long long) * 8 * ctas));
+      cudaMemcpyFromSymbol(host, g_timeline, sizeof(unsigned long long) * 12 * ctas));
 }
 #endif
 

@@ -14,6 +14,32 @@ enum KvLayout : int {
   kKvVllm = 1,  // vLLM: K [num_blocks, Hkv, D/8, BS, 8], V [num_blocks, Hkv, D, BS]
 };
 
+// KV-range exchange buffer (one per rank, the same layout on every rank; the peers'
+// copies are mapped into this process). Header, then two generations (step parity)
+// of partial rows in 8-byte words (value bits | step << 32): a reader knows a word is
+// from the step it wants by its upper half, so no fence or flag is needed between the
+// peer stores and the reads. O [2][world][max_rows][D], (m log2, l) [2][world][max_rows][2].
+constexpr int kMaxRanks = 8;
+struct XHeader {
+  unsigned step;              // steps this rank has merged (its merge kernels)
+  unsigned merge_ctas;        // merge CTAs of the running step that have finished
+  unsigned pad[62];           // 256 bytes in all
+};
+static_assert(sizeof(XHeader) == 256, "exchange header is 256 bytes");
+inline __host__ __device__ long long x_o_word(int parity, int world, int rank, int max_rows,
+                                               long long row, int d) {
+  return ((static_cast<long long>(parity) * world + rank) * max_rows + row) * d;
+}
+inline __host__ __device__ long long x_ml_word(int parity, int world, int rank, int max_rows,
+                                                long long row, int d) {
+  return 2LL * world * max_rows * d +
+         ((static_cast<long long>(parity) * world + rank) * max_rows + row) * 2;
+}
+// Bytes of one exchange buffer.
+inline long long x_buffer_bytes(int world, int max_rows, int d) {
+  return static_cast<long long>(sizeof(XHeader)) + 8LL * 2 * world * max_rows * (d + 2);
+}
+
 struct Params {
   const void* q;           // [S, H, D] (T)
   const void* k_cache;     // used by the bulk-copy (vLLM layout) path
@@ -43,7 +69,25 @@ struct Params {
   int rope_max_pos;
   unsigned* err;           // device error word
   long long dbg_kv_rows;   // rows of the K/V tensor maps (bounds checks in debug builds)
+  // KV-range exchange (partials mode with xworld > 0): every finished partial row is
+  // stored, tagged with the step, into all xworld ranks' exchange buffers (peer stores
+  // over NVLink) at this rank's slot instead of merged_o / merged_ml. xbuf[xrank] is
+  // this rank's own buffer.
+  char* xbuf[kMaxRanks];
+  int xworld, xrank, xmax_rows;
 };
+
+// Merge of one KV-range exchange step on this rank: reads every rank's partials of
+// each row, re-reading (bounded) each word until it carries this step, combines them
+// and writes the output row; the last merge CTA advances the step count.
+struct XMergeParams {
+  char* xbuf;              // this rank's exchange buffer
+  int world, max_rows, rows, head_dim;
+  void* out;               // [rows, D] final output
+  int out_dtype;           // 0 f32, 1 bf16, 3 fp16
+  unsigned* err;
+};
+cudaError_t launch_xmerge(const XMergeParams& xp, cudaStream_t stream);
 
 struct MergeParams {
   const float* part_out;   // [ranks, rows, parts_per_rank, D]

@@ -48,6 +48,15 @@ _SIGS = {
     "fe_paged_decode_partials_bf16": ([_P] * 5 + [_I] * 7 + [_F, _I, _I, _P, ctypes.c_size_t,
                                                               _P, _P, _P], _I),
     "fe_merge_partials": ([_P, _P, _I, _I, _I, _I, _P, _P, _I, _P], _I),
+    "fe_kv_exchange_bytes": ([_I, _I, _I], ctypes.c_size_t),
+    "fe_kv_exchange_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], _I),
+    "fe_kv_exchange_free": ([_P], _I),
+    "fe_kv_exchange_ipc_handle": ([_P, _P], _I),
+    "fe_kv_exchange_ipc_open": ([_P, ctypes.POINTER(ctypes.c_void_p)], _I),
+    "fe_kv_exchange_ipc_close": ([_P], _I),
+    "fe_paged_decode_kv_exchange_bf16": ([_P] * 5 + [_I] * 7 + [_F, _I, _I, _P, ctypes.c_size_t,
+                                                                 _P, _I, _I, _I, _P, _I, _P],
+                                         _I),
     "fe_graph_capture": ([None, _P, _P, ctypes.POINTER(ctypes.c_void_p)], _I),
     "fe_graph_launch": ([_P, _P], _I),
     "fe_graph_destroy": ([_P], None),
@@ -91,3 +100,4 @@ def device_errors() -> int:
 ERR_WAIT_TIMEOUT = 1
 ERR_BAD_BLOCK = 2
 ERR_TMEM = 4
+ERR_WORKSPACE = 8

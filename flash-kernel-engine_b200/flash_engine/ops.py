@@ -230,6 +230,39 @@ def paged_decode_partials(query, key_cache, value_cache, block_tables, context_l
     return out, out_stats
 
 
+def paged_decode_kv_exchange(query, key_cache, value_cache, block_tables, context_lens,
+                             token_begin: int, token_end: int, xbufs, rank: int, max_rows: int,
+                             block_size: int = 16, scale: float | None = None, workspace=None,
+                             out=None, phases: int = 3):
+    """KV-range decode step with the all-gather done over peer memory (bf16 cache).
+
+    ``xbufs``: device addresses (ints) of every rank's exchange buffer as mapped in
+    this process (``xbufs[rank]`` is this rank's own), each of
+    ``fe_kv_exchange_bytes(len(xbufs), max_rows, d)`` bytes, zero-filled at creation
+    (``sharding.KVRangeExchange`` manages them). ``phases`` 1: decode the window
+    [token_begin, token_end) and store this rank's partial rows into every buffer;
+    2: wait for every rank's rows and merge them into ``out`` [S, H, d] bf16; 3: both.
+    Returns ``out``."""
+    import ctypes
+
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
+    if query.dtype != torch.bfloat16:
+        raise TypeError("the KV-range exchange decode takes bf16")
+    S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
+                                           context_lens, block_size)
+    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+    if out is None:
+        out = torch.empty_like(query)
+    arr = (ctypes.c_void_p * len(xbufs))(*[int(x) for x in xbufs])
+    with torch.cuda.device(query.device):
+        _lib.check(_lib_c.fe_paged_decode_kv_exchange_bf16(
+            _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+            _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
+            int(token_begin), int(token_end), _ptr(ws), n, arr, len(xbufs), int(rank),
+            int(max_rows), _ptr(out), int(phases), _stream()), "paged_decode_kv_exchange")
+    return out
+
+
 def merge_partials(part_out, part_stats, ranks: int, parts_per_rank: int, out_dtype: str = "bf16",
                    out=None, out_stats=None):
     """Log-sum-exp combine of partials laid out [ranks, rows, parts_per_rank, d]

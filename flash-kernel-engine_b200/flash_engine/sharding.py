@@ -16,10 +16,16 @@ work is partitioned here:
 The exchange step (``allgather_merge``) takes the local-partial and merge functions
 as arguments, so the same protocol runs with the CUDA kernels on NCCL ranks and
 with the CPU oracle on gloo ranks in the tests.
+
+``KVRangeExchange`` is the fused form used on NVLink-connected GPUs: the decode
+kernel itself stores each partial row into every rank's exchange buffer (peer
+memory mapped through CUDA IPC) and raises a per-rank step flag; a small merge
+kernel waits for all flags (bounded) and combines. No NCCL call on the data path.
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -96,3 +102,73 @@ def paged_decode_kv_range(query, key_cache, value_cache, block_tables, context_l
                                   out_dtype).view(S, H, d)
 
     return allgather_merge(o.view(S * H, d), st.view(S * H, 2), merge, group)
+
+
+class KVRangeExchange:
+    """Peer-memory exchange buffers of KV-range-sharded decode for one process group
+    (one process per GPU, all GPUs of one node, at most 8 ranks).
+
+    Each rank allocates one buffer (``fe_kv_exchange_alloc``), all-gathers the CUDA IPC
+    handles over the group and maps the peers' buffers. ``decode`` then runs one step:
+    ``ops.paged_decode_kv_exchange`` over this rank's token window. Every rank must call
+    ``decode`` the same number of times; ``close`` (collective) releases the buffers.
+    """
+
+    def __init__(self, max_rows: int, head_dim: int, group=None):
+        from . import _lib
+
+        self._lib = _lib
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the exchange supports at most 8 ranks")
+        self.max_rows, self.head_dim = int(max_rows), int(head_dim)
+        L = _lib.lib
+        nbytes = int(L.fe_kv_exchange_bytes(self.world, self.max_rows, self.head_dim))
+        if nbytes == 0:
+            raise ValueError("bad exchange shape")
+        own = ctypes.c_void_p()
+        _lib.check(L.fe_kv_exchange_alloc(nbytes, ctypes.byref(own)), "fe_kv_exchange_alloc")
+        self._own = own.value
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.check(L.fe_kv_exchange_ipc_handle(self._own, handle), "fe_kv_exchange_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        self.ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                self.ptrs.append(self._own)
+                continue
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r])
+            p = ctypes.c_void_p()
+            _lib.check(L.fe_kv_exchange_ipc_open(hb, ctypes.byref(p)), "fe_kv_exchange_ipc_open")
+            self._opened.append(p.value)
+            self.ptrs.append(p.value)
+        dist.barrier(group=group)
+
+    def decode(self, query, key_cache, value_cache, block_tables, context_lens,
+               max_context_len: int, block_size: int = 16, scale=None, workspace=None,
+               out=None):
+        """One KV-range-sharded decode step; returns the full [S, H, d] bf16 output."""
+        from . import ops
+
+        tb, te = kv_range_bounds(max_context_len, self.world, self.rank, block_size)
+        return ops.paged_decode_kv_exchange(query, key_cache, value_cache, block_tables,
+                                            context_lens, tb, te, self.ptrs, self.rank,
+                                            self.max_rows, block_size, scale, workspace, out)
+
+    def close(self):
+        """Collective: unmap the peers' buffers and free this rank's own."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        L = self._lib.lib
+        for p in self._opened:
+            L.fe_kv_exchange_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        L.fe_kv_exchange_free(self._own)
+        self._own = None

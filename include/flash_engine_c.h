@@ -231,6 +231,46 @@ int fe_merge_partials(const float* part_out, const float* part_stats, int rows, 
                       int parts_per_rank, int head_dim, void* out, float* out_stats,
                       int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------- KV-range exchange
+ * KV-range-sharded decode with the all-gather done by the decode kernel itself over
+ * peer memory (NVLink), replacing fe_paged_decode_partials_bf16 + an NCCL all-gather
+ * + fe_merge_partials. New: the reference is single-GPU.
+ *
+ * Every rank owns one exchange buffer of fe_kv_exchange_bytes(world, max_rows,
+ * head_dim) bytes (fe_kv_exchange_alloc: cudaMalloc + zero fill, synchronous) and maps
+ * the other ranks' buffers (fe_kv_exchange_ipc_handle on the owner, the 64-byte handle
+ * sent to the others, fe_kv_exchange_ipc_open there). xbufs[r] is rank r's buffer as
+ * seen by this process (xbufs[rank] is its own).
+ *
+ * fe_paged_decode_kv_exchange_bf16 over the token window [token_begin, token_end):
+ *   phases & 1: the decode kernel computes one (O, m, l) partial per (sequence, query
+ *     head) row, as fe_paged_decode_partials_bf16 does, and stores it into slot
+ *     [rank] of every rank's buffer as 8-byte words tagged with the step number.
+ *   phases & 2: a merge kernel reads every rank's words of each row, re-reading
+ *     (bounded, 2 s) those not yet tagged with this step, combines the world partials
+ *     (log-sum-exp, as fe_merge_partials) into out [S, H, d] bf16, and advances the
+ *     step count. head_dim 64 or 128.
+ * phases = 3 on one GPU per rank. Ranks emulated on one GPU must run phase 1 of
+ * every rank before phase 2 of any. All ranks must call it the same number of times;
+ * two generations of slots let a rank run one step ahead of a slower one. Requires
+ * num_seqs <= 4096 and num_seqs * num_heads <= max_rows; workspace as for
+ * fe_paged_attention_v2_bf16. A wait that runs out sets bit 0 of the device error
+ * word and writes zeros. */
+size_t fe_kv_exchange_bytes(int world, int max_rows, int head_dim);
+int fe_kv_exchange_alloc(size_t bytes, void** ptr);
+int fe_kv_exchange_free(void* ptr);
+int fe_kv_exchange_ipc_handle(void* ptr, void* handle_out /* 64 bytes */);
+int fe_kv_exchange_ipc_open(const void* handle /* 64 bytes */, void** ptr);
+int fe_kv_exchange_ipc_close(void* ptr);
+int fe_paged_decode_kv_exchange_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                     const int* block_tables, const int* context_lens,
+                                     int num_seqs, int num_heads, int num_kv_heads,
+                                     int head_dim, int block_size, int max_blocks_per_seq,
+                                     int num_blocks, float scale, int token_begin, int token_end,
+                                     float* workspace, size_t workspace_floats,
+                                     void* const* xbufs, int world, int rank, int max_rows,
+                                     void* out, int phases, void* stream);
+
 /* ---------------------------------------------------------------- CUDA graphs
  * Capture-once / replay-per-step of a decode step (kernels, merges and -- when the
  * recorded function issues them -- NCCL collectives). Wraps the CUDAGraphRunner of

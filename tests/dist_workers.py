@@ -174,3 +174,61 @@ def nccl_graph_worker(rank, world, port, result_path):
     dist.destroy_process_group()
     with open(f"{result_path}.{rank}", "w") as f:
         f.write(repr(max(errs)))
+
+
+def p2p_exchange_worker(rank, world, port, result_path):
+    """KV-range decode with the all-gather done by the decode kernel over peer memory
+    (KVRangeExchange): three eager steps on new query tokens, then two replays of the
+    step captured in a CUDA graph, each checked against the oracle."""
+    import torch
+    import torch.distributed as dist
+    import flash_engine
+    from flash_engine import graph, sharding
+    from oracle import attention_oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    lens = [0, 5, 16, 300, 1500, 2047]
+    S, H, Hkv, d = len(lens), 32, 8, 128
+    p = O.make_paged_problem(61, S, H, Hkv, d, lens)
+    M = int(max(lens))
+    dev = torch.device("cuda", rank)
+    q, kc, vc = (torch.from_numpy(p[x]).to(dev).to(torch.bfloat16)
+                 for x in ("q", "k_cache", "v_cache"))
+    bt = torch.from_numpy(p["block_tables"]).to(dev)
+    cl = torch.from_numpy(p["context_lens"]).to(dev)
+    ws = torch.zeros(flash_engine.paged_attention_workspace_floats(H, Hkv, d),
+                     dtype=torch.float32, device=dev)
+    ex = sharding.KVRangeExchange(S * H, d)
+    errs = []
+
+    def check(seed):
+        q2 = O.make_paged_problem(seed, S, H, Hkv, d, lens)["q"]
+        q.copy_(torch.from_numpy(q2).to(dev).to(torch.bfloat16))
+        return q2
+
+    for seed in (62, 63, 64):
+        q2 = check(seed)
+        out = ex.decode(q, kc, vc, bt, cl, M, 16, workspace=ws)
+        ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        errs.append(float(np.abs(out.float().cpu().numpy() - ref).max()))
+    g = graph.DecodeGraph(lambda: ex.decode(q, kc, vc, bt, cl, M, 16, workspace=ws))
+    for seed in (65, 66):
+        q2 = check(seed)
+        out = g.replay()
+        torch.cuda.synchronize()
+        ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        errs.append(float(np.abs(out.float().cpu().numpy() - ref).max()))
+    dev_errs = flash_engine.device_errors()
+    del g
+    ex.close()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((max(errs), dev_errs)))

@@ -78,3 +78,51 @@ def test_partials_match_oracle_partials():
         lse_ref = m_ref[seq] + np.log(l_ref[seq])
         np.testing.assert_allclose(lse_gpu, lse_ref, atol=2e-3)
         assert_bf16_close(o[seq] / s[seq, :, 1:2], O_ref[seq] / l_ref[seq][:, None])
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_kv_exchange_emulated_ranks_one_gpu(world):
+    """The peer-memory KV-range exchange with its ranks emulated on one GPU: every
+    rank's exchange buffer lives here, phase 1 (decode + stores into every buffer) runs
+    for all ranks before phase 2 (wait for all flags + merge) of any. Two steps use the
+    two slot generations; every rank's output must match the oracle."""
+    import ctypes
+    import flash_engine
+    from flash_engine import _lib, ops, sharding
+    lens = [0, 1, 40, 333, 1024, 2047]
+    S, H, Hkv, d = len(lens), 32, 8, 128
+    p = O.make_paged_problem(70 + world, S, H, Hkv, d, lens)
+    kc, vc = (cuda(p[x], torch.bfloat16) for x in ("k_cache", "v_cache"))
+    bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
+    M = int(max(lens))
+    L = _lib.lib
+    nbytes = L.fe_kv_exchange_bytes(world, S * H, d)
+    bufs = []
+    for _ in range(world):
+        b = ctypes.c_void_p()
+        assert L.fe_kv_exchange_alloc(nbytes, ctypes.byref(b)) == 0
+        bufs.append(b.value)
+    wss = [torch.zeros(flash_engine.paged_attention_workspace_floats(H, Hkv, d),
+                       dtype=torch.float32, device="cuda") for _ in range(world)]
+    try:
+        for step in range(2):
+            q_np = O.make_paged_problem(80 + step, S, H, Hkv, d, lens)["q"]
+            q = cuda(q_np, torch.bfloat16)
+            ref = O.paged_attention_gqa(q_np, p["k_cache"], p["v_cache"], p["block_tables"],
+                                        p["context_lens"])
+            outs = [torch.full_like(q, float("nan")) for _ in range(world)]
+            for r in range(world):
+                tb, te = sharding.kv_range_bounds(M, world, r, 16)
+                ops.paged_decode_kv_exchange(q, kc, vc, bt, cl, tb, te, bufs, r, S * H,
+                                             workspace=wss[r], out=outs[r], phases=1)
+            for r in range(world):
+                ops.paged_decode_kv_exchange(q, kc, vc, bt, cl, 0, 0, bufs, r, S * H,
+                                             workspace=wss[r], out=outs[r], phases=2)
+            torch.cuda.synchronize()
+            assert flash_engine.device_errors() == 0
+            for r in range(world):
+                assert_bf16_close(host(outs[r]), ref)
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            L.fe_kv_exchange_free(b)
