@@ -50,7 +50,7 @@ def test_rejects_unsupported_arguments_without_launch():
     assert L.fe_merge_partials(None, None, 1, 1, 1, 64, None, None, 7, None) == 1
     # KV-range exchange: bad world / phases; buffer size of a bad shape is 0
     assert L.fe_kv_exchange_bytes(9, 128, 128) == 0
-    assert L.fe_kv_exchange_bytes(2, 128, 128) == 256 + 4 * (2 * 2 * 128 * 128 + 2 * 2 * 128 * 2)
+    assert L.fe_kv_exchange_bytes(2, 128, 128) == 256 + 8 * 2 * 2 * 128 * (128 + 2)
     for world, rank, phases in ((9, 0, 3), (2, 2, 3), (2, 0, 0), (2, 0, 4)):
         assert L.fe_paged_decode_kv_exchange_bf16(None, None, None, None, None, 1, 8, 2, 128,
                                                   16, 1, 0, 0.0, 0, 16, None, 0, None, world,
