@@ -425,12 +425,18 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
             return ex.decode(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
         return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
 
-    # A step (decode, all-gather and merge at N > 1) is one CUDA-graph replay.
+    # A step (decode, all-gather and merge at N > 1) is one CUDA-graph replay, except
+    # with the peer-memory exchange: its two launches are not CPU-bound, and replaying
+    # them as a graph measured slower at N = 8 (88 vs 70 us a step), so they are issued
+    # directly.
     from flash_engine.graph import DecodeGraph
-    graph = DecodeGraph(lambda: call(0))
+    graph = DecodeGraph(lambda: call(0)) if ex is None else None
 
     def step(i):
-        graph.replay()
+        if graph is not None:
+            graph.replay()
+        else:
+            call(i)
 
     sampler = ClockSampler(local).start()
     ms_rank, t0, t1 = _time_steps(step, steps, warmup, ws, dev)
