@@ -25,6 +25,7 @@
 //    final O / l). At the end it reads O, divides by l and stores the row.
 // Every wait is bounded (mbar_wait); on a timeout the CTA records an error, drains
 // its TMA and MMA work, frees tensor memory and exits.
+#include <algorithm>
 #include <limits.h>
 
 #include <type_traits>
@@ -66,6 +67,7 @@ struct PParams {
   int causal;
   float scale_log2;
   unsigned* err;
+  int group;  // (batch, head)s per scheduling group (see the block mapping)
 };
 
 // 2^x on the FMA pipe: round x to the nearest integer n with the 1.5 * 2^23 trick,
@@ -145,9 +147,20 @@ __global__ void __launch_bounds__(384, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
+  // Block mapping: the (batch, head)s are cut into groups of p.group whose K/V fit in
+  // L2 together. CTAs are dispatched group by group; inside a group, the query-tile
+  // pairs go longest-first across all of its heads, so the causal work is scheduled
+  // longest-first (few heads: one group, the whole grid) while the CTAs resident at
+  // any time share the K/V of a few heads.
   const int npairs = (p.N + 2 * BM - 1) / (2 * BM);
-  const int pair = npairs - 1 - static_cast<int>(blockIdx.x);  // longest causal rows first
+  const long long L = blockIdx.x;
+  const long long per_group = static_cast<long long>(p.group) * npairs;
+  const int grp = static_cast<int>(L / per_group);
+  const int bh0 = grp * p.group;
+  const int gsz = min(p.group, p.BH - bh0);
+  const int idx = static_cast<int>(L - grp * per_group);
+  const int bh = bh0 + idx % gsz;
+  const int pair = npairs - 1 - idx / gsz;
   int m0[2], nkv[2];
   const int kv_tiles = (p.M + BN - 1) / BN;
 #pragma unroll
@@ -470,7 +483,12 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
   p.scale_log2 = scale * kLog2e;
   p.err = device_error_word();
   if (!p.err) return cudaErrorInitializationError;
-  dim3 grid((N + 255) / 256, static_cast<unsigned>(BH));
+  // heads per scheduling group: their K and V together within ~32 MB of L2
+  const long long kv_bytes = 2LL * M * D * 2;
+  p.group = static_cast<int>(std::max(1LL, std::min<long long>(BH, (32LL << 20) / kv_bytes)));
+  const long long blocks = BH * ((N + 255) / 256);
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  dim3 grid(static_cast<unsigned>(blocks));
   kern<<<grid, C::NTHREADS, C::SMEM, st>>>(qm, km, vm, p);
   return cudaGetLastError();
 }
