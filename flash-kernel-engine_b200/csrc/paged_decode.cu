@@ -23,7 +23,7 @@
 //        (indexed by the chunk the sequence starts in); the CTA whose piece
 //        arrives last combines all pieces with the log-sum-exp merge and resets
 //        the counter to zero. No second kernel and no waiting; counting at the end
-//        keeps the fence and atomic out of the streaming loop.
+//        keeps the counter updates out of the streaming loop.
 //    Both modes read context_lens and build the page prefix with a block-wide scan
 //    in every CTA, so no host synchronisation or scratch is needed to skip or
 //    place work.
@@ -934,16 +934,20 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   if (flat) {
     named_bar(2, NCW * 32);
     if (tid == 0) {
-      __threadfence();
+      // both updates in flight together; acq_rel at GPU scope is the release of this
+      // CTA's pieces and the acquire of the earlier arrivals' pieces
+      const bool has0 = pend[0].nslots > 1, has1 = pend[1].nslots > 1;
+      const int old0 = has0 ? atom_add_acq_rel_gpu(p.counters + pend[0].cfirst, 1) : 0;
+      const int old1 = has1 ? atom_add_acq_rel_gpu(p.counters + pend[1].cfirst, 1) : 0;
+#pragma unroll
       for (int k = 0; k < 2; ++k) {
         Pending& pd = pend[k];
         if (pd.nslots <= 1) continue;
-        const int old = atomicAdd(p.counters + pd.cfirst, 1);
+        const int old = k == 0 ? old0 : old1;
         if (old >= pd.nslots) atomicOr(p.err, kErrWorkspace);
         pd.last = old == pd.nslots - 1;
-        if (pd.last) atomicExch(p.counters + pd.cfirst, 0);  // zero for the next launch
+        if (pd.last) st_relaxed_gpu(p.counters + pd.cfirst, 0);  // zero for the next launch
       }
-      __threadfence();
     }
     named_bar(2, NCW * 32);
 #ifdef FE_TIMELINE

@@ -73,6 +73,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// ---------------------------------------------------------------- counters
+// Arrival counter update with release (this CTA's earlier writes, ordered before it by
+// a CTA barrier) and acquire (the writes of CTAs that arrived before) at GPU scope.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_relaxed_gpu(int* p, int v) {
+  asm volatile("st.relaxed.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- tagged words
 // Exchange words written by other GPUs over NVLink: 8-byte stores and loads, each
 // single-copy atomic, so a word's upper half (the step tag) and its lower half (the
