@@ -10,8 +10,11 @@
 
 #include <string.h>
 
+#include <algorithm>
+#include <map>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "../../include/flash_engine.h"
 #include "fp32_kernels.h"
@@ -172,6 +175,58 @@ int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st
   return paged_tc_run<T>(a, pl, ws, st);
 }
 
+// Scratch the library keeps for callers of the reference's v1 entry points, which pass
+// none: one zero-initialised split-KV workspace per (device, stream), sized for every
+// supported head configuration, allocated on the first call on that stream and kept
+// for the life of the process. Calls on one stream are ordered, so they can share it;
+// calls on different streams get different ones. Returns nullptr (and the caller uses
+// the single-pass kernel) while the stream is being captured and has none yet, since
+// cudaMalloc must not run inside a capture.
+float* managed_workspace(cudaStream_t st, size_t* floats_out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, float*> cache;
+  static long long need = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (need < 0) {
+    for (int d : {64, 128})
+      for (int bs : {16, 32})
+        for (int nt : {1, 2}) need = std::max(need, fe::paged::fixup_layout(d, bs, nt).floats);
+  }
+  if (need <= 0) return nullptr;
+  *floats_out = static_cast<size_t>(need);
+  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return nullptr;
+  float* p = nullptr;
+  if (cudaMalloc(&p, sizeof(float) * static_cast<size_t>(need)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaMemsetAsync(p, 0, sizeof(int) * fe::paged::kCounterSlots, st) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
+  cache.emplace(key, p);
+  return p;
+}
+
+// The reference's v1 entry points: the split-KV kernel with the library's own scratch
+// (the single-pass kernel when none can be had).
+template <typename T>
+int paged_v1_entry(const PagedArgs& a, cudaStream_t st) {
+  const int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (a.S == 0) return 0;
+  size_t n = 0;
+  float* ws = managed_workspace(st, &n);
+  return ws ? paged_v2_tc<T>(a, ws, n, st) : paged_v1_tc<T>(a, st);
+}
+
 }  // namespace
 
 // =========================================================================
@@ -237,7 +292,7 @@ int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, vo
                                void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
   a.kv_layout = fe::paged::kKvVllm;  // the layout include/paged_attention.cuh:29-30 declares
-  return paged_v1_tc<half>(a, as_stream(stream));
+  return paged_v1_entry<half>(a, as_stream(stream));
 }
 
 int fe_paged_attention_ex(const void* q, const void* kc, const void* vc, void* out,
@@ -269,7 +324,7 @@ int fe_paged_attention_v1_bf16(const void* q, const void* kc, const void* vc, vo
                                int bs, int max_ctx, int maxb, int num_blocks, float scale,
                                void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
-  return paged_v1_tc<__nv_bfloat16>(a, as_stream(stream));
+  return paged_v1_entry<__nv_bfloat16>(a, as_stream(stream));
 }
 
 int fe_paged_attention_v2_bf16(const void* q, const void* kc, const void* vc, void* out,

@@ -101,7 +101,8 @@ int fe_paged_attention_v1_fp32(const float* q, const float* k_cache, const float
  * K [num_blocks, Hkv, head_dim/8, block_size, 8], V [num_blocks, Hkv, head_dim,
  * block_size]. Replaces the launch_paged_attention_v1_fp16 stub
  * (src/paged_attention.cu:218-230, which launches nothing). block_size 16,
- * head_dim 64 or 128. */
+ * head_dim 64 or 128. Runs the split-KV kernel on scratch the library owns (see
+ * fe_paged_attention_v1_bf16). */
 int fe_paged_attention_v1_fp16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
@@ -125,10 +126,14 @@ int fe_paged_attention_ex(const void* q, const void* k_cache, const void* v_cach
                           int rope_max_pos, float* workspace, size_t workspace_floats,
                           void* stream);
 
-/* bf16 cache, single pass, no scratch: one unit of work per (sequence, KV head),
- * its pages spread over the CTA's consumer warps and merged in shared memory.
- * New bf16 sibling of launch_paged_attention_v1_fp32. block_size 16 or 32,
- * head_dim 64 or 128. */
+/* bf16 cache, v1 calling convention (the caller passes no scratch). New bf16 sibling
+ * of launch_paged_attention_v1_fp32. block_size 16 or 32, head_dim 64 or 128.
+ * Runs the split-KV kernel of fe_paged_attention_v2_bf16 on a workspace the library
+ * allocates on the first call on each (device, stream) (cudaMalloc, about 5 MB, kept
+ * until the process exits). Calls made while the stream is being captured into a CUDA
+ * graph, before any call on that stream outside the capture, run the single-pass
+ * kernel instead (one unit of work per (sequence, KV head), no scratch). The
+ * single-pass kernel is also what fe_paged_attention_ex runs without a workspace. */
 int fe_paged_attention_v1_bf16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,

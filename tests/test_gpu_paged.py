@@ -285,3 +285,46 @@ def test_paged_decode_fused_query_rope(version, kv_layout):
                                        kv_layout=kv_layout, rope=(cuda(cos), cuda(sin)))
     assert flash_engine.device_errors() == 0
     assert_bf16_close(host(out), ref)
+
+
+def _v1_bf16(lib, x, out, stream):
+    S = x["q"].shape[0]
+    return lib.fe_paged_attention_v1_bf16(
+        x["q"].data_ptr(), x["kc"].data_ptr(), x["vc"].data_ptr(), out.data_ptr(),
+        x["bt"].data_ptr(), x["lens"].data_ptr(), S, x["H"], x["Hkv"], x["d"], 16,
+        x["max_ctx"], x["bt"].shape[1], x["kc"].shape[0], 0.0, stream)
+
+
+def test_v1_c_entry_splits_on_library_scratch_and_in_capture():
+    """The reference's v1 calling convention (no scratch): the library runs the
+    split-KV kernel on its own per-stream workspace. A first call captured into a CUDA
+    graph on a new stream runs the single-pass kernel instead; both match the oracle."""
+    import ctypes
+    from flash_engine import _lib
+    lens = [4096, 1, 0, 3000, 700, 2049]
+    p = O.make_paged_problem(90, len(lens), 32, 8, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    x = dict(q=cuda(p["q"], torch.bfloat16), kc=cuda(p["k_cache"], torch.bfloat16),
+             vc=cuda(p["v_cache"], torch.bfloat16), bt=cuda(p["block_tables"]),
+             lens=cuda(p["context_lens"]), H=32, Hkv=8, d=128, max_ctx=max(lens))
+    lib = _lib.lib
+    # eager, twice (the second call reuses the stream's workspace)
+    for _ in range(2):
+        out = torch.full_like(x["q"], float("nan"))
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        assert _v1_bf16(lib, x, out, st) == 0
+        torch.cuda.synchronize()
+        assert _lib.device_errors() == 0
+        assert_bf16_close(host(out), ref)
+    # first call on a new stream happens inside a capture
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    out = torch.full_like(x["q"], float("nan"))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        assert _v1_bf16(lib, x, out, ctypes.c_void_p(side.cuda_stream)) == 0
+    g.replay()
+    torch.cuda.synchronize()
+    assert _lib.device_errors() == 0
+    assert_bf16_close(host(out), ref)
