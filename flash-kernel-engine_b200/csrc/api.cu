@@ -175,44 +175,54 @@ int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st
   return paged_tc_run<T>(a, pl, ws, st);
 }
 
-// Scratch the library keeps for callers of the reference's v1 entry points, which pass
-// none: one zero-initialised split-KV workspace per (device, stream), sized for every
-// supported head configuration, allocated on the first call on that stream and kept
-// for the life of the process. Calls on one stream are ordered, so they can share it;
-// calls on different streams get different ones. Returns nullptr (and the caller uses
-// the single-pass kernel) while the stream is being captured and has none yet, since
-// cudaMalloc must not run inside a capture.
-float* managed_workspace(cudaStream_t st, size_t* floats_out) {
+// Scratch the library keeps for entry points whose reference signature passes none:
+// one zero-initialised block per (device, stream), allocated on the first call on that
+// stream and kept for the life of the process. It holds a split-KV decode workspace
+// sized for every supported head configuration (after 256 reserved bytes). Calls on one stream are ordered, so they can share
+// it; calls on different streams get different ones. Returns false while the stream
+// is being captured and has none yet (cudaMalloc must not run inside a capture); the
+// callers then use their scratch-free variants.
+struct StreamScratch {
+  float* ws;         // split-KV decode workspace
+  size_t ws_floats;
+};
+bool stream_scratch(cudaStream_t st, StreamScratch* out) {
   static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, float*> cache;
+  static std::map<std::pair<int, uintptr_t>, char*> cache;
   static long long need = -1;
+  constexpr size_t kHead = 256;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lk(mu);
   if (need < 0) {
     for (int d : {64, 128})
       for (int bs : {16, 32})
         for (int nt : {1, 2}) need = std::max(need, fe::paged::fixup_layout(d, bs, nt).floats);
   }
-  if (need <= 0) return nullptr;
-  *floats_out = static_cast<size_t>(need);
+  if (need <= 0) return false;
   const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
+  char* base = nullptr;
   auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
-    return nullptr;
-  float* p = nullptr;
-  if (cudaMalloc(&p, sizeof(float) * static_cast<size_t>(need)) != cudaSuccess) {
-    cudaGetLastError();
-    return nullptr;
+  if (it != cache.end()) {
+    base = it->second;
+  } else {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      return false;
+    if (cudaMalloc(&base, kHead + sizeof(float) * static_cast<size_t>(need)) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (cudaMemsetAsync(base, 0, kHead + sizeof(int) * fe::paged::kCounterSlots, st) !=
+        cudaSuccess) {
+      cudaFree(base);
+      return false;
+    }
+    cache.emplace(key, base);
   }
-  if (cudaMemsetAsync(p, 0, sizeof(int) * fe::paged::kCounterSlots, st) != cudaSuccess) {
-    cudaFree(p);
-    return nullptr;
-  }
-  cache.emplace(key, p);
-  return p;
+  out->ws = reinterpret_cast<float*>(base + kHead);
+  out->ws_floats = static_cast<size_t>(need);
+  return true;
 }
 
 // The reference's v1 entry points: the split-KV kernel with the library's own scratch
@@ -222,9 +232,9 @@ int paged_v1_entry(const PagedArgs& a, cudaStream_t st) {
   const int rc = paged_check(a, true);
   if (rc) return rc;
   if (a.S == 0) return 0;
-  size_t n = 0;
-  float* ws = managed_workspace(st, &n);
-  return ws ? paged_v2_tc<T>(a, ws, n, st) : paged_v1_tc<T>(a, st);
+  StreamScratch sc;
+  return stream_scratch(st, &sc) ? paged_v2_tc<T>(a, sc.ws, sc.ws_floats, st)
+                                 : paged_v1_tc<T>(a, st);
 }
 
 }  // namespace

@@ -91,3 +91,50 @@ def test_bf16_reference_scale_inputs(golden):
     out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
                                        cuda(v, torch.bfloat16), True)
     assert_bf16_close(host(out), ref)
+
+
+def _heads_case(B, H, N, d, seed):
+    rng = np.random.default_rng(seed)
+    q, k, v = (O.bf16_round(rng.standard_normal((B, H, N, d), dtype=np.float32))
+               for _ in range(3))
+    return q, k, v
+
+
+def test_bf16_many_heads_ragged():
+    """Many (batch, head)s over several head groups of the longest-first schedule, a
+    ragged sequence length, two calls in a row."""
+    import flash_engine
+    B, H, N, d = 2, 40, 1000, 128
+    q, k, v = _heads_case(B, H, N, d, 7)
+    sel = [(0, 0), (0, 17), (1, 39)]
+    for _ in range(2):
+        out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
+                                           cuda(v, torch.bfloat16), True)
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        o = host(out)
+        for b, h in sel:
+            ref = O.flash_attention_sliced(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                                           v[b:b + 1, h:h + 1], True)
+            assert_bf16_close(o[b:b + 1, h:h + 1], ref)
+
+
+def test_bf16_first_call_inside_graph_capture():
+    """The prefill captured into a CUDA graph as the first call on a new stream; the
+    replay matches the oracle."""
+    import flash_engine
+    B, H, N, d = 1, 24, 700, 64
+    q, k, v = _heads_case(B, H, N, d, 8)
+    qd, kd, vd = (cuda(x, torch.bfloat16) for x in (q, k, v))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        out = flash_engine.flash_attention(qd, kd, vd, True)
+    g.replay()
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    o = host(out)
+    for h in (0, 11, 23):
+        ref = O.flash_attention_sliced(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], True)
+        assert_bf16_close(o[:, h:h + 1], ref)
