@@ -4,7 +4,9 @@
 // the kernels live in paged_decode.cu, attention_fp32.cu and prefill_sm100.cu.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <dlfcn.h>
 #include <limits.h>
+#include <nccl.h>  // types only: the functions are resolved at run time
 #include <math.h>
 #include <stdint.h>
 
@@ -235,6 +237,49 @@ int paged_v1_entry(const PagedArgs& a, cudaStream_t st) {
   StreamScratch sc;
   return stream_scratch(st, &sc) ? paged_v2_tc<T>(a, sc.ws, sc.ws_floats, st)
                                  : paged_v1_tc<T>(a, st);
+}
+
+// NCCL, resolved at run time from the libnccl.so.2 the process already holds (e.g.
+// the one PyTorch loaded), else the system one; the library does not link NCCL.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*);
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t);
+  bool ok;
+};
+const NcclApi& nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi a{};
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+      a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+      a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+      a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    }
+    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.all_gather;
+    return a;
+  }();
+  return api;
+}
+constexpr int kNcclErrBase = 1000;  // status = 1000 + ncclResult_t for NCCL failures
+inline int nccl_status(ncclResult_t r) { return r == ncclSuccess ? 0 : kNcclErrBase + static_cast<int>(r); }
+
+// Token window of `rank` under KV-range sharding: ceil(M / world) rounded up to whole
+// blocks (the split rule of python/flash_engine/ops.py:112-121 across GPUs); the last
+// rank ends at M; an empty window is [0, 0).
+void kv_range_window(int M, int world, int rank, int bs, int* tb, int* te) {
+  const int mm = M > 1 ? M : 1;
+  int per = (mm + world - 1) / world;
+  per = (per + bs - 1) / bs * bs;
+  const long long b = std::min<long long>(static_cast<long long>(rank) * per, M);
+  const long long e = rank == world - 1 ? M : std::min<long long>(static_cast<long long>(rank + 1) * per, M);
+  *tb = static_cast<int>(b);
+  *te = static_cast<int>(e);
+  if (*te <= *tb) *tb = *te = 0;
 }
 
 }  // namespace
@@ -530,6 +575,91 @@ int fe_kv_exchange_ipc_open(const void* handle, void** ptr) {
 
 int fe_kv_exchange_ipc_close(void* ptr) { return static_cast<int>(cudaIpcCloseMemHandle(ptr)); }
 
+int fe_nccl_unique_id(void* id_out) {
+  const NcclApi& n = nccl_api();
+  if (!n.ok) return static_cast<int>(cudaErrorNotSupported);
+  if (!id_out) return kErr;
+  ncclUniqueId id;
+  const int rc = nccl_status(n.get_unique_id(&id));
+  if (rc == 0) memcpy(id_out, &id, sizeof(id));
+  return rc;
+}
+
+int fe_nccl_comm_init(void** comm_out, int world, const void* id, int rank) {
+  const NcclApi& n = nccl_api();
+  if (!n.ok) return static_cast<int>(cudaErrorNotSupported);
+  if (!comm_out || !id || world < 1 || rank < 0 || rank >= world) return kErr;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t c = nullptr;
+  const int rc = nccl_status(n.comm_init_rank(&c, world, uid, rank));
+  *comm_out = rc == 0 ? c : nullptr;
+  return rc;
+}
+
+int fe_nccl_comm_destroy(void* comm) {
+  const NcclApi& n = nccl_api();
+  if (!n.ok) return static_cast<int>(cudaErrorNotSupported);
+  return comm ? nccl_status(n.comm_destroy(static_cast<ncclComm_t>(comm))) : 0;
+}
+
+size_t fe_kv_range_nccl_scratch_floats(int world, int num_seqs, int num_heads, int head_dim) {
+  if (world < 1 || num_seqs < 0 || num_heads < 1 || head_dim < 1) return 0;
+  return static_cast<size_t>(world + 1) * num_seqs * num_heads * (head_dim + 2);
+}
+
+int fe_paged_decode_kv_range_nccl_bf16(const void* q, const void* kc, const void* vc,
+                                       const int* bt, const int* lens, int S, int H, int Hkv,
+                                       int d, int bs, int maxb, int num_blocks, float scale,
+                                       int max_context_len, float* workspace,
+                                       size_t workspace_floats, void* comm, int rank, int world,
+                                       float* scratch, size_t scratch_floats, void* out,
+                                       void* stream) {
+  PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
+  int rc = paged_check(a, true);
+  if (rc) return rc;
+  if (!comm || world < 1 || rank < 0 || rank >= world || max_context_len < 0 || !out ||
+      !aligned(out, 2))
+    return kErr;
+  const long long need = workspace_floats_for(H, Hkv, d, bs);
+  if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
+  const size_t sneed = fe_kv_range_nccl_scratch_floats(world, S, H, d);
+  if (!scratch || scratch_floats < sneed || S > kMaxSeqsPerLaunch) return kErr;
+  const NcclApi& n = nccl_api();
+  if (!n.ok) return static_cast<int>(cudaErrorNotSupported);
+  if (S == 0) return 0;
+  cudaStream_t st = as_stream(stream);
+  const long long rows = static_cast<long long>(S) * H;
+  const long long blk = rows * (d + 2);  // one rank's partials: O rows, then (m, l) pairs
+  float* send = scratch;
+  float* recv = scratch + blk;
+  // 1. this rank's window: one merged (O, m, l) partial per (sequence, query head)
+  DecodePlan pl;
+  kv_range_window(max_context_len, world, rank, bs, &pl.tok_begin, &pl.tok_end);
+  pl.flat = true;
+  pl.direct_final = false;
+  pl.merged_out = send;
+  pl.merged_stats = send + rows * d;
+  rc = paged_tc_run<__nv_bfloat16>(a, pl, workspace, st);
+  if (rc) return rc;
+  // 2. all-gather the partials of every rank
+  rc = nccl_status(n.all_gather(send, recv, static_cast<size_t>(blk), ncclFloat,
+                                static_cast<ncclComm_t>(comm), st));
+  if (rc) return rc;
+  // 3. log-sum-exp merge of the world partials of each row
+  fe::paged::MergeParams mp{};
+  mp.part_out = recv;
+  mp.part_stats = recv + rows * d;
+  mp.rows = static_cast<int>(rows);
+  mp.ranks = world;
+  mp.parts_per_rank = 1;
+  mp.rank_stride_out = blk;
+  mp.rank_stride_stats = blk;
+  mp.out = out;
+  mp.out_dtype = 1;
+  return static_cast<int>(fe::paged::launch_merge(mp, d, st));
+}
+
 int fe_merge_partials(const float* part_out, const float* part_stats, int rows, int ranks,
                       int parts_per_rank, int d, void* out, float* out_stats, int out_dtype,
                       void* stream) {
@@ -621,6 +751,17 @@ cudaError_t launch_paged_attention_v2_bf16(const __nv_bfloat16* q, const __nv_bf
   return static_cast<cudaError_t>(fe_paged_attention_v2_bf16(
       q, kc, vc, out, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
       c.max_context_len, c.max_num_blocks_per_seq, 0, c.scale, workspace, workspace_floats, s));
+}
+
+cudaError_t launch_paged_decode_kv_range_bf16(
+    const __nv_bfloat16* q, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+    __nv_bfloat16* out, const int* bt, const int* lens, const PagedAttentionConfig& c,
+    ncclComm_t comm, int rank, int world, float* workspace, size_t workspace_floats,
+    float* scratch, size_t scratch_floats, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_paged_decode_kv_range_nccl_bf16(
+      q, kc, vc, bt, lens, c.num_seqs, c.num_heads, c.num_kv_heads, c.head_dim, c.block_size,
+      c.max_num_blocks_per_seq, 0, c.scale, c.max_context_len, workspace, workspace_floats, comm,
+      rank, world, scratch, scratch_floats, out, s));
 }
 
 }  // namespace paged_attention

@@ -254,30 +254,31 @@ struct StageOf {
 
 // Log-sum-exp combine of the `total` partials of one output row by one warp
 // (src/flash_decoding.cu:151-223: g = max m_p, L = sum l_p 2^(m_p - g),
-// O = sum O_p 2^(m_p - g)); part j lives at slot slot_of(j) of part_out (D floats)
-// and part_stats (m in log2 units, l); empty parts (l = 0) carry no weight.
+// O = sum O_p 2^(m_p - g)); part j is slot slot_of(j), its O row (D floats) at
+// part_out + o_off(slot) and its (m in log2 units, l) at part_stats + s_off(slot);
+// empty parts (l = 0) carry no weight.
 // Returns M = g (-inf if every part is empty), L, and acc[e] = O at dim lane + 32e.
 // Loads bypass L1: the partials may have been written by other CTAs of this grid.
 // Up to BATCH parts take one memory round trip (stats and O rows loaded together);
 // more take one for the stats and one per BATCH parts of O rows.
-template <int PER, int BATCH, typename SlotOf>
+template <int PER, int BATCH, typename SlotOf, typename OOff, typename SOff>
 __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_out,
                                                  const float* __restrict__ part_stats, int total,
-                                                 int D, SlotOf slot_of, float& M_out, float& L_out,
-                                                 float (&acc)[PER]) {
+                                                 int D, SlotOf slot_of, OOff o_off, SOff s_off,
+                                                 float& M_out, float& L_out, float (&acc)[PER]) {
   const int lane = threadIdx.x & 31;
   if (total <= BATCH) {
     // Few parts: the stats and every O row are loaded at once (one round trip).
     float m = NEG_INF, l = 0.f;
     if (lane < total) {
       const size_t slot = slot_of(lane);
-      m = __ldcg(part_stats + slot * 2);
-      l = __ldcg(part_stats + slot * 2 + 1);
+      m = __ldcg(part_stats + s_off(slot));
+      l = __ldcg(part_stats + s_off(slot) + 1);
     }
     float v[BATCH][PER];
 #pragma unroll
     for (int k = 0; k < BATCH; ++k) {
-      const float* po = part_out + (k < total ? slot_of(k) : 0) * D;
+      const float* po = part_out + o_off(k < total ? slot_of(k) : slot_of(0));
 #pragma unroll
       for (int e = 0; e < PER; ++e) {
         const int dim = lane + 32 * e;
@@ -306,8 +307,8 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
   float M = NEG_INF;
   for (int j = lane; j < total; j += 32) {
     const size_t slot = slot_of(j);
-    const float l = __ldcg(part_stats + slot * 2 + 1);
-    if (l > 0.f) M = fmaxf(M, __ldcg(part_stats + slot * 2));
+    const float l = __ldcg(part_stats + s_off(slot) + 1);
+    if (l > 0.f) M = fmaxf(M, __ldcg(part_stats + s_off(slot)));
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -320,8 +321,8 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
     size_t myslot = 0;
     if (j < total) {
       myslot = slot_of(j);
-      l = __ldcg(part_stats + myslot * 2 + 1);
-      if (l > 0.f) wt = ex2(__ldcg(part_stats + myslot * 2) - M);
+      l = __ldcg(part_stats + s_off(myslot) + 1);
+      if (l > 0.f) wt = ex2(__ldcg(part_stats + s_off(myslot)) - M);
     }
     L += l * wt;
     const int cnt = min(32, total - j0);
@@ -333,7 +334,7 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
         const int kk = min(k0 + k, cnt - 1);
         w8[k] = k0 + k < cnt ? __shfl_sync(0xffffffffu, wt, kk) : 0.f;
         const size_t sl = __shfl_sync(0xffffffffu, static_cast<unsigned long long>(myslot), kk);
-        const float* po = part_out + sl * D;
+        const float* po = part_out + o_off(sl);
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
           const int dim = lane + 32 * e;
@@ -967,7 +968,8 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
               return (static_cast<size_t>(pd.cfirst + j) * 2 + (j == 0 ? pd.kfirst : 0)) * HPC +
                      hl;
             },
-            M, L, acc);
+            [&](size_t slot) { return slot * D; }, [&](size_t slot) { return slot * 2; }, M, L,
+            acc);
         const size_t row = static_cast<size_t>(pd.seq) * p.num_heads + pd.kvh * G + gh;
         const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
@@ -1005,11 +1007,20 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
     if (row >= mp.rows) break;
     const int nparts = mp.parts_per_rank;
     float M, L, acc[PER];
+    // part j = (rank j / nparts, split j % nparts)
+    const long long rs_o = mp.rank_stride_out ? mp.rank_stride_out
+                                              : static_cast<long long>(mp.rows) * nparts * D;
+    const long long rs_s = mp.rank_stride_stats ? mp.rank_stride_stats
+                                                : static_cast<long long>(mp.rows) * nparts * 2;
     lse_combine_warp<PER, 8>(
-        mp.part_out, mp.part_stats, mp.ranks * nparts, D,
-        [&](int j) -> size_t {
-          const int rk = j / nparts, pj = j - rk * nparts;
-          return (static_cast<size_t>(rk) * mp.rows + row) * nparts + pj;
+        mp.part_out, mp.part_stats, mp.ranks * nparts, D, [&](int j) -> size_t { return j; },
+        [&](size_t j) {
+          const int rk = static_cast<int>(j) / nparts, pj = static_cast<int>(j) - rk * nparts;
+          return rk * rs_o + (static_cast<long long>(row) * nparts + pj) * D;
+        },
+        [&](size_t j) {
+          const int rk = static_cast<int>(j) / nparts, pj = static_cast<int>(j) - rk * nparts;
+          return rk * rs_s + (static_cast<long long>(row) * nparts + pj) * 2;
         },
         M, L, acc);
     const float inv = L > 0.f ? 1.f / L : 0.f;

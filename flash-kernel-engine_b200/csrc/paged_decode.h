@@ -99,6 +99,9 @@ struct MergeParams {
   float* out_stats;
   int out_dtype;           // 0 f32 final, 1 bf16 final, 2 merged partial, 3 fp16 final
   int head_dim;            // set by launch_merge
+  // floats between consecutive ranks' blocks of part_out / part_stats; 0 = packed
+  // ([ranks, rows, parts_per_rank, ...] contiguous)
+  long long rank_stride_out, rank_stride_stats;
 };
 
 // Splits of the page range [0, pages) into `splits` pieces of pages_per_split.

@@ -57,6 +57,13 @@ _SIGS = {
     "fe_paged_decode_kv_exchange_bf16": ([_P] * 5 + [_I] * 7 + [_F, _I, _I, _P, ctypes.c_size_t,
                                                                  _P, _I, _I, _I, _P, _I, _P],
                                          _I),
+    "fe_nccl_unique_id": ([_P], _I),
+    "fe_nccl_comm_init": ([ctypes.POINTER(ctypes.c_void_p), _I, _P, _I], _I),
+    "fe_nccl_comm_destroy": ([_P], _I),
+    "fe_kv_range_nccl_scratch_floats": ([_I, _I, _I, _I], ctypes.c_size_t),
+    "fe_paged_decode_kv_range_nccl_bf16": ([_P] * 5 + [_I] * 7 + [_F, _I, _P, ctypes.c_size_t,
+                                                                   _P, _I, _I, _P, ctypes.c_size_t,
+                                                                   _P, _P], _I),
     "fe_graph_capture": ([None, _P, _P, ctypes.POINTER(ctypes.c_void_p)], _I),
     "fe_graph_launch": ([_P, _P], _I),
     "fe_graph_destroy": ([_P], None),

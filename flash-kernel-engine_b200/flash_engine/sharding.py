@@ -47,13 +47,16 @@ def head_shard_bounds(num_heads: int, num_kv_heads: int, world: int, rank: int):
 def kv_range_bounds(max_context_len: int, world: int, rank: int, block_size: int = 16):
     """Token window [begin, end) of `rank` under KV-range sharding: split size
     ceil(M / N) (ops.py:112), rounded up to whole blocks so that no cache block is
-    shared by two GPUs. The last rank's window ends at max_context_len."""
+    shared by two GPUs. The last rank's window ends at max_context_len; a rank whose
+    window is empty (few tokens, many ranks) gets (0, 0)."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError("bad rank / world")
     per = math.ceil(max(max_context_len, 1) / world)
     per = math.ceil(per / block_size) * block_size
     begin = min(rank * per, max_context_len)
     end = max_context_len if rank == world - 1 else min((rank + 1) * per, max_context_len)
+    if end <= begin:
+        return 0, 0
     return begin, end
 
 

@@ -276,6 +276,35 @@ int fe_paged_decode_kv_exchange_bf16(const void* q, const void* k_cache, const v
                                      void* const* xbufs, int world, int rank, int max_rows,
                                      void* out, int phases, void* stream);
 
+/* ---------------------------------------------------------------- KV-range over NCCL
+ * The same KV-range-sharded step with the exchange done by NCCL, for hosts that hold an
+ * NCCL communicator (one rank per GPU). New: the reference is single-GPU.
+ * NCCL is not linked: its functions are taken at run time from the libnccl.so.2
+ * already loaded in the process, else the system's. Without NCCL these return
+ * cudaErrorNotSupported (801); an NCCL failure returns 1000 + its ncclResult_t.
+ *   fe_nccl_unique_id: ncclGetUniqueId into 128 bytes (rank 0 sends them to the others).
+ *   fe_nccl_comm_init / fe_nccl_comm_destroy: ncclCommInitRank / ncclCommDestroy on
+ *     the current device; the communicator is an ncclComm_t.
+ *   fe_paged_decode_kv_range_nccl_bf16: rank `rank` of `world` decodes the token window
+ *     of its KV range (ceil(max_context_len / world) rounded up to whole blocks, the
+ *     last rank to the end; the cache and block table hold that window's blocks), one
+ *     ncclAllGather of the (O, m, l) partials, then the log-sum-exp merge into out
+ *     [S, H, d] bf16 on every rank. scratch: fe_kv_range_nccl_scratch_floats floats;
+ *     workspace as for fe_paged_attention_v2_bf16. Stream-ordered on `stream`, which
+ *     must be the communicator's device's. */
+int fe_nccl_unique_id(void* id_out /* 128 bytes */);
+int fe_nccl_comm_init(void** comm_out, int world, const void* id /* 128 bytes */, int rank);
+int fe_nccl_comm_destroy(void* comm);
+size_t fe_kv_range_nccl_scratch_floats(int world, int num_seqs, int num_heads, int head_dim);
+int fe_paged_decode_kv_range_nccl_bf16(const void* q, const void* k_cache, const void* v_cache,
+                                       const int* block_tables, const int* context_lens,
+                                       int num_seqs, int num_heads, int num_kv_heads,
+                                       int head_dim, int block_size, int max_blocks_per_seq,
+                                       int num_blocks, float scale, int max_context_len,
+                                       float* workspace, size_t workspace_floats, void* comm,
+                                       int rank, int world, float* scratch,
+                                       size_t scratch_floats, void* out, void* stream);
+
 /* ---------------------------------------------------------------- CUDA graphs
  * Capture-once / replay-per-step of a decode step (kernels, merges and -- when the
  * recorded function issues them -- NCCL collectives). Wraps the CUDAGraphRunner of

@@ -5,6 +5,8 @@
 // K [num_blocks, num_kv_heads, head_dim/8, block_size, 8], V [num_blocks,
 // num_kv_heads, head_dim, block_size].
 #pragma once
+// The NCCL communicator handle, declared as nccl.h does (no NCCL headers needed).
+typedef struct ncclComm* ncclComm_t;
 
 #include <cmath>
 
@@ -63,6 +65,16 @@ cudaError_t launch_paged_attention_v2_bf16(const __nv_bfloat16* d_query,
                                            const PagedAttentionConfig& config,
                                            float* d_workspace, size_t workspace_floats,
                                            cudaStream_t stream = nullptr);
+
+// New: the KV-range-sharded bf16 decode step on `world` GPUs (this process is `rank`),
+// decode of this rank's token window + ncclAllGather of the partials on `comm` + the
+// log-sum-exp merge into the full [S, H, d] output (fe_paged_decode_kv_range_nccl_bf16).
+cudaError_t launch_paged_decode_kv_range_bf16(
+    const __nv_bfloat16* d_query, const __nv_bfloat16* d_key_cache,
+    const __nv_bfloat16* d_value_cache, __nv_bfloat16* d_output, const int* d_block_tables,
+    const int* d_context_lens, const PagedAttentionConfig& config, ncclComm_t comm, int rank,
+    int world, float* d_workspace, size_t workspace_floats, float* d_scratch,
+    size_t scratch_floats, cudaStream_t stream = nullptr);
 
 }  // namespace paged_attention
 }  // namespace flash_engine

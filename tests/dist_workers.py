@@ -232,3 +232,59 @@ def p2p_exchange_worker(rank, world, port, result_path):
     dist.destroy_process_group()
     with open(f"{result_path}.{rank}", "w") as f:
         f.write(repr((max(errs), dev_errs)))
+
+
+def nccl_c_entry_worker(rank, world, port, result_path):
+    """The C entry that takes an NCCL communicator (fe_paged_decode_kv_range_nccl_bf16):
+    the communicator is made by the library from a unique id that rank 0 creates and
+    the process group broadcasts; every rank decodes its KV range of the same cache."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    import flash_engine
+    from flash_engine import _lib
+    from oracle import attention_oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    L = _lib.lib
+    uid = (ctypes.c_ubyte * 128)()
+    if rank == 0:
+        assert L.fe_nccl_unique_id(uid) == 0
+    obj = [bytes(uid)]
+    dist.broadcast_object_list(obj, src=0)
+    uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+    comm = ctypes.c_void_p()
+    assert L.fe_nccl_comm_init(ctypes.byref(comm), world, uid, rank) == 0
+    lens = [0, 5, 16, 300, 1500, 2047]
+    S, H, Hkv, d = len(lens), 32, 8, 128
+    p = O.make_paged_problem(71, S, H, Hkv, d, lens)
+    dev = torch.device("cuda", rank)
+    q, kc, vc = (torch.from_numpy(p[x]).to(dev).to(torch.bfloat16)
+                 for x in ("q", "k_cache", "v_cache"))
+    bt = torch.from_numpy(p["block_tables"]).to(dev)
+    cl = torch.from_numpy(p["context_lens"]).to(dev)
+    ws = torch.zeros(flash_engine.paged_attention_workspace_floats(H, Hkv, d), dtype=torch.float32,
+                     device=dev)
+    scratch = torch.empty(L.fe_kv_range_nccl_scratch_floats(world, S, H, d), dtype=torch.float32,
+                          device=dev)
+    out = torch.empty_like(q)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = L.fe_paged_decode_kv_range_nccl_bf16(
+        q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), cl.data_ptr(), S, H, Hkv, d, 16,
+        bt.shape[1], kc.shape[0], 0.0, int(max(lens)), ws.data_ptr(), ws.numel(), comm, rank,
+        world, scratch.data_ptr(), scratch.numel(), out.data_ptr(), st)
+    torch.cuda.synchronize()
+    errs = flash_engine.device_errors()
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    err = float(np.abs(out.float().cpu().numpy() - ref).max()) if rc == 0 else float("inf")
+    L.fe_nccl_comm_destroy(comm)
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(repr((rc, err, errs)))

@@ -39,3 +39,16 @@ def test_kv_range_peer_exchange_two_gpus(tmp_path):
     for err, dev_errors in res:
         assert dev_errors == 0
         assert err <= 2e-2
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_kv_range_c_entry_with_nccl_communicator_two_gpus(tmp_path):
+    """The C/C++ multi-GPU entry that takes an ncclComm_t: decode, all-gather and merge
+    on every rank must match the oracle."""
+    res = _run(dist_workers.nccl_c_entry_worker, 2, tmp_path, join_timeout=180)
+    assert all(r is not None for r in res), res
+    for rc, err, dev_errors in res:
+        assert rc == 0
+        assert dev_errors == 0
+        assert err <= 2e-2

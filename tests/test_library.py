@@ -55,6 +55,12 @@ def test_rejects_unsupported_arguments_without_launch():
         assert L.fe_paged_decode_kv_exchange_bf16(None, None, None, None, None, 1, 8, 2, 128,
                                                   16, 1, 0, 0.0, 0, 16, None, 0, None, world,
                                                   rank, 8, None, phases, None) == 1
+    # KV range over NCCL: scratch size, and rejection before any NCCL or GPU work
+    assert L.fe_kv_range_nccl_scratch_floats(4, 6, 32, 128) == 5 * 6 * 32 * 130
+    assert L.fe_kv_range_nccl_scratch_floats(0, 6, 32, 128) == 0
+    assert L.fe_paged_decode_kv_range_nccl_bf16(None, None, None, None, None, 1, 8, 2, 128, 16,
+                                                1, 0, 0.0, 16, None, 0, None, 0, 2, None, 0,
+                                                None, None) == 1
     # empty problems are a no-op success
     assert L.fe_flash_attention_forward_fp32(None, None, None, None, 0, 4, 16, 16, 64, 0, 0.0,
                                              None) == 0

@@ -44,6 +44,9 @@ def test_bounds():
     # rounding to blocks: 100 tokens over 3 ranks -> 48-token (3-block) windows
     assert [sharding.kv_range_bounds(100, 3, r) for r in range(3)] == [(0, 48), (48, 96),
                                                                        (96, 100)]
+    # more ranks than blocks: the ranks past the end get an empty window
+    assert [sharding.kv_range_bounds(20, 8, r) for r in range(4)] == [(0, 16), (16, 20), (0, 0),
+                                                                      (0, 0)]
     assert sharding.head_shard_bounds(32, 8, 4, 3) == (6, 8, 24, 32)
     with pytest.raises(ValueError):
         sharding.head_shard_bounds(32, 8, 3, 0)
