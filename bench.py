@@ -320,6 +320,51 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     for i in range(n_e2e):
         e2e_step(i)
     te1 = time.perf_counter()
+    e2e_serial_ms = _max_over_ranks((te1 - te0) * 1e3 / n_e2e, ws, dev)
+
+    # The same steps two deep, as a serving loop runs them: step i+1's inputs are copied
+    # in (one copy stream) while step i decodes, and step i's output is copied out (a
+    # second copy stream) while step i+1 decodes; the host reads step i's output before
+    # it reuses that step's buffers two steps later. Every step still moves its own
+    # inputs in and its own output out.
+    comp = torch.cuda.current_stream()
+    in_s, out_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    qb = [torch.empty_like(q) for _ in range(2)]
+    btb = [torch.empty_like(bts[0]) for _ in range(2)]
+    lb = [torch.empty_like(lens_t) for _ in range(2)]
+    ob = [torch.empty_like(out) for _ in range(2)]
+    ohb = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_pipelined(n):
+        for i in range(n):
+            b = i % 2
+            if i >= 2:
+                ev_done[b].synchronize()  # step i-2's output is on the host
+            with torch.cuda.stream(in_s):
+                if i >= 2:
+                    in_s.wait_event(ev_used[b])
+                qb[b].copy_(q_h, non_blocking=True)
+                btb[b].copy_(bt_h[i % R], non_blocking=True)
+                lb[b].copy_(lens_h, non_blocking=True)
+                ev_in[b].record(in_s)
+            comp.wait_event(ev_in[b])
+            flash_engine.paged_attention(qb[b], kc, vc, btb[b], lb[b], bs, max_context_len=max_ctx,
+                                         out=ob[b], workspace=wsp)
+            ev_used[b].record(comp)
+            with torch.cuda.stream(out_s):
+                out_s.wait_event(ev_used[b])
+                ohb[b].copy_(ob[b], non_blocking=True)
+                ev_done[b].record(out_s)
+        torch.cuda.synchronize()
+
+    e2e_pipelined(4)
+    _barrier(ws, dev)
+    te0 = time.perf_counter()
+    e2e_pipelined(n_e2e)
+    te1 = time.perf_counter()
     e2e_ms = _max_over_ranks((te1 - te0) * 1e3 / n_e2e, ws, dev)
     del graphs
 
@@ -342,7 +387,10 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
         "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 2)},
+                "d2h_bytes_per_step": int(out_h.numel() * 2),
+                "mode": "two steps in flight (copies overlap the neighbouring steps' decode)",
+                "serial_value": round(total / (e2e_serial_ms * 1e-3) / 1e9, 2),
+                "serial_ms_per_step": round(e2e_serial_ms, 4)},
         "gpu_launches": steps,
         "clocks": sampler.summary(t0, t1),
     }
@@ -529,10 +577,36 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
     total = prefill_flops(B, H, N, d, causal)
     rank_flops = prefill_flops(B, h_l, N, d, causal)
     achieved = rank_flops / (ms_rank * 1e-3) / 1e12
+
+    # End to end through the public API: Q, K, V from pinned host memory and O back,
+    # every step (the host link, not the kernel, bounds this number).
+    q_h, k_h, v_h = (x.cpu().pin_memory() for x in (q, k, v))
+    o_h = torch.empty(q.shape, dtype=dt).pin_memory()
+    qd, kd, vd = (torch.empty_like(x) for x in (q, k, v))
+
+    def e2e_step(i):
+        qd.copy_(q_h, non_blocking=True)
+        kd.copy_(k_h, non_blocking=True)
+        vd.copy_(v_h, non_blocking=True)
+        o_h.copy_(flash_engine.flash_attention(qd, kd, vd, causal), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_step(0)
+    _barrier(ws, dev)
+    n_e2e = max(1, min(steps, 5 if not fp32 else 100))
+    te0 = time.perf_counter()
+    for i in range(n_e2e):
+        e2e_step(i)
+    e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n_e2e, ws, dev)
+    elt = 4 if fp32 else 2
     _, peak, peak_sus, src = _peaks()
     return {
         "metric": metric, "value": round(total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
         "ms_per_step": round(ms, 4),
+        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": int(3 * q.numel() * elt),
+                "d2h_bytes_per_step": int(q.numel() * elt)},
         "config": {"workload": name, "batch": B, "heads": H, "seq_len": N, "head_dim": d,
                    "causal": causal, "parallelism": f"head shard x{ws}",
                    "flops_per_step": total},
