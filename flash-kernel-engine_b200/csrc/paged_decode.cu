@@ -412,8 +412,10 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   __shared__ Pending pend[2];  // flat mode: pieces written as slot 0 / slot 1
   __shared__ unsigned xstep_s;
 
-  // Let the merge kernel that follows (programmatic dependent launch) start its
-  // prologue; it waits for this grid's results before reading them.
+  // Programmatic dependent launch, both ways: the next kernel in the stream may start
+  // its CTAs as soon as SM room frees up (it waits for this grid's results before
+  // reading them), and this grid, launched the same way, waits below for the previous
+  // kernel's results before its first global access.
   griddep_launch_dependents();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -432,6 +434,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   const bool flat = p.flat != 0;
   const bool direct_final = p.direct_final != 0;
 
+  griddep_wait();
   if (tid == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
@@ -1185,8 +1188,18 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   pp.dbg_kv_rows = kv_rows;
   pp.k_cache = kc;
   pp.v_cache = vc;
-  kern<<<grid, C::NTHREADS, smem, stream>>>(km, vm, pp);
-  return cudaGetLastError();
+  // programmatic dependent launch: see the top of paged_decode_kernel
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::NTHREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, km, vm, pp);
 }
 
 template <typename T>
