@@ -200,6 +200,10 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: let the next kernel place its CTAs as ours retire,
+  // and wait for the previous kernel's results before the first global access.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp >= 8) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
@@ -489,8 +493,17 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
   const long long blocks = BH * ((N + 255) / 256);
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
   dim3 grid(static_cast<unsigned>(blocks));
-  kern<<<grid, C::NTHREADS, C::SMEM, st>>>(qm, km, vm, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::NTHREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p);
 }
 
 cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o, int B, int H,
