@@ -94,6 +94,7 @@ __device__ __forceinline__ uint64_t f2(float lo, float hi) {
 __device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
+#ifndef FE_PREFILL_SCALAR_PAIRS
 __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
@@ -104,6 +105,21 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+#else  // profiling variant: the same arithmetic as two scalar instructions
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  float a0, a1, b0, b1, c0, c1;
+  f2_split(a, a0, a1);
+  f2_split(b, b0, b1);
+  f2_split(c, c0, c1);
+  return f2(fmaf(a0, b0, c0), fmaf(a1, b1, c1));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  float a0, a1, b0, b1;
+  f2_split(a, a0, a1);
+  f2_split(b, b0, b1);
+  return f2(a0 + b0, a1 + b1);
+}
+#endif
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
