@@ -42,7 +42,7 @@ constexpr float NEG_INF = -__builtin_huge_valf();
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
 // One exponential pair in every kPolyEvery goes to the FMA-pipe polynomial (0: none).
 #ifndef FE_PREFILL_POLY_EVERY
-#define FE_PREFILL_POLY_EVERY 0
+#define FE_PREFILL_POLY_EVERY 8
 #endif
 constexpr int kPolyEvery = FE_PREFILL_POLY_EVERY;
 
