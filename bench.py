@@ -573,10 +573,18 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
     h_l = H // ws
     g = torch.Generator(device=dev)
     g.manual_seed(2000 + a.seed * 31 + rank)
-    q, k, v = (torch.randn((B, h_l, N, d), generator=g, device=dev).to(dt) for _ in range(3))
+    # Enough input sets, used in turn, that consecutive steps never find their Q/K/V/O
+    # in L2 (>= 2 x L2 over a cycle; one set at N = 1, several for small shards).
+    set_bytes = 4 * B * h_l * N * d * (4 if fp32 else 2)
+    nsets = max(1, math.ceil(2 * L2_BYTES / set_bytes))
+    sets = [tuple(torch.randn((B, h_l, N, d), generator=g, device=dev).to(dt) for _ in range(3))
+            for _ in range(nsets)]
+    outs = [torch.empty_like(sets[0][0]) for _ in range(nsets)]
+    q, k, v = sets[0]
 
     def step(i):
-        return flash_engine.flash_attention(q, k, v, causal)
+        qq, kk, vv = sets[i % nsets]
+        return flash_engine.flash_attention(qq, kk, vv, causal, out=outs[i % nsets])
 
     sampler = ClockSampler(local).start()
     ms_rank, t0, t1 = _time_steps(step, steps, warmup, ws, dev)
@@ -618,7 +626,8 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
                 "d2h_bytes_per_step": int(q.numel() * elt)},
         "config": {"workload": name, "batch": B, "heads": H, "seq_len": N, "head_dim": d,
                    "causal": causal, "parallelism": f"head shard x{ws}",
-                   "flops_per_step": total},
+                   "flops_per_step": total,
+                   "l2": f"{nsets} input set(s) of {set_bytes / 2**20:.0f} MiB used in turn"},
         "roofline": {"bound": "tensor" if not fp32 else "fma",
                      "achieved": round(achieved, 3), "peak": None if fp32 else peak,
                      "unit": "TFLOP/s", "frac": None if fp32 else round(achieved / peak, 4),

@@ -55,10 +55,12 @@ def _scale_arg(scale, d):
 
 
 # --------------------------------------------------------------------------- prefill
-def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None):
+def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None, *,
+                    out=None):
     """FA2 forward: softmax(q k^T * scale [+ top-left causal mask]) v.
 
-    q: [B, H, N, d]; k, v: [B, H, M, d]; dtype float32, bfloat16 or float16.
+    q: [B, H, N, d]; k, v: [B, H, M, d]; dtype float32, bfloat16 or float16. ``out``
+    (optional, new): a contiguous tensor like q to write into.
     """
     _require_cuda(q, k, v)
     B, H, N, d = q.shape
@@ -67,7 +69,10 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
         raise ValueError("k and v must be [B, H, M, d] matching q")
     if not (q.dtype == k.dtype == v.dtype):
         raise ValueError("q, k, v must share a dtype")
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor like q")
     fn = {torch.float32: _lib_c.fe_flash_attention_forward_fp32,
           torch.bfloat16: _lib_c.fe_flash_attention_forward_bf16,
           torch.float16: _lib_c.fe_flash_attention_forward_fp16}.get(q.dtype)
