@@ -328,3 +328,25 @@ def test_v1_c_entry_splits_on_library_scratch_and_in_capture():
     torch.cuda.synchronize()
     assert _lib.device_errors() == 0
     assert_bf16_close(host(out), ref)
+
+
+def test_more_sequences_than_one_launch():
+    """More sequences than one kernel launch takes (4096): the library issues several
+    launches that share one workspace; every row must match the oracle."""
+    import flash_engine
+    rng = np.random.default_rng(91)
+    S = 4300
+    lens = rng.integers(0, 48, size=S).astype(np.int32)
+    lens[7] = 700  # one longer sequence among many short ones
+    lens[4200] = 900
+    p = O.make_paged_problem(92, S, 8, 2, 64, lens)
+    sel = np.array([0, 7, 100, 4095, 4096, 4200, S - 1])
+    ref = O.paged_attention_gqa(p["q"][sel], p["k_cache"], p["v_cache"], p["block_tables"][sel],
+                                p["context_lens"][sel])
+    q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+    bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
+    for version in ("v2", "v1"):
+        out = flash_engine.paged_attention(q, kc, vc, bt, cl, 16, version=version)
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        assert_bf16_close(host(out)[sel], ref)
