@@ -30,8 +30,22 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Asynchronous 4-byte global -> shared copies (cp.async), completed per group.
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // =========================================================================
-// FA2 forward, fp32. CTA = 64 query rows of one (b, h); 8 warps x 8 rows.
+// FA2 forward, fp32. CTA = 64 query rows of one (b, h); 8 warps x 8 rows. The K/V
+// tiles are double-buffered: tile t+1 is copied in (cp.async) while tile t is used.
 // Per 64-key tile: lane j scores keys j and j+32 for its warp's 8 rows, the warp
 // does the online-softmax update per row, then every lane accumulates P V for
 // its D/32 output columns. D is the padded head dim (multiple of 32).
@@ -44,9 +58,9 @@ __global__ void __launch_bounds__(256) fa2_fp32_kernel(const float* __restrict__
   constexpr int BM = 64, BN = 64, KS = D + 1, E = D / 32;
   extern __shared__ float sm[];
   float* sQ = sm;                 // [BM][KS]
-  float* sK = sQ + BM * KS;       // [BN][KS]
-  float* sV = sK + BN * KS;       // [BN][D]
-  float* sP = sV + BN * D;        // [8 warps][8 rows][BN]
+  float* sKb = sQ + BM * KS;      // [2][BN][KS]
+  float* sVb = sKb + 2 * BN * KS; // [2][BN][D]
+  float* sP = sVb + 2 * BN * D;   // [8 warps][8 rows][BN]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t bh = blockIdx.y;
   const int r0 = blockIdx.x * BM;
@@ -69,15 +83,35 @@ __global__ void __launch_bounds__(256) fa2_fp32_kernel(const float* __restrict__
   int ntiles = (M + BN - 1) / BN;
   if (causal) ntiles = min(ntiles, (r0 + BM + BN - 1) / BN);
   float* myP = sP + warp * 8 * BN;
-  for (int t = 0; t < ntiles; ++t) {
+  // copies of key tile t into buffer t & 1 (rows past M are zeroed)
+  auto issue_tile = [&](int t) {
     const int c0 = t * BN;
-    __syncthreads();
+    float* sK = sKb + (t & 1) * BN * KS;
+    float* sV = sVb + (t & 1) * BN * D;
     for (int i = tid; i < BN * D; i += 256) {
       const int r = i / D, c = i - r * D;
-      const bool ok = c0 + r < M && c < d;
-      const size_t gi = static_cast<size_t>(c0 + r) * d + c;
-      sK[r * KS + c] = ok ? Kb[gi] : 0.f;
-      sV[r * D + c] = ok ? Vb[gi] : 0.f;
+      if (c0 + r < M && c < d) {
+        const size_t gi = static_cast<size_t>(c0 + r) * d + c;
+        cp_async4(sK + r * KS + c, Kb + gi);
+        cp_async4(sV + r * D + c, Vb + gi);
+      } else {
+        sK[r * KS + c] = 0.f;
+        sV[r * D + c] = 0.f;
+      }
+    }
+    cp_async_commit();
+  };
+  if (ntiles > 0) issue_tile(0);
+  for (int t = 0; t < ntiles; ++t) {
+    const int c0 = t * BN;
+    const float* sK = sKb + (t & 1) * BN * KS;
+    const float* sV = sVb + (t & 1) * BN * D;
+    // the buffer of tile t+1 was last read in iteration t-1, which ended in a barrier
+    if (t + 1 < ntiles) {
+      issue_tile(t + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
     float s[8][2];
@@ -130,7 +164,7 @@ __global__ void __launch_bounds__(256) fa2_fp32_kernel(const float* __restrict__
         for (int e = 0; e < E; ++e) acc[r][e] = fmaf(pr, vv[e], acc[r][e]);
       }
     }
-    __syncwarp();
+    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
@@ -151,7 +185,7 @@ template <int D>
 static cudaError_t launch_fa2_fp32_d(const float* q, const float* k, const float* v, float* o,
                                      int B, int H, int N, int M, int d, float sl, int causal,
                                      cudaStream_t st) {
-  const int smem = (64 * (D + 1) * 2 + 64 * D + 8 * 8 * 64) * 4;
+  const int smem = (64 * (D + 1) * 3 + 2 * 64 * D + 8 * 8 * 64) * 4;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(fa2_fp32_kernel<D>), smem);
   if (e != cudaSuccess) return e;
   dim3 grid((N + 63) / 64, B * H);
