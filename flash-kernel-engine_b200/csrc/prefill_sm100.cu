@@ -56,7 +56,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 16;
+  static constexpr int NBARS = 17;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_full = bars + 11;  // [2]
   uint64_t* o_done = bars + 13;  // [2]
   uint64_t* drain = bars + 15;
+  uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_full1, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -231,14 +233,15 @@ __global__ void __launch_bounds__(384, 1)
       prefetch_tensormap(&vmap);
       const uint64_t pol_keep = l2_policy_evict_last();   // K/V are re-read by other CTAs
       const uint64_t pol_once = l2_policy_evict_first();  // Q is read once
-      int nq = (nkv[0] > 0) + (nkv[1] > 0);
-      mbar_arrive_expect_tx(q_full, nq * TILE);
-      for (int t = 0; t < 2; ++t) {
-        if (nkv[t] == 0) continue;
+      // Q0, then K_0, then Q1: the first product S0(0) needs only Q0 and K_0.
+      auto load_q = [&](int t) {
+        uint64_t* bar = t == 0 ? q_full : q_full1;
+        mbar_arrive_expect_tx(bar, TILE);
         for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(smem + C::Q_OFF + t * TILE + h * HALF, &qmap, h * 64, m0[t], bh, q_full,
+          tma_load_3d(smem + C::Q_OFF + t * TILE + h * HALF, &qmap, h * 64, m0[t], bh, bar,
                       pol_once);
-      }
+      };
+      if (nkv[0] > 0) load_q(0);
       bool ok = true;
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nmax && ok; ++j) {
@@ -249,6 +252,7 @@ __global__ void __launch_bounds__(384, 1)
           tma_load_3d(smem + C::K_OFF + st * TILE + h * HALF, &kmap, h * 64, j * BN, bh,
                       &k_full[st], pol_keep);
         ++issued_k;
+        if (j == 0 && nkv[1] > 0) load_q(1);
         if (rnd > 0 && !mbar_wait(&v_empty[st], (rnd - 1) & 1)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], TILE);
         for (int h = 0; h < HALVES; ++h)
@@ -258,7 +262,8 @@ __global__ void __launch_bounds__(384, 1)
       }
       if (!ok) atomicOr(p.err, kErrWaitTimeout);
       // Drain: every bulk copy issued here has landed before the CTA can exit.
-      mbar_wait(q_full, 0);
+      if (nkv[0] > 0) mbar_wait(q_full, 0);
+      if (nkv[1] > 0 && issued_k > 0) mbar_wait(q_full1, 0);
       for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1);
       for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
     }
@@ -290,15 +295,20 @@ __global__ void __launch_bounds__(384, 1)
         }
         tc::commit(&o_done[t]);
       };
-      bool ok = mbar_wait(q_full, 0);
-      // prologue: S0(0), S1(0)
-      if (ok) ok = mbar_wait(&k_full[0], 0);
-      if (ok) {
+      // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
+      bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
+      if (ok && nkv[0] > 0) {
         tc::fence_after_sync();
-        if (nkv[0] > 0) issue_s(0, 0);
-        if (nkv[1] > 0) issue_s(1, 0);
-        tc::commit(&k_empty[0]);
+        issue_s(0, 0);
       }
+      if (ok && nkv[1] > 0) {
+        ok = mbar_wait(q_full1, 0);
+        if (ok) {
+          tc::fence_after_sync();
+          issue_s(1, 0);
+        }
+      }
+      if (ok) tc::commit(&k_empty[0]);
       for (int j = 0; j < nmax && ok; ++j) {
         const int st = j & 1;
         if (!mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
