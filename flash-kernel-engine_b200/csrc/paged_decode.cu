@@ -1059,6 +1059,11 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams mp) {
 template <int DMAX, int ROWS>
 __global__ void __launch_bounds__(256) xmerge_kernel(const XMergeParams xp) {
   constexpr int PER = DMAX / 32;
+  // Launched with programmatic dependent launch: the CTAs may be placed while this
+  // GPU's decode is still finishing; griddepcontrol.wait holds them until it has
+  // completed, so the re-reads below only ever wait for other GPUs.
+  griddep_launch_dependents();
+  griddep_wait();
   XHeader* h = reinterpret_cast<XHeader*>(xp.xbuf);
   const unsigned step = ld_volatile_u32(&h->step) + 1u;  // the step being merged
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1261,10 +1266,20 @@ cudaError_t launch_xmerge(const XMergeParams& xp, cudaStream_t stream) {
   if (xp.world < 1 || xp.world > kMaxRanks || xp.head_dim < 1) return cudaErrorInvalidValue;
   constexpr int ROWS = 8;
   const dim3 grid((xp.rows + ROWS - 1) / ROWS);
-  if (xp.head_dim <= 64) xmerge_kernel<64, ROWS><<<grid, 256, 0, stream>>>(xp);
-  else if (xp.head_dim <= 128) xmerge_kernel<128, ROWS><<<grid, 256, 0, stream>>>(xp);
+  void (*kern)(XMergeParams) = nullptr;
+  if (xp.head_dim <= 64) kern = xmerge_kernel<64, ROWS>;
+  else if (xp.head_dim <= 128) kern = xmerge_kernel<128, ROWS>;
   else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, xp);
 }
 
 #ifdef FE_TIMELINE
