@@ -633,7 +633,8 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
                      "unit": "TFLOP/s", "frac": None if fp32 else round(achieved / peak, 4),
                      "frac_of_sustained": None if fp32 else round(achieved / peak_sus, 4),
                      "peak_source": src + ("" if fp32 else " bf16 burst"),
-                     "kernel": "fa2_fp32_kernel (FMA pipes)" if fp32 else "fa_prefill_kernel"},
+                     "kernel": "fa2_fp32_kernel (FMA pipes)" if fp32 else "fa_prefill_kernel",
+                     "traffic": None if fp32 or ws > 1 else _traffic("fa_prefill_config2_traffic.json")},
         "clocks": sampler.summary(t0, t1),
         "gpu_launches": steps,
     }
