@@ -9,6 +9,7 @@
 // All softmax arithmetic is done in the log2 domain: s2 = (q.k) * scale * log2(e),
 // p = 2^(s2 - m2); this is the same softmax as exp(s - m) (2^(x log2 e) = e^x).
 #include <limits.h>
+#include <stdlib.h>
 
 #include "fp32_kernels.h"
 #include "internal.h"
@@ -44,157 +45,386 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // =========================================================================
-// FA2 forward, fp32. CTA = 64 query rows of one (b, h); 8 warps x 8 rows. The K/V
-// tiles are double-buffered: tile t+1 is copied in (cp.async) while tile t is used.
-// Per 64-key tile: lane j scores keys j and j+32 for its warp's 8 rows, the warp
-// does the online-softmax update per row, then every lane accumulates P V for
-// its D/32 output columns. D is the padded head dim (multiple of 32).
+// FA2 forward, fp32. A CTA owns 64 query rows of one (b, h) and a share of their key
+// tiles; the `nsplit` CTAs of one row tile form a thread-block cluster and take the
+// 64-key tiles t = split, split + nsplit, ... of the row tile. Eight warps each own 8
+// rows. Lane (tr = lane / 16, tc = lane % 16) of warp w scores rows w*8 + tr*4 + i
+// (i < 4) against keys tc + 16 j (j < 4) of the tile: per 4 head dims it loads four
+// 128-bit Q words and four 128-bit K words from shared memory and issues 64 FMAs.
+// The softmax row max and sum reduce over the 16 lanes of the row group with shuffles.
+// P goes to shared memory transposed ([key][row]), so that the P V product reads one
+// 128-bit word of P (4 rows) and D/64 128-bit words of V (4 head dims each) for 4 D/16
+// FMAs. K/V tiles are double-buffered with cp.async.
+// With nsplit > 1 the CTAs of the cluster exchange (m, l, O) partials through
+// distributed shared memory: CTA c merges rows [c*64/nsplit, (c+1)*64/nsplit) of every
+// partner (the log-sum-exp combine of src/flash_decoding.cu:151-223) and writes them.
+constexpr int kFaBM = 64, kFaBN = 64;
+
 template <int D>
-__global__ void __launch_bounds__(256) fa2_fp32_kernel(const float* __restrict__ Q,
-                                                       const float* __restrict__ K,
-                                                       const float* __restrict__ V,
-                                                       float* __restrict__ O, int N, int M, int d,
-                                                       float sl, int causal) {
-  constexpr int BM = 64, BN = 64, KS = D + 1, E = D / 32;
-  extern __shared__ float sm[];
-  float* sQ = sm;                 // [BM][KS]
-  float* sKb = sQ + BM * KS;      // [2][BN][KS]
-  float* sVb = sKb + 2 * BN * KS; // [2][BN][D]
-  float* sP = sVb + 2 * BN * D;   // [8 warps][8 rows][BN]
+struct FaSmem {
+  static constexpr int QS = D + 4;          // row stride of Q and K tiles (floats)
+  static constexpr int PS = kFaBM + 4;      // row stride of the transposed P tile
+  static constexpr int kQ = kFaBM * QS;
+  static constexpr int kK = kFaBN * QS;
+  static constexpr int kV = kFaBN * D;
+  static constexpr int kP = kFaBN * PS;
+  static constexpr int floats = kQ + 2 * kK + 2 * kV + kP;
+  static constexpr int bytes = floats * 4;
+  // the cluster combine reuses the K buffers: O [64][D], then m [64], l [64]
+  static_assert(kFaBM * D + 2 * kFaBM <= 2 * kK, "combine buffer does not fit");
+};
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+// Every thread of every CTA of the cluster arrives; shared-memory writes before it
+// (local and remote) are visible to the whole cluster after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Copies rows [r_begin, r_begin + 64) of a [rows, d] fp32 matrix into a [64][stride]
+// shared tile (columns up to D); rows past `rows` and columns past d read as zeros.
+template <int D>
+__device__ __forceinline__ void fa_load_tile(float* dst, int stride, const float* src, int r_begin,
+                                             int rows, int d, bool vec, int tid) {
+  if (vec) {
+    constexpr int C4 = D / 4;
+    for (int i = tid; i < kFaBN * C4; i += 256) {
+      const int r = i / C4, c = (i - r * C4) * 4;
+      float* s = dst + r * stride + c;
+      if (r_begin + r < rows && c < d)
+        cp_async16(s, src + static_cast<size_t>(r_begin + r) * d + c);
+      else
+        *reinterpret_cast<float4*>(s) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+    for (int i = tid; i < kFaBN * D; i += 256) {
+      const int r = i / D, c = i - r * D;
+      float* s = dst + r * stride + c;
+      if (r_begin + r < rows && c < d)
+        cp_async4(s, src + static_cast<size_t>(r_begin + r) * d + c);
+      else
+        *s = 0.f;
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256, D <= 64 ? 2 : 1)
+    fa2_fp32_kernel(const float* __restrict__ Q, const float* __restrict__ K,
+                    const float* __restrict__ V, float* __restrict__ O, int N, int M, int d,
+                    float sl, int causal, int nsplit, int vec) {
+  using L = FaSmem<D>;
+  constexpr int QS = L::QS, PS = L::PS;
+  constexpr int G = D >= 64 ? 4 : 2;   // consecutive head dims a lane owns per group
+  constexpr int NG = D / (16 * G);     // groups: head dims e*16*G + tc*G + [0, G)
+  constexpr int CW = NG * G;           // head dims per lane = D / 16
+  extern __shared__ __align__(16) float sm[];
+  float* sQ = sm;
+  float* sKb = sQ + L::kQ;
+  float* sVb = sKb + 2 * L::kK;
+  float* sPT = sVb + 2 * L::kV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tr = lane >> 4, tc = lane & 15;
+  const int rb = warp * 8 + tr * 4;   // first of this lane's 4 rows within the tile
   const size_t bh = blockIdx.y;
-  const int r0 = blockIdx.x * BM;
+  const int split = nsplit > 1 ? static_cast<int>(cluster_rank()) : 0;
+  const int r0 = (blockIdx.x / nsplit) * kFaBM;
   const float* Qb = Q + bh * N * d;
   const float* Kb = K + bh * M * d;
   const float* Vb = V + bh * M * d;
 
-  for (int i = tid; i < BM * D; i += 256) {
-    const int r = i / D, c = i - r * D;
-    sQ[r * KS + c] = (r0 + r < N && c < d) ? Qb[static_cast<size_t>(r0 + r) * d + c] : 0.f;
-  }
-  float m[8], l[8], acc[8][E];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    m[r] = NEG_INF;
-    l[r] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[r][e] = 0.f;
-  }
-  int ntiles = (M + BN - 1) / BN;
-  if (causal) ntiles = min(ntiles, (r0 + BM + BN - 1) / BN);
-  float* myP = sP + warp * 8 * BN;
-  // copies of key tile t into buffer t & 1 (rows past M are zeroed)
-  auto issue_tile = [&](int t) {
-    const int c0 = t * BN;
-    float* sK = sKb + (t & 1) * BN * KS;
-    float* sV = sVb + (t & 1) * BN * D;
-    for (int i = tid; i < BN * D; i += 256) {
-      const int r = i / D, c = i - r * D;
-      if (c0 + r < M && c < d) {
-        const size_t gi = static_cast<size_t>(c0 + r) * d + c;
-        cp_async4(sK + r * KS + c, Kb + gi);
-        cp_async4(sV + r * D + c, Vb + gi);
-      } else {
-        sK[r * KS + c] = 0.f;
-        sV[r * D + c] = 0.f;
-      }
-    }
+  int ntiles = (M + kFaBN - 1) / kFaBN;
+  if (causal) ntiles = min(ntiles, (r0 + kFaBM + kFaBN - 1) / kFaBN);
+  const int nloc = ntiles > split ? (ntiles - split + nsplit - 1) / nsplit : 0;
+
+  fa_load_tile<D>(sQ, QS, Qb, r0, N, d, vec, tid);
+  auto issue_tile = [&](int it) {
+    const int c0 = (split + it * nsplit) * kFaBN;
+    fa_load_tile<D>(sKb + (it & 1) * L::kK, QS, Kb, c0, M, d, vec, tid);
+    fa_load_tile<D>(sVb + (it & 1) * L::kV, D, Vb, c0, M, d, vec, tid);
     cp_async_commit();
   };
-  if (ntiles > 0) issue_tile(0);
-  for (int t = 0; t < ntiles; ++t) {
-    const int c0 = t * BN;
-    const float* sK = sKb + (t & 1) * BN * KS;
-    const float* sV = sVb + (t & 1) * BN * D;
-    // the buffer of tile t+1 was last read in iteration t-1, which ended in a barrier
-    if (t + 1 < ntiles) {
-      issue_tile(t + 1);
+  if (nloc > 0) issue_tile(0);
+  else cp_async_commit();
+
+  float m[4], l[4], acc[4][CW];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = NEG_INF;
+    l[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CW; ++c) acc[i][c] = 0.f;
+  }
+
+  for (int it = 0; it < nloc; ++it) {
+    const int c0 = (split + it * nsplit) * kFaBN;
+    const float* sK = sKb + (it & 1) * L::kK;
+    const float* sV = sVb + (it & 1) * L::kV;
+    // the buffer of tile it+1 was last read in iteration it-1, which ended in a barrier
+    if (it + 1 < nloc) {
+      issue_tile(it + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    float s[8][2];
+
+    float s[4][4];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) s[r][0] = s[r][1] = 0.f;
-    const float* k0 = sK + lane * KS;
-    const float* k1 = sK + (lane + 32) * KS;
-    const float* qw = sQ + warp * 8 * KS;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+    const float* qrow = sQ + rb * QS;
+    const float* krow = sK + tc * QS;
 #pragma unroll 4
-    for (int c = 0; c < D; ++c) {
-      const float a0 = k0[c], a1 = k1[c];
+    for (int k = 0; k < D; k += 4) {
+      float4 qv[4], kv[4];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float qv = qw[r * KS + c];
-        s[r][0] = fmaf(qv, a0, s[r][0]);
-        s[r][1] = fmaf(qv, a1, s[r][1]);
-      }
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(qrow + i * QS + k);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        kv[j] = *reinterpret_cast<const float4*>(krow + j * 16 * QS + k);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+          s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+          s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+          s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+        }
     }
+
+    // online softmax per row over the 16 lanes of the row group
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int row = r0 + warp * 8 + r;
+    for (int i = 0; i < 4; ++i) {
+      const int row = r0 + rb + i;
+      float tmax = NEG_INF;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int col = c0 + lane + 32 * jj;
+      for (int j = 0; j < 4; ++j) {
+        const int col = c0 + tc + 16 * j;
         const bool valid = col < M && (!causal || col <= row);
-        s[r][jj] = valid ? s[r][jj] * sl : NEG_INF;
+        s[i][j] = valid ? s[i][j] * sl : NEG_INF;
+        tmax = fmaxf(tmax, s[i][j]);
       }
-      const float tmax = warp_max(fmaxf(s[r][0], s[r][1]));
-      const float mn = fmaxf(m[r], tmax);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mn = fmaxf(m[i], tmax);
       const float mu = mn == NEG_INF ? 0.f : mn;
-      const float corr = ex2(m[r] - mu);
-      m[r] = mn;
-      const float p0 = ex2(s[r][0] - mu), p1 = ex2(s[r][1] - mu);
-      l[r] = l[r] * corr + p0 + p1;  // per-lane partial; reduced at the end
+      const float corr = ex2(m[i] - mu);
+      m[i] = mn;
+      float ps = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[r][e] *= corr;
-      myP[r * BN + lane] = p0;
-      myP[r * BN + lane + 32] = p1;
+      for (int j = 0; j < 4; ++j) {
+        s[i][j] = ex2(s[i][j] - mu);
+        ps += s[i][j];
+      }
+      l[i] = l[i] * corr + ps;   // this lane's share; reduced over the row group at the end
+#pragma unroll
+      for (int c = 0; c < CW; ++c) acc[i][c] *= corr;
     }
-    __syncwarp();
-#pragma unroll 2
-    for (int j = 0; j < BN; ++j) {
-      float vv[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) vv[e] = sV[j * D + lane + 32 * e];
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(sPT + (tc + 16 * j) * PS + rb) =
+          make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    __syncwarp();   // the warp reads back only its own 8 rows of P
+
+#pragma unroll 4
+    for (int j = 0; j < kFaBN; ++j) {
+      const float4 p = *reinterpret_cast<const float4*>(sPT + j * PS + rb);
+      const float pr[4] = {p.x, p.y, p.z, p.w};
+      float vv[CW];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float pr = myP[r * BN + j];
+      for (int e = 0; e < NG; ++e) {
+        const float* vp = sV + j * D + e * 16 * G + tc * G;
+        if constexpr (G == 4) {
+          const float4 t = *reinterpret_cast<const float4*>(vp);
+          vv[e * 4 + 0] = t.x;
+          vv[e * 4 + 1] = t.y;
+          vv[e * 4 + 2] = t.z;
+          vv[e * 4 + 3] = t.w;
+        } else {
+          const float2 t = *reinterpret_cast<const float2*>(vp);
+          vv[e * 2 + 0] = t.x;
+          vv[e * 2 + 1] = t.y;
+        }
+      }
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[r][e] = fmaf(pr, vv[e], acc[r][e]);
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < CW; ++c) acc[i][c] = fmaf(pr[i], vv[c], acc[i][c]);
+    }
+    __syncthreads();   // every warp is done with this K/V buffer before it is refilled
+  }
+  cp_async_wait<0>();
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) l[i] += __shfl_xor_sync(0xffffffffu, l[i], o);
+
+  float* Ob = O + bh * N * d;
+  if (nsplit == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = r0 + rb + i;
+      if (row >= N) continue;
+      const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
+      float* orow = Ob + static_cast<size_t>(row) * d;
+#pragma unroll
+      for (int e = 0; e < NG; ++e)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const int c = e * 16 * G + tc * G + g;
+          if (c < d) orow[c] = acc[i][e * G + g] * inv;
+        }
+    }
+    return;
+  }
+
+  // ---- cluster combine. Rows of slice c = [c*SR, (c+1)*SR) go to CTA c; a lane's 4 rows
+  // lie in one slice (SR >= 8 for nsplit <= 8).
+  const int SR = kFaBM / nsplit;
+  float* rO = sKb;                    // [nsplit][SR][D]
+  float* rM = rO + kFaBM * D;         // [nsplit][SR]
+  float* rL = rM + kFaBM;             // [nsplit][SR]
+  cluster_sync_all();                 // every CTA of the cluster is done with its K buffers
+  {
+    const int dst = rb / SR;
+    const int rr = (split * SR + rb - dst * SR);   // row index in dst's [nsplit*SR] rows
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t orow = cluster_map(smem_u32(rO + (rr + i) * D), dst);
+#pragma unroll
+      for (int e = 0; e < NG; ++e) {
+        const uint32_t a = orow + (e * 16 * G + tc * G) * 4;
+        if constexpr (G == 4)
+          st_cluster_v4(a, acc[i][e * 4 + 0], acc[i][e * 4 + 1], acc[i][e * 4 + 2],
+                        acc[i][e * 4 + 3]);
+        else
+          st_cluster_v2(a, acc[i][e * 2 + 0], acc[i][e * 2 + 1]);
+      }
+      if (tc == 0) {
+        st_cluster_f32(cluster_map(smem_u32(rM + rr + i), dst), m[i]);
+        st_cluster_f32(cluster_map(smem_u32(rL + rr + i), dst), l[i]);
       }
     }
-    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int row = r0 + warp * 8 + r;
-    const float L = warp_sum(l[r]);
-    if (row >= N) continue;
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    float* orow = O + bh * N * d + static_cast<size_t>(row) * d;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int c = lane + 32 * e;
-      if (c < d) orow[c] = acc[r][e] * inv;
+  cluster_sync_all();                 // all partials of this CTA's slice have landed
+  constexpr int C4 = D / 4;
+  for (int idx = tid; idx < SR * C4; idx += 256) {
+    const int rr = idx / C4, c = (idx - rr * C4) * 4;
+    const int row = r0 + split * SR + rr;
+    if (row >= N || c >= d) continue;
+    float mx = NEG_INF;
+    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, rM[s2 * SR + rr]);
+    float tot = 0.f;
+    float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mx != NEG_INF) {
+      for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float w = ex2(rM[s2 * SR + rr] - mx);
+        tot += rL[s2 * SR + rr] * w;
+        const float4 t = *reinterpret_cast<const float4*>(rO + (s2 * SR + rr) * D + c);
+        o4.x = fmaf(w, t.x, o4.x);
+        o4.y = fmaf(w, t.y, o4.y);
+        o4.z = fmaf(w, t.z, o4.z);
+        o4.w = fmaf(w, t.w, o4.w);
+      }
+    }
+    const float inv = tot > 0.f ? 1.f / tot : 0.f;
+    float* op = Ob + static_cast<size_t>(row) * d + c;
+    if (vec) {
+      *reinterpret_cast<float4*>(op) = make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+    } else {
+      const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
+      for (int g = 0; g < 4 && c + g < d; ++g) op[g] = ov[g] * inv;
     }
   }
+}
+
+// Number of CTAs (one cluster) that share a row tile's key tiles: the most (up to 8 and
+// up to the key-tile count) that still fit the grid in one wave of resident CTAs (two
+// per SM at D <= 64, one at D = 128). Config 1 ([1, 8, 512, 64]) takes 4: 256 CTAs.
+// FE_FP32_SPLIT=1,2,4,8 overrides the choice (tuning).
+static int fa2_fp32_split(int row_tiles, int bh, int M, int d) {
+  static const int forced = [] {
+    const char* s = getenv("FE_FP32_SPLIT");
+    const int v = s ? atoi(s) : 0;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }();
+  const int ktiles = (M + kFaBN - 1) / kFaBN;
+  int n = 1;
+  if (forced) {
+    n = forced;
+  } else {
+    const long long slots = static_cast<long long>(sm_count()) * (d <= 64 ? 2 : 1);
+    const long long base = static_cast<long long>(row_tiles) * bh;
+    while (n < 8 && base * n * 2 <= slots) n *= 2;
+  }
+  while (n > 1 && n > ktiles) n /= 2;
+  return n;
 }
 
 template <int D>
 static cudaError_t launch_fa2_fp32_d(const float* q, const float* k, const float* v, float* o,
                                      int B, int H, int N, int M, int d, float sl, int causal,
                                      cudaStream_t st) {
-  const int smem = (64 * (D + 1) * 3 + 2 * 64 * D + 8 * 8 * 64) * 4;
+  const int smem = FaSmem<D>::bytes;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(fa2_fp32_kernel<D>), smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((N + 63) / 64, B * H);
-  fa2_fp32_kernel<D><<<grid, 256, smem, st>>>(q, k, v, o, N, M, d, sl, causal);
+  const int row_tiles = (N + kFaBM - 1) / kFaBM;
+  const int nsplit = fa2_fp32_split(row_tiles, B * H, M, d);
+  const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const int vec = (d % 4 == 0) && al(q) && al(k) && al(v) && al(o);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(row_tiles * nsplit, B * H);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = nsplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = nsplit > 1 ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, fa2_fp32_kernel<D>, q, k, v, o, N, M, d, sl, causal, nsplit, vec);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 cudaError_t launch_fa2_fp32(const float* q, const float* k, const float* v, float* o, int B, int H,
                             int N, int M, int d, float scale, int causal, cudaStream_t st) {
+  if (fa2_tf32_eligible(q, k, v, o, B, H, N, M, d))
+    return launch_fa2_tf32(q, k, v, o, B, H, N, M, d, scale, causal, st);
   const float sl = scale * kLog2e;
   if (d <= 32) return launch_fa2_fp32_d<32>(q, k, v, o, B, H, N, M, d, sl, causal, st);
   if (d <= 64) return launch_fa2_fp32_d<64>(q, k, v, o, B, H, N, M, d, sl, causal, st);

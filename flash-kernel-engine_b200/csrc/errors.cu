@@ -105,9 +105,9 @@ cudaError_t encode_tma_2d_b16(CUtensorMap* map, const void* base, bool bf16, uin
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t encode_tma_3d_b16(CUtensorMap* map, const void* base, bool bf16, uint64_t cols,
-                              uint64_t rows, uint64_t outer, uint32_t box_cols,
-                              uint32_t box_rows) {
+static cudaError_t encode_tma_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt,
+                                 uint64_t elem, uint64_t cols, uint64_t rows, uint64_t outer,
+                                 uint32_t box_cols, uint32_t box_rows) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_encode) {
@@ -120,17 +120,30 @@ cudaError_t encode_tma_3d_b16(CUtensorMap* map, const void* base, bool bf16, uin
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   }
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * 2) % 16 != 0)
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * elem) % 16 != 0)
     return cudaErrorInvalidValue;
   cuuint64_t dims[3] = {cols, rows, outer};
-  cuuint64_t strides[2] = {cols * 2, rows * cols * 2};
+  cuuint64_t strides[2] = {cols * elem, rows * cols * elem};
   cuuint32_t box[3] = {box_cols, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        3, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t encode_tma_3d_b16(CUtensorMap* map, const void* base, bool bf16, uint64_t cols,
+                              uint64_t rows, uint64_t outer, uint32_t box_cols,
+                              uint32_t box_rows) {
+  return encode_tma_3d(map, base,
+                       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       2, cols, rows, outer, box_cols, box_rows);
+}
+
+cudaError_t encode_tma_3d_f32(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                              uint64_t outer, uint32_t box_cols, uint32_t box_rows) {
+  return encode_tma_3d(map, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, cols, rows, outer,
+                       box_cols, box_rows);
 }
 
 }  // namespace fe

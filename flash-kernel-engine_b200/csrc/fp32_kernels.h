@@ -1,4 +1,4 @@
-// Internal interface of the fp32 CUDA-core kernels (attention_fp32.cu).
+// Internal interface of the fp32 kernels (attention_fp32.cu, prefill_tf32.cu).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -7,6 +7,12 @@ namespace fe {
 namespace simt {
 
 cudaError_t launch_fa2_fp32(const float* q, const float* k, const float* v, float* o, int B, int H,
+                            int N, int M, int d, float scale, int causal, cudaStream_t st);
+// fp32 FA2 forward on the tensor core with 3xTF32 products (prefill_tf32.cu), used by
+// launch_fa2_fp32 for head dim 64 with 16-byte aligned tensors.
+bool fa2_tf32_eligible(const float* q, const float* k, const float* v, const float* o, int B,
+                       int H, int N, int M, int d);
+cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, float* o, int B, int H,
                             int N, int M, int d, float scale, int causal, cudaStream_t st);
 cudaError_t launch_naive_fp32(const float* q, const float* k, const float* v, float* o, int B,
                               int H, int N, int M, int d, float scale, int causal, cudaStream_t st);

@@ -34,6 +34,10 @@ cudaError_t encode_tma_3d_b16(CUtensorMap* map, const void* base, bool bf16, uin
                               uint64_t rows, uint64_t outer, uint32_t box_cols,
                               uint32_t box_rows);
 
+// The same over fp32 elements (box_cols * 4 must be <= 128 bytes).
+cudaError_t encode_tma_3d_f32(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                              uint64_t outer, uint32_t box_cols, uint32_t box_rows);
+
 // Calls cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per
 // (function, device).
 cudaError_t ensure_smem_optin(const void* func, int bytes);

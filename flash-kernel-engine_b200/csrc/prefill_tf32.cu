@@ -1,0 +1,591 @@
+// FA2 forward for fp32 Q, K, V, O on the 5th-generation tensor core (sm_100a), with
+// fp32-class accuracy from three TF32 products per fp32 product ("3xTF32"): every
+// operand x is split into hi = x with the low 13 mantissa bits cleared (exact in TF32)
+// and lo = x - hi (exact in fp32), and a.b is formed as a_hi.b_hi + a_hi.b_lo +
+// a_lo.b_hi with fp32 accumulation. The dropped a_lo.b_lo term and the TF32 rounding
+// of lo are each about 2^-20 of |a.b|.
+//
+// It computes the reference's launch_flash_attention_forward_fp32
+// (src/flash_attention.cu:111-345): O = softmax(Q K^T * scale [+ causal mask]) V over
+// [B, H, N|M, d] fp32 tensors, causal mask top-left aligned (query row i sees keys
+// j <= i, src/flash_attention.cu:224). Head dim 64; the other head dims run on the
+// CUDA-core kernel of attention_fp32.cu.
+//
+// A CTA owns one 128-row query tile of one (batch, head) and the 64-key tiles
+// t = split, split + nsplit, ... of it. The nsplit CTAs of a row tile form a thread-block
+// cluster and merge their (m, l, O) partials through distributed shared memory (the
+// log-sum-exp combine of src/flash_decoding.cu:151-223).
+//  * warp 4 (TMA): Q once, then K_j and V_j into a two-stage ring (3-D TMA, 128-byte
+//    swizzle; rows past N or M read as zeros).
+//  * warps 6-9 (split): rewrite each landed tile as hi in place and lo beside it; V is
+//    transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
+//  * warp 5 (MMA): allocates tensor memory [S0 | S1 | PL0 | PL1 | O] and, from one
+//    thread, issues
+//      S_j = Qhi Khi^T + Qhi Klo^T + Qlo Khi^T   (kind::tf32, A and B from shared memory)
+//      O  += Phi Vhi + Phi Vlo + Plo Vhi         (A = P from tensor memory, B = V^T)
+//    with S double-buffered, so S_{j+1} is computed while the softmax of tile j runs.
+//  * warps 0-3 (softmax): thread i owns query row i. It reads S_j, applies mask and
+//    scale, updates the running max m and sum l in the log2 domain, and writes
+//    P_hi = hi(2^(s - m)) over S_j and P_lo into PL_j. O is rescaled in tensor memory
+//    only when the row max grows by more than 2^8 (the stale max is exact for O / l).
+// Every wait is bounded (mbar_wait); on a timeout the CTA records an error, drains its
+// copies and MMAs, frees tensor memory and exits.
+#include <stdlib.h>
+
+#include "fp32_kernels.h"
+#include "internal.h"
+#include "ptx.cuh"
+#include "tcgen05.cuh"
+
+namespace fe {
+namespace tf32 {
+
+constexpr float NEG_INF = -__builtin_huge_valf();
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
+
+template <int D>
+struct TCfg {
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int HALVES = D / 32;  // 128-byte swizzle atom columns along d
+  static constexpr int QH = BM * 128;    // bytes of one Q atom column
+  static constexpr int KH = BN * 128;    // bytes of one K or V atom column
+  static constexpr int VTH = D * 128;    // bytes of one V^T atom column (D rows)
+  static constexpr int Q_BYTES = BM * D * 4;
+  static constexpr int KV_BYTES = BN * D * 4;
+  static constexpr int Q_HI = 0, Q_LO = Q_BYTES;
+  static constexpr int K_HI = 0, K_LO = KV_BYTES, V_HI = 2 * KV_BYTES, V_LO = 3 * KV_BYTES;
+  static constexpr int STAGE = 4 * KV_BYTES;
+  static constexpr int ST_OFF = 2 * Q_BYTES;  // stage s at ST_OFF + s * STAGE
+  static constexpr int BAR_OFF = ST_OFF + 2 * STAGE;
+  static constexpr int NBARS = 15;
+  static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static constexpr int NTHREADS = 320;
+  // tensor-memory columns
+  static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN;
+  static_assert(T_O + D <= 512, "tensor memory");
+  // the cluster combine reuses stage 0: O [BM][D], then m [BM] and l [BM]
+  static_assert((BM * D + 2 * BM) * 4 <= STAGE, "combine buffer");
+};
+
+struct TParams {
+  float* out;
+  int N, M;
+  int causal;
+  int nsplit;
+  float scale_log2;
+  unsigned* err;
+};
+
+__device__ __forceinline__ float tf32_hi(float x) {
+  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
+// hi in place, lo at lo_base, over `bytes` of one tile (the layout is kept: the
+// transform is elementwise).
+__device__ __forceinline__ void split_tile(uint8_t* hi_base, uint8_t* lo_base, int bytes, int tid,
+                                           int nthreads) {
+  float4* h = reinterpret_cast<float4*>(hi_base);
+  float4* l = reinterpret_cast<float4*>(lo_base);
+  for (int i = tid; i < bytes / 16; i += nthreads) {
+    const float4 x = h[i];
+    const float4 a = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+    h[i] = a;
+    l[i] = make_float4(x.x - a.x, x.y - a.y, x.z - a.z, x.w - a.w);
+  }
+}
+
+// V as loaded ([BN keys] rows of 128-byte swizzle atoms, 32 floats of d per atom column)
+// -> V^T hi in place and V^T lo at vt_lo: [D] rows of keys in the same swizzle, the
+// K-major B operand of O += P V. (A TF32 B operand in MN-major form, V as loaded,
+// produced no result on this hardware.) The 128 split threads read all of V into
+// registers before any of them overwrites it.
+template <int D, int BN>
+__device__ __forceinline__ void split_transpose_v(uint8_t* v, uint8_t* vt_lo, int tid) {
+  constexpr int PER = BN * (D / 4) / 128;  // float4 chunks per thread
+  float4 x[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = tid + j * 128;
+    const int key = i % BN, dc = i / BN;  // lanes take consecutive keys
+    x[j] = *reinterpret_cast<const float4*>(v + (dc >> 3) * (BN * 128) + key * 128 +
+                                            (((dc & 7) ^ (key & 7)) << 4));
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = tid + j * 128;
+    const int key = i % BN, dc = i / BN;
+    const float xs[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = dc * 4 + e;
+      const int off = (key >> 5) * (D * 128) + d * 128 + ((((key & 31) >> 2) ^ (d & 7)) << 4) +
+                      (key & 3) * 4;
+      const float h = tf32_hi(xs[e]);
+      *reinterpret_cast<float*>(v + off) = h;
+      *reinterpret_cast<float*>(vt_lo + off) = xs[e] - h;
+    }
+  }
+}
+
+// AND of `pred` over the 128 split threads (named barrier 1); every one of them calls it.
+__device__ __forceinline__ bool split_group_all(bool pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(pred ? 1 : 0)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+// Every thread of every CTA of the cluster arrives; shared-memory writes before it
+// (local and remote) are visible to the whole cluster after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    fa_tf32_kernel(const __grid_constant__ CUtensorMap qmap,
+                   const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const TParams p) {
+  using C = TCfg<D>;
+  constexpr int BM = C::BM, BN = C::BN, HALVES = C::HALVES;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [2] TMA landed
+  uint64_t* kv_ready = bars + 4;  // [2] split into hi / lo
+  uint64_t* kv_empty = bars + 6;  // [2] MMAs done with the stage
+  uint64_t* s_full = bars + 8;    // [2] S_j in tensor memory
+  uint64_t* p_full = bars + 10;   // [2] P_j in tensor memory
+  uint64_t* o_done = bars + 12;   // [2] P_j V_j accumulated
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsplit = p.nsplit;
+  const int split = nsplit > 1 ? static_cast<int>(cluster_rank()) : 0;
+  const int bh = blockIdx.y;
+  const int m0 = (blockIdx.x / nsplit) * BM;
+  int ntiles = (p.M + BN - 1) / BN;
+  if (p.causal && p.M > 0) ntiles = min(p.M - 1, min(p.N - 1, m0 + BM - 1)) / BN + 1;
+  const int nloc = ntiles > split ? (ntiles - split + nsplit - 1) / nsplit : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_ready[i], 128);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc<512>(tmem_slot);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: let the next kernel place its CTAs as ours retire,
+  // and wait for the previous kernel's results before the first global access.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  float ov[D];  // softmax threads: this row's unnormalised O (for the cluster combine)
+  float m_run = NEG_INF, l_run = 0.f;
+#pragma unroll
+  for (int i = 0; i < D; ++i) ov[i] = 0.f;
+
+  if (warp == 4) {
+    // ========================================================= TMA producer
+    if (lane == 0 && nloc > 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      const uint64_t pol_keep = l2_policy_evict_last();   // K/V are re-read by other CTAs
+      const uint64_t pol_once = l2_policy_evict_first();  // Q is read once
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int h = 0; h < HALVES; ++h)
+        tma_load_3d(smem + C::Q_HI + h * C::QH, &qmap, h * 32, m0, bh, q_full, pol_once);
+      bool ok = true;
+      int issued = 0;
+      for (int it = 0; it < nloc; ++it) {
+        const int st = it & 1, rnd = it >> 1;
+        if (rnd > 0 && !mbar_wait(&kv_empty[st], (rnd - 1) & 1)) { ok = false; break; }
+        const int key0 = (split + it * nsplit) * BN;
+        uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * C::KV_BYTES);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(sb + C::K_HI + h * C::KH, &kmap, h * 32, key0, bh, &kv_full[st], pol_keep);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(sb + C::V_HI + h * C::KH, &vmap, h * 32, key0, bh, &kv_full[st], pol_keep);
+        ++issued;
+      }
+      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: every bulk copy issued here has landed before the CTA can exit.
+      mbar_wait(q_full, 0);
+      for (int it = max(0, issued - 2); it < issued; ++it)
+        mbar_wait(&kv_full[it & 1], (it >> 1) & 1);
+    }
+  } else if (warp == 5) {
+    // ========================================================= MMA issuer
+    if (lane == 0 && nloc > 0) {
+      constexpr uint32_t idesc_qk = tc::idesc_tf32(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = tc::idesc_tf32(BM, D, false, false);
+      const uint32_t sbase = smem_u32(smem);
+      auto issue_s = [&](int it) {
+        const int b = it & 1;
+        const uint32_t kbase = sbase + C::ST_OFF + b * C::STAGE;
+#pragma unroll
+        for (int pass = 0; pass < 3; ++pass) {
+          const uint32_t qa = sbase + (pass == 2 ? C::Q_LO : C::Q_HI);
+          const uint32_t kb = kbase + (pass == 1 ? C::K_LO : C::K_HI);
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk) {
+            const uint32_t qoff = (kk >> 2) * C::QH + (kk & 3) * 32;
+            const uint32_t koff = (kk >> 2) * C::KH + (kk & 3) * 32;
+            tc::mma_ss_tf32(tmem + C::T_S + b * BN, tc::smem_desc_sw128(qa + qoff, 16, 1024),
+                            tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk,
+                            (pass > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc::commit(&s_full[b]);
+      };
+      auto issue_pv = [&](int it) {
+        const int b = it & 1;
+        const uint32_t vbase = sbase + C::ST_OFF + b * C::STAGE;
+#pragma unroll
+        for (int pass = 0; pass < 3; ++pass) {
+          const uint32_t pa = tmem + (pass == 2 ? C::T_PL : C::T_S) + b * BN;
+          const uint32_t vb = vbase + (pass == 1 ? C::V_LO : C::V_HI);
+#pragma unroll
+          for (int kk = 0; kk < BN / 8; ++kk)
+            tc::mma_ts_tf32(tmem + C::T_O, pa + kk * 8,
+                            tc::smem_desc_sw128(vb + (kk >> 2) * C::VTH + (kk & 3) * 32, 16, 1024),
+                            idesc_pv, (it > 0 || pass > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(&o_done[b]);
+        tc::commit(&kv_empty[b]);
+      };
+      // S_{it+1} goes in before P_it V_it, so the tensor core computes it while the
+      // softmax of tile it runs. MMAs from this thread execute in issue order, so
+      // S_{it+2} overwrites P_it only after P_it V_it has read it.
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&kv_ready[0], 0);
+      if (ok) {
+        tc::fence_after_sync();
+        issue_s(0);
+      }
+      for (int it = 0; it < nloc && ok; ++it) {
+        if (it + 1 < nloc) {
+          if (!mbar_wait(&kv_ready[(it + 1) & 1], ((it + 1) >> 1) & 1)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_s(it + 1);
+        }
+        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1)) { ok = false; break; }
+        tc::fence_after_sync();
+        issue_pv(it);
+      }
+      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: all MMAs issued by this thread have completed.
+      tc::commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else if (warp >= 6) {
+    // ========================================================= hi / lo split
+    const int sid = threadIdx.x - 192;
+    if (nloc > 0) {
+      // The 128 split threads meet on named barrier 1 (inside split_transpose_v), so they
+      // take every go / give-up decision together: a wait result is AND-reduced first.
+      bool ok = split_group_all(mbar_wait(q_full, 0));
+      if (ok) {
+        split_tile(smem + C::Q_HI, smem + C::Q_LO, C::Q_BYTES, sid, 128);
+        fence_proxy_async_smem();
+        mbar_arrive(q_ready);
+      }
+      for (int it = 0; it < nloc && ok; ++it) {
+        const int st = it & 1;
+        if (!split_group_all(mbar_wait(&kv_full[st], (it >> 1) & 1))) { ok = false; break; }
+        uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
+        split_tile(sb + C::K_HI, sb + C::K_LO, C::KV_BYTES, sid, 128);
+        split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
+        fence_proxy_async_smem();
+        mbar_arrive(&kv_ready[st]);
+      }
+      if (!ok && sid == 0) atomicOr(p.err, kErrWaitTimeout);
+    }
+  } else {
+    // ========================================================= softmax (warps 0-3)
+    const int row = warp * 32 + lane;  // row within the tile = tensor-memory lane
+    const int r = m0 + row;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off + C::T_S;
+    const uint32_t tPL = tmem + lane_off + C::T_PL;
+    const uint32_t tO = tmem + lane_off + C::T_O;
+    const float sl = p.scale_log2;
+    const int lim = p.causal ? min(r + 1, p.M) : p.M;  // valid keys: c < lim
+    bool ok = true;
+    for (int it = 0; it < nloc && ok; ++it) {
+      const int b = it & 1;
+      const bool got = mbar_wait(&s_full[b], (it >> 1) & 1);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      tc::fence_after_sync();
+      uint32_t u[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tc::ld32(tS + b * BN + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+      tc::wait_ld();
+      const int c0 = (split + it * nsplit) * BN;
+      if (c0 + BN > lim) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i)
+          if (c0 + i >= lim) u[i] = __float_as_uint(NEG_INF);
+      }
+      float m4[4] = {NEG_INF, NEG_INF, NEG_INF, NEG_INF};
+#pragma unroll
+      for (int i = 0; i < BN; ++i) m4[i & 3] = fmaxf(m4[i & 3], __uint_as_float(u[i]));
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl;
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new > m_run + kRescaleThreshold;  // also true while m_run = -inf
+      const float m_use = need ? m_new : m_run;
+      const float mu = m_use == NEG_INF ? 0.f : m_use;
+      const float corr = need ? ex2(m_run - mu) : 1.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t ph[32], pl[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = ex2(fmaf(__uint_as_float(u[c * 32 + i]), sl, -mu));
+          s4[i & 3] += x;
+          const float h = tf32_hi(x);
+          ph[i] = __float_as_uint(h);
+          pl[i] = __float_as_uint(x - h);
+        }
+        tc::st32(tS + b * BN + c * 32, ph);
+        tc::st32(tPL + b * BN + c * 32, pl);
+      }
+      l_run = l_run * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+      m_run = m_use;
+      if (it > 0 && __any_sync(0xffffffffu, need)) {
+        // O must hold P V of tile it-1 before it is rescaled.
+        const bool got_o = mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1);
+        if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t w[32];
+          tc::ld32(tO + c * 32, w);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(w[i]) * corr);
+          tc::st32(tO + c * 32, w);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&p_full[b]);
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
+      m_run = NEG_INF;
+      l_run = 0.f;
+    } else if (nloc > 0) {
+      const bool got = mbar_wait(&o_done[(nloc - 1) & 1], ((nloc - 1) >> 1) & 1);
+      if (__all_sync(0xffffffffu, got)) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t w[32];
+          tc::ld32(tO + c * 32, w);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[c * 32 + i] = __uint_as_float(w[i]);
+        }
+      } else {
+        if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
+        m_run = NEG_INF;
+        l_run = 0.f;
+      }
+    }
+    if (nsplit == 1 && r < p.N) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float* orow = p.out + (static_cast<size_t>(bh) * p.N + r) * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 4)
+        *reinterpret_cast<float4*>(orow + c) =
+            make_float4(ov[c] * inv, ov[c + 1] * inv, ov[c + 2] * inv, ov[c + 3] * inv);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc<512>(tmem);
+  }
+  if (nsplit == 1) return;
+
+  // ---- cluster combine: rows [c*SR, (c+1)*SR) of the tile are merged by CTA c.
+  // Stage 0 is free: its copies landed and every MMA has completed (drained above).
+  float* rO = reinterpret_cast<float*>(smem + C::ST_OFF);  // [nsplit][SR][D]
+  float* rM = rO + BM * D;                                  // [nsplit][SR]
+  float* rL = rM + BM;                                      // [nsplit][SR]
+  const int SR = BM / nsplit;
+  cluster_sync_all();  // every CTA of the cluster is past its main loop
+  if (warp < 4) {
+    const int row = warp * 32 + lane;
+    const int dst = row / SR;
+    const int rr = split * SR + row - dst * SR;
+    const uint32_t ob = cluster_map(smem_u32(rO + rr * D), dst);
+#pragma unroll
+    for (int c = 0; c < D; c += 4) st_cluster_v4(ob + c * 4, ov[c], ov[c + 1], ov[c + 2], ov[c + 3]);
+    st_cluster_f32(cluster_map(smem_u32(rM + rr), dst), m_run);
+    st_cluster_f32(cluster_map(smem_u32(rL + rr), dst), l_run);
+  }
+  cluster_sync_all();  // this CTA's slice has arrived from every partner
+  constexpr int C4 = D / 4;
+  for (int idx = threadIdx.x; idx < SR * C4; idx += C::NTHREADS) {
+    const int rr = idx / C4, c = (idx - rr * C4) * 4;
+    const int row = m0 + split * SR + rr;
+    if (row >= p.N) continue;
+    float mx = NEG_INF;
+    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, rM[s2 * SR + rr]);
+    float tot = 0.f;
+    float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mx != NEG_INF) {
+      for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float w = ex2(rM[s2 * SR + rr] - mx);
+        tot = fmaf(rL[s2 * SR + rr], w, tot);
+        const float4 t = *reinterpret_cast<const float4*>(rO + (s2 * SR + rr) * D + c);
+        o4.x = fmaf(w, t.x, o4.x);
+        o4.y = fmaf(w, t.y, o4.y);
+        o4.z = fmaf(w, t.z, o4.z);
+        o4.w = fmaf(w, t.w, o4.w);
+      }
+    }
+    const float inv = tot > 0.f ? 1.f / tot : 0.f;
+    *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c) =
+        make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+  }
+}
+
+// CTAs (one cluster) per 128-row tile: the most (up to 8 and up to the key-tile count)
+// that still keep the grid within one CTA per SM. FE_TF32_SPLIT=1,2,4,8 overrides the
+// choice (tuning).
+static int tf32_split(long long row_tiles_bh, int kv_tiles) {
+  static const int forced = [] {
+    const char* s = getenv("FE_TF32_SPLIT");
+    const int v = s ? atoi(s) : 0;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }();
+  int n = 1;
+  if (forced) {
+    n = forced;
+  } else {
+    const long long slots = sm_count();
+    while (n < 8 && row_tiles_bh * n * 2 <= slots) n *= 2;
+  }
+  while (n > 1 && n > kv_tiles) n /= 2;
+  return n;
+}
+
+}  // namespace tf32
+
+namespace simt {
+
+// True when the fp32 forward of this shape runs on the tensor-core kernel above.
+bool fa2_tf32_eligible(const float* q, const float* k, const float* v, const float* o, int B,
+                       int H, int N, int M, int d) {
+  static const bool off = [] {
+    const char* s = getenv("FE_FP32_SIMT");
+    return s && atoi(s) != 0;
+  }();
+  const auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
+  return !off && d == 64 && N > 0 && M > 0 && static_cast<long long>(B) * H <= 65535 && al(q) &&
+         al(k) && al(v) && al(o);
+}
+
+cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, float* o, int B, int H,
+                            int N, int M, int d, float scale, int causal, cudaStream_t st) {
+  using namespace tf32;
+  constexpr int D = 64;
+  using C = TCfg<D>;
+  if (!fa2_tf32_eligible(q, k, v, o, B, H, N, M, d)) return cudaErrorInvalidValue;
+  auto kern = fa_tf32_kernel<D>;
+  cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
+  if (e != cudaSuccess) return e;
+  const long long BH = static_cast<long long>(B) * H;
+  CUtensorMap qm, km, vm;
+  e = encode_tma_3d_f32(&qm, q, D, N, BH, 32, C::BM);
+  if (e != cudaSuccess) return e;
+  e = encode_tma_3d_f32(&km, k, D, M, BH, 32, C::BN);
+  if (e != cudaSuccess) return e;
+  e = encode_tma_3d_f32(&vm, v, D, M, BH, 32, C::BN);
+  if (e != cudaSuccess) return e;
+  const int row_tiles = (N + C::BM - 1) / C::BM;
+  const int kv_tiles = (M + C::BN - 1) / C::BN;
+  TParams p;
+  p.out = o;
+  p.N = N;
+  p.M = M;
+  p.causal = causal;
+  p.nsplit = tf32_split(static_cast<long long>(row_tiles) * BH, kv_tiles);
+  p.scale_log2 = scale * kLog2e;
+  p.err = device_error_word();
+  if (!p.err) return cudaErrorInitializationError;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(row_tiles * p.nsplit), static_cast<unsigned>(BH));
+  cfg.blockDim = dim3(C::NTHREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.nsplit;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.nsplit > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p);
+}
+
+}  // namespace simt
+}  // namespace fe

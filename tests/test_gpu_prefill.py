@@ -33,8 +33,38 @@ def test_fp32_config1():
     assert_fp32_close(host(out), ref)
 
 
+def test_fp32_config1_cuda_core_kernel():
+    """Head dim 64 runs on the 3xTF32 tensor-core kernel; FE_FP32_SIMT=1 selects the
+    CUDA-core kernel instead. Both must match the oracle (run in a child process, since
+    the switch is read once per process)."""
+    import os
+    import subprocess
+    import sys
+    code = (
+        "import numpy as np, torch, flash_engine\n"
+        "from gpu_util import assert_fp32_close, cuda, host\n"
+        "from oracle import attention_oracle as O\n"
+        "rng = np.random.default_rng(42)\n"
+        "q, k, v = (rng.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))\n"
+        "for causal in (False, True):\n"
+        "    out = flash_engine.flash_attention(cuda(q), cuda(k), cuda(v), causal)\n"
+        "    assert_fp32_close(host(out), O.flash_attention(q, k, v, causal))\n"
+        "assert flash_engine.device_errors() == 0\n")
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, FE_FP32_SIMT="1",
+               PYTHONPATH=os.pathsep.join([here, os.path.dirname(here),
+                                           os.path.join(os.path.dirname(here),
+                                                        "flash-kernel-engine_b200"),
+                                           os.environ.get("PYTHONPATH", "")]))
+    r = subprocess.run([sys.executable, "-c", code], env=env, cwd=here, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("N,M,d", [(1, 1, 64), (65, 130, 32), (200, 77, 128), (128, 128, 100)])
+@pytest.mark.parametrize("N,M,d", [(1, 1, 64), (65, 130, 32), (200, 77, 128), (128, 128, 100),
+                                   (100, 300, 64), (100, 300, 50), (70, 1000, 32), (1, 700, 128),
+                                   (1000, 1000, 64), (129, 700, 64)])
 def test_fp32_shapes(causal, N, M, d):
     import flash_engine
     rng = np.random.default_rng(N + M + d)
