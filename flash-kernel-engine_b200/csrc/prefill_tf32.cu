@@ -17,8 +17,9 @@
 // log-sum-exp combine of src/flash_decoding.cu:151-223).
 //  * warp 4 (TMA): Q once, then K_j and V_j into a two-stage ring (3-D TMA, 128-byte
 //    swizzle; rows past N or M read as zeros).
-//  * warps 6-9 (split): rewrite each landed tile as hi in place and lo beside it; V is
-//    transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
+//  * warps 6-9 (split): rewrite each landed K / V tile as hi in place and lo beside it;
+//    V is transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
+//    The softmax warps split Q the same way before their first S tile.
 //  * warp 5 (MMA): allocates tensor memory [S0 | S1 | PL0 | PL1 | O] and, from one
 //    thread, issues
 //      S_j = Qhi Khi^T + Qhi Klo^T + Qlo Khi^T   (kind::tf32, A and B from shared memory)
@@ -63,8 +64,6 @@ struct TCfg {
   // tensor-memory columns
   static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN;
   static_assert(T_O + D <= 512, "tensor memory");
-  // the cluster combine reuses stage 0: O [BM][D], then m [BM] and l [BM]
-  static_assert((BM * D + 2 * BM) * 4 <= STAGE, "combine buffer");
 };
 
 struct TParams {
@@ -80,17 +79,23 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
-// hi in place, lo at lo_base, over `bytes` of one tile (the layout is kept: the
-// transform is elementwise).
-__device__ __forceinline__ void split_tile(uint8_t* hi_base, uint8_t* lo_base, int bytes, int tid,
-                                           int nthreads) {
+// hi in place, lo at lo_base, over BYTES of one tile, by NT threads (the layout is kept:
+// the transform is elementwise). All loads are issued before the first store.
+template <int BYTES, int NT>
+__device__ __forceinline__ void split_tile(uint8_t* hi_base, uint8_t* lo_base, int tid) {
+  constexpr int PER = BYTES / 16 / NT;
+  static_assert(PER * 16 * NT == BYTES, "tile split");
   float4* h = reinterpret_cast<float4*>(hi_base);
   float4* l = reinterpret_cast<float4*>(lo_base);
-  for (int i = tid; i < bytes / 16; i += nthreads) {
-    const float4 x = h[i];
-    const float4 a = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-    h[i] = a;
-    l[i] = make_float4(x.x - a.x, x.y - a.y, x.z - a.z, x.w - a.w);
+  float4 x[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) x[j] = h[tid + j * NT];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const float4 a =
+        make_float4(tf32_hi(x[j].x), tf32_hi(x[j].y), tf32_hi(x[j].z), tf32_hi(x[j].w));
+    h[tid + j * NT] = a;
+    l[tid + j * NT] = make_float4(x[j].x - a.x, x[j].y - a.y, x[j].z - a.z, x[j].w - a.w);
   }
 }
 
@@ -153,13 +158,18 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b),
-               "f"(c), "f"(d)
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
                : "memory");
+  return v;
 }
 // Every thread of every CTA of the cluster arrives; shared-memory writes before it
 // (local and remote) are visible to the whole cluster after it.
@@ -333,17 +343,12 @@ __global__ void __launch_bounds__(320, 1)
     if (nloc > 0) {
       // The 128 split threads meet on named barrier 1 (inside split_transpose_v), so they
       // take every go / give-up decision together: a wait result is AND-reduced first.
-      bool ok = split_group_all(mbar_wait(q_full, 0));
-      if (ok) {
-        split_tile(smem + C::Q_HI, smem + C::Q_LO, C::Q_BYTES, sid, 128);
-        fence_proxy_async_smem();
-        mbar_arrive(q_ready);
-      }
+      bool ok = true;
       for (int it = 0; it < nloc && ok; ++it) {
         const int st = it & 1;
         if (!split_group_all(mbar_wait(&kv_full[st], (it >> 1) & 1))) { ok = false; break; }
         uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
-        split_tile(sb + C::K_HI, sb + C::K_LO, C::KV_BYTES, sid, 128);
+        split_tile<C::KV_BYTES, 128>(sb + C::K_HI, sb + C::K_LO, sid);
         split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
         fence_proxy_async_smem();
         mbar_arrive(&kv_ready[st]);
@@ -361,6 +366,15 @@ __global__ void __launch_bounds__(320, 1)
     const float sl = p.scale_log2;
     const int lim = p.causal ? min(r + 1, p.M) : p.M;  // valid keys: c < lim
     bool ok = true;
+    // Q is split here (these warps are idle until S_0) while warps 6-9 split K_0 / V_0.
+    if (nloc > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0));
+      if (ok) {
+        split_tile<C::Q_BYTES, 128>(smem + C::Q_HI, smem + C::Q_LO, threadIdx.x);
+        fence_proxy_async_smem();
+        mbar_arrive(q_ready);
+      }
+    }
     for (int it = 0; it < nloc && ok; ++it) {
       const int b = it & 1;
       const bool got = mbar_wait(&s_full[b], (it >> 1) & 1);
@@ -462,48 +476,70 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (nsplit == 1) return;
 
-  // ---- cluster combine: rows [c*SR, (c+1)*SR) of the tile are merged by CTA c.
-  // Stage 0 is free: its copies landed and every MMA has completed (drained above).
-  float* rO = reinterpret_cast<float*>(smem + C::ST_OFF);  // [nsplit][SR][D]
-  float* rM = rO + BM * D;                                  // [nsplit][SR]
-  float* rL = rM + BM;                                      // [nsplit][SR]
-  const int SR = BM / nsplit;
-  cluster_sync_all();  // every CTA of the cluster is past its main loop
+  // ---- cluster combine. Each CTA leaves its partial rows (O unnormalised, m, l) in its
+  // own stage 0, which is free: its copies landed and every MMA has completed (drained
+  // above). After a cluster barrier, CTA c reads rows [c*SR, (c+1)*SR) of every partner
+  // (consecutive threads take consecutive 16-byte words of a row) and writes them.
+  // (Sending the slices with bulk async copies into the partners' shared memory measured
+  // the same; the cluster barriers dominate this phase.)
+  constexpr int OS = D + 4;                                 // padded row stride (floats)
+  float* pO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [BM][OS]
+  float* pM = pO + BM * OS;                                 // [BM]
+  float* pL = pM + BM;                                      // [BM]
+  static_assert((BM * OS + 2 * BM) * 4 <= C::STAGE, "combine buffer");
   if (warp < 4) {
     const int row = warp * 32 + lane;
-    const int dst = row / SR;
-    const int rr = split * SR + row - dst * SR;
-    const uint32_t ob = cluster_map(smem_u32(rO + rr * D), dst);
 #pragma unroll
-    for (int c = 0; c < D; c += 4) st_cluster_v4(ob + c * 4, ov[c], ov[c + 1], ov[c + 2], ov[c + 3]);
-    st_cluster_f32(cluster_map(smem_u32(rM + rr), dst), m_run);
-    st_cluster_f32(cluster_map(smem_u32(rL + rr), dst), l_run);
+    for (int c = 0; c < D; c += 4)
+      *reinterpret_cast<float4*>(pO + row * OS + c) =
+          make_float4(ov[c], ov[c + 1], ov[c + 2], ov[c + 3]);
+    pM[row] = m_run;
+    pL[row] = l_run;
   }
-  cluster_sync_all();  // this CTA's slice has arrived from every partner
+  cluster_sync_all();  // every partial of the cluster is in place
+  const int SR = BM / nsplit;
   constexpr int C4 = D / 4;
   for (int idx = threadIdx.x; idx < SR * C4; idx += C::NTHREADS) {
     const int rr = idx / C4, c = (idx - rr * C4) * 4;
-    const int row = m0 + split * SR + rr;
+    const int trow = split * SR + rr;
+    const int row = m0 + trow;
     if (row >= p.N) continue;
+    const uint32_t a_m = smem_u32(pM + trow), a_l = smem_u32(pL + trow);
+    const uint32_t a_o = smem_u32(pO + trow * OS + c);
+    float ms[8], ls[8];
+    float4 os[8];
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < nsplit) {
+        ms[s2] = ld_cluster_f32(cluster_map(a_m, s2));
+        ls[s2] = ld_cluster_f32(cluster_map(a_l, s2));
+        os[s2] = ld_cluster_v4(cluster_map(a_o, s2));
+      }
+    }
     float mx = NEG_INF;
-    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, rM[s2 * SR + rr]);
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2)
+      if (s2 < nsplit) mx = fmaxf(mx, ms[s2]);
     float tot = 0.f;
     float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (mx != NEG_INF) {
-      for (int s2 = 0; s2 < nsplit; ++s2) {
-        const float w = ex2(rM[s2 * SR + rr] - mx);
-        tot = fmaf(rL[s2 * SR + rr], w, tot);
-        const float4 t = *reinterpret_cast<const float4*>(rO + (s2 * SR + rr) * D + c);
-        o4.x = fmaf(w, t.x, o4.x);
-        o4.y = fmaf(w, t.y, o4.y);
-        o4.z = fmaf(w, t.z, o4.z);
-        o4.w = fmaf(w, t.w, o4.w);
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (s2 < nsplit) {
+          const float w = ex2(ms[s2] - mx);
+          tot = fmaf(ls[s2], w, tot);
+          o4.x = fmaf(w, os[s2].x, o4.x);
+          o4.y = fmaf(w, os[s2].y, o4.y);
+          o4.z = fmaf(w, os[s2].z, o4.z);
+          o4.w = fmaf(w, os[s2].w, o4.w);
+        }
       }
     }
     const float inv = tot > 0.f ? 1.f / tot : 0.f;
     *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c) =
         make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
   }
+  cluster_sync_all();  // no CTA exits while a partner may still read its partials
 }
 
 // CTAs (one cluster) per 128-row tile: the most (up to 8 and up to the key-tile count)
