@@ -4,19 +4,24 @@
 Headline (``value``): BASELINE config 3, paged decode bf16 -- batch 64, 32 query /
 8 KV heads, head_dim 128, block size 16, context lengths U[512, 4096] (seed 0),
 physical blocks a random permutation of the pool. One step = one
-``flash_engine.paged_attention`` call (split-KV kernel + log-sum-exp merge) over the
-whole batch, replayed from a CUDA graph. With N GPUs (torchrun) the KV heads are
-sharded: rank r owns KV heads [r*8/N, (r+1)*8/N) and their query heads; no
-communication (strong scaling). Metric: KV GB/s = algorithmic bytes per step (K and
-V rows of every context token and KV head, q, out, block-table entries, context
-lengths) / step time, whole job; ``roofline`` against the measured HBM copy peak.
+``flash_engine.paged_attention`` call over the whole batch (one persistent split-KV
+kernel with the log-sum-exp merge fused in), replayed from CUDA graphs of 10 steps.
+With N GPUs (torchrun) the KV heads are sharded: rank r owns KV heads
+[r*8/N, (r+1)*8/N) and their query heads; no communication (strong scaling). Metric:
+KV GB/s = algorithmic bytes per step (K and V rows of every context token and KV head,
+q, out, block-table entries, context lengths) / step time, whole job; ``roofline``
+against the measured HBM copy peak.
 
 ``secondary`` reports the other BASELINE configs measured in the same run:
   config 2 -- FA2 prefill bf16 causal [4, 32, 4096, 128], heads sharded (TFLOP/s);
   config 4 -- split-KV decode, 131072-token context, KV range sharded over the
-              ranks with an NCCL all-gather of the (O, m, l) partials (KV GB/s);
+              ranks; the decode kernel stores its (O, m, l) partials into every
+              rank's exchange buffer over NVLink and a merge kernel combines them
+              (``--kv-exchange nccl``: an NCCL all-gather instead) (KV GB/s);
   config 5 -- serving-mix paged decode, 256 seqs, 64q/8kv, lognormal contexts,
-              KV-head sharded (KV GB/s).
+              KV-head sharded (KV GB/s);
+  config 1 -- FA2 forward fp32 [1, 8, 512, 64], non-causal (3xTF32 tensor-core
+              kernel), heads sharded (TFLOP/s).
 ``--workload`` makes any of them the headline instead. ``--impl reference`` times the
 reference's CPU implementation of the path (the NumPy port in oracle/, all host
 threads) on a bounded sample per step.
@@ -726,7 +731,7 @@ def main():
         res["dtype"] = "f32"
     if not a.no_secondary:
         sec = {}
-        for name in ("prefill", "splitkv", "serving"):
+        for name in ("prefill", "splitkv", "serving", "prefill_fp32"):
             if name == a.workload:
                 continue
             try:
