@@ -410,12 +410,11 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   int* pre = stage_valid + NSTAGE;  // [num_seqs + 1]
   __shared__ int warp_tot[NCW + 1];
   __shared__ Pending pend[2];  // flat mode: pieces written as slot 0 / slot 1
-  __shared__ unsigned xstep_s;
 
   // Programmatic dependent launch, both ways: the next kernel in the stream may start
   // its CTAs as soon as SM room frees up (it waits for this grid's results before
-  // reading them), and this grid, launched the same way, waits below for the previous
-  // kernel's results before its first global access.
+  // reading them), and this grid, launched the same way, waits (griddepcontrol.wait)
+  // for the previous kernel's results before it reads anything that kernel may write.
   griddep_launch_dependents();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -434,7 +433,12 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   const bool flat = p.flat != 0;
   const bool direct_final = p.direct_final != 0;
 
-  griddep_wait();
+  // Until griddepcontrol.wait below, this grid touches only shared memory and the two
+  // inputs that no kernel of this library writes, context_lens and block_tables: the
+  // prefix over the sequences and the producer's first block-table group are read
+  // while the previous grid (typically the previous decode step) is still finishing.
+  // q, the KV cache, the workspace, the exchange buffers and the outputs are accessed
+  // only after the wait.
   if (tid == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
@@ -442,11 +446,6 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     }
     fence_mbar_init();
     pend[0].nslots = pend[1].nslots = 0;
-    // exchange mode: the step this launch produces (one read per CTA; the block-wide
-    // prefix below orders it before every use)
-    xstep_s = p.xworld > 0
-                  ? ld_volatile_u32(&reinterpret_cast<const XHeader*>(p.xbuf[p.xrank])->step) + 1u
-                  : 0u;
   }
 
   SegIter it;
@@ -513,6 +512,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     int base = 0;
     int ph_cur = 0, vd_cur = 0;
     if (have) load_group(cur, 0, ph_cur, vd_cur);
+    griddep_wait();  // the KV cache may have been written by the previous kernel
     while (have && ok) {
       // Look one 32-page group ahead and start its block-table loads now.
       Seg ns = cur;
@@ -592,6 +592,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   }
 
   // ======================================================= consumer warps
+  griddep_wait();
   using E = Elem<T>;
   const int g = lane >> 2, c = lane & 3;
   const T* __restrict__ qbase = reinterpret_cast<const T*>(p.q);
@@ -645,7 +646,13 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   // exchange mode, to this rank's slot of every rank's exchange buffer (generation
   // xstep & 1) as words tagged with xstep -- the all-gather of KV-range sharding done
   // by peer stores.
-  const unsigned xstep = xstep_s;
+  // Exchange mode: the step this launch produces. The header is advanced only by the
+  // merge of the previous step, which is complete (wait above), so every thread reads
+  // the same value.
+  const unsigned xstep =
+      p.xworld > 0
+          ? ld_volatile_u32(&reinterpret_cast<const XHeader*>(p.xbuf[p.xrank])->step) + 1u
+          : 0u;
   auto emit_partial = [&](size_t row, int dim, float O, float M, float L) {
     if (p.xworld > 0) {
       const int par = static_cast<int>(xstep & 1u);

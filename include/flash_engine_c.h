@@ -86,6 +86,12 @@ int fe_naive_attention_forward_fp32(const float* q, const float* k, const float*
  * num_blocks > 0 enables a device-side range check of every block-table entry
  * (bad entries are skipped and flagged in the device error word); 0 = unknown.
  * scale <= 0 selects 1/sqrt(head_dim).
+ * The bf16/fp16 decode kernels are launched with programmatic dependent launch and
+ * read context_lens and the first block-table entries before they wait for the
+ * previous kernel in the stream. No kernel of this library writes those two arrays,
+ * and a kernel that does not trigger programmatic launch itself (or a copy) always
+ * completes first. So the one case to avoid is a kernel of the caller's that writes
+ * them and signals programmatic completion early, placed directly before a decode.
  */
 
 /* fp32 cache. Replaces launch_paged_attention_v1_fp32 (include/paged_attention.cuh:39-48,
