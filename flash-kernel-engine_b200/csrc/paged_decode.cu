@@ -267,8 +267,9 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
                                                  int D, SlotOf slot_of, OOff o_off, SOff s_off,
                                                  float& M_out, float& L_out, float (&acc)[PER]) {
   const int lane = threadIdx.x & 31;
-  if (total <= BATCH) {
-    // Few parts: the stats and every O row are loaded at once (one round trip).
+  if (total <= 32) {
+    // Up to 32 parts: lane j loads part j's stats while the O rows of the first BATCH
+    // parts load too (one round trip); further O rows follow BATCH at a time.
     float m = NEG_INF, l = 0.f;
     if (lane < total) {
       const size_t slot = slot_of(lane);
@@ -276,15 +277,19 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
       l = __ldcg(part_stats + s_off(slot) + 1);
     }
     float v[BATCH][PER];
+    auto load_rows = [&](int k0) {
 #pragma unroll
-    for (int k = 0; k < BATCH; ++k) {
-      const float* po = part_out + o_off(k < total ? slot_of(k) : slot_of(0));
+      for (int k = 0; k < BATCH; ++k) {
+        const bool in = k0 + k < total;
+        const float* po = part_out + o_off(in ? slot_of(k0 + k) : slot_of(0));
 #pragma unroll
-      for (int e = 0; e < PER; ++e) {
-        const int dim = lane + 32 * e;
-        v[k][e] = (k < total && dim < D) ? __ldcg(po + dim) : 0.f;
+        for (int e = 0; e < PER; ++e) {
+          const int dim = lane + 32 * e;
+          v[k][e] = (in && dim < D) ? __ldcg(po + dim) : 0.f;
+        }
       }
-    }
+    };
+    load_rows(0);
     float M = l > 0.f ? m : NEG_INF;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -294,11 +299,14 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
 #pragma unroll
     for (int e = 0; e < PER; ++e) acc[e] = 0.f;
+    for (int k0 = 0; k0 < total; k0 += BATCH) {
+      if (k0 > 0) load_rows(k0);
 #pragma unroll
-    for (int k = 0; k < BATCH; ++k) {
-      const float wk = __shfl_sync(0xffffffffu, w, k);
+      for (int k = 0; k < BATCH; ++k) {
+        const float wk = __shfl_sync(0xffffffffu, w, (k0 + k) & 31);
 #pragma unroll
-      for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * wk;
+        for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * wk;
+      }
     }
     M_out = M;
     L_out = L;

@@ -201,6 +201,19 @@ def test_single_long_sequence_many_pieces():
         assert_bf16_close(out, ref)
 
 
+@pytest.mark.parametrize("n_seqs", [16, 24])
+def test_sequences_cut_into_9_to_32_pieces(n_seqs):
+    """One KV head, n_seqs sequences of 4096 tokens: the flat split gives each
+    sequence 9-32 pieces on 148 SMs (16 seqs: about 19; 24 seqs: about 13), so the
+    combine takes its multi-batch path (stats of every part in the first round trip,
+    O rows 8 at a time)."""
+    lens = [4096] * n_seqs
+    p = O.make_paged_problem(60 + n_seqs, n_seqs, 4, 1, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    assert_bf16_close(_run(p, torch.bfloat16, "v2"), ref)
+
+
 def test_nonzero_workspace_counters_are_flagged():
     """A workspace whose counters were not zero-filled is reported through the device
     error word (bit 3) instead of being trusted silently."""
