@@ -227,6 +227,38 @@ bool stream_scratch(cudaStream_t st, StreamScratch* out) {
   return true;
 }
 
+// fp32 scratch the library keeps for the split fp32 paged decode, one block per
+// (device, stream) grown to the largest request seen. Growth waits for the stream's
+// earlier work (which may still read the old block) before freeing it. Returns
+// nullptr while the stream is being captured and the block is too small.
+float* stream_scratch_f32(cudaStream_t st, size_t floats) {
+  static std::mutex mu;
+  static std::map<std::pair<int, uintptr_t>, std::pair<float*, size_t>> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
+  auto it = cache.find(key);
+  if (it != cache.end() && it->second.second >= floats) return it->second.first;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return nullptr;
+  size_t want = floats;
+  if (it != cache.end()) {
+    want = std::max(floats, 2 * it->second.second);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return nullptr;
+    cudaFree(it->second.first);
+    cache.erase(it);
+  }
+  float* p = nullptr;
+  if (cudaMalloc(&p, want * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  cache.emplace(key, std::make_pair(p, want));
+  return p;
+}
+
 // The reference's v1 entry points: the split-KV kernel with the library's own scratch
 // (the single-pass kernel when none can be had).
 template <typename T>
@@ -336,9 +368,39 @@ int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc,
   const int rc = paged_check(a, false);
   if (rc) return rc;
   if (S == 0) return 0;
+  cudaStream_t st = as_stream(stream);
+  const float sc = resolve_scale(scale, d);
+  // Contexts longer than one split: the key range is cut into kFp32SplitTokens-token
+  // splits (as many as the block-table row can hold, so every context is covered) and
+  // merged; shorter ones, or no scratch (a capture), take the single-pass kernel.
+  constexpr int kFp32SplitTokens = 512;
+  const long long row_tokens = static_cast<long long>(maxb) * bs;
+  const long long splits = (row_tokens + kFp32SplitTokens - 1) / kFp32SplitTokens;
+  if (splits > 1 && splits <= 4096 && S <= 65535) {
+    const size_t rows = static_cast<size_t>(S) * H;
+    const size_t need = rows * static_cast<size_t>(splits) * (d + 2);
+    float* ws = stream_scratch_f32(st, need);
+    if (ws) {
+      float* po = ws;
+      float* pml = ws + rows * static_cast<size_t>(splits) * d;
+      cudaError_t e = fe::simt::launch_paged_split_fp32(q, kc, vc, po, pml, bt, lens, S, H, Hkv, d,
+                                                        bs, maxb, num_blocks,
+                                                        static_cast<int>(splits),
+                                                        kFp32SplitTokens, sc, st);
+      if (e != cudaSuccess) return static_cast<int>(e);
+      fe::paged::MergeParams mp{};
+      mp.part_out = po;
+      mp.part_stats = pml;
+      mp.rows = static_cast<int>(rows);
+      mp.ranks = 1;
+      mp.parts_per_rank = static_cast<int>(splits);
+      mp.out = out;
+      mp.out_dtype = 0;
+      return static_cast<int>(fe::paged::launch_merge(mp, d, st));
+    }
+  }
   return static_cast<int>(fe::simt::launch_paged_fp32(q, kc, vc, out, bt, lens, S, H, Hkv, d, bs,
-                                                      maxb, num_blocks, resolve_scale(scale, d),
-                                                      as_stream(stream)));
+                                                      maxb, num_blocks, sc, st));
 }
 
 int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, void* out,

@@ -11,6 +11,8 @@
 #include <limits.h>
 #include <stdlib.h>
 
+#include <type_traits>
+
 #include "fp32_kernels.h"
 #include "internal.h"
 #include "ptx.cuh"
@@ -476,52 +478,100 @@ cudaError_t launch_naive_fp32(const float* q, const float* k, const float* v, fl
 }
 
 // =========================================================================
-// Warp-per-token decode core shared by the paged and dense fp32 decoders.
-// CTA = 4 warps working on up to HG query heads that read the same KV head.
-// Each warp takes tokens round-robin; lanes own D/32 dims; per token and head the
-// warp reduces the dot product with shuffles and updates its own (m, l, acc);
-// the four warp states are merged through shared memory at the end.
+// Warp decode core shared by the paged and dense fp32 decoders. A CTA of NW warps
+// works on up to HG query heads that read the same KV head. Each warp takes groups of
+// TB consecutive tokens round-robin.
+//  * It loads the K and V rows of all TB tokens before it uses the first, so TB rows
+//    per warp are in flight.
+//  * It forms all TB x HG partial dot products, then reduces them together (each
+//    butterfly step over every value, so the shuffles overlap).
+//  * It updates the online softmax once per head per group: one rescale and TB
+//    exponentials.
+// One row at a time, with a reduction and a rescale per token and head, left these
+// HBM-bound kernels latency-bound at 14% of the copy bandwidth. Lanes own D/32 dims,
+// and q lives in registers. The NW warp states are merged through shared memory at
+// the end.
+template <int D, int HG>
+constexpr int decode_tb() { return (D <= 128 && HG <= 4) ? 8 : 4; }
+
 template <int D, int HG>
 struct WarpDecode {
   static constexpr int E = D / 32;
-  float m[HG], l[HG], acc[HG][E];
-  __device__ __forceinline__ void init() {
+  static constexpr int TB = decode_tb<D, HG>();
+  float m[HG], l[HG], acc[HG][E], qr[HG][E];
+  // q: [HG][D] in shared memory (zero padded), read into registers once.
+  __device__ __forceinline__ void init(const float* q, int lane) {
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
       m[h] = NEG_INF;
       l[h] = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[h][e] = 0.f;
+      for (int e = 0; e < E; ++e) {
+        acc[h][e] = 0.f;
+        qr[h][e] = q[h * D + lane + 32 * e];
+      }
     }
   }
-  // q: [HG][D] in shared memory (zero padded); k, v: token rows (d valid floats).
-  __device__ __forceinline__ void token(const float* q, const float* k, const float* v, int d,
-                                        int nh, float sl, int lane) {
-    float kv[E], vv[E];
+  // k[j], v[j]: rows of token j of the group (d valid floats), used where valid bit j
+  // is set (warp-uniform).
+  __device__ __forceinline__ void tokens(const float* const (&k)[TB], const float* const (&v)[TB],
+                                         unsigned valid, int d, int nh, float sl, int lane) {
+    if (valid == 0) return;
+    float kv[TB][E], vv[TB][E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int c = lane + 32 * e;
-      kv[e] = c < d ? __ldg(k + c) : 0.f;
-      vv[e] = c < d ? __ldg(v + c) : 0.f;
-    }
+    for (int j = 0; j < TB; ++j)
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int c = lane + 32 * e;
+        const bool in = ((valid >> j) & 1u) && c < d;
+        kv[j][e] = in ? __ldg(k[j] + c) : 0.f;
+        vv[j][e] = in ? __ldg(v[j] + c) : 0.f;
+      }
+    float sp[TB][HG];
+#pragma unroll
+    for (int j = 0; j < TB; ++j)
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        float t = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) t = fmaf(qr[h][e], kv[j][e], t);
+        sp[j][h] = t;
+      }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int j = 0; j < TB; ++j)
+#pragma unroll
+        for (int h = 0; h < HG; ++h) sp[j][h] += __shfl_xor_sync(0xffffffffu, sp[j][h], off);
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
       if (h >= nh) break;
-      float s = 0.f;
+      float mx = NEG_INF;
 #pragma unroll
-      for (int e = 0; e < E; ++e) s = fmaf(q[h * D + lane + 32 * e], kv[e], s);
-      s = warp_sum(s) * sl;
-      const float mn = fmaxf(m[h], s);
-      const float corr = ex2(m[h] - mn), p = ex2(s - mn);
-      l[h] = l[h] * corr + p;
+      for (int j = 0; j < TB; ++j)
+        if ((valid >> j) & 1u) mx = fmaxf(mx, sp[j][h] * sl);
+      const float mn = fmaxf(m[h], mx);  // finite: at least one token is valid
+      const float corr = ex2(m[h] - mn);
+      float psum = 0.f;
+      float pv[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[h][e] = fmaf(p, vv[e], acc[h][e] * corr);
+      for (int e = 0; e < E; ++e) pv[e] = 0.f;
+#pragma unroll
+      for (int j = 0; j < TB; ++j) {
+        const float pj = ((valid >> j) & 1u) ? ex2(fmaf(sp[j][h], sl, -mn)) : 0.f;
+        psum += pj;
+#pragma unroll
+        for (int e = 0; e < E; ++e) pv[e] = fmaf(pj, vv[j][e], pv[e]);
+      }
+      l[h] = fmaf(l[h], corr, psum);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[h][e] = fmaf(acc[h][e], corr, pv[e]);
       m[h] = mn;
     }
   }
-  // Merge 4 warp states through smem (cm/cl: [4][HG], co: [4][HG][D]); returns the
+  // Merge NW warp states through smem (cm/cl: [NW][HG], co: [NW][HG][D]); returns the
   // merged (M, L, O) for (h, c) pairs handled by the calling thread via `emit`.
-  template <typename Emit>
+  template <int NW, typename Emit>
   __device__ __forceinline__ void merge(float* cm, float* cl, float* co, int nh, int d, int warp,
                                         int lane, Emit emit) {
     if (lane == 0) {
@@ -540,9 +590,9 @@ struct WarpDecode {
       const int h = i / D, c = i - h * D;
       if (c >= d) continue;
       float Mx = NEG_INF;
-      for (int w = 0; w < 4; ++w) Mx = fmaxf(Mx, cm[w * HG + h]);
+      for (int w = 0; w < NW; ++w) Mx = fmaxf(Mx, cm[w * HG + h]);
       float L = 0.f, Ov = 0.f;
-      for (int w = 0; w < 4; ++w) {
+      for (int w = 0; w < NW; ++w) {
         const float mw = cm[w * HG + h];
         const float wt = mw == NEG_INF ? 0.f : ex2(mw - Mx);
         L += cl[w * HG + h] * wt;
@@ -553,42 +603,224 @@ struct WarpDecode {
   }
 };
 
-// Paged fp32 decode: grid (Hkv * head_chunks, S); the chunk's query heads share
-// every K/V row read.
+// Vectorised variant of WarpDecode for head dim D = d in {64, 128}, HG in {4, 8} and
+// 16-byte aligned rows. TB * HG = 32 (token, head) scores per group.
+//  * Lane i owns dims [i*C, (i+1)*C), C = D/32, and loads a row's share as one 64- or
+//    128-bit word.
+//  * The 32 partial dot products are reduce-scattered: five butterfly steps that halve
+//    the set each time, 31 shuffles in all. Lane l then holds the full score of token
+//    l / HG, head l % HG.
+//  * The softmax of a group takes one exponential per lane, plus one per head for the
+//    rescale; the group maxima of the heads are exchanged by shuffles.
+//  * P V takes each p by shuffle from the lane that holds it.
+// The sum l stays split over the lanes of each head until the end.
 template <int D, int HG>
+struct WarpDecodeV {
+  static constexpr int C = D / 32;
+  static constexpr int TB = 32 / HG;
+  static_assert((D == 64 || D == 128) && (HG == 4 || HG == 8), "vector decode shape");
+  using VecT = typename std::conditional<C == 4, float4, float2>::type;
+  float m[HG], acc[HG][C], qr[HG][C];
+  float m_own, l_part;  // running max and partial sum of head (lane % HG)
+  __device__ __forceinline__ void init(const float* q, int lane) {
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      m[h] = NEG_INF;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        acc[h][c] = 0.f;
+        qr[h][c] = q[h * D + lane * C + c];
+      }
+    }
+    m_own = NEG_INF;
+    l_part = 0.f;
+  }
+  __device__ __forceinline__ static void load_row(const float* p, bool in, float (&x)[C]) {
+    if (in) {
+      const VecT t = __ldg(reinterpret_cast<const VecT*>(p));
+      x[0] = t.x;
+      x[1] = t.y;
+      if constexpr (C == 4) {
+        x[2] = t.z;
+        x[3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) x[c] = 0.f;
+    }
+  }
+  __device__ __forceinline__ void tokens(const float* const (&k)[TB], const float* const (&v)[TB],
+                                         unsigned valid, int, int, float sl, int lane) {
+    if (valid == 0) return;
+    float kv[TB][C], vv[TB][C];
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      const bool in = (valid >> j) & 1u;
+      load_row(k[j] + lane * C, in, kv[j]);
+      load_row(v[j] + lane * C, in, vv[j]);
+    }
+    float x[32];  // x[j * HG + h]: this lane's part of q_h . k_j
+#pragma unroll
+    for (int j = 0; j < TB; ++j)
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) t = fmaf(qr[h][c], kv[j][c], t);
+        x[j * HG + h] = t;
+      }
+    // reduce-scatter: after the step over lane bit b, the lane keeps the half of the
+    // remaining indices selected by its bit b; at the end x[0] is index = lane
+#pragma unroll
+    for (int half = 16; half >= 1; half >>= 1) {
+      const bool up = lane & half;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? x[i] : x[i + half];
+        const float keep = up ? x[i + half] : x[i];
+        x[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+      }
+    }
+    const int j_own = lane / HG;
+    const bool v_own = (valid >> j_own) & 1u;
+    const float s_own = v_own ? x[0] * sl : NEG_INF;
+    // group max per head over the lanes of that head (lane % HG equal)
+    float mx = s_own;
+#pragma unroll
+    for (int off = HG; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float m_new = fmaxf(m_own, mx);  // finite: at least one token is valid
+    const float p_own = v_own ? ex2(s_own - m_new) : 0.f;
+    l_part = fmaf(l_part, ex2(m_own - m_new), p_own);
+    m_own = m_new;
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      const float mh = __shfl_sync(0xffffffffu, m_new, h);  // lane h holds head h
+      const float corr = ex2(m[h] - mh);
+      m[h] = mh;
+#pragma unroll
+      for (int c = 0; c < C; ++c) acc[h][c] *= corr;
+    }
+#pragma unroll
+    for (int j = 0; j < TB; ++j)
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        const float pj = __shfl_sync(0xffffffffu, p_own, j * HG + h);
+#pragma unroll
+        for (int c = 0; c < C; ++c) acc[h][c] = fmaf(pj, vv[j][c], acc[h][c]);
+      }
+  }
+  // Merge NW warp states through smem (cm/cl: [NW][HG], co: [NW][HG][D]), as WarpDecode.
+  template <int NW, typename Emit>
+  __device__ __forceinline__ void merge(float* cm, float* cl, float* co, int nh, int d, int warp,
+                                        int lane, Emit emit) {
+    float lsum = l_part;
+#pragma unroll
+    for (int off = HG; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    if (lane < HG) {  // lane h holds head h's max and, now, its sum
+      cm[warp * HG + lane] = m_own;
+      cl[warp * HG + lane] = lsum;
+    }
+#pragma unroll
+    for (int h = 0; h < HG; ++h)
+#pragma unroll
+      for (int c = 0; c < C; ++c) co[(warp * HG + h) * D + lane * C + c] = acc[h][c];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nh * D; i += blockDim.x) {
+      const int h = i / D, c = i - h * D;
+      if (c >= d) continue;
+      float Mx = NEG_INF;
+      for (int w = 0; w < NW; ++w) Mx = fmaxf(Mx, cm[w * HG + h]);
+      float L = 0.f, Ov = 0.f;
+      for (int w = 0; w < NW; ++w) {
+        const float mw = cm[w * HG + h];
+        const float wt = mw == NEG_INF ? 0.f : ex2(mw - Mx);
+        L += cl[w * HG + h] * wt;
+        Ov += co[(w * HG + h) * D + c] * wt;
+      }
+      emit(h, c, Mx, L, Ov);
+    }
+  }
+};
+
+// The decoder a paged kernel instantiates: vectorised for the shapes it supports.
+template <int D, int HG, bool VEC>
+using PagedDecoder = typename std::conditional<VEC, WarpDecodeV<D, HG>, WarpDecode<D, HG>>::type;
+
+// Paged fp32 decode: grid (Hkv * head_chunks, S), 4 warps; the chunk's query heads
+// share every K/V row read.
+template <int D, int HG, bool VEC>
 __global__ void __launch_bounds__(128) paged_fp32_kernel(
     const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
     float* __restrict__ out, const int* __restrict__ bt, const int* __restrict__ lens, int H,
     int Hkv, int d, int bs, int maxb, int num_blocks, float sl, unsigned* err) {
+  constexpr int NW = 4;
+  using WD = PagedDecoder<D, HG, VEC>;
+  constexpr int TB = WD::TB;
   __shared__ float sq[HG * D];
-  __shared__ float cm[4 * HG], cl[4 * HG];
-  __shared__ float co[4 * HG * D];
+  __shared__ float cm[NW * HG], cl[NW * HG];
+  __shared__ float co[NW * HG * D];
   const int G = H / Hkv, chunks = (G + HG - 1) / HG;
   const int kvh = blockIdx.x / chunks, ch = blockIdx.x - kvh * chunks;
   const int seq = blockIdx.y;
   const int h0 = kvh * G + ch * HG;
   const int nh = min(HG, G - ch * HG);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < HG * D; i += 128) {
+  for (int i = threadIdx.x; i < HG * D; i += NW * 32) {
     const int h = i / D, c = i - h * D;
     sq[i] = (h < nh && c < d) ? q[(static_cast<size_t>(seq) * H + h0 + h) * d + c] : 0.f;
   }
   __syncthreads();
   const int ctx = lens[seq];
-  WarpDecode<D, HG> st;
-  st.init();
-  for (int t = warp; t < ctx; t += 4) {
-    const int phys = __ldg(bt + static_cast<size_t>(seq) * maxb + t / bs);
-    if (phys < 0 || (num_blocks > 0 && phys >= num_blocks)) {
-      if (lane == 0) atomicOr(err, kErrBadBlock);
-      continue;
+  WD st;
+  st.init(sq, lane);
+  for (int t0 = warp * TB; t0 < ctx; t0 += NW * TB) {
+    const float* kp[TB];
+    const float* vp[TB];
+    unsigned valid = 0;
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      const int t = t0 + j;
+      kp[j] = vp[j] = kc;
+      if (t >= ctx) continue;
+      if (t / bs >= maxb) {  // context longer than the block-table row
+        if (lane == 0) atomicOr(err, kErrBadBlock);
+        continue;
+      }
+      const int phys = __ldg(bt + static_cast<size_t>(seq) * maxb + t / bs);
+      if (phys < 0 || (num_blocks > 0 && phys >= num_blocks)) {
+        if (lane == 0) atomicOr(err, kErrBadBlock);
+        continue;
+      }
+      const size_t off = ((static_cast<size_t>(phys) * Hkv + kvh) * bs + t % bs) * d;
+      kp[j] = kc + off;
+      vp[j] = vc + off;
+      valid |= 1u << j;
     }
-    const size_t off = ((static_cast<size_t>(phys) * Hkv + kvh) * bs + t % bs) * d;
-    st.token(sq, kc + off, vc + off, d, nh, sl, lane);
+    st.tokens(kp, vp, valid, d, nh, sl, lane);
   }
-  st.merge(cm, cl, co, nh, d, warp, lane, [&](int h, int c, float, float L, float Ov) {
-    out[(static_cast<size_t>(seq) * H + h0 + h) * d + c] = L > 0.f ? Ov / L : 0.f;
-  });
+  st.template merge<NW>(cm, cl, co, nh, d, warp, lane,
+                        [&](int h, int c, float, float L, float Ov) {
+                          out[(static_cast<size_t>(seq) * H + h0 + h) * d + c] =
+                              L > 0.f ? Ov / L : 0.f;
+                        });
+}
+
+// Launches the vectorised decoder where the shape allows it, else the generic one.
+template <int D, int HG>
+static cudaError_t launch_paged_fp32_v(bool vec, dim3 grid, const float* q, const float* kc,
+                                       const float* vc, float* out, const int* bt,
+                                       const int* lens, int H, int Hkv, int d, int bs, int maxb,
+                                       int num_blocks, float sl, unsigned* err, cudaStream_t st) {
+  if constexpr ((D == 64 || D == 128) && (HG == 4 || HG == 8)) {
+    if (vec) {
+      paged_fp32_kernel<D, HG, true><<<grid, 128, 0, st>>>(q, kc, vc, out, bt, lens, H, Hkv, d,
+                                                           bs, maxb, num_blocks, sl, err);
+      return cudaGetLastError();
+    }
+  }
+  paged_fp32_kernel<D, HG, false><<<grid, 128, 0, st>>>(q, kc, vc, out, bt, lens, H, Hkv, d, bs,
+                                                        maxb, num_blocks, sl, err);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_paged_fp32(const float* q, const float* kc, const float* vc, float* out,
@@ -601,12 +833,12 @@ cudaError_t launch_paged_fp32(const float* q, const float* kc, const float* vc, 
   dim3 grid(Hkv * chunks, S);
   const float sl = scale * kLog2e;
   unsigned* err = device_error_word();
-#define FE_P(D_, HG_)                                                                      \
-  if (d <= D_ && HG == HG_) {                                                              \
-    paged_fp32_kernel<D_, HG_><<<grid, 128, 0, st>>>(q, kc, vc, out, bt, lens, H, Hkv, d, bs, \
-                                                     maxb, num_blocks, sl, err);           \
-    return cudaGetLastError();                                                             \
-  }
+  const bool vec = (d == 64 || d == 128) && (HG == 4 || HG == 8) &&
+                   ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) == 0;
+#define FE_P(D_, HG_)                                                                  \
+  if (d <= D_ && HG == HG_)                                                            \
+    return launch_paged_fp32_v<D_, HG_>(vec, grid, q, kc, vc, out, bt, lens, H, Hkv, d, bs, \
+                                        maxb, num_blocks, sl, err, st);
   FE_P(64, 1) FE_P(64, 2) FE_P(64, 4) FE_P(64, 8)
   FE_P(128, 1) FE_P(128, 2) FE_P(128, 4) FE_P(128, 8)
   FE_P(256, 1) FE_P(256, 2) FE_P(256, 4)
@@ -614,36 +846,182 @@ cudaError_t launch_paged_fp32(const float* q, const float* kc, const float* vc, 
   return cudaErrorInvalidValue;
 }
 
-// Dense split-KV stage 1 (fp32): grid (splits, B*H). Writes the unnormalised O,
-// m (log2 units) and l of split s of row bh; an empty split writes (-inf, 0).
+// Paged fp32 decode, split: grid (splits, Hkv * head_chunks, S), 8 warps. CTA
+// (s, chunk, seq) covers tokens [s*T, (s+1)*T) of its sequence (T = split_tokens) and
+// writes the unnormalised O, m (log2 units) and l of each of its query heads to part
+// slot (seq*H + h)*splits + s; a split past the context writes (0, -inf, 0). A merge
+// over the splits (the log-sum-exp combine, merge_kernel) gives the output. With the
+// key range cut this way, a long sequence no longer sets the kernel's length, as it
+// does with one CTA per (sequence, KV head).
+template <int D, int HG, bool VEC>
+__global__ void __launch_bounds__(256, 2) paged_split_fp32_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ part_o, float* __restrict__ part_ml, const int* __restrict__ bt,
+    const int* __restrict__ lens, int H, int Hkv, int d, int bs, int maxb, int num_blocks,
+    int split_tokens, float sl, unsigned* err) {
+  constexpr int NW = 8;
+  using WD = PagedDecoder<D, HG, VEC>;
+  constexpr int TB = WD::TB;
+  __shared__ float sq[HG * D];
+  __shared__ float cm[NW * HG], cl[NW * HG];
+  __shared__ float co[NW * HG * D];
+  const int splits = gridDim.x, s = blockIdx.x;
+  const int G = H / Hkv, chunks = (G + HG - 1) / HG;
+  const int kvh = blockIdx.y / chunks, ch = blockIdx.y - kvh * chunks;
+  const int seq = blockIdx.z;
+  const int h0 = kvh * G + ch * HG;
+  const int nh = min(HG, G - ch * HG);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ctx = lens[seq];
+  const int t0 = s * split_tokens, t1 = min(ctx, t0 + split_tokens);
+  // the splits cover the block-table row; a longer context is a bad input
+  if (s == splits - 1 && ctx > t0 + split_tokens && threadIdx.x == 0) atomicOr(err, kErrBadBlock);
+  if (t0 >= t1) {  // nothing of this sequence here: an empty part
+    for (int i = threadIdx.x; i < nh * d; i += NW * 32) {
+      const int h = i / d, c = i - h * d;
+      const size_t slot = (static_cast<size_t>(seq) * H + h0 + h) * splits + s;
+      part_o[slot * d + c] = 0.f;
+      if (c == 0) {
+        part_ml[slot * 2] = NEG_INF;
+        part_ml[slot * 2 + 1] = 0.f;
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < HG * D; i += NW * 32) {
+    const int h = i / D, c = i - h * D;
+    sq[i] = (h < nh && c < d) ? q[(static_cast<size_t>(seq) * H + h0 + h) * d + c] : 0.f;
+  }
+  __syncthreads();
+  WD st;
+  st.init(sq, lane);
+  for (int tb = t0 + warp * TB; tb < t1; tb += NW * TB) {
+    const float* kp[TB];
+    const float* vp[TB];
+    unsigned valid = 0;
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      const int t = tb + j;
+      kp[j] = vp[j] = kc;
+      if (t >= t1) continue;
+      if (t / bs >= maxb) {  // context longer than the block-table row
+        if (lane == 0) atomicOr(err, kErrBadBlock);
+        continue;
+      }
+      const int phys = __ldg(bt + static_cast<size_t>(seq) * maxb + t / bs);
+      if (phys < 0 || (num_blocks > 0 && phys >= num_blocks)) {
+        if (lane == 0) atomicOr(err, kErrBadBlock);
+        continue;
+      }
+      const size_t off = ((static_cast<size_t>(phys) * Hkv + kvh) * bs + t % bs) * d;
+      kp[j] = kc + off;
+      vp[j] = vc + off;
+      valid |= 1u << j;
+    }
+    st.tokens(kp, vp, valid, d, nh, sl, lane);
+  }
+  st.template merge<NW>(cm, cl, co, nh, d, warp, lane,
+                        [&](int h, int c, float Mx, float L, float Ov) {
+                          const size_t slot = (static_cast<size_t>(seq) * H + h0 + h) * splits + s;
+                          part_o[slot * d + c] = Ov;
+                          if (c == 0) {
+                            part_ml[slot * 2] = Mx;
+                            part_ml[slot * 2 + 1] = L;
+                          }
+                        });
+}
+
+template <int D, int HG>
+static cudaError_t launch_paged_split_fp32_v(bool vec, dim3 grid, const float* q, const float* kc,
+                                             const float* vc, float* part_o, float* part_ml,
+                                             const int* bt, const int* lens, int H, int Hkv, int d,
+                                             int bs, int maxb, int num_blocks, int split_tokens,
+                                             float sl, unsigned* err, cudaStream_t st) {
+  if constexpr ((D == 64 || D == 128) && (HG == 4 || HG == 8)) {
+    if (vec) {
+      paged_split_fp32_kernel<D, HG, true><<<grid, 256, 0, st>>>(
+          q, kc, vc, part_o, part_ml, bt, lens, H, Hkv, d, bs, maxb, num_blocks, split_tokens, sl,
+          err);
+      return cudaGetLastError();
+    }
+  }
+  paged_split_fp32_kernel<D, HG, false><<<grid, 256, 0, st>>>(
+      q, kc, vc, part_o, part_ml, bt, lens, H, Hkv, d, bs, maxb, num_blocks, split_tokens, sl,
+      err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_split_fp32(const float* q, const float* kc, const float* vc,
+                                    float* part_o, float* part_ml, const int* bt, const int* lens,
+                                    int S, int H, int Hkv, int d, int bs, int maxb, int num_blocks,
+                                    int splits, int split_tokens, float scale, cudaStream_t st) {
+  if (S <= 0) return cudaSuccess;
+  if (S > 65535 || splits < 1 || split_tokens < 1) return cudaErrorInvalidValue;
+  const int G = H / Hkv;
+  const int HG = G >= 8 ? 8 : G >= 4 ? 4 : G >= 2 ? 2 : 1;
+  const int chunks = (G + HG - 1) / HG;
+  if (static_cast<long long>(Hkv) * chunks > 65535) return cudaErrorInvalidValue;
+  dim3 grid(splits, Hkv * chunks, S);
+  const float sl = scale * kLog2e;
+  unsigned* err = device_error_word();
+  const bool vec = (d == 64 || d == 128) && (HG == 4 || HG == 8) &&
+                   ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) == 0;
+#define FE_P(D_, HG_)                                                                       \
+  if (d <= D_ && HG == HG_)                                                                 \
+    return launch_paged_split_fp32_v<D_, HG_>(vec, grid, q, kc, vc, part_o, part_ml, bt, lens, \
+                                              H, Hkv, d, bs, maxb, num_blocks, split_tokens,   \
+                                              sl, err, st);
+  FE_P(64, 1) FE_P(64, 2) FE_P(64, 4) FE_P(64, 8)
+  FE_P(128, 1) FE_P(128, 2) FE_P(128, 4) FE_P(128, 8)
+  FE_P(256, 1) FE_P(256, 2) FE_P(256, 4)
+#undef FE_P
+  return cudaErrorInvalidValue;
+}
+
+// Dense split-KV stage 1 (fp32): grid (splits, B*H), 8 warps. Writes the
+// unnormalised O, m (log2 units) and l of split s of row bh; an empty split writes
+// (-inf, 0).
 template <int D>
-__global__ void __launch_bounds__(128) decode_split_fp32_kernel(
+__global__ void __launch_bounds__(256) decode_split_fp32_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     float* __restrict__ part_o, float* __restrict__ part_ml, int M, int d, int splits, float sl) {
+  constexpr int NW = 8;
+  using WD = WarpDecode<D, 1>;
+  constexpr int TB = WD::TB;
   __shared__ float sq[D];
-  __shared__ float cm[4], cl[4];
-  __shared__ float co[4 * D];
+  __shared__ float cm[NW], cl[NW];
+  __shared__ float co[NW * D];
   const int s = blockIdx.x;
   const size_t bh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = (M + splits - 1) / splits;
   const int t0 = s * per, t1 = min(M, t0 + per);
-  for (int c = threadIdx.x; c < D; c += 128) sq[c] = c < d ? q[bh * d + c] : 0.f;
+  for (int c = threadIdx.x; c < D; c += NW * 32) sq[c] = c < d ? q[bh * d + c] : 0.f;
   __syncthreads();
-  WarpDecode<D, 1> st;
-  st.init();
-  for (int t = t0 + warp; t < t1; t += 4) {
-    const size_t off = (bh * M + t) * d;
-    st.token(sq, k + off, v + off, d, 1, sl, lane);
+  WD st;
+  st.init(sq, lane);
+  for (int tb = t0 + warp * TB; tb < t1; tb += NW * TB) {
+    const float* kp[TB];
+    const float* vp[TB];
+    unsigned valid = 0;
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      const int t = min(tb + j, t1 - 1);
+      kp[j] = k + (bh * M + t) * d;
+      vp[j] = v + (bh * M + t) * d;
+      if (tb + j < t1) valid |= 1u << j;
+    }
+    st.tokens(kp, vp, valid, d, 1, sl, lane);
   }
   const size_t slot = bh * splits + s;
-  st.merge(cm, cl, co, 1, d, warp, lane, [&](int, int c, float Mx, float L, float Ov) {
-    part_o[slot * d + c] = Ov;
-    if (c == 0) {
-      part_ml[slot * 2] = Mx;
-      part_ml[slot * 2 + 1] = L;
-    }
-  });
+  st.template merge<NW>(cm, cl, co, 1, d, warp, lane,
+                        [&](int, int c, float Mx, float L, float Ov) {
+                          part_o[slot * d + c] = Ov;
+                          if (c == 0) {
+                            part_ml[slot * 2] = Mx;
+                            part_ml[slot * 2 + 1] = L;
+                          }
+                        });
 }
 
 cudaError_t launch_decode_split_fp32(const float* q, const float* k, const float* v,
@@ -653,11 +1031,11 @@ cudaError_t launch_decode_split_fp32(const float* q, const float* k, const float
   dim3 grid(splits, BH);
   const float sl = scale * kLog2e;
   if (d <= 64)
-    decode_split_fp32_kernel<64><<<grid, 128, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
+    decode_split_fp32_kernel<64><<<grid, 256, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
   else if (d <= 128)
-    decode_split_fp32_kernel<128><<<grid, 128, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
+    decode_split_fp32_kernel<128><<<grid, 256, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
   else if (d <= 256)
-    decode_split_fp32_kernel<256><<<grid, 128, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
+    decode_split_fp32_kernel<256><<<grid, 256, 0, st>>>(q, k, v, part_o, part_ml, M, d, splits, sl);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();

@@ -80,6 +80,62 @@ def test_paged_fp32_random(H, Hkv, d):
     assert_fp32_close(out, ref)
 
 
+@pytest.mark.parametrize("H,Hkv,d", [(8, 2, 64), (32, 8, 128), (12, 4, 96), (64, 8, 128),
+                                     (4, 4, 256)])
+def test_paged_fp32_long_contexts_split(H, Hkv, d):
+    """Contexts longer than one 512-token split: the fp32 entry cuts the key range into
+    splits over the block-table row and merges them (boundaries at 511/512/513)."""
+    lens = [0, 1, 511, 512, 513, 1500, 2049]
+    p = O.make_paged_problem(19 + d, len(lens), H, Hkv, d, lens, bf16=False)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    out = _run(p, torch.float32)
+    assert_fp32_close(out, ref)
+
+
+def test_paged_fp32_split_in_graph_capture():
+    """fp32 paged decode inside a CUDA-graph capture: on a fresh stream (no library
+    scratch yet) it takes the single-pass kernel, after an eager call on that stream the
+    split kernel and merge; both replays match the oracle."""
+    import flash_engine
+    lens = [700, 1300, 64, 2000]
+    p = O.make_paged_problem(77, len(lens), 16, 4, 128, lens, bf16=False)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    q, kc, vc = (cuda(p[k], torch.float32) for k in ("q", "k_cache", "v_cache"))
+    bt, ln = cuda(p["block_tables"]), cuda(p["context_lens"])
+    for eager_first in (False, True):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            if eager_first:
+                flash_engine.paged_attention(q, kc, vc, bt, ln, 16)
+            out = torch.empty_like(q)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                flash_engine.paged_attention(q, kc, vc, bt, ln, 16, out=out)
+            out.zero_()
+            g.replay()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        assert_fp32_close(host(out), ref)
+
+
+def test_paged_fp32_context_past_block_row_is_flagged():
+    """A context longer than max_blocks_per_seq * block_size is a bad input: flagged in
+    the device error word, no read past the row."""
+    import flash_engine
+    lens = [600, 40]
+    p = O.make_paged_problem(5, len(lens), 8, 2, 64, lens, bf16=False)
+    ln = cuda(np.array([600 + 16 * 5, 40], dtype=np.int32))
+    flash_engine.paged_attention(cuda(p["q"], torch.float32), cuda(p["k_cache"], torch.float32),
+                                 cuda(p["v_cache"], torch.float32), cuda(p["block_tables"]),
+                                 ln, 16)
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() != 0
+
+
 @pytest.mark.parametrize("version", ["v1", "v2"])
 def test_block_table_gather_is_bit_exact(version):
     """One-hot attention: token j of each sequence carries a key that dominates by
