@@ -95,7 +95,12 @@ int fe_naive_attention_forward_fp32(const float* q, const float* k, const float*
  */
 
 /* fp32 cache. Replaces launch_paged_attention_v1_fp32 (include/paged_attention.cuh:39-48,
- * src/paged_attention.cu:181-215). Any block_size >= 1, head_dim % 4 == 0, <= 256. */
+ * src/paged_attention.cu:181-215). Any block_size >= 1, head_dim % 4 == 0, <= 256.
+ * When max_blocks_per_seq * block_size exceeds 512, the key range runs in 512-token
+ * splits that a merge kernel combines. The splits' partials go to fp32 scratch the
+ * library owns, one block per (device, stream), allocated on the first such call
+ * outside a stream capture. Inside a capture with no large enough block yet, the
+ * single-pass kernel runs instead. */
 int fe_paged_attention_v1_fp32(const float* q, const float* k_cache, const float* v_cache,
                                float* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
