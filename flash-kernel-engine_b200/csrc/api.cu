@@ -376,7 +376,8 @@ int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc,
   constexpr int kFp32SplitTokens = 512;
   const long long row_tokens = static_cast<long long>(maxb) * bs;
   const long long splits = (row_tokens + kFp32SplitTokens - 1) / kFp32SplitTokens;
-  if (splits > 1 && splits <= 4096 && S <= 65535) {
+  if (splits > 1 && splits <= 4096 && S <= 65535 &&
+      static_cast<long long>(S) * H <= static_cast<long long>(INT_MAX)) {
     const size_t rows = static_cast<size_t>(S) * H;
     const size_t need = rows * static_cast<size_t>(splits) * (d + 2);
     float* ws = stream_scratch_f32(st, need);
