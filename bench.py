@@ -21,7 +21,9 @@ against the measured HBM copy peak.
   config 5 -- serving-mix paged decode, 256 seqs, 64q/8kv, lognormal contexts,
               KV-head sharded (KV GB/s);
   config 1 -- FA2 forward fp32 [1, 8, 512, 64], non-causal (3xTF32 tensor-core
-              kernel), heads sharded (TFLOP/s).
+              kernel), heads sharded (TFLOP/s);
+  paged_fp32 -- the reference's fp32 paged entry on config 3's shapes with an fp32
+              cache (KV GB/s).
 ``--workload`` makes any of them the headline instead. ``--impl reference`` times the
 reference's CPU implementation of the path (the NumPy port in oracle/, all host
 threads) on a bounded sample per step.
@@ -49,7 +51,7 @@ for _p in (ROOT, PKG):
 import numpy as np  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
-WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32")
+WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32", "paged_fp32")
 
 
 def _args():
@@ -62,6 +64,9 @@ def _args():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--num-seqs", type=int, default=0,
+                    help="paged_fp32 only: use the first N sequences of config 3 (a small "
+                         "case for profiler captures); 0 = all 64")
     ap.add_argument("--kv-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="KV-range all-gather at N > 1: the decode kernel's own peer stores "
                          "(p2p) or NCCL all-gather + merge kernel (nccl)")
@@ -413,6 +418,104 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     return res
 
 
+def bench_paged_fp32(a, ws, rank, local, steps, warmup):
+    """The reference's fp32 paged entry (launch_paged_attention_v1_fp32) on config 3's
+    shapes with an fp32 cache: one step = one flash_engine.paged_attention call (512-token
+    split kernel + merge). KV heads sharded over the ranks as in config 3."""
+    import torch
+    import flash_engine
+
+    dev = torch.device("cuda", local)
+    c = CFG3
+    H, Hkv, d, bs = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["block_size"]
+    if Hkv % ws:
+        raise ValueError(f"{ws} ranks cannot split {Hkv} KV heads")
+    hkv_l, h_l = Hkv // ws, H // ws
+    lens = _lens(c, a.seed)
+    if a.num_seqs > 0:
+        lens = lens[:a.num_seqs]
+    S = len(lens)
+    nblk = (lens + bs - 1) // bs
+    pool = int(nblk.sum())
+    kv_set = pool * hkv_l * bs * d * 4 * 2
+    R = max(1, math.ceil(2 * L2_BYTES / kv_set))
+    rng = np.random.default_rng(a.seed + 1)
+    perm = rng.permutation(pool * R).astype(np.int32)
+    maxb = int(nblk.max())
+    bts = []
+    for r in range(R):
+        bt = np.zeros((S, maxb), np.int32)
+        off = r * pool
+        for s_ in range(S):
+            bt[s_, :nblk[s_]] = perm[off:off + nblk[s_]]
+            off += nblk[s_]
+        bts.append(torch.from_numpy(bt).to(dev))
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + a.seed * 17 + rank)
+    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev)
+    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev)
+    q = torch.randn((S, h_l, d), generator=g, device=dev)
+    lens_t = torch.from_numpy(lens).to(dev)
+    out = torch.empty_like(q)
+
+    def step(i):
+        flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, out=out)
+
+    sampler = ClockSampler(local).start()
+    ms_rank, t0, t1 = _time_steps(step, steps, max(3, warmup), ws, dev)
+    sampler.stop()
+    assert flash_engine.device_errors() == 0
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    total = decode_bytes(lens, Hkv, H, d, bs, elt=4)
+    rank_bytes = decode_bytes(lens, hkv_l, h_l, d, bs, elt=4)
+
+    # End to end through the public API: q, block table and lengths in from pinned host
+    # memory, the output back, one step at a time on the wall clock.
+    q_h, lens_h = q.cpu().pin_memory(), lens_t.cpu().pin_memory()
+    bt_h = [b.cpu().pin_memory() for b in bts]
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_d, lens_d, bt_d = torch.empty_like(q), torch.empty_like(lens_t), torch.empty_like(bts[0])
+
+    def e2e_step(i):
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h[i % R], non_blocking=True)
+        lens_d.copy_(lens_h, non_blocking=True)
+        out_h.copy_(flash_engine.paged_attention(q_d, kc, vc, bt_d, lens_d, bs), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(3):
+        e2e_step(i)
+    _barrier(ws, dev)
+    n_e2e = max(1, min(steps, 50))
+    te0 = time.perf_counter()
+    for i in range(n_e2e):
+        e2e_step(i)
+    e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n_e2e, ws, dev)
+    peak_hbm, _, _, src = _peaks()
+    return {
+        "metric": "paged decode fp32 KV GB/s (the reference's v1 fp32 entry on config 3 shapes)",
+        "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "ms_per_step": round(ms, 5),
+        "config": {"workload": "paged_decode_fp32_config3", "num_seqs": S, "num_heads": H,
+                   "num_kv_heads": Hkv, "head_dim": d, "block_size": bs,
+                   "total_context_tokens": int(lens.sum()), "bytes_per_step": total,
+                   "parallelism": f"kv-head shard x{ws}",
+                   "l2": f"{R} block set(s) of {kv_set / 2**20:.0f} MiB per rank used in turn"},
+        "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (ms_rank * 1e-3) / 1e9, 2),
+                     "peak": peak_hbm, "unit": "GB/s",
+                     "frac": round(rank_bytes / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
+                     "peak_source": src,
+                     "kernel": "paged_split_fp32_kernel (512-token splits) + merge_kernel",
+                     "traffic": None},
+        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": int(q_h.numel() * 4 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4)},
+        "gpu_launches": 2 * steps,
+        "clocks": sampler.summary(t0, t1),
+    }
+
+
 def cpu_paged_baseline(cfg, lens, seed, budget_s=12.0, steps=1):
     """The NumPy port of the reference's paged_attention (per KV-head group), timed on
     the host over a bounded prefix of the workload's sequences."""
@@ -705,6 +808,8 @@ def run_workload(name, a, ws, rank, local, primary):
         return bench_splitkv(a, ws, rank, local, steps, warmup)
     if name == "prefill":
         return bench_prefill(a, ws, rank, local, steps, warmup)
+    if name == "paged_fp32":
+        return bench_paged_fp32(a, ws, rank, local, steps, warmup)
     return bench_prefill(a, ws, rank, local, steps, warmup, fp32=True)
 
 
@@ -727,11 +832,11 @@ def main():
     res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded N(0,1) bf16 inputs; BASELINE config shapes)"})
-    if a.workload == "prefill_fp32":
+    if a.workload in ("prefill_fp32", "paged_fp32"):
         res["dtype"] = "f32"
     if not a.no_secondary:
         sec = {}
-        for name in ("prefill", "splitkv", "serving", "prefill_fp32"):
+        for name in ("prefill", "splitkv", "serving", "prefill_fp32", "paged_fp32"):
             if name == a.workload:
                 continue
             try:
