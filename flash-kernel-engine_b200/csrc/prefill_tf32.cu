@@ -8,8 +8,8 @@
 // It computes the reference's launch_flash_attention_forward_fp32
 // (src/flash_attention.cu:111-345): O = softmax(Q K^T * scale [+ causal mask]) V over
 // [B, H, N|M, d] fp32 tensors, causal mask top-left aligned (query row i sees keys
-// j <= i, src/flash_attention.cu:224). Head dim 64; the other head dims run on the
-// CUDA-core kernel of attention_fp32.cu.
+// j <= i, src/flash_attention.cu:224). Head dims 32 and 64; the other head dims run on
+// the CUDA-core kernel of attention_fp32.cu.
 //
 // A CTA owns one 128-row query tile of one (batch, head) and the 64-key tiles
 // t = split, split + nsplit, ... of it. The nsplit CTAs of a row tile form a thread-block
@@ -60,6 +60,10 @@ struct TCfg {
   static constexpr int BAR_OFF = ST_OFF + 2 * STAGE;
   static constexpr int NBARS = 15;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  // Dynamic shared memory requested at launch: enough that two CTAs never share an SM.
+  // Each allocates all 512 tensor-memory columns, and two on one SM in one cluster would
+  // wait on each other (one in tcgen05.alloc, the other at the cluster barrier).
+  static constexpr int SMEM_LAUNCH = SMEM > 120 * 1024 ? SMEM : 120 * 1024;
   static constexpr int NTHREADS = 320;
   // tensor-memory columns
   static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN;
@@ -574,18 +578,18 @@ bool fa2_tf32_eligible(const float* q, const float* k, const float* v, const flo
     return s && atoi(s) != 0;
   }();
   const auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
-  return !off && d == 64 && N > 0 && M > 0 && static_cast<long long>(B) * H <= 65535 && al(q) &&
-         al(k) && al(v) && al(o);
+  return !off && (d == 32 || d == 64) && N > 0 && M > 0 &&
+         static_cast<long long>(B) * H <= 65535 && al(q) && al(k) && al(v) && al(o);
 }
 
-cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, float* o, int B, int H,
-                            int N, int M, int d, float scale, int causal, cudaStream_t st) {
+template <int D>
+static cudaError_t launch_fa2_tf32_d(const float* q, const float* k, const float* v, float* o,
+                                     int B, int H, int N, int M, float scale, int causal,
+                                     cudaStream_t st) {
   using namespace tf32;
-  constexpr int D = 64;
   using C = TCfg<D>;
-  if (!fa2_tf32_eligible(q, k, v, o, B, H, N, M, d)) return cudaErrorInvalidValue;
   auto kern = fa_tf32_kernel<D>;
-  cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
+  cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM_LAUNCH);
   if (e != cudaSuccess) return e;
   const long long BH = static_cast<long long>(B) * H;
   CUtensorMap qm, km, vm;
@@ -609,7 +613,7 @@ cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, floa
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(row_tiles * p.nsplit), static_cast<unsigned>(BH));
   cfg.blockDim = dim3(C::NTHREADS);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = C::SMEM_LAUNCH;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -621,6 +625,13 @@ cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, floa
   cfg.attrs = attr;
   cfg.numAttrs = p.nsplit > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, qm, km, vm, p);
+}
+
+cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, float* o, int B, int H,
+                            int N, int M, int d, float scale, int causal, cudaStream_t st) {
+  if (!fa2_tf32_eligible(q, k, v, o, B, H, N, M, d)) return cudaErrorInvalidValue;
+  if (d == 32) return launch_fa2_tf32_d<32>(q, k, v, o, B, H, N, M, scale, causal, st);
+  return launch_fa2_tf32_d<64>(q, k, v, o, B, H, N, M, scale, causal, st);
 }
 
 }  // namespace simt

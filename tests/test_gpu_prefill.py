@@ -34,9 +34,9 @@ def test_fp32_config1():
 
 
 def test_fp32_config1_cuda_core_kernel():
-    """Head dim 64 runs on the 3xTF32 tensor-core kernel; FE_FP32_SIMT=1 selects the
-    CUDA-core kernel instead. Both must match the oracle (run in a child process, since
-    the switch is read once per process)."""
+    """Head dims 32 and 64 run on the 3xTF32 tensor-core kernel; FE_FP32_SIMT=1 selects
+    the CUDA-core kernel instead. Both must match the oracle (run in a child process,
+    since the switch is read once per process)."""
     import os
     import subprocess
     import sys
@@ -49,6 +49,9 @@ def test_fp32_config1_cuda_core_kernel():
         "for causal in (False, True):\n"
         "    out = flash_engine.flash_attention(cuda(q), cuda(k), cuda(v), causal)\n"
         "    assert_fp32_close(host(out), O.flash_attention(q, k, v, causal))\n"
+        "    a, b, c = (x[..., :32].copy() for x in (q, k, v))\n"
+        "    out = flash_engine.flash_attention(cuda(a), cuda(b), cuda(c), causal)\n"
+        "    assert_fp32_close(host(out), O.flash_attention(a, b, c, causal))\n"
         "assert flash_engine.device_errors() == 0\n")
     here = os.path.dirname(os.path.abspath(__file__))
     env = dict(os.environ, FE_FP32_SIMT="1",
