@@ -9,7 +9,7 @@ namespace simt {
 cudaError_t launch_fa2_fp32(const float* q, const float* k, const float* v, float* o, int B, int H,
                             int N, int M, int d, float scale, int causal, cudaStream_t st);
 // fp32 FA2 forward on the tensor core with 3xTF32 products (prefill_tf32.cu), used by
-// launch_fa2_fp32 for head dims 32 and 64 with 16-byte aligned tensors.
+// launch_fa2_fp32 for head dims 32, 64 and 128 with 16-byte aligned tensors.
 bool fa2_tf32_eligible(const float* q, const float* k, const float* v, const float* o, int B,
                        int H, int N, int M, int d);
 cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, float* o, int B, int H,

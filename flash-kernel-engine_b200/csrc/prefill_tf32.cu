@@ -8,8 +8,9 @@
 // It computes the reference's launch_flash_attention_forward_fp32
 // (src/flash_attention.cu:111-345): O = softmax(Q K^T * scale [+ causal mask]) V over
 // [B, H, N|M, d] fp32 tensors, causal mask top-left aligned (query row i sees keys
-// j <= i, src/flash_attention.cu:224). Head dims 32 and 64; the other head dims run on
-// the CUDA-core kernel of attention_fp32.cu.
+// j <= i, src/flash_attention.cu:224). Head dims 32, 64 and 128; the other head dims run
+// on the CUDA-core kernel of attention_fp32.cu. At d = 128 the key tile is 32 and Q lo
+// sits in tensor memory (shared memory holds Q hi and the two K/V stages).
 //
 // A CTA owns one 128-row query tile of one (batch, head) and the 64-key tiles
 // t = split, split + nsplit, ... of it. The nsplit CTAs of a row tile form a thread-block
@@ -46,17 +47,20 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows
 
 template <int D>
 struct TCfg {
-  static constexpr int BM = 128, BN = 64;
+  // d = 128: Q hi / lo and two K/V stages of 64 keys do not fit shared memory, so the
+  // key tile is 32 and Q lo lives in tensor memory (the A operand of its S pass).
+  static constexpr bool QLO_TMEM = D > 64;
+  static constexpr int BM = 128, BN = D > 64 ? 32 : 64;
   static constexpr int HALVES = D / 32;  // 128-byte swizzle atom columns along d
   static constexpr int QH = BM * 128;    // bytes of one Q atom column
   static constexpr int KH = BN * 128;    // bytes of one K or V atom column
   static constexpr int VTH = D * 128;    // bytes of one V^T atom column (D rows)
   static constexpr int Q_BYTES = BM * D * 4;
   static constexpr int KV_BYTES = BN * D * 4;
-  static constexpr int Q_HI = 0, Q_LO = Q_BYTES;
+  static constexpr int Q_HI = 0, Q_LO = Q_BYTES;  // Q_LO: shared-memory Q lo (d <= 64)
   static constexpr int K_HI = 0, K_LO = KV_BYTES, V_HI = 2 * KV_BYTES, V_LO = 3 * KV_BYTES;
   static constexpr int STAGE = 4 * KV_BYTES;
-  static constexpr int ST_OFF = 2 * Q_BYTES;  // stage s at ST_OFF + s * STAGE
+  static constexpr int ST_OFF = (QLO_TMEM ? 1 : 2) * Q_BYTES;  // stage s at ST_OFF + s*STAGE
   static constexpr int BAR_OFF = ST_OFF + 2 * STAGE;
   static constexpr int NBARS = 15;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
@@ -65,9 +69,10 @@ struct TCfg {
   // wait on each other (one in tcgen05.alloc, the other at the cluster barrier).
   static constexpr int SMEM_LAUNCH = SMEM > 120 * 1024 ? SMEM : 120 * 1024;
   static constexpr int NTHREADS = 320;
-  // tensor-memory columns
-  static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN;
-  static_assert(T_O + D <= 512, "tensor memory");
+  // tensor-memory columns: S / P_hi double-buffered, P_lo double-buffered, O, Q lo
+  static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN, T_QL = T_O + D;
+  static_assert(T_QL + (QLO_TMEM ? D : 0) <= 512, "tensor memory");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 struct TParams {
@@ -242,10 +247,8 @@ __global__ void __launch_bounds__(320, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  float ov[D];  // softmax threads: this row's unnormalised O (for the cluster combine)
-  float m_run = NEG_INF, l_run = 0.f;
-#pragma unroll
-  for (int i = 0; i < D; ++i) ov[i] = 0.f;
+  float m_run = NEG_INF, l_run = 0.f;  // softmax threads: this row's running max and sum
+  bool have_o = false;                 // softmax threads: O in tensor memory is final
 
   if (warp == 4) {
     // ========================================================= TMA producer
@@ -295,9 +298,13 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < D / 8; ++kk) {
             const uint32_t qoff = (kk >> 2) * C::QH + (kk & 3) * 32;
             const uint32_t koff = (kk >> 2) * C::KH + (kk & 3) * 32;
-            tc::mma_ss_tf32(tmem + C::T_S + b * BN, tc::smem_desc_sw128(qa + qoff, 16, 1024),
-                            tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk,
-                            (pass > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t acc = (pass > 0 || kk > 0) ? 1u : 0u;
+            if (C::QLO_TMEM && pass == 2)  // A = Q lo from tensor memory
+              tc::mma_ts_tf32(tmem + C::T_S + b * BN, tmem + C::T_QL + kk * 8,
+                              tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk, acc);
+            else
+              tc::mma_ss_tf32(tmem + C::T_S + b * BN, tc::smem_desc_sw128(qa + qoff, 16, 1024),
+                              tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk, acc);
           }
         }
         tc::commit(&s_full[b]);
@@ -374,7 +381,30 @@ __global__ void __launch_bounds__(320, 1)
     if (nloc > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0));
       if (ok) {
-        split_tile<C::Q_BYTES, 128>(smem + C::Q_HI, smem + C::Q_LO, threadIdx.x);
+        if constexpr (C::QLO_TMEM) {
+          // this thread's row: hi back in place, lo to tensor-memory columns T_QL + d
+#pragma unroll
+          for (int a = 0; a < HALVES; ++a) {
+            uint32_t lo[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              float4* q4 = reinterpret_cast<float4*>(smem + C::Q_HI + a * C::QH + row * 128 +
+                                                     ((c ^ (row & 7)) << 4));
+              const float4 x = *q4;
+              const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+              *q4 = h;
+              lo[c * 4 + 0] = __float_as_uint(x.x - h.x);
+              lo[c * 4 + 1] = __float_as_uint(x.y - h.y);
+              lo[c * 4 + 2] = __float_as_uint(x.z - h.z);
+              lo[c * 4 + 3] = __float_as_uint(x.w - h.w);
+            }
+            tc::st32(tmem + lane_off + C::T_QL + a * 32, lo);
+          }
+          tc::wait_st();
+          tc::fence_before_sync();
+        } else {
+          split_tile<C::Q_BYTES, 128>(smem + C::Q_HI, smem + C::Q_LO, threadIdx.x);
+        }
         fence_proxy_async_smem();
         mbar_arrive(q_ready);
       }
@@ -442,65 +472,93 @@ __global__ void __launch_bounds__(320, 1)
     }
     if (!ok) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
-      m_run = NEG_INF;
-      l_run = 0.f;
     } else if (nloc > 0) {
       const bool got = mbar_wait(&o_done[(nloc - 1) & 1], ((nloc - 1) >> 1) & 1);
-      if (__all_sync(0xffffffffu, got)) {
+      have_o = __all_sync(0xffffffffu, got);
+      if (have_o) {
         tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t w[32];
-          tc::ld32(tO + c * 32, w);
-          tc::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[c * 32 + i] = __uint_as_float(w[i]);
-        }
-      } else {
-        if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
-        m_run = NEG_INF;
-        l_run = 0.f;
+      } else if (lane == 0) {
+        atomicOr(p.err, kErrWaitTimeout);
       }
     }
-    if (nsplit == 1 && r < p.N) {
+    if (!have_o) {
+      m_run = NEG_INF;
+      l_run = 0.f;
+    }
+    if (nsplit == 1) {
+      // O / l straight from tensor memory, 32 columns at a time
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       float* orow = p.out + (static_cast<size_t>(bh) * p.N + r) * D;
 #pragma unroll
-      for (int c = 0; c < D; c += 4)
-        *reinterpret_cast<float4*>(orow + c) =
-            make_float4(ov[c] * inv, ov[c + 1] * inv, ov[c + 2] * inv, ov[c + 3] * inv);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t w[32];
+        if (have_o) {
+          tc::ld32(tO + c * 32, w);
+          tc::wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = 0u;
+        }
+        if (r < p.N) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(orow + c * 32 + i) =
+                make_float4(__uint_as_float(w[i]) * inv, __uint_as_float(w[i + 1]) * inv,
+                            __uint_as_float(w[i + 2]) * inv, __uint_as_float(w[i + 3]) * inv);
+        }
+      }
     }
   }
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc<512>(tmem);
+  if (nsplit == 1) {
+    if (warp == 5) {
+      tc::fence_after_sync();
+      tc::tmem_dealloc<512>(tmem);
+    }
+    return;
   }
-  if (nsplit == 1) return;
 
   // ---- cluster combine. Each CTA leaves its partial rows (O unnormalised, m, l) in its
-  // own stage 0, which is free: its copies landed and every MMA has completed (drained
-  // above). After a cluster barrier, CTA c reads rows [c*SR, (c+1)*SR) of every partner
+  // own stage buffers, which are free: their copies landed and every MMA has completed
+  // (drained above). After a cluster barrier, CTA c reads rows [c*SR, (c+1)*SR) of every partner
   // (consecutive threads take consecutive 16-byte words of a row) and writes them.
   // (Sending the slices with bulk async copies into the partners' shared memory measured
   // the same; the cluster barriers dominate this phase.)
   constexpr int OS = D + 4;                                 // padded row stride (floats)
-  float* pO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [BM][OS]
+  float* pO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [BM][OS] (both stages)
   float* pM = pO + BM * OS;                                 // [BM]
   float* pL = pM + BM;                                      // [BM]
-  static_assert((BM * OS + 2 * BM) * 4 <= C::STAGE, "combine buffer");
+  static_assert((BM * OS + 2 * BM) * 4 <= 2 * C::STAGE, "combine buffer");
   if (warp < 4) {
     const int row = warp * 32 + lane;
+    const uint32_t tO = tmem + (static_cast<uint32_t>(warp * 32) << 16) + C::T_O;
 #pragma unroll
-    for (int c = 0; c < D; c += 4)
-      *reinterpret_cast<float4*>(pO + row * OS + c) =
-          make_float4(ov[c], ov[c + 1], ov[c + 2], ov[c + 3]);
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t w[32];
+      if (have_o) {
+        tc::ld32(tO + c * 32, w);
+        tc::wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = 0u;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(pO + row * OS + c * 32 + i) =
+            make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
+                        __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
+    }
     pM[row] = m_run;
     pL[row] = l_run;
   }
+  tc::fence_before_sync();
   cluster_sync_all();  // every partial of the cluster is in place
+  if (warp == 5) {     // every tensor-memory read of this CTA is done
+    tc::fence_after_sync();
+    tc::tmem_dealloc<512>(tmem);
+  }
   const int SR = BM / nsplit;
   constexpr int C4 = D / 4;
   for (int idx = threadIdx.x; idx < SR * C4; idx += C::NTHREADS) {
@@ -578,7 +636,7 @@ bool fa2_tf32_eligible(const float* q, const float* k, const float* v, const flo
     return s && atoi(s) != 0;
   }();
   const auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
-  return !off && (d == 32 || d == 64) && N > 0 && M > 0 &&
+  return !off && (d == 32 || d == 64 || d == 128) && N > 0 && M > 0 &&
          static_cast<long long>(B) * H <= 65535 && al(q) && al(k) && al(v) && al(o);
 }
 
@@ -631,6 +689,7 @@ cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, floa
                             int N, int M, int d, float scale, int causal, cudaStream_t st) {
   if (!fa2_tf32_eligible(q, k, v, o, B, H, N, M, d)) return cudaErrorInvalidValue;
   if (d == 32) return launch_fa2_tf32_d<32>(q, k, v, o, B, H, N, M, scale, causal, st);
+  if (d == 128) return launch_fa2_tf32_d<128>(q, k, v, o, B, H, N, M, scale, causal, st);
   return launch_fa2_tf32_d<64>(q, k, v, o, B, H, N, M, scale, causal, st);
 }
 

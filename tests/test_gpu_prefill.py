@@ -67,7 +67,8 @@ def test_fp32_config1_cuda_core_kernel():
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M,d", [(1, 1, 64), (65, 130, 32), (200, 77, 128), (128, 128, 100),
                                    (100, 300, 64), (100, 300, 50), (70, 1000, 32), (1, 700, 128),
-                                   (1000, 1000, 64), (129, 700, 64)])
+                                   (1000, 1000, 64), (129, 700, 64), (300, 900, 128),
+                                   (129, 33, 128)])
 def test_fp32_shapes(causal, N, M, d):
     import flash_engine
     rng = np.random.default_rng(N + M + d)
