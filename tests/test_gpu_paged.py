@@ -93,6 +93,29 @@ def test_paged_fp32_long_contexts_split(H, Hkv, d):
     assert_fp32_close(out, ref)
 
 
+def test_paged_fp32_misaligned_cache_generic_decoder():
+    """An fp32 cache that is only 4-byte aligned cannot take the vectorised decoder's
+    128-bit loads: the generic decoder runs, in both the split and single-pass kernels."""
+    import flash_engine
+    for lens in ([900, 40, 1], [300, 17]):
+        p = O.make_paged_problem(31, len(lens), 32, 8, 128, lens, bf16=False)
+        ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        caches = []
+        for name in ("k_cache", "v_cache"):
+            x = p[name]
+            flat = torch.empty(x.size + 4, dtype=torch.float32, device="cuda")
+            t = flat[1:1 + x.size].view(x.shape)
+            t.copy_(torch.from_numpy(np.ascontiguousarray(x)))
+            assert t.data_ptr() % 16 == 4
+            caches.append(t)
+        out = flash_engine.paged_attention(cuda(p["q"]), caches[0], caches[1],
+                                           cuda(p["block_tables"]), cuda(p["context_lens"]), 16)
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        assert_fp32_close(host(out), ref)
+
+
 def test_paged_fp32_split_in_graph_capture():
     """fp32 paged decode inside a CUDA-graph capture: on a fresh stream (no library
     scratch yet) it takes the single-pass kernel, after an eager call on that stream the

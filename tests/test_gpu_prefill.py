@@ -64,6 +64,29 @@ def test_fp32_config1_cuda_core_kernel():
     assert r.returncode == 0, r.stdout + r.stderr
 
 
+def _misaligned(x):
+    """A contiguous CUDA copy of x whose data pointer is 4 bytes past a 16-byte boundary."""
+    flat = torch.empty(x.size + 4, dtype=torch.float32, device="cuda")
+    t = flat[1:1 + x.size].view(x.shape)
+    t.copy_(torch.from_numpy(np.ascontiguousarray(x)))
+    assert t.data_ptr() % 16 == 4
+    return t
+
+
+@pytest.mark.parametrize("d", [32, 64, 128])
+def test_fp32_misaligned_tensors_take_cuda_core_kernel(d):
+    """Tensors that are only 4-byte aligned cannot be read by TMA: the fp32 entry takes
+    the CUDA-core kernel (scalar loads) and must still match the oracle."""
+    import flash_engine
+    rng = np.random.default_rng(d)
+    q, k, v = (rng.standard_normal((1, 2, 150, d), dtype=np.float32) for _ in range(3))
+    for causal in (False, True):
+        out = flash_engine.flash_attention(_misaligned(q), _misaligned(k), _misaligned(v), causal,
+                                           out=_misaligned(np.zeros_like(q)))
+        torch.cuda.synchronize()
+        assert_fp32_close(host(out), O.flash_attention(q, k, v, causal))
+
+
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M,d", [(1, 1, 64), (65, 130, 32), (200, 77, 128), (128, 128, 100),
                                    (100, 300, 64), (100, 300, 50), (70, 1000, 32), (1, 700, 128),
