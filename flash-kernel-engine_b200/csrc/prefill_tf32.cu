@@ -16,10 +16,11 @@
 // t = split, split + nsplit, ... of it. The nsplit CTAs of a row tile form a thread-block
 // cluster and merge their (m, l, O) partials through distributed shared memory (the
 // log-sum-exp combine of src/flash_decoding.cu:151-223).
-//  * warp 4 (TMA): Q once, then K_j and V_j into a two-stage ring (3-D TMA, 128-byte
-//    swizzle; rows past N or M read as zeros).
-//  * warps 6-9 (split): rewrite each landed K / V tile as hi in place and lo beside it;
-//    V is transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
+//  * warp 4 (TMA): Q once, then K_j and V_j (3-D TMA, 128-byte swizzle; rows past N or
+//    M read as zeros): tiles 0 and 1 straight into the two stages, later tiles into a
+//    landing buffer as soon as the split warps have read the previous one.
+//  * warps 6-9 (split): write each landed K / V tile into its stage as hi and lo; V is
+//    transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
 //    The softmax warps split Q the same way before their first S tile.
 //  * warp 5 (MMA): allocates tensor memory [S0 | S1 | PL0 | PL1 | O] and, from one
 //    thread, issues
@@ -61,8 +62,11 @@ struct TCfg {
   static constexpr int K_HI = 0, K_LO = KV_BYTES, V_HI = 2 * KV_BYTES, V_LO = 3 * KV_BYTES;
   static constexpr int STAGE = 4 * KV_BYTES;
   static constexpr int ST_OFF = (QLO_TMEM ? 1 : 2) * Q_BYTES;  // stage s at ST_OFF + s*STAGE
-  static constexpr int BAR_OFF = ST_OFF + 2 * STAGE;
-  static constexpr int NBARS = 15;
+  // Landing buffer of raw K and V for key tiles 2, 3, ...: their copies need only the
+  // previous tile's raw data to have been read, not a free stage.
+  static constexpr int L_OFF = ST_OFF + 2 * STAGE, L_K = 0, L_V = KV_BYTES;
+  static constexpr int BAR_OFF = L_OFF + 2 * KV_BYTES;
+  static constexpr int NBARS = 17;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   // Dynamic shared memory requested at launch: enough that two CTAs never share an SM.
   // Each allocates all 512 tensor-memory columns, and two on one SM in one cluster would
@@ -88,45 +92,60 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
-// hi in place, lo at lo_base, over BYTES of one tile, by NT threads (the layout is kept:
-// the transform is elementwise). All loads are issued before the first store.
+// The hi / lo split of a tile, by NT threads, in two phases: all loads (into registers)
+// before the first store, so the source may be the destination (in place) or a buffer
+// that is released between the phases. hi = x with the low 13 mantissa bits cleared,
+// lo = x - hi; the layout is kept (the transform is elementwise).
 template <int BYTES, int NT>
-__device__ __forceinline__ void split_tile(uint8_t* hi_base, uint8_t* lo_base, int tid) {
-  constexpr int PER = BYTES / 16 / NT;
-  static_assert(PER * 16 * NT == BYTES, "tile split");
+__device__ __forceinline__ void load_tile(const uint8_t* src, float4 (&x)[BYTES / 16 / NT],
+                                          int tid) {
+  static_assert((BYTES / 16 / NT) * 16 * NT == BYTES, "tile split");
+  const float4* h = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int j = 0; j < BYTES / 16 / NT; ++j) x[j] = h[tid + j * NT];
+}
+template <int BYTES, int NT>
+__device__ __forceinline__ void store_split(const float4 (&x)[BYTES / 16 / NT], uint8_t* hi_base,
+                                            uint8_t* lo_base, int tid) {
   float4* h = reinterpret_cast<float4*>(hi_base);
   float4* l = reinterpret_cast<float4*>(lo_base);
-  float4 x[PER];
 #pragma unroll
-  for (int j = 0; j < PER; ++j) x[j] = h[tid + j * NT];
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
+  for (int j = 0; j < BYTES / 16 / NT; ++j) {
     const float4 a =
         make_float4(tf32_hi(x[j].x), tf32_hi(x[j].y), tf32_hi(x[j].z), tf32_hi(x[j].w));
     h[tid + j * NT] = a;
     l[tid + j * NT] = make_float4(x[j].x - a.x, x[j].y - a.y, x[j].z - a.z, x[j].w - a.w);
   }
 }
+// hi in place, lo at lo_base.
+template <int BYTES, int NT>
+__device__ __forceinline__ void split_tile(uint8_t* hi_base, uint8_t* lo_base, int tid) {
+  float4 x[BYTES / 16 / NT];
+  load_tile<BYTES, NT>(hi_base, x, tid);
+  store_split<BYTES, NT>(x, hi_base, lo_base, tid);
+}
 
 // V as loaded ([BN keys] rows of 128-byte swizzle atoms, 32 floats of d per atom column)
-// -> V^T hi in place and V^T lo at vt_lo: [D] rows of keys in the same swizzle, the
-// K-major B operand of O += P V. (A TF32 B operand in MN-major form, V as loaded,
-// produced no result on this hardware.) The 128 split threads read all of V into
-// registers before any of them overwrites it.
+// -> V^T hi and V^T lo: [D] rows of keys in the same swizzle, the K-major B operand of
+// O += P V. (A TF32 B operand in MN-major form, V as loaded, produced no result on this
+// hardware.) Lanes take consecutive keys of one 4-float chunk of d.
 template <int D, int BN>
-__device__ __forceinline__ void split_transpose_v(uint8_t* v, uint8_t* vt_lo, int tid) {
-  constexpr int PER = BN * (D / 4) / 128;  // float4 chunks per thread
-  float4 x[PER];
+constexpr int v_per() { return BN * (D / 4) / 128; }  // float4 chunks per split thread
+template <int D, int BN>
+__device__ __forceinline__ void load_v(const uint8_t* v, float4 (&x)[v_per<D, BN>()], int tid) {
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
+  for (int j = 0; j < v_per<D, BN>(); ++j) {
     const int i = tid + j * 128;
-    const int key = i % BN, dc = i / BN;  // lanes take consecutive keys
+    const int key = i % BN, dc = i / BN;
     x[j] = *reinterpret_cast<const float4*>(v + (dc >> 3) * (BN * 128) + key * 128 +
                                             (((dc & 7) ^ (key & 7)) << 4));
   }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+template <int D, int BN>
+__device__ __forceinline__ void store_vt(const float4 (&x)[v_per<D, BN>()], uint8_t* vt_hi,
+                                         uint8_t* vt_lo, int tid) {
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
+  for (int j = 0; j < v_per<D, BN>(); ++j) {
     const int i = tid + j * 128;
     const int key = i % BN, dc = i / BN;
     const float xs[4] = {x[j].x, x[j].y, x[j].z, x[j].w};
@@ -136,10 +155,19 @@ __device__ __forceinline__ void split_transpose_v(uint8_t* v, uint8_t* vt_lo, in
       const int off = (key >> 5) * (D * 128) + d * 128 + ((((key & 31) >> 2) ^ (d & 7)) << 4) +
                       (key & 3) * 4;
       const float h = tf32_hi(xs[e]);
-      *reinterpret_cast<float*>(v + off) = h;
+      *reinterpret_cast<float*>(vt_hi + off) = h;
       *reinterpret_cast<float*>(vt_lo + off) = xs[e] - h;
     }
   }
+}
+// In place: V^T hi over V, V^T lo at vt_lo. The 128 split threads read all of V into
+// registers before any of them overwrites it (named barrier 1).
+template <int D, int BN>
+__device__ __forceinline__ void split_transpose_v(uint8_t* v, uint8_t* vt_lo, int tid) {
+  float4 x[v_per<D, BN>()];
+  load_v<D, BN>(v, x, tid);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  store_vt<D, BN>(x, v, vt_lo, tid);
 }
 
 // AND of `pred` over the 128 split threads (named barrier 1); every one of them calls it.
@@ -209,6 +237,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = bars + 10;   // [2] P_j in tensor memory
   uint64_t* o_done = bars + 12;   // [2] P_j V_j accumulated
   uint64_t* drain = bars + 14;
+  uint64_t* l_full = bars + 15;   // landing buffer holds the next tile's raw K / V
+  uint64_t* l_empty = bars + 16;  // the split warps have read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,6 +262,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(l_full, 1);
+    mbar_init(l_empty, 128);
     fence_mbar_init();
   }
   if (warp == 5) {
@@ -263,23 +295,35 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_3d(smem + C::Q_HI + h * C::QH, &qmap, h * 32, m0, bh, q_full, pol_once);
       bool ok = true;
       int issued = 0;
+      // Tiles 0 and 1 land in their stages; later tiles in the landing buffer, each once
+      // the split warps have read the one before (l_empty).
       for (int it = 0; it < nloc; ++it) {
-        const int st = it & 1, rnd = it >> 1;
-        if (rnd > 0 && !mbar_wait(&kv_empty[st], (rnd - 1) & 1)) { ok = false; break; }
         const int key0 = (split + it * nsplit) * BN;
-        uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * C::KV_BYTES);
+        uint8_t *kdst, *vdst;
+        uint64_t* bar;
+        if (it < 2) {
+          uint8_t* sb = smem + C::ST_OFF + it * C::STAGE;
+          kdst = sb + C::K_HI;
+          vdst = sb + C::V_HI;
+          bar = &kv_full[it];
+        } else {
+          if (it > 2 && !mbar_wait(l_empty, (it - 3) & 1)) { ok = false; break; }
+          kdst = smem + C::L_OFF + C::L_K;
+          vdst = smem + C::L_OFF + C::L_V;
+          bar = l_full;
+        }
+        mbar_arrive_expect_tx(bar, 2 * C::KV_BYTES);
         for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(sb + C::K_HI + h * C::KH, &kmap, h * 32, key0, bh, &kv_full[st], pol_keep);
+          tma_load_3d(kdst + h * C::KH, &kmap, h * 32, key0, bh, bar, pol_keep);
         for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(sb + C::V_HI + h * C::KH, &vmap, h * 32, key0, bh, &kv_full[st], pol_keep);
+          tma_load_3d(vdst + h * C::KH, &vmap, h * 32, key0, bh, bar, pol_keep);
         ++issued;
       }
       if (!ok) atomicOr(p.err, kErrWaitTimeout);
       // Drain: every bulk copy issued here has landed before the CTA can exit.
       mbar_wait(q_full, 0);
-      for (int it = max(0, issued - 2); it < issued; ++it)
-        mbar_wait(&kv_full[it & 1], (it >> 1) & 1);
+      for (int it = 0; it < min(issued, 2); ++it) mbar_wait(&kv_full[it], 0);
+      if (issued > 2) mbar_wait(l_full, (issued - 3) & 1);
     }
   } else if (warp == 5) {
     // ========================================================= MMA issuer
@@ -357,10 +401,24 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       for (int it = 0; it < nloc && ok; ++it) {
         const int st = it & 1;
-        if (!split_group_all(mbar_wait(&kv_full[st], (it >> 1) & 1))) { ok = false; break; }
         uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
-        split_tile<C::KV_BYTES, 128>(sb + C::K_HI, sb + C::K_LO, sid);
-        split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
+        if (it < 2) {  // raw tile in its stage: split in place
+          if (!split_group_all(mbar_wait(&kv_full[it], 0))) { ok = false; break; }
+          split_tile<C::KV_BYTES, 128>(sb + C::K_HI, sb + C::K_LO, sid);
+          split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
+        } else {
+          // raw tile in the landing buffer; the stage is free once P V of tile it-2 is done
+          const bool got = mbar_wait(l_full, (it - 2) & 1) &&
+                           mbar_wait(&kv_empty[st], ((it >> 1) - 1) & 1);
+          if (!split_group_all(got)) { ok = false; break; }
+          float4 kx[C::KV_BYTES / 16 / 128];
+          float4 vx[v_per<D, BN>()];
+          load_tile<C::KV_BYTES, 128>(smem + C::L_OFF + C::L_K, kx, sid);
+          load_v<D, BN>(smem + C::L_OFF + C::L_V, vx, sid);
+          mbar_arrive(l_empty);  // this thread's reads of the landing buffer are done
+          store_split<C::KV_BYTES, 128>(kx, sb + C::K_HI, sb + C::K_LO, sid);
+          store_vt<D, BN>(vx, sb + C::V_HI, sb + C::V_LO, sid);
+        }
         fence_proxy_async_smem();
         mbar_arrive(&kv_ready[st]);
       }
