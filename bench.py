@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the inference-attention hot path on B200 (one process per GPU).
 
-Headline (``value``): BASELINE config 3, paged decode bf16 -- batch 64, 32 query /
+Headline (``value``): benchmark config 3, paged decode bf16 -- batch 64, 32 query /
 8 KV heads, head_dim 128, block size 16, context lengths U[512, 4096] (seed 0),
 physical blocks a random permutation of the pool. One step = one
 ``flash_engine.paged_attention`` call over the whole batch (one persistent split-KV
@@ -12,7 +12,7 @@ KV GB/s = algorithmic bytes per step (K and V rows of every context token and KV
 q, out, block-table entries, context lengths) / step time, whole job; ``roofline``
 against the measured HBM copy peak.
 
-``secondary`` reports the other BASELINE configs measured in the same run:
+``secondary`` reports the other benchmark configs measured in the same run:
   config 2 -- FA2 prefill bf16 causal [4, 32, 4096, 128], heads sharded (TFLOP/s);
   config 4 -- split-KV decode, 131072-token context, KV range sharded over the
               ranks; the decode kernel stores its (O, m, l) partials into every
@@ -862,7 +862,7 @@ def main():
     res = run_workload(a.workload, a, ws, rank, local, True)
     res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded N(0,1) bf16 inputs; BASELINE config shapes)"})
+                "data": "synthetic (seeded N(0,1) bf16 inputs; benchmark config shapes)"})
     if a.workload in ("prefill_fp32", "paged_fp32"):
         res["dtype"] = "f32"
     if not a.no_secondary:

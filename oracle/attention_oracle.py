@@ -276,7 +276,7 @@ def lse_merge(outs, maxs, sums):
 
 
 # --------------------------------------------------------------------------
-# Seeded input generators for the BASELINE configurations
+# Seeded input generators for the benchmark configurations
 # --------------------------------------------------------------------------
 
 def make_paged_problem(seed: int, num_seqs: int, num_heads: int, num_kv_heads: int,

@@ -201,7 +201,7 @@ def test_bad_block_index_is_flagged_not_read():
 
 
 def test_config3_shape_parity():
-    """BASELINE config 3 shape (B64, 32q/8kv, d128, ctx U[512,4096], bs 16), on a
+    """Benchmark config 3 shape (B64, 32q/8kv, d128, ctx U[512,4096], bs 16), on a
     seeded subset of 8 sequences for oracle speed, with the full split logic."""
     lens = O.config3_context_lens(0)[:8]
     p = O.make_paged_problem(0, 8, 32, 8, 128, lens)

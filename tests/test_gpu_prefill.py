@@ -24,7 +24,7 @@ def test_fp32_golden(golden, name, kind):
 
 
 def test_fp32_config1():
-    """fp32, non-causal, [1, 8, 512, 64], N(0,1) inputs, seed 42."""
+    """Benchmark config 1: fp32, non-causal, [1, 8, 512, 64], N(0,1) inputs, seed 42."""
     import flash_engine
     rng = np.random.default_rng(42)
     q, k, v = (rng.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))
@@ -133,7 +133,7 @@ def test_fp16_tcgen05():
 
 
 def test_bf16_config2_shape_slice():
-    """BASELINE config 2 shape (causal, seq 4096, d 128) on 2 heads: the oracle runs
+    """Benchmark config 2 shape (causal, seq 4096, d 128) on 2 heads: the oracle runs
     per (b, h) slice."""
     out, ref = _bf16_case(1, 2, 4096, 4096, 128, True, 42)
     assert_bf16_close(out, ref)
