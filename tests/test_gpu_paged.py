@@ -212,7 +212,7 @@ def test_config3_shape_parity():
 
 
 def test_config3_full_batch():
-    """All 64 sequences of BASELINE config 3 (seed 0) against the oracle, through the
+    """All 64 sequences of benchmark config 3 (seed 0) against the oracle, through the
     single-pass kernel and the split-KV kernel (whose flat chunking cuts sequences
     at arbitrary pages)."""
     import flash_engine
