@@ -1,18 +1,19 @@
 #!/usr/bin/env python
 """Benchmark of the inference-attention hot path on B200 (one process per GPU).
 
-Headline (``value``): benchmark config 3, paged decode bf16 -- batch 64, 32 query /
-8 KV heads, head_dim 128, block size 16, context lengths U[512, 4096] (seed 0),
-physical blocks a random permutation of the pool. One step = one
+Headline (the LAST line printed): benchmark config 3, paged decode bf16 -- batch 64,
+32 query / 8 KV heads, head_dim 128, block size 16, context lengths U[512, 4096]
+(seed 0), physical blocks a random permutation of the pool. One step = one
 ``flash_engine.paged_attention`` call over the whole batch (one persistent split-KV
 kernel with the log-sum-exp merge fused in), replayed from CUDA graphs of 10 steps.
 With N GPUs (torchrun) the KV heads are sharded: rank r owns KV heads
-[r*8/N, (r+1)*8/N) and their query heads; no communication (strong scaling). Metric:
-KV GB/s = algorithmic bytes per step (K and V rows of every context token and KV head,
-q, out, block-table entries, context lengths) / step time, whole job; ``roofline``
-against the measured HBM copy peak.
+[r*8/N, (r+1)*8/N) and their query heads; no communication. Metric: KV GB/s =
+algorithmic bytes per step (K and V rows of every context token and KV head, q, out,
+block-table entries, context lengths) / step time, whole job; ``roofline`` against the
+measured HBM copy peak (and the nominal 8 TB/s).
 
-``secondary`` reports the other benchmark configs measured in the same run:
+Before the headline, one JSON line per other benchmark config measured in the same run
+(``"secondary": true``):
   config 2 -- FA2 prefill bf16 causal [4, 32, 4096, 128], heads sharded (TFLOP/s);
   config 4 -- split-KV decode, 131072-token context, KV range sharded over the
               ranks; the decode kernel stores its (O, m, l) partials into every
@@ -24,9 +25,13 @@ against the measured HBM copy peak.
               kernel), heads sharded (TFLOP/s);
   paged_fp32 -- the reference's fp32 paged entry on config 3's shapes with an fp32
               cache (KV GB/s).
-``--workload`` makes any of them the headline instead. ``--impl reference`` times the
-reference's CPU implementation of the path (the NumPy port in oracle/, all host
-threads) on a bounded sample per step.
+Every line carries ``parity``: after the timed steps each rank checks a seeded sample of
+its output rows against the CPU oracle (the NumPy restatement of the reference's
+attention) and the worst error over the ranks is reported with the tolerance (bf16:
+2e-2 absolute; fp32: 1e-3 relative). At N = 1, rank 0 also times the oracle on the host
+cores for every config (``cpu_baseline``). ``--workload`` makes any config the headline.
+``--impl reference`` times the reference's CPU implementation of the path (the NumPy
+port in oracle/, all host threads) on a bounded sample per step.
 """
 
 from __future__ import annotations
@@ -52,6 +57,10 @@ import numpy as np  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
 WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32", "paged_fp32")
+NOMINAL_HBM_GBS = 8000.0       # B200 HBM3e (DGX figure)
+NOMINAL_BF16_TFLOPS = 2250.0   # B200 dense bf16 tensor
+BF16_ATOL = 2e-2
+FP32_RTOL = 1e-3
 
 
 def _args():
@@ -63,6 +72,7 @@ def _args():
     ap.add_argument("--workload", choices=WORKLOADS, default="decode")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="paged_fp32 only: use the first N sequences of config 3 (a small "
@@ -84,12 +94,16 @@ def _peaks():
 
 
 def _traffic(name):
-    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary
+    (profiles/<name>), with its source; (None, None) if there is none."""
     try:
         with open(os.path.join(ROOT, "profiles", name)) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+            d = json.load(f)
+        return d.get("dram_bytes_per_launch"), (
+            f"profiles/{name}: dram__bytes_read.sum + dram__bytes_write.sum of one ncu "
+            f"capture of this kernel on this config (committed; not measured in this run)")
     except Exception:
-        return None
+        return None, None
 
 
 def _cpu_threads():
@@ -103,9 +117,22 @@ def _cpu_threads():
     return os.cpu_count() or 1
 
 
+def _hbm_roofline(rank_bytes, ms_rank, kernel, traffic_file=None):
+    peak, _, _, src = _peaks()
+    ach = rank_bytes / (ms_rank * 1e-3) / 1e9
+    traffic, tsrc = _traffic(traffic_file) if traffic_file else (None, None)
+    r = {"bound": "hbm", "achieved": round(ach, 2), "peak": peak, "unit": "GB/s",
+         "frac": round(ach / peak, 4), "peak_source": src,
+         "frac_nominal": round(ach / NOMINAL_HBM_GBS, 4),
+         "peak_nominal": NOMINAL_HBM_GBS, "kernel": kernel, "traffic": traffic}
+    if tsrc:
+        r["traffic_source"] = tsrc
+    return r
+
+
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML (read-only) every 5 ms."""
+    """Samples SM clock and throttle reasons through NVML (read-only) every 0.5 ms."""
 
     REASONS = {
         0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -136,7 +163,7 @@ class ClockSampler:
                 self.samples.append((time.perf_counter(), mhz, rs))
             except Exception:
                 pass
-            time.sleep(0.005)
+            time.sleep(0.0005)
 
     def start(self):
         if self.ok:
@@ -209,6 +236,56 @@ def _time_steps(step, steps, warmup, ws, dev):
     return e0.elapsed_time(e1) / steps, t0, t1
 
 
+# --------------------------------------------------------------------------- parity
+def _parity(err, tol, kind, sample, ws, dev):
+    """Worst error over the ranks against the tolerance (kind "abs" or "rel")."""
+    e = _max_over_ranks(float(err), ws, dev)
+    return {"max_err": float(f"{e:.4g}"), "tol": tol, "kind": kind, "ok": bool(e <= tol),
+            "ranks": ws, "sample": sample}
+
+
+def _err(got, ref, rel):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    if not np.isfinite(got).all():
+        return float("inf")
+    e = float(np.abs(got - ref).max()) if ref.size else 0.0
+    if rel:
+        e /= float(np.abs(ref).max()) or 1.0
+    return e
+
+
+def _sample_seqs(lens, seed, n=6):
+    """Seeded sample of sequence indices, with the longest and the shortest."""
+    rng = np.random.default_rng(seed + 12345)
+    S = len(lens)
+    pick = set(int(x) for x in rng.choice(S, size=min(n, S), replace=False))
+    pick.add(int(np.argmax(lens)))
+    pick.add(int(np.argmin(lens)))
+    return sorted(pick)
+
+
+def _paged_oracle_rows(q, kc, vc, bt, lens, sel, bs):
+    """Oracle rows (the reference's paged_attention per KV-head group) of sequences `sel`:
+    their pages are copied to the host as a compact cache and the block table is
+    remapped onto it (same gather rule: token t -> block bt[s, t // bs], row t % bs)."""
+    import torch
+    from oracle import attention_oracle as O
+    bt_np = bt[sel].cpu().numpy()
+    ls = np.asarray(lens)[sel].astype(np.int32)
+    nb = (np.maximum(ls, 0) + bs - 1) // bs
+    used = np.concatenate([bt_np[i, :nb[i]] for i in range(len(sel))] + [np.zeros(1, np.int32)])
+    blocks = np.unique(used)
+    idx = torch.from_numpy(blocks.astype(np.int64)).to(kc.device)
+    kc_h = kc.index_select(0, idx).float().cpu().numpy()
+    vc_h = vc.index_select(0, idx).float().cpu().numpy()
+    bt_sub = np.zeros_like(bt_np)
+    for i in range(len(sel)):
+        bt_sub[i, :nb[i]] = np.searchsorted(blocks, bt_np[i, :nb[i]])
+    q_h = q[sel].float().cpu().numpy()
+    return O.paged_attention_gqa(q_h, kc_h, vc_h, bt_sub, ls, bs)
+
+
 # --------------------------------------------------------------------------- paged decode
 CFG3 = dict(name="paged_decode_config3", num_seqs=64, num_heads=32, num_kv_heads=8,
             head_dim=128, block_size=16,
@@ -236,7 +313,115 @@ def decode_bytes(lens, Hkv, H, d, bs, elt=2):
     return tokens * Hkv * d * 2 * elt + 2 * S * H * d * elt + pages * 4 + S * 4
 
 
-def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
+def _block_sets(lens, bs, R, seed):
+    """R disjoint block tables over a pool of R * sum(ceil(ctx / bs)) blocks."""
+    nblk = (lens + bs - 1) // bs
+    pool = int(nblk.sum())
+    rng = np.random.default_rng(seed + 1)
+    perm = rng.permutation(pool * R).astype(np.int32)
+    maxb = int(nblk.max())
+    bts = []
+    for r in range(R):
+        bt = np.zeros((len(lens), maxb), np.int32)
+        off = r * pool
+        for s in range(len(lens)):
+            bt[s, :nblk[s]] = perm[off:off + nblk[s]]
+            off += nblk[s]
+        bts.append(bt)
+    return pool, bts
+
+
+def _e2e_decode(q, kc, vc, bts, lens_t, bs, max_ctx, wsp, R, steps, ws, dev, elt):
+    """End to end through the public API with host buffers: every step moves that step's
+    q, block table and context lengths in from pinned host memory as ONE packed copy,
+    runs the decode and copies the output back to pinned host memory; two steps are in
+    flight (the host reuses a step's buffers only after that step's output is on the
+    host). Two forms, both on one stream:
+      graph -- the step (copy in, flash_engine.paged_attention, copy out) captured once
+               per (buffer, block set) into a CUDA graph and replayed, as a serving loop
+               replays its captured decode step;
+      eager -- the same three operations issued from Python every step.
+    Returns (graph_ms, eager_ms, h2d_bytes, d2h_bytes) per step on this rank."""
+    import torch
+    import flash_engine
+
+    S = q.shape[0]
+    nq = q.numel() * q.element_size()
+    nbt = bts[0].numel() * 4
+    nl = S * 4
+
+    def al(x):
+        return (x + 255) // 256 * 256
+    o_bt, o_l = al(nq), al(nq) + al(nbt)
+    total = o_l + al(nl)
+    stage_h = []
+    for r in range(R):
+        h = torch.zeros(total, dtype=torch.uint8).pin_memory()
+        h[:nq].copy_(q.detach().cpu().contiguous().view(-1).view(torch.uint8))
+        h[o_bt:o_bt + nbt].copy_(bts[r].cpu().contiguous().view(-1).view(torch.uint8))
+        h[o_l:o_l + nl].copy_(lens_t.cpu().contiguous().view(torch.uint8))
+        stage_h.append(h)
+    stage_d = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
+    views = [(sd[:nq].view(q.dtype).view(q.shape), sd[o_bt:o_bt + nbt].view(torch.int32)
+              .view(bts[0].shape), sd[o_l:o_l + nl].view(torch.int32)) for sd in stage_d]
+    outs_d = [torch.empty_like(q) for _ in range(2)]
+    outs_h = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+    evs = [torch.cuda.Event() for _ in range(2)]
+
+    def body(b, r):
+        stage_d[b].copy_(stage_h[r], non_blocking=True)
+        qv, btv, lv = views[b]
+        flash_engine.paged_attention(qv, kc, vc, btv, lv, bs, max_context_len=max_ctx,
+                                     out=outs_d[b], workspace=wsp)
+        outs_h[b].copy_(outs_d[b], non_blocking=True)
+
+    # graphs: one per (buffer, block set)
+    for b in range(2):
+        body(b, 0)
+    torch.cuda.synchronize()
+    graphs = {}
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        for b in range(2):
+            for r in range(R):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    body(b, r)
+                graphs[(b, r)] = g
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+
+    def run(n, graph):
+        for i in range(n):
+            b = i % 2
+            if i >= 2:
+                evs[b].synchronize()
+            if graph:
+                graphs[(b, i % R)].replay()
+            else:
+                body(b, i % R)
+            evs[b].record()
+        torch.cuda.synchronize()
+
+    n = max(4, min(steps, 200))
+    res = []
+    for graph in (True, False):
+        run(4, graph)
+        _barrier(ws, dev)
+        t0 = time.perf_counter()
+        run(n, graph)
+        res.append(_max_over_ranks((time.perf_counter() - t0) * 1e3 / n, ws, dev))
+    # the outputs that came back must be the decode's
+    for b in range(2):
+        assert torch.equal(outs_h[b].to(dev), outs_d[b])
+    del graphs
+    return res[0], res[1], nq + nbt + nl, nq
+
+
+def bench_paged(a, ws, rank, local, cfg, steps, warmup, fp32=False):
+    """Config 3 / config 5 paged decode (bf16), or the reference's fp32 paged entry on
+    config 3's shapes with an fp32 cache (``fp32``)."""
     import torch
     import flash_engine
 
@@ -247,44 +432,40 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
         raise ValueError(f"{ws} ranks cannot split {Hkv} KV heads")
     hkv_l, h_l = Hkv // ws, H // ws
     lens = _lens(cfg, a.seed)
+    if fp32 and a.num_seqs > 0:
+        lens = lens[:a.num_seqs]
+    S = len(lens)
+    elt = 4 if fp32 else 2
+    dt = torch.float32 if fp32 else torch.bfloat16
     nblk = (lens + bs - 1) // bs
-    pool = int(nblk.sum())
-    # Disjoint block sets rotated between steps: >= 4 x L2 of distinct KV over a cycle.
-    kv_set = pool * hkv_l * bs * d * 2 * 2
-    R = max(1, math.ceil(4 * L2_BYTES / kv_set))
-    rng = np.random.default_rng(a.seed + 1)
-    perm = rng.permutation(pool * R).astype(np.int32)
-    maxb = int(nblk.max())
-    bts = []
-    for r in range(R):
-        bt = np.zeros((S, maxb), np.int32)
-        off = r * pool
-        for s in range(S):
-            bt[s, :nblk[s]] = perm[off:off + nblk[s]]
-            off += nblk[s]
-        bts.append(torch.from_numpy(bt).to(dev))
+    pool1 = int(nblk.sum())
+    # Disjoint block sets used in turn: >= 4 x L2 (2 x L2 for fp32) of distinct KV over a
+    # cycle, so no step finds its KV in L2.
+    kv_set = pool1 * hkv_l * bs * d * elt * 2
+    R = max(1, math.ceil((2 if fp32 else 4) * L2_BYTES / kv_set))
+    pool, bts_np = _block_sets(lens, bs, R, a.seed)
+    bts = [torch.from_numpy(b).to(dev) for b in bts_np]
     g = torch.Generator(device=dev)
-    g.manual_seed(1000 + a.seed * 17 + rank)
-    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(torch.bfloat16)
-    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(torch.bfloat16)
-    q = torch.randn((S, h_l, d), generator=g, device=dev).to(torch.bfloat16)
+    g.manual_seed((3000 if fp32 else 1000) + a.seed * 17 + rank)
+    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(dt)
+    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev).to(dt)
+    q = torch.randn((S, h_l, d), generator=g, device=dev).to(dt)
     lens_t = torch.from_numpy(lens).to(dev)
     out = torch.empty_like(q)
     max_ctx = int(lens.max())
     wsp = torch.zeros(flash_engine.paged_attention_workspace_floats(h_l, hkv_l, d, bs),
                       dtype=torch.float32, device=dev)
 
-    def call(i):
+    def call(i, o=out):
         flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, max_context_len=max_ctx,
-                                     out=out, workspace=wsp)
+                                     out=o, workspace=wsp)
 
     # A decode step is one call of the public API. The calls are captured GSTEPS at a
     # time into CUDA graphs (one per starting block set) and replayed back to back, as a
     # serving loop replays its captured decode steps. The decode kernel is launched with
     # programmatic dependent launch, so inside a graph each call's CTAs are placed as
     # the previous call's CTAs retire (they wait for its results before reading
-    # anything). One graph per call measured 26.8 us a step on the N = 8 shard, 24.4 us
-    # with 10 calls per graph.
+    # anything).
     GSTEPS = 10 if steps % 10 == 0 and warmup >= 3 else 1
     for i in range(3):
         call(i)
@@ -310,237 +491,59 @@ def bench_paged(a, ws, rank, local, cfg, with_cpu, steps, warmup):
     ms_rank /= GSTEPS
     sampler.stop()
     assert flash_engine.device_errors() == 0
-    ms = _max_over_ranks(ms_rank, ws, dev)
-    total = decode_bytes(lens, Hkv, H, d, bs)
-    rank_bytes = decode_bytes(lens, hkv_l, h_l, d, bs)
-
-    # End to end through the public API: the step's q, block table and context lengths
-    # from pinned host memory, the output back to pinned host memory, wall clock.
-    q_h = q.cpu().pin_memory()
-    bt_h = [b.cpu().pin_memory() for b in bts]
-    lens_h = lens_t.cpu().pin_memory()
-    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d, lens_d, bt_d = torch.empty_like(q), torch.empty_like(lens_t), torch.empty_like(bts[0])
-
-    def e2e_step(i):
-        q_d.copy_(q_h, non_blocking=True)
-        bt_d.copy_(bt_h[i % R], non_blocking=True)
-        lens_d.copy_(lens_h, non_blocking=True)
-        o = flash_engine.paged_attention(q_d, kc, vc, bt_d, lens_d, bs, max_context_len=max_ctx,
-                                         workspace=wsp)
-        out_h.copy_(o, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-
-    for i in range(3):
-        e2e_step(i)
-    _barrier(ws, dev)
-    n_e2e = max(1, min(steps, 200))
-    te0 = time.perf_counter()
-    for i in range(n_e2e):
-        e2e_step(i)
-    te1 = time.perf_counter()
-    e2e_serial_ms = _max_over_ranks((te1 - te0) * 1e3 / n_e2e, ws, dev)
-
-    # The same steps two deep, as a serving loop runs them: step i+1's inputs are copied
-    # in (one copy stream) while step i decodes, and step i's output is copied out (a
-    # second copy stream) while step i+1 decodes; the host reads step i's output before
-    # it reuses that step's buffers two steps later. Every step still moves its own
-    # inputs in and its own output out.
-    comp = torch.cuda.current_stream()
-    in_s, out_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    qb = [torch.empty_like(q) for _ in range(2)]
-    btb = [torch.empty_like(bts[0]) for _ in range(2)]
-    lb = [torch.empty_like(lens_t) for _ in range(2)]
-    ob = [torch.empty_like(out) for _ in range(2)]
-    ohb = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_used = [torch.cuda.Event() for _ in range(2)]
-    ev_done = [torch.cuda.Event() for _ in range(2)]
-
-    def e2e_pipelined(n):
-        for i in range(n):
-            b = i % 2
-            if i >= 2:
-                ev_done[b].synchronize()  # step i-2's output is on the host
-            with torch.cuda.stream(in_s):
-                if i >= 2:
-                    in_s.wait_event(ev_used[b])
-                qb[b].copy_(q_h, non_blocking=True)
-                btb[b].copy_(bt_h[i % R], non_blocking=True)
-                lb[b].copy_(lens_h, non_blocking=True)
-                ev_in[b].record(in_s)
-            comp.wait_event(ev_in[b])
-            flash_engine.paged_attention(qb[b], kc, vc, btb[b], lb[b], bs, max_context_len=max_ctx,
-                                         out=ob[b], workspace=wsp)
-            ev_used[b].record(comp)
-            with torch.cuda.stream(out_s):
-                out_s.wait_event(ev_used[b])
-                ohb[b].copy_(ob[b], non_blocking=True)
-                ev_done[b].record(out_s)
-        torch.cuda.synchronize()
-
-    e2e_pipelined(4)
-    _barrier(ws, dev)
-    te0 = time.perf_counter()
-    e2e_pipelined(n_e2e)
-    te1 = time.perf_counter()
-    e2e_ms = _max_over_ranks((te1 - te0) * 1e3 / n_e2e, ws, dev)
     del graphs
+    ms = _max_over_ranks(ms_rank, ws, dev)
+    total = decode_bytes(lens, Hkv, H, d, bs, elt)
+    rank_bytes = decode_bytes(lens, hkv_l, h_l, d, bs, elt)
 
-    peak_hbm, _, _, src = _peaks()
+    gms, ems, h2d, d2h = _e2e_decode(q, kc, vc, bts, lens_t, bs, max_ctx, wsp, R, steps, ws,
+                                     dev, elt)
+    parity = None
+    if not a.no_parity:
+        call(0)
+        torch.cuda.synchronize()
+        sel = _sample_seqs(lens, a.seed)
+        ref = _paged_oracle_rows(q, kc, vc, bts[0], lens, sel, bs)
+        err = _err(out[sel].float().cpu().numpy(), ref, rel=fp32)
+        parity = _parity(err, FP32_RTOL if fp32 else BF16_ATOL, "rel" if fp32 else "abs",
+                         f"{len(sel)} sequences (seeded, incl. longest and shortest), all "
+                         f"{h_l} query heads of each rank, vs the CPU oracle", ws, dev)
+    if fp32:
+        metric = "paged decode fp32 KV GB/s (the reference's v1 fp32 entry on config 3 shapes)"
+        name = "paged_decode_fp32_config3"
+        kernel = "paged_decode_kernel<float> (fp32 CUDA-core consumer, merge fused)"
+        tfile = "paged_decode_fp32_config3_traffic.json" if ws == 1 else None
+    else:
+        metric, name = cfg["metric"], cfg["name"]
+        kernel = "paged_decode_kernel (merge fused)"
+        tfile = ({"paged_decode_config3": "paged_decode_config3_traffic.json",
+                  "paged_decode_config5_serving": "paged_decode_config5_traffic.json"}[name]
+                 if ws == 1 else None)
     res = {
-        "metric": cfg["metric"], "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "metric": metric, "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
         "ms_per_step": round(ms, 5),
-        "config": {"workload": cfg["name"], "num_seqs": S, "num_heads": H, "num_kv_heads": Hkv,
+        "config": {"workload": name, "num_seqs": S, "num_heads": H, "num_kv_heads": Hkv,
                    "head_dim": d, "block_size": bs, "total_context_tokens": int(lens.sum()),
                    "bytes_per_step": total, "workspace_floats": int(wsp.numel()),
                    "parallelism": f"kv-head shard x{ws}",
                    "l2": f"{R} disjoint block sets rotated per step "
                          f"({R * kv_set / 2**20:.0f} MiB per rank)"},
-        "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (ms_rank * 1e-3) / 1e9, 2),
-                     "peak": peak_hbm, "unit": "GB/s",
-                     "frac": round(rank_bytes / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
-                     "peak_source": src, "kernel": "paged_decode_kernel (merge fused)",
-                     "traffic": _traffic("paged_decode_config3_traffic.json")
-                     if cfg is CFG3 and ws == 1 else None},
-        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 2),
-                "mode": "two steps in flight (copies overlap the neighbouring steps' decode)",
-                "serial_value": round(total / (e2e_serial_ms * 1e-3) / 1e9, 2),
-                "serial_ms_per_step": round(e2e_serial_ms, 4)},
+        "roofline": _hbm_roofline(rank_bytes, ms_rank, kernel, tfile),
+        "e2e": {"value": round(total / (gms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(gms, 4), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "mode": "per step: one packed H2D copy of q, block table and lengths from "
+                        "pinned memory, the public paged_attention call, one D2H copy of "
+                        "the output; captured per step into a CUDA graph and replayed, two "
+                        "steps in flight",
+                "eager_value": round(total / (ems * 1e-3) / 1e9, 2),
+                "eager_ms_per_step": round(ems, 4)},
         "gpu_launches": steps,
         "clocks": sampler.summary(t0, t1),
     }
-    if with_cpu and rank == 0 and ws == 1:
-        res["cpu_baseline"] = cpu_paged_baseline(cfg, lens, a.seed, budget_s=12.0)
+    if parity:
+        res["parity"] = parity
     return res
-
-
-def bench_paged_fp32(a, ws, rank, local, steps, warmup):
-    """The reference's fp32 paged entry (launch_paged_attention_v1_fp32) on config 3's
-    shapes with an fp32 cache: one step = one flash_engine.paged_attention call (512-token
-    split kernel + merge). KV heads sharded over the ranks as in config 3."""
-    import torch
-    import flash_engine
-
-    dev = torch.device("cuda", local)
-    c = CFG3
-    H, Hkv, d, bs = c["num_heads"], c["num_kv_heads"], c["head_dim"], c["block_size"]
-    if Hkv % ws:
-        raise ValueError(f"{ws} ranks cannot split {Hkv} KV heads")
-    hkv_l, h_l = Hkv // ws, H // ws
-    lens = _lens(c, a.seed)
-    if a.num_seqs > 0:
-        lens = lens[:a.num_seqs]
-    S = len(lens)
-    nblk = (lens + bs - 1) // bs
-    pool = int(nblk.sum())
-    kv_set = pool * hkv_l * bs * d * 4 * 2
-    R = max(1, math.ceil(2 * L2_BYTES / kv_set))
-    rng = np.random.default_rng(a.seed + 1)
-    perm = rng.permutation(pool * R).astype(np.int32)
-    maxb = int(nblk.max())
-    bts = []
-    for r in range(R):
-        bt = np.zeros((S, maxb), np.int32)
-        off = r * pool
-        for s_ in range(S):
-            bt[s_, :nblk[s_]] = perm[off:off + nblk[s_]]
-            off += nblk[s_]
-        bts.append(torch.from_numpy(bt).to(dev))
-    g = torch.Generator(device=dev)
-    g.manual_seed(3000 + a.seed * 17 + rank)
-    kc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev)
-    vc = torch.randn((pool * R, hkv_l, bs, d), generator=g, device=dev)
-    q = torch.randn((S, h_l, d), generator=g, device=dev)
-    lens_t = torch.from_numpy(lens).to(dev)
-    out = torch.empty_like(q)
-
-    def step(i):
-        flash_engine.paged_attention(q, kc, vc, bts[i % R], lens_t, bs, out=out)
-
-    sampler = ClockSampler(local).start()
-    ms_rank, t0, t1 = _time_steps(step, steps, max(3, warmup), ws, dev)
-    sampler.stop()
-    assert flash_engine.device_errors() == 0
-    ms = _max_over_ranks(ms_rank, ws, dev)
-    total = decode_bytes(lens, Hkv, H, d, bs, elt=4)
-    rank_bytes = decode_bytes(lens, hkv_l, h_l, d, bs, elt=4)
-
-    # End to end through the public API: q, block table and lengths in from pinned host
-    # memory, the output back, one step at a time on the wall clock.
-    q_h, lens_h = q.cpu().pin_memory(), lens_t.cpu().pin_memory()
-    bt_h = [b.cpu().pin_memory() for b in bts]
-    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d, lens_d, bt_d = torch.empty_like(q), torch.empty_like(lens_t), torch.empty_like(bts[0])
-
-    def e2e_step(i):
-        q_d.copy_(q_h, non_blocking=True)
-        bt_d.copy_(bt_h[i % R], non_blocking=True)
-        lens_d.copy_(lens_h, non_blocking=True)
-        out_h.copy_(flash_engine.paged_attention(q_d, kc, vc, bt_d, lens_d, bs), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-
-    for i in range(3):
-        e2e_step(i)
-    _barrier(ws, dev)
-    n_e2e = max(1, min(steps, 50))
-    te0 = time.perf_counter()
-    for i in range(n_e2e):
-        e2e_step(i)
-    e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n_e2e, ws, dev)
-    peak_hbm, _, _, src = _peaks()
-    return {
-        "metric": "paged decode fp32 KV GB/s (the reference's v1 fp32 entry on config 3 shapes)",
-        "value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-        "ms_per_step": round(ms, 5),
-        "config": {"workload": "paged_decode_fp32_config3", "num_seqs": S, "num_heads": H,
-                   "num_kv_heads": Hkv, "head_dim": d, "block_size": bs,
-                   "total_context_tokens": int(lens.sum()), "bytes_per_step": total,
-                   "parallelism": f"kv-head shard x{ws}",
-                   "l2": f"{R} block set(s) of {kv_set / 2**20:.0f} MiB per rank used in turn"},
-        "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (ms_rank * 1e-3) / 1e9, 2),
-                     "peak": peak_hbm, "unit": "GB/s",
-                     "frac": round(rank_bytes / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
-                     "peak_source": src,
-                     "kernel": "paged_split_fp32_kernel (512-token splits) + merge_kernel",
-                     "traffic": None},
-        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": int(q_h.numel() * 4 + bt_h[0].numel() * 4 + lens_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 4)},
-        "gpu_launches": 2 * steps,
-        "clocks": sampler.summary(t0, t1),
-    }
-
-
-def cpu_paged_baseline(cfg, lens, seed, budget_s=12.0, steps=1):
-    """The NumPy port of the reference's paged_attention (per KV-head group), timed on
-    the host over a bounded prefix of the workload's sequences."""
-    from oracle import attention_oracle as O
-    H, Hkv, d, bs = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"], cfg["block_size"]
-    p1 = O.make_paged_problem(seed, 1, H, Hkv, d, lens[:1])
-    t = time.perf_counter()
-    O.paged_attention_gqa(p1["q"], p1["k_cache"], p1["v_cache"], p1["block_tables"],
-                          p1["context_lens"])
-    per_tok = (time.perf_counter() - t) / max(1, int(lens[0]))
-    n = 1
-    while n < len(lens) and per_tok * int(lens[:n + 1].sum()) * steps < budget_s:
-        n += 1
-    sub = lens[:n]
-    p = O.make_paged_problem(seed, n, H, Hkv, d, sub)
-    t = time.perf_counter()
-    for _ in range(steps):
-        O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
-                              p["context_lens"])
-    dt = (time.perf_counter() - t) / steps
-    b = decode_bytes(sub, Hkv, H, d, bs)
-    return {"value": round(b / dt / 1e9, 4), "unit": "GB/s", "cores": _cpu_threads(),
-            "kind": "port",
-            "sample": f"first {n} of {len(lens)} sequences of {cfg['name']} "
-                      f"({int(sub.sum())} tokens), {dt:.2f} s per pass; bytes counted as bf16"}
 
 
 # --------------------------------------------------------------------------- split-KV (config 4)
@@ -610,15 +613,21 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
     ms = _max_over_ranks(ms_rank, ws, dev)
     kv_total = B * M * Hkv * d * 2 * 2
     kv_rank = B * (te - tb) * Hkv * d * 2 * 2
-    # end to end: q, block table and lengths from pinned host, output back to host
-    q_h, bt_h, l_h = q_all.cpu().pin_memory(), bt_t.cpu().pin_memory(), lens_t.cpu().pin_memory()
+    # end to end: q, block table and lengths from pinned host as one packed copy, the
+    # output back to host
+    nq, nbt, nl = q_all.numel() * 2, bt_t.numel() * 4, B * 4
+    stage_h = torch.zeros(nq + nbt + nl, dtype=torch.uint8).pin_memory()
+    stage_h[:nq].copy_(q_all.cpu().view(-1).view(torch.uint8))
+    stage_h[nq:nq + nbt].copy_(bt_t.cpu().view(-1).view(torch.uint8))
+    stage_h[nq + nbt:].copy_(lens_t.cpu().view(torch.uint8))
+    stage_d = torch.empty_like(stage_h, device=dev)
+    q_d = stage_d[:nq].view(torch.bfloat16).view(q_all.shape)
+    bt_d = stage_d[nq:nq + nbt].view(torch.int32).view(bt_t.shape)
+    l_d = stage_d[nq + nbt:].view(torch.int32)
     out_h = torch.empty(q_all.shape, dtype=q_all.dtype).pin_memory()
-    q_d, bt_d, l_d = torch.empty_like(q_all), torch.empty_like(bt_t), torch.empty_like(lens_t)
 
     def e2e(i):
-        q_d.copy_(q_h, non_blocking=True)
-        bt_d.copy_(bt_h, non_blocking=True)
-        l_d.copy_(l_h, non_blocking=True)
+        stage_d.copy_(stage_h, non_blocking=True)
         out_h.copy_(call(i, q_d, bt_d, l_d), non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -630,11 +639,17 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
     for i in range(n):
         e2e(i)
     e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n, ws, dev)
+
+    parity = None
+    if not a.no_parity:
+        out = call(0)
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        parity = _splitkv_parity(q_all, kc, vc, bt, tb, te, M, bs, got, ws, dev)
     del graph
     if ex is not None:
         ex.close()
-    peak_hbm, _, _, src = _peaks()
-    return {
+    res = {
         "metric": c["metric"], "value": round(kv_total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
         "ms_per_step": round(ms, 5),
         "config": {"workload": c["name"], "batch": B, "num_heads": H, "num_kv_heads": Hkv,
@@ -644,18 +659,66 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
                                      " by the decode kernel's peer stores" if ex is not None
                                      else " by NCCL"),
                    "l2": f"{kv_rank / 2**20:.0f} MiB of KV per rank"},
-        "roofline": {"bound": "hbm", "achieved": round(kv_rank / (ms_rank * 1e-3) / 1e9, 2),
-                     "peak": peak_hbm, "unit": "GB/s",
-                     "frac": round(kv_rank / (ms_rank * 1e-3) / 1e9 / peak_hbm, 4),
-                     "peak_source": src},
+        "roofline": _hbm_roofline(kv_rank, ms_rank, "paged_decode_kernel (partials / exchange "
+                                  "mode) + merge" if ws > 1 else "paged_decode_kernel (merge "
+                                  "fused)", "splitkv_decode_config4_traffic.json"
+                                  if ws == 1 else None),
         "e2e": {"value": round(kv_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": int(q_h.numel() * 2 + bt_h.numel() * 4 + l_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 2)},
+                "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": int(nq + nbt + nl),
+                "d2h_bytes_per_step": int(out_h.numel() * 2),
+                "mode": "one packed H2D copy, the step, one D2H copy, one step at a time"},
+        "gpu_launches": steps * (1 if ws == 1 else 2),
         "clocks": sampler.summary(t0, t1),
     }
+    if parity:
+        res["parity"] = parity
+    return res
 
 
-# --------------------------------------------------------------------------- prefill (config 2)
+def _splitkv_parity(q_all, kc, vc, bt, tb, te, M, bs, got, ws, dev):
+    """Each rank computes the oracle's split-KV stage 1 (ops.py:117-131) over its own
+    token window for two sequences and the query heads of two KV heads (the first and
+    the last), the partials of all ranks are gathered and merged with the oracle's
+    log-sum-exp combine (ops.py:133-143), and every rank compares the result with its
+    output rows."""
+    import torch
+    from oracle import attention_oracle as O
+    sel = [0, q_all.shape[0] - 1]
+    H, d = q_all.shape[1], q_all.shape[2]
+    Hkv = kc.shape[1]
+    G = H // Hkv
+    kvs = [0, Hkv - 1]
+    heads = [g * G + j for g in kvs for j in range(G)]
+    nb0, nb1 = tb // bs, (te + bs - 1) // bs
+    if te > tb:
+        blocks = np.unique(bt[sel, nb0:nb1])
+        idx = torch.from_numpy(blocks.astype(np.int64)).to(kc.device)
+        kh = torch.tensor(kvs, device=kc.device)
+        kc_h = kc.index_select(0, idx).index_select(1, kh).float().cpu().numpy()
+        vc_h = vc.index_select(0, idx).index_select(1, kh).float().cpu().numpy()
+        bt_sub = np.zeros((len(sel), bt.shape[1]), np.int32)
+        bt_sub[:, nb0:nb1] = np.searchsorted(blocks, bt[sel, nb0:nb1])
+        qs = q_all[sel][:, heads].float().cpu().numpy()
+        Op, mp, lp = O.kv_range_partials(qs, kc_h, vc_h, bt_sub,
+                                         np.full(len(sel), M, np.int32), tb, te, bs)
+    else:
+        Op, mp, lp = (np.zeros((len(sel), len(heads), d)), np.full((len(sel), len(heads)),
+                      -np.inf), np.zeros((len(sel), len(heads))))
+    parts = [(Op, mp, lp)]
+    if ws > 1:
+        import torch.distributed as dist
+        parts = [None] * ws
+        dist.all_gather_object(parts, (Op, mp, lp))
+    ref = O.lse_merge([p[0] for p in parts], [p[1] for p in parts], [p[2] for p in parts])
+    err = _err(got[sel][:, heads], ref, rel=False)
+    return _parity(err, BF16_ATOL, "abs",
+                   f"sequences {sel}, the {len(heads)} query heads of KV heads {kvs}: "
+                   f"per-rank oracle partials over each rank's window, gathered and merged "
+                   f"by the oracle's LSE combine", ws, dev)
+
+
+# --------------------------------------------------------------------------- prefill
 def prefill_flops(B, H, N, d, causal=True):
     """4*B*H*N^2*d, halved for causal (the reference's convention,
     benchmarks/bench_attention.cu:48-49)."""
@@ -733,16 +796,19 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
     rank_flops = prefill_flops(B, h_l, N, d, causal)
     achieved = rank_flops / (ms_rank * 1e-3) / 1e12
 
-    # End to end through the public API: Q, K, V from pinned host memory and O back,
-    # every step (the host link, not the kernel, bounds this number).
-    q_h, k_h, v_h = (x.cpu().pin_memory() for x in (q, k, v))
+    # End to end through the public API: Q, K, V from pinned host memory (one packed
+    # copy) and O back, every step (the host link, not the kernel, bounds this number).
+    elt = 4 if fp32 else 2
+    nb = q.numel() * elt
+    stage_h = torch.empty(3 * nb, dtype=torch.uint8).pin_memory()
+    for j, x in enumerate((q, k, v)):
+        stage_h[j * nb:(j + 1) * nb].copy_(x.cpu().view(-1).view(torch.uint8))
+    stage_d = torch.empty_like(stage_h, device=dev)
+    qd, kd, vd = (stage_d[j * nb:(j + 1) * nb].view(dt).view(q.shape) for j in range(3))
     o_h = torch.empty(q.shape, dtype=dt).pin_memory()
-    qd, kd, vd = (torch.empty_like(x) for x in (q, k, v))
 
     def e2e_step(i):
-        qd.copy_(q_h, non_blocking=True)
-        kd.copy_(k_h, non_blocking=True)
-        vd.copy_(v_h, non_blocking=True)
+        stage_d.copy_(stage_h, non_blocking=True)
         o_h.copy_(flash_engine.flash_attention(qd, kd, vd, causal), non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -753,35 +819,138 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
     for i in range(n_e2e):
         e2e_step(i)
     e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n_e2e, ws, dev)
-    elt = 4 if fp32 else 2
+
+    parity = None
+    if not a.no_parity:
+        from oracle import attention_oracle as O
+        o = call(0)
+        torch.cuda.synchronize()
+        if fp32:
+            ref = O.flash_attention(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), causal)
+            err = _err(o.cpu().numpy(), ref, rel=True)
+            smp = f"all {h_l} heads of each rank"
+        else:
+            rng = np.random.default_rng(a.seed + 99 + rank)
+            pairs = [(int(rng.integers(B)), int(rng.integers(h_l))) for _ in range(2)]
+            err = 0.0
+            for b, h in pairs:
+                sl = (slice(b, b + 1), slice(h, h + 1))
+                ref = O.flash_attention(q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy(),
+                                        v[sl].float().cpu().numpy(), causal)
+                err = max(err, _err(o[sl].float().cpu().numpy(), ref, rel=False))
+            smp = "2 seeded (batch, head) slices of each rank, all 4096 rows"
+        parity = _parity(err, FP32_RTOL if fp32 else BF16_ATOL, "rel" if fp32 else "abs",
+                         smp + ", vs the CPU oracle", ws, dev)
+
     _, peak, peak_sus, src = _peaks()
     # fp32 runs on the tensor core as 3xTF32 (three TF32 products per fp32 product, TF32 at
     # half the bf16 rate): its ceiling in fp32 FLOP/s is the bf16 peak / 6.
-    pk, pk_sus = (peak / 6, peak_sus / 6) if fp32 else (peak, peak_sus)
-    return {
+    pk, pk_sus, pk_nom = ((peak / 6, peak_sus / 6, NOMINAL_BF16_TFLOPS / 6) if fp32
+                          else (peak, peak_sus, NOMINAL_BF16_TFLOPS))
+    tfile = None if fp32 or ws > 1 else "fa_prefill_config2_traffic.json"
+    traffic, tsrc = _traffic(tfile) if tfile else (None, None)
+    roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(pk, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / pk, 4),
+            "frac_of_sustained": round(achieved / pk_sus, 4),
+            "frac_nominal": round(achieved / pk_nom, 4), "peak_nominal": round(pk_nom, 1),
+            "peak_source": src + (" bf16 burst / 6: TF32 runs at half the bf16 rate "
+                                  "and each fp32 product takes 3 TF32 products"
+                                  if fp32 else " bf16 burst"),
+            "kernel": "fa_tf32_kernel (3xTF32 tcgen05)" if fp32 else "fa_prefill_kernel",
+            "traffic": traffic}
+    if tsrc:
+        roof["traffic_source"] = tsrc
+    res = {
         "metric": metric, "value": round(total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
         "ms_per_step": round(ms, 4),
         "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3),
-                "h2d_bytes_per_step": int(3 * q.numel() * elt),
-                "d2h_bytes_per_step": int(q.numel() * elt)},
+                "h2d_bytes_per_step": int(3 * nb), "d2h_bytes_per_step": int(nb),
+                "mode": "one packed H2D copy of Q, K, V, the call, one D2H copy of O"},
         "config": {"workload": name, "batch": B, "heads": H, "seq_len": N, "head_dim": d,
                    "causal": causal, "parallelism": f"head shard x{ws}",
                    "flops_per_step": total,
                    "l2": f"{nsets} input set(s) of {set_bytes / 2**20:.0f} MiB used in turn",
                    "steps_per_graph": GSTEPS},
-        "roofline": {"bound": "tensor",
-                     "achieved": round(achieved, 3), "peak": round(pk, 1),
-                     "unit": "TFLOP/s", "frac": round(achieved / pk, 4),
-                     "frac_of_sustained": round(achieved / pk_sus, 4),
-                     "peak_source": src + (" bf16 burst / 6: TF32 runs at half the bf16 rate "
-                                           "and each fp32 product takes 3 TF32 products"
-                                           if fp32 else " bf16 burst"),
-                     "kernel": "fa_tf32_kernel (3xTF32 tcgen05)" if fp32 else "fa_prefill_kernel",
-                     "traffic": None if fp32 or ws > 1 else _traffic("fa_prefill_config2_traffic.json")},
+        "roofline": roof,
         "clocks": sampler.summary(t0, t1),
         "gpu_launches": steps,
     }
+    if parity:
+        res["parity"] = parity
+    return res
+
+
+# --------------------------------------------------------------------------- CPU baselines
+def cpu_baseline(name, a, budget_s):
+    """The reference's CPU implementation of the workload (the NumPy port in oracle/),
+    timed on this host's cores over a bounded sample; returns the cpu_baseline object."""
+    from oracle import attention_oracle as O
+    if name in ("decode", "serving", "paged_fp32"):
+        cfg = CFG5 if name == "serving" else CFG3
+        lens = _lens(cfg, a.seed)
+        H, Hkv, d, bs = cfg["num_heads"], cfg["num_kv_heads"], cfg["head_dim"], cfg["block_size"]
+        elt = 4 if name == "paged_fp32" else 2
+        p1 = O.make_paged_problem(a.seed, 1, H, Hkv, d, lens[:1], bf16=elt == 2)
+        t = time.perf_counter()
+        O.paged_attention_gqa(p1["q"], p1["k_cache"], p1["v_cache"], p1["block_tables"],
+                              p1["context_lens"])
+        per_tok = (time.perf_counter() - t) / max(1, int(lens[0]))
+        n = 1
+        while n < len(lens) and per_tok * int(lens[:n + 1].sum()) < budget_s:
+            n += 1
+        sub = lens[:n]
+        p = O.make_paged_problem(a.seed, n, H, Hkv, d, sub, bf16=elt == 2)
+        t = time.perf_counter()
+        O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                              p["context_lens"])
+        dt = time.perf_counter() - t
+        b = decode_bytes(sub, Hkv, H, d, bs, elt)
+        return {"value": round(b / dt / 1e9, 4), "unit": "GB/s", "cores": _cpu_threads(),
+                "kind": "port",
+                "sample": f"first {n} of {len(lens)} sequences of {cfg['name']} "
+                          f"({int(sub.sum())} tokens), {dt:.2f} s; bytes counted as "
+                          f"{'fp32' if elt == 4 else 'bf16'}"}
+    if name == "splitkv":
+        c = CFG4
+        H, Hkv, d, bs, M = (c[k] for k in ("num_heads", "num_kv_heads", "head_dim",
+                                           "block_size", "context"))
+        # one sequence, KV heads taken one at a time until the budget is spent
+        tok = M
+        p = O.make_paged_problem(a.seed, 1, H // Hkv, 1, d, [tok])
+        t = time.perf_counter()
+        done = 0
+        while True:
+            O.paged_flash_decoding_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                       p["context_lens"], 1, bs)
+            done += 1
+            if time.perf_counter() - t > budget_s / 2 or done >= 4:
+                break
+        dt = (time.perf_counter() - t) / done
+        b = tok * d * 2 * 2
+        return {"value": round(b / dt / 1e9, 4), "unit": "GB/s", "cores": _cpu_threads(),
+                "kind": "port",
+                "sample": f"one (sequence, KV head) of config 4 ({tok} tokens, {H // Hkv} query "
+                          f"heads) per pass, {done} passes of {dt:.2f} s; bytes counted as bf16"}
+    if name in ("prefill", "prefill_fp32"):
+        fp32 = name == "prefill_fp32"
+        B, H, N, d, causal = (1, 8, 512, 64, False) if fp32 else (4, 32, 4096, 128, True)
+        rng = np.random.default_rng(a.seed)
+        q, k, v = (rng.standard_normal((1, 1, N, d), dtype=np.float32) for _ in range(3))
+        t = time.perf_counter()
+        done = 0
+        while True:
+            O.flash_attention(q, k, v, causal)
+            done += 1
+            if time.perf_counter() - t > budget_s or done >= (8 if fp32 else 4):
+                break
+        dt = (time.perf_counter() - t) / done
+        f = prefill_flops(1, 1, N, d, causal)
+        return {"value": round(f / dt / 1e12, 6), "unit": "TFLOP/s", "cores": _cpu_threads(),
+                "kind": "port",
+                "sample": f"one (batch, head) slice [{N}, {d}] of the config per pass "
+                          f"({done} passes of {dt * 1e3:.1f} ms), FLOPs counted as on the GPU"}
+    raise ValueError(name)
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -830,18 +999,26 @@ def run_workload(name, a, ws, rank, local, primary):
     steps = a.steps if primary else min(a.steps, 30)
     warmup = a.warmup if primary else min(a.warmup, 3)
     if name == "decode":
-        return bench_paged(a, ws, rank, local, CFG3, primary and not a.no_cpu_baseline, steps,
-                           warmup)
+        return bench_paged(a, ws, rank, local, CFG3, steps, warmup)
     if name == "serving":
-        return bench_paged(a, ws, rank, local, CFG5, primary and not a.no_cpu_baseline, steps,
-                           warmup)
+        return bench_paged(a, ws, rank, local, CFG5, steps, warmup)
+    if name == "paged_fp32":
+        return bench_paged(a, ws, rank, local, CFG3, steps, warmup, fp32=True)
     if name == "splitkv":
         return bench_splitkv(a, ws, rank, local, steps, warmup)
     if name == "prefill":
         return bench_prefill(a, ws, rank, local, steps, warmup)
-    if name == "paged_fp32":
-        return bench_paged_fp32(a, ws, rank, local, steps, warmup)
     return bench_prefill(a, ws, rank, local, steps, warmup, fp32=True)
+
+
+def _common(res, a, ws, name):
+    # every config keeps its total work fixed as N grows (heads or the KV range are
+    # divided over the ranks): strong scaling
+    res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32" if name in ("prefill_fp32", "paged_fp32") else "bf16",
+                "data": "synthetic (seeded N(0,1) inputs; benchmark config shapes)"})
+    return res
 
 
 def main():
@@ -854,36 +1031,46 @@ def main():
         return
     import torch
     torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if ws > 1:
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
-    res = run_workload(a.workload, a, ws, rank, local, True)
-    res.update({"n_gpus": ws, "steps": a.steps, "warmup": a.warmup, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded N(0,1) bf16 inputs; benchmark config shapes)"})
-    if a.workload in ("prefill_fp32", "paged_fp32"):
-        res["dtype"] = "f32"
+    head = _common(run_workload(a.workload, a, ws, rank, local, True), a, ws, a.workload)
+    lines = []
     if not a.no_secondary:
-        sec = {}
-        for name in ("prefill", "splitkv", "serving", "prefill_fp32", "paged_fp32"):
+        for name in ("prefill", "splitkv", "serving", "prefill_fp32", "paged_fp32", "decode"):
             if name == a.workload:
                 continue
             try:
-                r = run_workload(name, a, ws, rank, local, False)
-                sec[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step",
-                                               "roofline", "config", "e2e") if k in r}
+                r = _common(run_workload(name, a, ws, rank, local, False), a, ws, name)
+                r["secondary"] = True
+                r["steps"] = min(a.steps, 30)
+                r["warmup"] = min(a.warmup, 3)
             except Exception as e:  # recorded, never silently dropped
-                sec[name] = {"error": f"{type(e).__name__}: {e}"}
+                r = {"workload": name, "secondary": True, "error": f"{type(e).__name__}: {e}"}
                 if rank == 0:
                     traceback.print_exc()
-        res["secondary"] = sec
+            lines.append((name, r))
+    # CPU baselines (the reference's NumPy path on the host cores), rank 0 at N = 1,
+    # after all GPU timing
+    if ws == 1 and rank == 0 and not a.no_cpu_baseline:
+        for name, r in [(a.workload, head)] + lines:
+            if "error" in r:
+                continue
+            try:
+                r["cpu_baseline"] = cpu_baseline(name, a, 12.0 if r is head else 4.0)
+            except Exception as e:
+                r["cpu_baseline"] = {"error": f"{type(e).__name__}: {e}"}
     if ws > 1:
         import torch.distributed as dist
+        dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        for _, r in lines:
+            print(json.dumps(r), flush=True)
+        print(json.dumps(head), flush=True)
 
 
 if __name__ == "__main__":

@@ -15,6 +15,8 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <thread>
+#include <tuple>
 #include <type_traits>
 #include <utility>
 
@@ -52,22 +54,43 @@ struct PagedArgs {
   int rope_max_pos = 0;
 };
 
-int paged_check(const PagedArgs& a, bool tensor_core) {
+template <typename T>
+constexpr int dtype_of() {
+  return std::is_same<T, float>::value ? fe::paged::kF32
+         : std::is_same<T, half>::value ? fe::paged::kF16
+                                        : fe::paged::kBf16;
+}
+
+// Shapes the persistent decode kernel takes (paged_decode.cu): head_dim 64 or 128,
+// block size 16 or 32, 16-byte aligned caches; the fp32 decode reads the flat layout
+// with 128-bit (d = 128) or 64-bit (d = 64) q loads.
+template <typename T>
+int paged_check(const PagedArgs& a) {
   if (a.S < 0 || a.H <= 0 || a.Hkv <= 0 || a.H % a.Hkv != 0 || a.d <= 0 || a.bs <= 0 ||
       a.maxb < 0)
     return kErr;
-  if (tensor_core) {
-    if (!(a.d == 64 || a.d == 128) || !(a.bs == 16 || a.bs == 32)) return kErr;
-    if (a.kv_layout == fe::paged::kKvVllm && a.bs != 16) return kErr;
-    if (a.kv_layout != fe::paged::kKvFlat && a.kv_layout != fe::paged::kKvVllm) return kErr;
-    if (!aligned(a.kc, 16) || !aligned(a.vc, 16) || !aligned(a.q, 4) || !aligned(a.out, 2))
-      return kErr;
-    if (a.num_blocks > 0 &&
-        static_cast<long long>(a.num_blocks) * a.Hkv * a.bs > static_cast<long long>(INT_MAX))
-      return kErr;
-  } else {
-    if (a.d > 256 || a.d % 4 != 0) return kErr;
+  if (!(a.d == 64 || a.d == 128) || !(a.bs == 16 || a.bs == 32)) return kErr;
+  if (a.kv_layout != fe::paged::kKvFlat && a.kv_layout != fe::paged::kKvVllm) return kErr;
+  if (a.kv_layout == fe::paged::kKvVllm && (a.bs != 16 || std::is_same<T, float>::value))
+    return kErr;
+  if (!aligned(a.kc, 16) || !aligned(a.vc, 16)) return kErr;
+  if (std::is_same<T, float>::value) {
+    if (!aligned(a.q, a.d == 128 ? 16 : 8) || !aligned(a.out, 4)) return kErr;
+  } else if (!aligned(a.q, 4) || !aligned(a.out, 2)) {
+    return kErr;
   }
+  if (a.num_blocks > 0 &&
+      static_cast<long long>(a.num_blocks) * a.Hkv * a.bs > static_cast<long long>(INT_MAX))
+    return kErr;
+  return 0;
+}
+
+// Arguments the generic fp32 kernels (attention_fp32.cu) take.
+int paged_check_generic(const PagedArgs& a) {
+  if (a.S < 0 || a.H <= 0 || a.Hkv <= 0 || a.H % a.Hkv != 0 || a.d <= 0 || a.bs <= 0 ||
+      a.maxb < 0)
+    return kErr;
+  if (a.d > 256 || a.d % 4 != 0) return kErr;
   return 0;
 }
 
@@ -81,13 +104,23 @@ struct DecodePlan {
   // exchange mode (partials stored into every rank's exchange buffer)
   char* xbuf[fe::paged::kMaxRanks] = {};
   int xworld = 0, xrank = 0, xmax_rows = 0;
+  // flat mode on a slot of the library's stream scratch instead of `ws`
+  int ws_slot = -1;
 };
 
-inline int decode_nt(int H, int Hkv) { return (H / Hkv) <= 8 ? 1 : 2; }
+inline int decode_nt(int dtype, int H, int Hkv) { return fe::paged::decode_nt(dtype, H / Hkv); }
 
-long long workspace_floats_for(int H, int Hkv, int d, int bs) {
+long long workspace_floats_dtype(int dtype, int H, int Hkv, int d, int bs) {
   if (H <= 0 || Hkv <= 0 || H % Hkv) return -1;
-  return fe::paged::fixup_layout(d, bs, decode_nt(H, Hkv)).floats;
+  return fe::paged::fixup_layout(dtype, d, bs, decode_nt(dtype, H, Hkv)).floats;
+}
+
+// Workspace of the split-KV decode for this head configuration: the largest over the
+// element types, so that one workspace serves bf16, fp16 and fp32 calls.
+long long workspace_floats_for(int H, int Hkv, int d, int bs) {
+  const long long a = workspace_floats_dtype(fe::paged::kBf16, H, Hkv, d, bs);
+  const long long b = workspace_floats_dtype(fe::paged::kF32, H, Hkv, d, bs);
+  return a < 0 || b < 0 ? -1 : std::max(a, b);
 }
 
 // Runs the tensor-core decode over all sequences, in launches of at most
@@ -95,8 +128,9 @@ long long workspace_floats_for(int H, int Hkv, int d, int bs) {
 // fixup slots (fixup_layout); the kernel merges split sequences itself.
 template <typename T>
 int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream_t st) {
-  const int nt = decode_nt(a.H, a.Hkv);
-  const int hpc = 8 * nt;
+  constexpr int dt = dtype_of<T>();
+  const int nt = decode_nt(dt, a.H, a.Hkv);
+  const int hpc = fe::paged::heads_per_cta(dt, nt);
   const int head_chunks = (a.H / a.Hkv + hpc - 1) / hpc;
   const long long kv_rows = a.num_blocks > 0
                                 ? static_cast<long long>(a.num_blocks) * a.Hkv * a.bs
@@ -106,8 +140,11 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
   float* part_o = nullptr;
   float* part_ml = nullptr;
   int* counters = nullptr;
-  if (pl.flat) {
-    const fe::paged::FixupLayout f = fe::paged::fixup_layout(a.d, a.bs, nt);
+  int max_grid = 0;
+  if (pl.flat && pl.ws_slot >= 0) {
+    max_grid = fe::paged::slot_grid_cap(dt, a.d, nt);
+  } else if (pl.flat) {
+    const fe::paged::FixupLayout f = fe::paged::fixup_layout(dt, a.d, a.bs, nt);
     if (f.floats <= 0 || !ws) return kErr;
     counters = reinterpret_cast<int*>(ws);
     part_o = ws + fe::paged::kCounterSlots;
@@ -124,6 +161,8 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.part_o = part_o;
     p.part_ml = part_ml;
     p.counters = counters;
+    p.ws_slot = pl.flat ? pl.ws_slot : -1;
+    p.max_grid = max_grid;
     p.merged_o = pl.merged_out ? pl.merged_out + row0 * a.d : nullptr;
     p.merged_ml = pl.merged_stats ? pl.merged_stats + row0 * 2 : nullptr;
     p.num_seqs = n;
@@ -155,7 +194,7 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
 
 template <typename T>
 int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
-  const int rc = paged_check(a, true);
+  const int rc = paged_check<T>(a);
   if (rc) return rc;
   if (a.S == 0) return 0;
   // Unit mode, one segment per sequence whatever its length: every segment
@@ -166,9 +205,9 @@ int paged_v1_tc(const PagedArgs& a, cudaStream_t st) {
 
 template <typename T>
 int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st) {
-  const int rc = paged_check(a, true);
+  const int rc = paged_check<T>(a);
   if (rc) return rc;
-  const long long need = workspace_floats_for(a.H, a.Hkv, a.d, a.bs);
+  const long long need = workspace_floats_dtype(dtype_of<T>(), a.H, a.Hkv, a.d, a.bs);
   if (need <= 0 || !ws || static_cast<long long>(ws_floats) < need) return kErr;
   if (a.S == 0) return 0;
   DecodePlan pl;
@@ -177,98 +216,47 @@ int paged_v2_tc(const PagedArgs& a, float* ws, size_t ws_floats, cudaStream_t st
   return paged_tc_run<T>(a, pl, ws, st);
 }
 
-// Scratch the library keeps for entry points whose reference signature passes none:
-// one zero-initialised block per (device, stream), allocated on the first call on that
-// stream and kept for the life of the process. It holds a split-KV decode workspace
-// sized for every supported head configuration (after 256 reserved bytes). Calls on one stream are ordered, so they can share
-// it; calls on different streams get different ones. Returns false while the stream
-// is being captured and has none yet (cudaMalloc must not run inside a capture); the
-// callers then use their scratch-free variants.
-struct StreamScratch {
-  float* ws;         // split-KV decode workspace
-  size_t ws_floats;
-};
-bool stream_scratch(cudaStream_t st, StreamScratch* out) {
+// Split-KV scratch for the entry points whose reference signature passes none (the
+// v1 paged launchers), which may not allocate: the kStreamSlots slots of the static
+// array in paged_decode.cu. A slot is bound to a stream on the first v1 call on that
+// stream and stays bound for the life of the process, so work captured into a CUDA
+// graph keeps a valid slot. Calls on one stream are ordered and can share its slot.
+// The per-thread default stream is one handle for every thread, so it is keyed with
+// the calling thread as well. Returns -1 once every slot is bound (those streams run
+// the single-pass kernel). Binding allocates nothing on the device and does not
+// synchronise, so it is also allowed while the stream is being captured.
+int stream_slot(cudaStream_t st) {
   static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, char*> cache;
-  static long long need = -1;
-  constexpr size_t kHead = 256;
+  static std::map<std::tuple<int, uintptr_t, std::thread::id>, int> bound;
+  static int used[64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  const std::thread::id tid =
+      st == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
+  const auto key = std::make_tuple(dev, reinterpret_cast<uintptr_t>(st), tid);
   std::lock_guard<std::mutex> lk(mu);
-  if (need < 0) {
-    for (int d : {64, 128})
-      for (int bs : {16, 32})
-        for (int nt : {1, 2}) need = std::max(need, fe::paged::fixup_layout(d, bs, nt).floats);
-  }
-  if (need <= 0) return false;
-  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
-  char* base = nullptr;
-  auto it = cache.find(key);
-  if (it != cache.end()) {
-    base = it->second;
-  } else {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
-      return false;
-    if (cudaMalloc(&base, kHead + sizeof(float) * static_cast<size_t>(need)) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    if (cudaMemsetAsync(base, 0, kHead + sizeof(int) * fe::paged::kCounterSlots, st) !=
-        cudaSuccess) {
-      cudaFree(base);
-      return false;
-    }
-    cache.emplace(key, base);
-  }
-  out->ws = reinterpret_cast<float*>(base + kHead);
-  out->ws_floats = static_cast<size_t>(need);
-  return true;
+  auto it = bound.find(key);
+  if (it != bound.end()) return it->second;
+  if (used[dev] >= fe::paged::kStreamSlots) return -1;
+  const int slot = used[dev]++;
+  bound.emplace(key, slot);
+  return slot;
 }
 
-// fp32 scratch the library keeps for the split fp32 paged decode, one block per
-// (device, stream) grown to the largest request seen. Growth waits for the stream's
-// earlier work (which may still read the old block) before freeing it. Returns
-// nullptr while the stream is being captured and the block is too small.
-float* stream_scratch_f32(cudaStream_t st, size_t floats) {
-  static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, std::pair<float*, size_t>> cache;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(st));
-  auto it = cache.find(key);
-  if (it != cache.end() && it->second.second >= floats) return it->second.first;
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
-    return nullptr;
-  size_t want = floats;
-  if (it != cache.end()) {
-    want = std::max(floats, 2 * it->second.second);
-    if (cudaStreamSynchronize(st) != cudaSuccess) return nullptr;
-    cudaFree(it->second.first);
-    cache.erase(it);
-  }
-  float* p = nullptr;
-  if (cudaMalloc(&p, want * sizeof(float)) != cudaSuccess) {
-    cudaGetLastError();
-    return nullptr;
-  }
-  cache.emplace(key, std::make_pair(p, want));
-  return p;
-}
-
-// The reference's v1 entry points: the split-KV kernel with the library's own scratch
-// (the single-pass kernel when none can be had).
+// The reference's v1 entry points: the split-KV kernel on the stream's scratch slot
+// (the single-pass kernel when every slot is taken).
 template <typename T>
 int paged_v1_entry(const PagedArgs& a, cudaStream_t st) {
-  const int rc = paged_check(a, true);
+  const int rc = paged_check<T>(a);
   if (rc) return rc;
   if (a.S == 0) return 0;
-  StreamScratch sc;
-  return stream_scratch(st, &sc) ? paged_v2_tc<T>(a, sc.ws, sc.ws_floats, st)
-                                 : paged_v1_tc<T>(a, st);
+  const int slot = stream_slot(st);
+  if (slot < 0) return paged_v1_tc<T>(a, st);
+  DecodePlan pl;
+  pl.flat = true;
+  pl.direct_final = true;
+  pl.ws_slot = slot;
+  return paged_tc_run<T>(a, pl, nullptr, st);
 }
 
 // NCCL, resolved at run time from the libnccl.so.2 the process already holds (e.g.
@@ -365,43 +353,16 @@ int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc,
                                int bs, int max_ctx, int maxb, int num_blocks, float scale,
                                void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
-  const int rc = paged_check(a, false);
+  cudaStream_t st = as_stream(stream);
+  // The persistent split-KV decode where its shapes allow (paged_decode.cu), else the
+  // generic single-pass kernel (any block size, head_dim % 4 == 0 up to 256).
+  if (paged_check<float>(a) == 0) return paged_v1_entry<float>(a, st);
+  const int rc = paged_check_generic(a);
   if (rc) return rc;
   if (S == 0) return 0;
-  cudaStream_t st = as_stream(stream);
-  const float sc = resolve_scale(scale, d);
-  // Contexts longer than one split: the key range is cut into kFp32SplitTokens-token
-  // splits (as many as the block-table row can hold, so every context is covered) and
-  // merged; shorter ones, or no scratch (a capture), take the single-pass kernel.
-  constexpr int kFp32SplitTokens = 512;
-  const long long row_tokens = static_cast<long long>(maxb) * bs;
-  const long long splits = (row_tokens + kFp32SplitTokens - 1) / kFp32SplitTokens;
-  if (splits > 1 && splits <= 4096 && S <= 65535 &&
-      static_cast<long long>(S) * H <= static_cast<long long>(INT_MAX)) {
-    const size_t rows = static_cast<size_t>(S) * H;
-    const size_t need = rows * static_cast<size_t>(splits) * (d + 2);
-    float* ws = stream_scratch_f32(st, need);
-    if (ws) {
-      float* po = ws;
-      float* pml = ws + rows * static_cast<size_t>(splits) * d;
-      cudaError_t e = fe::simt::launch_paged_split_fp32(q, kc, vc, po, pml, bt, lens, S, H, Hkv, d,
-                                                        bs, maxb, num_blocks,
-                                                        static_cast<int>(splits),
-                                                        kFp32SplitTokens, sc, st);
-      if (e != cudaSuccess) return static_cast<int>(e);
-      fe::paged::MergeParams mp{};
-      mp.part_out = po;
-      mp.part_stats = pml;
-      mp.rows = static_cast<int>(rows);
-      mp.ranks = 1;
-      mp.parts_per_rank = static_cast<int>(splits);
-      mp.out = out;
-      mp.out_dtype = 0;
-      return static_cast<int>(fe::paged::launch_merge(mp, d, st));
-    }
-  }
   return static_cast<int>(fe::simt::launch_paged_fp32(q, kc, vc, out, bt, lens, S, H, Hkv, d, bs,
-                                                      maxb, num_blocks, sc, st));
+                                                      maxb, num_blocks, resolve_scale(scale, d),
+                                                      st));
 }
 
 int fe_paged_attention_v1_fp16(const void* q, const void* kc, const void* vc, void* out,
@@ -426,6 +387,13 @@ int fe_paged_attention_ex(const void* q, const void* kc, const void* vc, void* o
   a.rope_sin = rope_sin;
   a.rope_max_pos = rope_max_pos;
   cudaStream_t st = as_stream(stream);
+  if (!workspace && workspace_floats == FE_WORKSPACE_LIBRARY) {
+    // split-KV on the stream's slot of the library scratch (as the v1 entries)
+    if (dtype == 0) return paged_v1_entry<__nv_bfloat16>(a, st);
+    if (dtype == 1) return paged_v1_entry<half>(a, st);
+    if (dtype == 2) return paged_v1_entry<float>(a, st);
+    return kErr;
+  }
   if (dtype == 0) {
     return workspace ? paged_v2_tc<__nv_bfloat16>(a, workspace, workspace_floats, st)
                      : paged_v1_tc<__nv_bfloat16>(a, st);
@@ -433,6 +401,10 @@ int fe_paged_attention_ex(const void* q, const void* kc, const void* vc, void* o
   if (dtype == 1) {
     return workspace ? paged_v2_tc<half>(a, workspace, workspace_floats, st)
                      : paged_v1_tc<half>(a, st);
+  }
+  if (dtype == 2) {
+    return workspace ? paged_v2_tc<float>(a, workspace, workspace_floats, st)
+                     : paged_v1_tc<float>(a, st);
   }
   return kErr;
 }
@@ -460,8 +432,16 @@ size_t fe_paged_attention_v2_workspace_floats(int H, int Hkv, int d, int bs) {
 
 // ---- no-alloc split-KV decode ------------------------------------------------
 // Scratch for callers that cannot allocate: one array per device that loads the
-// library, shared by every call (see flash_engine_c.h for the contract).
+// library, shared by every call (see flash_engine_c.h for the contract). It holds the
+// largest split-KV workspace any device can ask for (grids are capped at kCounterSlots
+// CTAs, at most 16 query heads a CTA, head_dim <= 128), so its size does not depend on
+// the GPU.
 static __device__ __align__(256) float g_noalloc_scratch[FE_NOALLOC_SCRATCH_FLOATS];
+static_assert(fe::paged::kStreamSlots == FE_STREAM_SCRATCH_SLOTS,
+              "the header states the library's scratch slot count");
+static_assert(FE_NOALLOC_SCRATCH_FLOATS >=
+                  fe::paged::kCounterSlots + 1LL * fe::paged::kCounterSlots * 2 * 16 * (128 + 2),
+              "the no-alloc scratch must hold the workspace of the largest decode grid");
 
 // Device address of g_noalloc_scratch on the current device, looked up once per
 // device. In host code the array's name only stands in for the symbol, so it is
@@ -475,12 +455,10 @@ static int noalloc_scratch_ptr(float** out) {
   if (dev < 0 || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   std::lock_guard<std::mutex> lk(mu);
   if (!ptrs[dev]) {
+    // The array is zero when the module loads, so the split-KV arrival counters at
+    // its start begin at zero; every call leaves them so.
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    // The split-KV arrival counters at the start of the scratch must begin at zero
-    // (every call leaves them so).
-    e = cudaMemset(p, 0, sizeof(int) * fe::paged::kCounterSlots);
     if (e != cudaSuccess) return static_cast<int>(e);
     ptrs[dev] = static_cast<float*>(p);
   }
@@ -493,10 +471,10 @@ int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* kc, const void
                                        int d, int bs, int max_ctx, int maxb, int num_blocks,
                                        float scale, void* stream) {
   if (S < 0 || H <= 0 || Hkv <= 0 || d <= 0) return kErr;
-  const long long need = workspace_floats_for(H, Hkv, d, bs);
+  const long long need = workspace_floats_dtype(fe::paged::kBf16, H, Hkv, d, bs);
   if (need <= 0 || need > FE_NOALLOC_SCRATCH_FLOATS) return kErr;
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
-  const int rc = paged_check(a, true);
+  const int rc = paged_check<__nv_bfloat16>(a);
   if (rc) return rc;
   if (S == 0) return 0;
   float* base = nullptr;
@@ -531,7 +509,7 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
                                   size_t workspace_floats, float* mout, float* mstats,
                                   void* stream) {
   PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
-  int rc = paged_check(a, true);
+  int rc = paged_check<__nv_bfloat16>(a);
   if (rc) return rc;
   const long long need = workspace_floats_for(H, Hkv, d, bs);
   if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
@@ -554,7 +532,7 @@ int fe_paged_decode_kv_exchange_bf16(const void* q, const void* kc, const void* 
                                      void* const* xbufs, int world, int rank, int max_rows,
                                      void* out, int phases, void* stream) {
   PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
-  int rc = paged_check(a, true);
+  int rc = paged_check<__nv_bfloat16>(a);
   if (rc) return rc;
   if (world < 1 || world > fe::paged::kMaxRanks || rank < 0 || rank >= world || !xbufs)
     return kErr;
@@ -679,7 +657,7 @@ int fe_paged_decode_kv_range_nccl_bf16(const void* q, const void* kc, const void
                                        float* scratch, size_t scratch_floats, void* out,
                                        void* stream) {
   PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
-  int rc = paged_check(a, true);
+  int rc = paged_check<__nv_bfloat16>(a);
   if (rc) return rc;
   if (!comm || world < 1 || rank < 0 || rank >= world || max_context_len < 0 || !out ||
       !aligned(out, 2))

@@ -1,7 +1,9 @@
 // fp32 (CUDA-core) kernels behind the reference's fp32 entry points:
 //  * FA2 forward          (launch_flash_attention_forward_fp32, src/flash_attention.cu:111-345)
 //  * naive forward        (launch_naive_attention_forward_fp32, src/flash_attention.cu:12-104)
-//  * paged decode, GQA    (launch_paged_attention_v1_fp32, src/paged_attention.cu:14-215)
+//  * paged decode, GQA, single pass, for the shapes the persistent decode of
+//    paged_decode.cu does not take (launch_paged_attention_v1_fp32,
+//    src/paged_attention.cu:14-215)
 //  * dense split-KV stage 1 (launch_flash_decoding_forward_fp32, src/flash_decoding.cu:14-142)
 // fp32 inputs need fp32 products to hold the 1e-3 relative tolerance, so these run
 // on the FMA pipes; the bf16/fp16 paths use tensor cores.
@@ -13,6 +15,7 @@
 
 #include <type_traits>
 
+#include "../../include/cuda_utils.cuh"
 #include "fp32_kernels.h"
 #include "internal.h"
 #include "ptx.cuh"
@@ -22,16 +25,11 @@ namespace simt {
 
 constexpr float NEG_INF = -__builtin_huge_valf();
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
+// Butterfly warp reductions of include/cuda_utils.cuh (result in every lane).
+using flash_engine::cuda::warp_reduce_max;
+using flash_engine::cuda::warp_reduce_sum;
+__device__ __forceinline__ float warp_sum(float v) { return warp_reduce_sum(v); }
+__device__ __forceinline__ float warp_max(float v) { return warp_reduce_max(v); }
 
 // Asynchronous 4-byte global -> shared copies (cp.async), completed per group.
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
@@ -839,138 +837,6 @@ cudaError_t launch_paged_fp32(const float* q, const float* kc, const float* vc, 
   if (d <= D_ && HG == HG_)                                                            \
     return launch_paged_fp32_v<D_, HG_>(vec, grid, q, kc, vc, out, bt, lens, H, Hkv, d, bs, \
                                         maxb, num_blocks, sl, err, st);
-  FE_P(64, 1) FE_P(64, 2) FE_P(64, 4) FE_P(64, 8)
-  FE_P(128, 1) FE_P(128, 2) FE_P(128, 4) FE_P(128, 8)
-  FE_P(256, 1) FE_P(256, 2) FE_P(256, 4)
-#undef FE_P
-  return cudaErrorInvalidValue;
-}
-
-// Paged fp32 decode, split: grid (splits, Hkv * head_chunks, S), 8 warps. CTA
-// (s, chunk, seq) covers tokens [s*T, (s+1)*T) of its sequence (T = split_tokens) and
-// writes the unnormalised O, m (log2 units) and l of each of its query heads to part
-// slot (seq*H + h)*splits + s; a split past the context writes (0, -inf, 0). A merge
-// over the splits (the log-sum-exp combine, merge_kernel) gives the output. With the
-// key range cut this way, a long sequence no longer sets the kernel's length, as it
-// does with one CTA per (sequence, KV head).
-template <int D, int HG, bool VEC>
-__global__ void __launch_bounds__(256, 2) paged_split_fp32_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-    float* __restrict__ part_o, float* __restrict__ part_ml, const int* __restrict__ bt,
-    const int* __restrict__ lens, int H, int Hkv, int d, int bs, int maxb, int num_blocks,
-    int split_tokens, float sl, unsigned* err) {
-  constexpr int NW = 8;
-  using WD = PagedDecoder<D, HG, VEC>;
-  constexpr int TB = WD::TB;
-  __shared__ float sq[HG * D];
-  __shared__ float cm[NW * HG], cl[NW * HG];
-  __shared__ float co[NW * HG * D];
-  const int splits = gridDim.x, s = blockIdx.x;
-  const int G = H / Hkv, chunks = (G + HG - 1) / HG;
-  const int kvh = blockIdx.y / chunks, ch = blockIdx.y - kvh * chunks;
-  const int seq = blockIdx.z;
-  const int h0 = kvh * G + ch * HG;
-  const int nh = min(HG, G - ch * HG);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ctx = lens[seq];
-  const int t0 = s * split_tokens, t1 = min(ctx, t0 + split_tokens);
-  // the splits cover the block-table row; a longer context is a bad input
-  if (s == splits - 1 && ctx > t0 + split_tokens && threadIdx.x == 0) atomicOr(err, kErrBadBlock);
-  if (t0 >= t1) {  // nothing of this sequence here: an empty part
-    for (int i = threadIdx.x; i < nh * d; i += NW * 32) {
-      const int h = i / d, c = i - h * d;
-      const size_t slot = (static_cast<size_t>(seq) * H + h0 + h) * splits + s;
-      part_o[slot * d + c] = 0.f;
-      if (c == 0) {
-        part_ml[slot * 2] = NEG_INF;
-        part_ml[slot * 2 + 1] = 0.f;
-      }
-    }
-    return;
-  }
-  for (int i = threadIdx.x; i < HG * D; i += NW * 32) {
-    const int h = i / D, c = i - h * D;
-    sq[i] = (h < nh && c < d) ? q[(static_cast<size_t>(seq) * H + h0 + h) * d + c] : 0.f;
-  }
-  __syncthreads();
-  WD st;
-  st.init(sq, lane);
-  for (int tb = t0 + warp * TB; tb < t1; tb += NW * TB) {
-    const float* kp[TB];
-    const float* vp[TB];
-    unsigned valid = 0;
-#pragma unroll
-    for (int j = 0; j < TB; ++j) {
-      const int t = tb + j;
-      kp[j] = vp[j] = kc;
-      if (t >= t1) continue;
-      if (t / bs >= maxb) {  // context longer than the block-table row
-        if (lane == 0) atomicOr(err, kErrBadBlock);
-        continue;
-      }
-      const int phys = __ldg(bt + static_cast<size_t>(seq) * maxb + t / bs);
-      if (phys < 0 || (num_blocks > 0 && phys >= num_blocks)) {
-        if (lane == 0) atomicOr(err, kErrBadBlock);
-        continue;
-      }
-      const size_t off = ((static_cast<size_t>(phys) * Hkv + kvh) * bs + t % bs) * d;
-      kp[j] = kc + off;
-      vp[j] = vc + off;
-      valid |= 1u << j;
-    }
-    st.tokens(kp, vp, valid, d, nh, sl, lane);
-  }
-  st.template merge<NW>(cm, cl, co, nh, d, warp, lane,
-                        [&](int h, int c, float Mx, float L, float Ov) {
-                          const size_t slot = (static_cast<size_t>(seq) * H + h0 + h) * splits + s;
-                          part_o[slot * d + c] = Ov;
-                          if (c == 0) {
-                            part_ml[slot * 2] = Mx;
-                            part_ml[slot * 2 + 1] = L;
-                          }
-                        });
-}
-
-template <int D, int HG>
-static cudaError_t launch_paged_split_fp32_v(bool vec, dim3 grid, const float* q, const float* kc,
-                                             const float* vc, float* part_o, float* part_ml,
-                                             const int* bt, const int* lens, int H, int Hkv, int d,
-                                             int bs, int maxb, int num_blocks, int split_tokens,
-                                             float sl, unsigned* err, cudaStream_t st) {
-  if constexpr ((D == 64 || D == 128) && (HG == 4 || HG == 8)) {
-    if (vec) {
-      paged_split_fp32_kernel<D, HG, true><<<grid, 256, 0, st>>>(
-          q, kc, vc, part_o, part_ml, bt, lens, H, Hkv, d, bs, maxb, num_blocks, split_tokens, sl,
-          err);
-      return cudaGetLastError();
-    }
-  }
-  paged_split_fp32_kernel<D, HG, false><<<grid, 256, 0, st>>>(
-      q, kc, vc, part_o, part_ml, bt, lens, H, Hkv, d, bs, maxb, num_blocks, split_tokens, sl,
-      err);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_paged_split_fp32(const float* q, const float* kc, const float* vc,
-                                    float* part_o, float* part_ml, const int* bt, const int* lens,
-                                    int S, int H, int Hkv, int d, int bs, int maxb, int num_blocks,
-                                    int splits, int split_tokens, float scale, cudaStream_t st) {
-  if (S <= 0) return cudaSuccess;
-  if (S > 65535 || splits < 1 || split_tokens < 1) return cudaErrorInvalidValue;
-  const int G = H / Hkv;
-  const int HG = G >= 8 ? 8 : G >= 4 ? 4 : G >= 2 ? 2 : 1;
-  const int chunks = (G + HG - 1) / HG;
-  if (static_cast<long long>(Hkv) * chunks > 65535) return cudaErrorInvalidValue;
-  dim3 grid(splits, Hkv * chunks, S);
-  const float sl = scale * kLog2e;
-  unsigned* err = device_error_word();
-  const bool vec = (d == 64 || d == 128) && (HG == 4 || HG == 8) &&
-                   ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) == 0;
-#define FE_P(D_, HG_)                                                                       \
-  if (d <= D_ && HG == HG_)                                                                 \
-    return launch_paged_split_fp32_v<D_, HG_>(vec, grid, q, kc, vc, part_o, part_ml, bt, lens, \
-                                              H, Hkv, d, bs, maxb, num_blocks, split_tokens,   \
-                                              sl, err, st);
   FE_P(64, 1) FE_P(64, 2) FE_P(64, 4) FE_P(64, 8)
   FE_P(128, 1) FE_P(128, 2) FE_P(128, 4) FE_P(128, 8)
   FE_P(256, 1) FE_P(256, 2) FE_P(256, 4)

@@ -19,12 +19,6 @@ cudaError_t launch_naive_fp32(const float* q, const float* k, const float* v, fl
 cudaError_t launch_paged_fp32(const float* q, const float* kc, const float* vc, float* out,
                               const int* bt, const int* lens, int S, int H, int Hkv, int d, int bs,
                               int maxb, int num_blocks, float scale, cudaStream_t st);
-// Split paged fp32 decode: partials [S*H rows][splits][d] and [..][2] for a
-// merge_kernel over the splits (split s covers tokens [s*split_tokens, ...)).
-cudaError_t launch_paged_split_fp32(const float* q, const float* kc, const float* vc,
-                                    float* part_o, float* part_ml, const int* bt, const int* lens,
-                                    int S, int H, int Hkv, int d, int bs, int maxb, int num_blocks,
-                                    int splits, int split_tokens, float scale, cudaStream_t st);
 cudaError_t launch_decode_split_fp32(const float* q, const float* k, const float* v,
                                      float* part_o, float* part_ml, int BH, int M, int d,
                                      int splits, float scale, cudaStream_t st);

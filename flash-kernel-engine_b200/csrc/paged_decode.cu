@@ -46,6 +46,7 @@
 
 #include <type_traits>
 
+#include "../../include/cuda_utils.cuh"
 #include "internal.h"
 #include "paged_decode.h"
 #include "ptx.cuh"
@@ -74,7 +75,17 @@ struct Elem<half> {
   static __device__ __forceinline__ half cvt(float x) { return __float2half_rn(x); }
 };
 
+// fp32 cache: the CUDA-core consumer of paged_decode_kernel (no tensor-core product).
+template <>
+struct Elem<float> {
+  static __device__ __forceinline__ float cvt(float x) { return x; }
+};
+
 constexpr float NEG_INF = -__builtin_huge_valf();
+
+// The library-owned split-KV scratch of the v1 entry points (see kStreamSlots).
+// Zero when the module loads; every launch leaves its slot's counters at zero.
+static __device__ __align__(256) float g_stream_scratch[kStreamSlots * kStreamSlotFloats];
 
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -291,12 +302,10 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
     };
     load_rows(0);
     float M = l > 0.f ? m : NEG_INF;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    M = flash_engine::cuda::warp_reduce_max(M);
     const float w = l > 0.f ? ex2(m - M) : 0.f;
     float L = l * w;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    L = flash_engine::cuda::warp_reduce_sum(L);
 #pragma unroll
     for (int e = 0; e < PER; ++e) acc[e] = 0.f;
     for (int k0 = 0; k0 < total; k0 += BATCH) {
@@ -318,8 +327,7 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
     const float l = __ldcg(part_stats + s_off(slot) + 1);
     if (l > 0.f) M = fmaxf(M, __ldcg(part_stats + s_off(slot)));
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  M = flash_engine::cuda::warp_reduce_max(M);
   float L = 0.f;
 #pragma unroll
   for (int k = 0; k < PER; ++k) acc[k] = 0.f;
@@ -355,8 +363,7 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
         for (int e = 0; e < PER; ++e) acc[e] += v[k][e] * w8[k];
     }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  L = flash_engine::cuda::warp_reduce_sum(L);
   M_out = M;
   L_out = L;
 }
@@ -380,9 +387,10 @@ struct Pending {
 
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
 struct Cfg {
-  static constexpr int HPC = 8 * NT;       // query heads per CTA
-  static constexpr int HALVES = D / 64;    // 128-byte swizzle atoms per row
-  static constexpr int TILE = BS * D * 2;  // bytes of one page of K (or V)
+  static constexpr bool F32 = std::is_same<T, float>::value;
+  static constexpr int HPC = F32 ? 4 * NT : 8 * NT;  // query heads per CTA
+  static constexpr int HALVES = D / 64;    // 128-byte swizzle atoms per row (16-bit caches)
+  static constexpr int TILE = BS * D * static_cast<int>(sizeof(T));  // one page of K (or V)
   static constexpr int STAGE = 2 * TILE;
   static constexpr int CSTRIDE = D + 4;    // padded row of the merge buffer (floats)
   static constexpr int NTHREADS = (NCW + 1) * 32;
@@ -393,12 +401,27 @@ struct Cfg {
 };
 
 // Two CTAs of NCW + 1 warps share an SM only if three warps fit one SM sub-partition's
-// 16K registers: at most 168 registers a thread (NT = 1). NT = 2 keeps one CTA per SM.
-template <int NT>
-constexpr int decode_max_regs() { return NT == 1 ? 168 : 255; }
+// 16K registers: at most 168 registers a thread (bf16/fp16 NT = 1, and the fp32 decode).
+// bf16/fp16 NT = 2 keeps one CTA per SM.
+template <typename T, int NT>
+struct DecodeRegs {
+  static constexpr int value = (NT == 1 || std::is_same<T, float>::value) ? 168 : 255;
+};
+
+// Stages of each consumer warp's private ring: about 64 KB of pages per CTA, 1 to 4
+// stages a warp.
+template <typename T, int D, int BS, int NCW>
+constexpr int ring_depth() {
+#ifndef FE_DECODE_RING_BYTES
+#define FE_DECODE_RING_BYTES 65536
+#endif
+  constexpr int stage = 2 * BS * D * static_cast<int>(sizeof(T));
+  constexpr int dpt = FE_DECODE_RING_BYTES / (NCW * stage);
+  return dpt < 1 ? 1 : dpt > 4 ? 4 : dpt;
+}
 
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE, int KVL>
-__global__ void __maxnreg__(decode_max_regs<NT>())
+__global__ void __maxnreg__((DecodeRegs<T, NT>::value))
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
@@ -440,6 +463,16 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   const int HC = p.head_chunks, Y = Hkv * HC;
   const bool flat = p.flat != 0;
   const bool direct_final = p.direct_final != 0;
+  // Split-KV scratch: the caller's workspace, or a slot of the library's own.
+  float* part_o = p.part_o;
+  float* part_ml = p.part_ml;
+  int* counters = p.counters;
+  if (p.ws_slot >= 0) {
+    float* base = g_stream_scratch + static_cast<size_t>(p.ws_slot) * kStreamSlotFloats;
+    counters = reinterpret_cast<int*>(base);
+    part_o = base + kCounterSlots;
+    part_ml = part_o + static_cast<size_t>(gridDim.x) * 2 * HPC * D;
+  }
 
   // Until griddepcontrol.wait below, this grid touches only shared memory and the two
   // inputs that no kernel of this library writes, context_lens and block_tables: the
@@ -491,7 +524,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
 
   if (warp == NCW) {
     // ===================================================== producer warp
-    if (lane == 0 && KVL == kKvFlat) {
+    if (lane == 0 && KVL == kKvFlat && !C::F32) {
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
     }
@@ -556,14 +589,15 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
 #ifdef FE_DEBUG_CHECKS
               if (static_cast<long long>(y) + BS > p.dbg_kv_rows) atomicOr(p.err, 1u << 8);
 #endif
-              if constexpr (KVL == kKvFlat) {
+              if constexpr (KVL == kKvFlat && !C::F32) {
 #pragma unroll
                 for (int h = 0; h < HALVES; ++h) {
                   tma_load_2d(ks + h * BS * 128, &kmap, h * 64, y, &full[s], pol);
                   tma_load_2d(vs + h * BS * 128, &vmap, h * 64, y, &full[s], pol);
                 }
               } else {
-                const size_t off = static_cast<size_t>(y) * D * 2;  // page = BS*D elements
+                // vLLM layout, or an fp32 page: one contiguous chunk of K and of V
+                const size_t off = static_cast<size_t>(y) * D * sizeof(T);  // page = BS*D elements
                 bulk_load(ks, static_cast<const uint8_t*>(p.k_cache) + off, TILE, &full[s], pol);
                 bulk_load(vs, static_cast<const uint8_t*>(p.v_cache) + off, TILE, &full[s], pol);
               }
@@ -613,17 +647,20 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
   // dimension pair (2i, 2i+1) with i = ks*8 + 4j + c, so the optional rotary
   // embedding (src/fused_rope.cu:33-43 arithmetic: x0 c - x1 s, x0 s + x1 c) is
   // applied pair by pair in fp32 before the repack.
-  auto load_q = [&](uint32_t (&dst)[NT][D / 16][2], const Seg& sg) {
-    const bool rope = p.rope_cos != nullptr;
-    int pos = 0;
-    if (rope) {
-      pos = __ldg(p.context_lens + sg.seq) - 1;
-      if (pos < 0) pos = 0;
-      if (pos >= p.rope_max_pos) {
-        if (lane == 0) atomicOr(p.err, kErrBadBlock);
-        pos = p.rope_max_pos - 1;
-      }
+  // Rotary position of a segment's query token: context_len - 1, clamped to the table.
+  auto rope_pos = [&](const Seg& sg) -> int {
+    int pos = __ldg(p.context_lens + sg.seq) - 1;
+    if (pos < 0) pos = 0;
+    if (pos >= p.rope_max_pos) {
+      if (lane == 0) atomicOr(p.err, kErrBadBlock);
+      pos = p.rope_max_pos - 1;
     }
+    return pos;
+  };
+  auto load_q = [&](uint32_t (&dst)[NT][D / 16][2], const Seg& sg) {
+    if constexpr (!C::F32) {
+    const bool rope = p.rope_cos != nullptr;
+    const int pos = rope ? rope_pos(sg) : 0;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int gh = sg.hc * HPC + nt * 8 + g;
@@ -647,6 +684,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
           dst[nt][ks][j] = w;
         }
       }
+    }
     }
   };
 
@@ -703,6 +741,179 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     }
   }
 
+  // fp32 consumer (CUDA cores). Lane i owns head dims [i*CW, (i+1)*CW) of every row,
+  // CW = D/32; q of the segment's HPC heads sits in registers, pre-scaled by
+  // scale*log2(e). Per group of TB = 32/HPC tokens of a page the warp forms the TB x HPC
+  // partial dot products, reduce-scatters them (five butterfly steps, 31 shuffles) so
+  // that lane l holds the score of token l / HPC, head l % HPC, updates the online
+  // softmax with one exponential per lane, and accumulates P V with each p taken by
+  // shuffle from the lane that holds it. The sum l stays split over the lanes of a head
+  // until the segment ends.
+  auto consume_f32 = [&](const Seg& sg, int npg, int first, int gb, bool& okr) {
+    if constexpr (C::F32) {
+      constexpr int HG = HPC;
+      constexpr int TB = 32 / HG;
+      constexpr int CW = D / 32;
+      using VecT = typename std::conditional<CW == 4, float4, float2>::type;
+      float qr[HG][CW];
+      {
+        const bool rope = p.rope_cos != nullptr;
+        const int pos = rope ? rope_pos(sg) : 0;
+        const float* qb = static_cast<const float*>(p.q);
+#pragma unroll
+        for (int h = 0; h < HG; ++h) {
+          const int gh = sg.hc * HG + h;
+          const bool v = gh < G;
+          float x[CW];
+          if (v) {
+            const VecT t = __ldg(reinterpret_cast<const VecT*>(
+                qb + (static_cast<size_t>(sg.seq) * p.num_heads + sg.kvh * G + gh) * D +
+                lane * CW));
+            x[0] = t.x;
+            x[1] = t.y;
+            if constexpr (CW == 4) {
+              x[2] = t.z;
+              x[3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < CW; ++cc) x[cc] = 0.f;
+          }
+          if (rope && v) {
+#pragma unroll
+            for (int cc = 0; cc < CW; cc += 2) {
+              const int i = (lane * CW + cc) >> 1;
+              const float cs = __ldg(p.rope_cos + static_cast<size_t>(pos) * (D / 2) + i);
+              const float sn = __ldg(p.rope_sin + static_cast<size_t>(pos) * (D / 2) + i);
+              const float x0 = x[cc], x1 = x[cc + 1];
+              x[cc] = x0 * cs - x1 * sn;
+              x[cc + 1] = x0 * sn + x1 * cs;
+            }
+          }
+#pragma unroll
+          for (int cc = 0; cc < CW; ++cc) qr[h][cc] = x[cc] * sl;
+        }
+      }
+      float acc[HG][CW], mh[HG];
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        mh[h] = NEG_INF;
+#pragma unroll
+        for (int cc = 0; cc < CW; ++cc) acc[h][cc] = 0.f;
+      }
+      float m_own = NEG_INF, l_part = 0.f;  // head lane % HG
+      for (int i = first; i < npg && okr; i += NCW) {
+        const int gi = gb + i;
+        const SO so(gi);
+        const int s = so.s;
+        const bool waited = mbar_wait(&full[s], so.round & 1);
+        if (!__all_sync(0xffffffffu, waited)) {
+          if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
+          okr = false;
+          break;
+        }
+        const int t0 = (sg.p0 + i) * BS;
+        const int vlo = max(sg.lo - t0, 0), vhi = min(sg.hi - t0, BS);
+        if (stage_valid[s]) {
+          const float* kt = reinterpret_cast<const float*>(smem + s * STAGE);
+          const float* vt = kt + BS * D;
+#pragma unroll 1
+          for (int j0 = 0; j0 < BS; j0 += TB) {
+            if (j0 >= vhi || j0 + TB <= vlo) continue;  // no token of the window here
+            float kv[TB][CW], vv[TB][CW];
+#pragma unroll
+            for (int j = 0; j < TB; ++j) {
+              const VecT a = *reinterpret_cast<const VecT*>(kt + (j0 + j) * D + lane * CW);
+              const VecT b = *reinterpret_cast<const VecT*>(vt + (j0 + j) * D + lane * CW);
+              kv[j][0] = a.x;
+              kv[j][1] = a.y;
+              vv[j][0] = b.x;
+              vv[j][1] = b.y;
+              if constexpr (CW == 4) {
+                kv[j][2] = a.z;
+                kv[j][3] = a.w;
+                vv[j][2] = b.z;
+                vv[j][3] = b.w;
+              }
+            }
+            float x[32];  // x[j * HG + h]: this lane's part of q_h . k_j
+#pragma unroll
+            for (int j = 0; j < TB; ++j)
+#pragma unroll
+              for (int h = 0; h < HG; ++h) {
+                float t = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < CW; ++cc) t = fmaf(qr[h][cc], kv[j][cc], t);
+                x[j * HG + h] = t;
+              }
+            // reduce-scatter: the step over lane bit `half` keeps the half of the
+            // remaining indices selected by that bit; x[0] ends as index = lane
+#pragma unroll
+            for (int half = 16; half >= 1; half >>= 1) {
+              const bool up = lane & half;
+#pragma unroll
+              for (int k = 0; k < half; ++k) {
+                const float send = up ? x[k] : x[k + half];
+                const float keep = up ? x[k + half] : x[k];
+                x[k] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+              }
+            }
+            const int tok = j0 + lane / HG;
+            const bool v_own = tok >= vlo && tok < vhi;
+            const float s_own = v_own ? x[0] : NEG_INF;  // rows outside may hold anything
+            float mx = s_own;
+#pragma unroll
+            for (int off = HG; off < 32; off <<= 1)
+              mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m_own, mx);  // finite: the group has a valid token
+            const float p_own = v_own ? ex2(s_own - m_new) : 0.f;
+            l_part = fmaf(l_part, ex2(m_own - m_new), p_own);
+            m_own = m_new;
+#pragma unroll
+            for (int h = 0; h < HG; ++h) {
+              const float mn = __shfl_sync(0xffffffffu, m_new, h);  // lane h: head h
+              const float corr = ex2(mh[h] - mn);
+              mh[h] = mn;
+#pragma unroll
+              for (int cc = 0; cc < CW; ++cc) acc[h][cc] *= corr;
+            }
+#pragma unroll
+            for (int j = 0; j < TB; ++j) {
+              if (j0 + j < vlo || j0 + j >= vhi) continue;  // warp-uniform; V may be NaN
+#pragma unroll
+              for (int h = 0; h < HG; ++h) {
+                const float pj = __shfl_sync(0xffffffffu, p_own, j * HG + h);
+#pragma unroll
+                for (int cc = 0; cc < CW; ++cc) acc[h][cc] = fmaf(pj, vv[j][cc], acc[h][cc]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // this warp's state of the segment into the merge buffers
+      float lsum = l_part;
+#pragma unroll
+      for (int off = HG; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+      if (lane < HG) {
+        comb_m[warp * HPC + lane] = m_own;
+        comb_l[warp * HPC + lane] = lsum;
+      }
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        VecT o;
+        o.x = acc[h][0];
+        o.y = acc[h][1];
+        if constexpr (CW == 4) {
+          o.z = acc[h][2];
+          o.w = acc[h][3];
+        }
+        *reinterpret_cast<VecT*>(comb_o + (warp * HPC + h) * CSTRIDE + lane * CW) = o;
+      }
+    }
+  };
+
   int gbase = 0;  // pages consumed by this CTA before the current segment
   bool ok = true;
   Seg sg, sn;
@@ -713,6 +924,11 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
     have_n = it.next(sn);
   }
   while (have) {
+    const int npg = max(0, sg.p1 - sg.p0);
+    const int first = ((warp - gbase) % NCW + NCW) % NCW;
+    if constexpr (C::F32) {
+      consume_f32(sg, npg, first, gbase, ok);
+    } else {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -731,8 +947,6 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
       for (int mt = 0; mt < D / 16; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
     }
 
-    const int npg = max(0, sg.p1 - sg.p0);
-    const int first = ((warp - gbase) % NCW + NCW) % NCW;
     for (int i = first; i < npg && ok; i += NCW) {
       const int gi = gbase + i;
       const SO so(gi);
@@ -859,9 +1073,8 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    gbase += npg;
 
-    // ---- merge the NCW warp states of this segment
+    // ---- this warp's state of the segment into the merge buffers
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -891,6 +1104,8 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
         r0[8] = o[nt][mt][2];
         r0[CSTRIDE + 8] = o[nt][mt][3];
       }
+    }  // bf16 / fp16 consumer
+    gbase += npg;
     __syncwarp();
     named_bar(1, NCW * 32);
 
@@ -920,10 +1135,10 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
         emit_partial(row, dim, O, L > 0.f ? M : NEG_INF, L);
       } else {
         const size_t fix = (static_cast<size_t>(blockIdx.x) * 2 + sg.slot) * HPC + hl;
-        p.part_o[fix * D + dim] = O;
+        part_o[fix * D + dim] = O;
         if (dim == 0) {
-          p.part_ml[fix * 2 + 0] = M;
-          p.part_ml[fix * 2 + 1] = L;
+          part_ml[fix * 2 + 0] = M;
+          part_ml[fix * 2 + 1] = L;
         }
       }
     }
@@ -956,8 +1171,8 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
       // both updates in flight together; acq_rel at GPU scope is the release of this
       // CTA's pieces and the acquire of the earlier arrivals' pieces
       const bool has0 = pend[0].nslots > 1, has1 = pend[1].nslots > 1;
-      const int old0 = has0 ? atom_add_acq_rel_gpu(p.counters + pend[0].cfirst, 1) : 0;
-      const int old1 = has1 ? atom_add_acq_rel_gpu(p.counters + pend[1].cfirst, 1) : 0;
+      const int old0 = has0 ? atom_add_acq_rel_gpu(counters + pend[0].cfirst, 1) : 0;
+      const int old1 = has1 ? atom_add_acq_rel_gpu(counters + pend[1].cfirst, 1) : 0;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         Pending& pd = pend[k];
@@ -965,7 +1180,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
         const int old = k == 0 ? old0 : old1;
         if (old >= pd.nslots) atomicOr(p.err, kErrWorkspace);
         pd.last = old == pd.nslots - 1;
-        if (pd.last) st_relaxed_gpu(p.counters + pd.cfirst, 0);  // zero for the next launch
+        if (pd.last) st_relaxed_gpu(counters + pd.cfirst, 0);  // zero for the next launch
       }
     }
     named_bar(2, NCW * 32);
@@ -981,7 +1196,7 @@ __global__ void __maxnreg__(decode_max_regs<NT>())
         if (gh >= G) break;
         float M, L, acc[PER];
         lse_combine_warp<PER, 8>(
-            p.part_o, p.part_ml, pd.nslots, D,
+            part_o, part_ml, pd.nslots, D,
             [&](int j) -> size_t {
               return (static_cast<size_t>(pd.cfirst + j) * 2 + (j == 0 ? pd.kfirst : 0)) * HPC +
                      hl;
@@ -1133,12 +1348,10 @@ __global__ void __launch_bounds__(256) xmerge_kernel(const XMergeParams xp) {
     const float m = __uint_as_float(static_cast<unsigned>(wm));
     const float l = lane < W ? __uint_as_float(static_cast<unsigned>(wl)) : 0.f;
     float M = l > 0.f ? m : NEG_INF;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    M = flash_engine::cuda::warp_reduce_max(M);
     const float wgt = l > 0.f ? ex2(m - M) : 0.f;
     float L = l * wgt;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    L = flash_engine::cuda::warp_reduce_sum(L);
     float acc[PER];
 #pragma unroll
     for (int e = 0; e < PER; ++e) acc[e] = 0.f;
@@ -1183,15 +1396,14 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
                               int* grid_out, cudaStream_t stream) {
   constexpr int NCW = 4;
   // NCW consumer warps x DEPTH private stages each; ~64 KB of stages per CTA.
-  constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
-  constexpr int NSTAGE = NCW * DEPTH;
+  constexpr int NSTAGE = NCW * ring_depth<T, D, BS, NCW>();
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
   auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE, KVL>;
   const int smem = C::smem_bytes(p.num_seqs);
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   CUtensorMap km = {}, vm = {};
-  if (KVL == kKvFlat) {
+  if (KVL == kKvFlat && !C::F32) {
     const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
     e = encode_tma_2d_b16(&km, kc, bf16, D, kv_rows, D, 64, BS);
     if (e != cudaSuccess) return e;
@@ -1202,7 +1414,11 @@ static cudaError_t launch_cfg(const Params& p, const void* kc, const void* vc, l
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, C::NTHREADS, smem);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
-  const int grid = min(sm_count() * occ, kCounterSlots);
+#ifdef FE_DECODE_CTAS_PER_SM
+  occ = min(occ, FE_DECODE_CTAS_PER_SM);  // build-time tuning of the resident grid
+#endif
+  int grid = min(sm_count() * occ, kCounterSlots);
+  if (p.max_grid > 0) grid = min(grid, p.max_grid);
   if (grid_out) *grid_out = grid;
   Params pp = p;
   pp.dbg_kv_rows = kv_rows;
@@ -1237,10 +1453,12 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
   FE_CASE(128, 32, 2, kKvFlat)
   FE_CASE(64, 32, 1, kKvFlat)
   FE_CASE(64, 32, 2, kKvFlat)
-  FE_CASE(128, 16, 1, kKvVllm)
-  FE_CASE(128, 16, 2, kKvVllm)
-  FE_CASE(64, 16, 1, kKvVllm)
-  FE_CASE(64, 16, 2, kKvVllm)
+  if constexpr (!std::is_same<T, float>::value) {
+    FE_CASE(128, 16, 1, kKvVllm)
+    FE_CASE(128, 16, 2, kKvVllm)
+    FE_CASE(64, 16, 1, kKvVllm)
+    FE_CASE(64, 16, 2, kKvVllm)
+  }
 #undef FE_CASE
   return cudaErrorInvalidValue;
 }
@@ -1248,8 +1466,7 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
 template <typename T, int D, int BS, int NT>
 static long long grid_max_cfg() {
   constexpr int NCW = 4;
-  constexpr int DEPTH = (D * BS <= 1024) ? 4 : (D * BS <= 2048) ? 2 : 1;
-  constexpr int NSTAGE = NCW * DEPTH;
+  constexpr int NSTAGE = NCW * ring_depth<T, D, BS, NCW>();
   using C = Cfg<T, D, BS, NT, NCW, NSTAGE>;
   auto kern = paged_decode_kernel<T, D, BS, NT, NCW, NSTAGE, kKvFlat>;
   const int smem = C::smem_bytes(1);
@@ -1261,17 +1478,25 @@ static long long grid_max_cfg() {
   return g < kCounterSlots ? g : kCounterSlots;
 }
 
-FixupLayout fixup_layout(int head_dim, int block_size, int nt) {
+template <typename T>
+static long long grid_max_of(int head_dim, int block_size, int nt) {
   long long g = -1;
 #define FE_CASE(D_, BS_, NT_)                                                           \
-  if (head_dim == D_ && block_size == BS_ && nt == NT_) g = grid_max_cfg<__nv_bfloat16, D_, BS_, NT_>();
+  if (head_dim == D_ && block_size == BS_ && nt == NT_) g = grid_max_cfg<T, D_, BS_, NT_>();
   FE_CASE(128, 16, 1) FE_CASE(128, 16, 2) FE_CASE(64, 16, 1) FE_CASE(64, 16, 2)
   FE_CASE(128, 32, 1) FE_CASE(128, 32, 2) FE_CASE(64, 32, 1) FE_CASE(64, 32, 2)
 #undef FE_CASE
+  return g;
+}
+
+FixupLayout fixup_layout(int dtype, int head_dim, int block_size, int nt) {
+  // bf16 and fp16 kernels share their shapes and occupancy
+  const long long g = dtype == kF32 ? grid_max_of<float>(head_dim, block_size, nt)
+                                    : grid_max_of<__nv_bfloat16>(head_dim, block_size, nt);
   FixupLayout f{-1, 0, -1};
   if (g < 0) return f;
   f.grid_max = g;
-  f.slot_rows = g * 2 * (8LL * nt);
+  f.slot_rows = g * 2 * heads_per_cta(dtype, nt);
   f.floats = kCounterSlots + f.slot_rows * (head_dim + 2);
   return f;
 }
@@ -1309,6 +1534,8 @@ template cudaError_t launch_decode<__nv_bfloat16>(const Params&, int, int, const
                                                   long long, int, int, int*, cudaStream_t);
 template cudaError_t launch_decode<half>(const Params&, int, int, const void*, const void*,
                                          long long, int, int, int*, cudaStream_t);
+template cudaError_t launch_decode<float>(const Params&, int, int, const void*, const void*,
+                                          long long, int, int, int*, cudaStream_t);
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream) {
   if (mp.rows <= 0) return cudaSuccess;

@@ -41,16 +41,19 @@ inline long long x_buffer_bytes(int world, int max_rows, int d) {
 }
 
 struct Params {
-  const void* q;           // [S, H, D] (T)
+  const void* q;           // [S, H, D] (T; float for the fp32 decode)
   const void* k_cache;     // used by the bulk-copy (vLLM layout) path
   const void* v_cache;
   void* out;               // [S, H, D] (T), written for single-split sequences
   const int* block_tables; // [S, max_blocks_per_seq]
   const int* context_lens; // [S]
-  float* part_o;           // fixup slots [grid][2][8*NT][D] fp32 partial O (unnormalised)
-  float* part_ml;          // fixup slots [grid][2][8*NT][2] (m in log2 units, l)
+  float* part_o;           // fixup slots [grid][2][HPC][D] fp32 partial O (unnormalised)
+  float* part_ml;          // fixup slots [grid][2][HPC][2] (m in log2 units, l)
   int* counters;           // flat mode: [grid] piece-arrival counters; zero before the
                            // launch, and left zero by it
+  int ws_slot;             // >= 0: counters and fixup slots live in slot ws_slot of the
+                           // library's static stream scratch (part_o etc. unused)
+  int max_grid;            // > 0: at most this many CTAs (the fixup slots must fit)
   float* merged_o;         // partials mode: [S, H, D] merged partial of whole rows
   float* merged_ml;        // partials mode: [S, H, 2]
   int num_seqs, num_heads, num_kv_heads, max_blocks_per_seq;
@@ -110,7 +113,8 @@ inline int pages_per_split_for(int max_pages, int splits) {
   return (max_pages + splits - 1) / splits;
 }
 
-// Launches the decode kernel; *grid_out receives its CTA count.
+// Launches the decode kernel; *grid_out receives its CTA count. T is __nv_bfloat16,
+// half or float (fp32 cache: flat layout only).
 template <typename T>
 cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const void* k_cache,
                           const void* v_cache, long long kv_rows, int nt, int kv_layout,
@@ -124,11 +128,32 @@ cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t strea
 constexpr int kCounterSlots = 1024;  // also the largest flat-mode grid
 struct FixupLayout {
   long long grid_max;   // largest CTA count of the decode grid on this device
-  long long slot_rows;  // grid_max * 2 * 8 * NT
+  long long slot_rows;  // grid_max * 2 * HPC
   long long floats;     // kCounterSlots + slot_rows * (D + 2)
 };
+// Element type of the decode (q, cache and output).
+enum DecodeType : int { kBf16 = 0, kF16 = 1, kF32 = 2 };
+// Query heads one CTA segment covers: 8 * nt for the tensor-core (bf16/fp16) decode,
+// 4 * nt for the fp32 decode.
+inline int heads_per_cta(int dtype, int nt) { return dtype == kF32 ? 4 * nt : 8 * nt; }
+// nt of a head group of G query heads.
+inline int decode_nt(int dtype, int G) { return G <= heads_per_cta(dtype, 1) ? 1 : 2; }
 // Layout for this shape, or floats = -1 if the shape is unsupported.
-FixupLayout fixup_layout(int head_dim, int block_size, int nt);
+FixupLayout fixup_layout(int dtype, int head_dim, int block_size, int nt);
+
+// Split-KV scratch owned by the library for the entry points whose reference
+// signature passes none (the v1 paged launchers): kStreamSlots slots of
+// kStreamSlotFloats floats in a static __device__ array of paged_decode.cu (zero
+// when the module loads; the kernel names it directly, so no host-side address is
+// needed). A launch with Params::ws_slot = k keeps its counters at the start of slot
+// k and its fixup slots after them, and must be capped (Params::max_grid) so that
+// kCounterSlots + grid * 2 * HPC * (D + 2) <= kStreamSlotFloats.
+constexpr int kStreamSlots = 4;
+constexpr long long kStreamSlotFloats = 1LL << 20;
+inline int slot_grid_cap(int dtype, int head_dim, int nt) {
+  const long long per_cta = 2LL * heads_per_cta(dtype, nt) * (head_dim + 2);
+  return static_cast<int>((kStreamSlotFloats - kCounterSlots) / per_cta);
+}
 
 }  // namespace paged
 }  // namespace fe

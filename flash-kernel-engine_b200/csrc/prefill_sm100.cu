@@ -64,6 +64,7 @@ struct PCfg {
 struct PParams {
   void* out;
   int N, M, BH;
+  int d_out;  // head dim of the tensors: D, or 32 when the D = 64 kernel runs d = 32
   int causal;
   float scale_log2;
   unsigned* err;
@@ -455,9 +456,10 @@ __global__ void __launch_bounds__(384, 1)
       if (__all_sync(0xffffffffu, got)) {
         tc::fence_after_sync();
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + (static_cast<size_t>(bh) * p.N + r) * D;
+        T* orow = reinterpret_cast<T*>(p.out) + (static_cast<size_t>(bh) * p.N + r) * p.d_out;
 #pragma unroll
         for (int c4 = 0; c4 < D / 32; ++c4) {
+          if (c4 * 32 >= p.d_out) break;  // d = 32 on the D = 64 kernel
           uint32_t u[32];
           tc::ld32(tO + c4 * 32, u);
           tc::wait_ld();
@@ -488,9 +490,13 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 // ---------------------------------------------------------------------------
+// d: the tensors' head dim, D or (D = 64) 32. For d = 32 the tensor maps span the 32
+// real columns and load 64-column boxes: TMA fills columns 32..63 with zeros, so Q K^T
+// and P V are those of d = 32 (the extra products are zero) and only 32 columns are
+// stored.
 template <typename T, int D>
 static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o, int B, int H,
-                            int N, int M, int causal, float scale, cudaStream_t st) {
+                            int N, int M, int d, int causal, float scale, cudaStream_t st) {
   using C = PCfg<D>;
   auto kern = fa_prefill_kernel<T, D>;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
@@ -498,23 +504,24 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const long long BH = static_cast<long long>(B) * H;
   CUtensorMap qm, km, vm;
-  e = encode_tma_3d_b16(&qm, q, bf16, D, N, BH, 64, 128);
+  e = encode_tma_3d_b16(&qm, q, bf16, d, N, BH, 64, 128);
   if (e != cudaSuccess) return e;
-  e = encode_tma_3d_b16(&km, k, bf16, D, M, BH, 64, 128);
+  e = encode_tma_3d_b16(&km, k, bf16, d, M, BH, 64, 128);
   if (e != cudaSuccess) return e;
-  e = encode_tma_3d_b16(&vm, v, bf16, D, M, BH, 64, 128);
+  e = encode_tma_3d_b16(&vm, v, bf16, d, M, BH, 64, 128);
   if (e != cudaSuccess) return e;
   PParams p;
   p.out = o;
   p.N = N;
   p.M = M;
+  p.d_out = d;
   p.BH = static_cast<int>(BH);
   p.causal = causal;
   p.scale_log2 = scale * kLog2e;
   p.err = device_error_word();
   if (!p.err) return cudaErrorInitializationError;
   // heads per scheduling group: their K and V together within ~32 MB of L2
-  const long long kv_bytes = 2LL * M * D * 2;
+  const long long kv_bytes = 2LL * M * d * 2;
   p.group = static_cast<int>(std::max(1LL, std::min<long long>(BH, (32LL << 20) / kv_bytes)));
   const long long blocks = BH * ((N + 255) / 256);
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
@@ -535,17 +542,18 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
 cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o, int B, int H,
                            int N, int M, int d, int causal, float scale, bool is_bf16,
                            cudaStream_t stream) {
-  if (!(d == 64 || d == 128)) return cudaErrorInvalidValue;
+  if (!(d == 32 || d == 64 || d == 128)) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15)
     return cudaErrorInvalidValue;
   if (static_cast<long long>(B) * H > 65535) return cudaErrorInvalidValue;
   if (is_bf16) {
-    if (d == 128) return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, causal, scale, stream);
-    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, causal, scale, stream);
+    if (d == 128)
+      return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
   }
-  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, causal, scale, stream);
-  return launch_d<half, 64>(q, k, v, o, B, H, N, M, causal, scale, stream);
+  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+  return launch_d<half, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
 }
 
 }  // namespace prefill

@@ -20,6 +20,7 @@ Differences, all deliberate:
 
 from __future__ import annotations
 
+import contextlib
 import math
 
 import torch
@@ -27,6 +28,13 @@ import torch
 from . import _lib
 
 _lib_c = _lib.lib
+
+
+def _on(device):
+    """Context that makes `device` current, or nothing when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _stream():
@@ -78,7 +86,7 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
           torch.float16: _lib_c.fe_flash_attention_forward_fp16}.get(q.dtype)
     if fn is None:
         raise TypeError(f"unsupported dtype {q.dtype}")
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.check(fn(_ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
                       _scale_arg(scale, d), _stream()), "flash_attention")
     return out
@@ -92,7 +100,7 @@ def naive_attention(q, k, v, is_causal: bool = False, scale: float | None = None
     B, H, N, d = q.shape
     M = k.shape[2]
     out = torch.empty_like(q)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.check(_lib_c.fe_naive_attention_forward_fp32(
             _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
             _scale_arg(scale, d), _stream()), "naive_attention")
@@ -126,8 +134,8 @@ def _paged_shapes(query, key_cache, value_cache, block_tables, context_lens, blo
 
 
 def paged_attention_workspace_floats(num_heads, num_kv_heads, head_dim, block_size=16) -> int:
-    """Float32 elements of workspace the split-KV (v2) bf16 decode needs on the current
-    device for this head configuration (independent of batch and context lengths).
+    """Float32 elements of workspace the split-KV decode needs on the current device
+    for this head configuration (independent of batch, context lengths and dtype).
 
     Allocate it zero-filled (``torch.zeros``): its first 4 KiB hold arrival counters
     that must be zero when a call starts, and every call leaves them at zero, so one
@@ -136,17 +144,69 @@ def paged_attention_workspace_floats(num_heads, num_kv_heads, head_dim, block_si
     n = int(_lib_c.fe_paged_attention_v2_workspace_floats(num_heads, num_kv_heads, head_dim,
                                                           block_size))
     if n == 0:
-        raise ValueError("unsupported head configuration for the bf16 decode")
+        raise ValueError("unsupported head configuration for the split-KV decode")
+    return n
+
+
+# One zero-filled workspace per (device, stream), made on the first call without a
+# caller workspace and kept for the life of the process: it is sized for every
+# supported head configuration, so it is never replaced (a CUDA graph that captured it
+# keeps a valid buffer), and calls on one stream are ordered, so they can share it.
+_WS_CACHE: dict = {}
+_WS_MAX: dict = {}
+# workspace_floats that asks the library for the stream's slot of its own scratch
+# (FE_WORKSPACE_LIBRARY of flash_engine_c.h, with a NULL workspace)
+WORKSPACE_LIBRARY = (1 << 64) - 1
+
+
+def _max_workspace_floats(device_index: int) -> int:
+    n = _WS_MAX.get(device_index)
+    if n is None:
+        n = max(int(_lib_c.fe_paged_attention_v2_workspace_floats(h, 1, d, bs))
+                for h in (1, 16) for d in (64, 128) for bs in (16, 32))
+        _WS_MAX[device_index] = n
     return n
 
 
 def _workspace(query, H, Hkv, d, bs, workspace):
-    n = paged_attention_workspace_floats(H, Hkv, d, bs)
+    """(workspace tensor, floats), or (None, WORKSPACE_LIBRARY) while the stream is being
+    captured before it has a cached workspace: nothing may be allocated and zero-filled
+    then, so the call uses the stream's slot of the library's own scratch."""
     if workspace is None:
-        return torch.zeros(n, dtype=torch.float32, device=query.device), n
+        stream = torch.cuda.current_stream(query.device)
+        key = (query.device.index, int(stream.cuda_stream))
+        ws = _WS_CACHE.get(key)
+        if ws is None:
+            if torch.cuda.is_current_stream_capturing():
+                return None, WORKSPACE_LIBRARY
+            with _on(query.device):
+                n = _max_workspace_floats(query.device.index)
+                ws = torch.zeros(n, dtype=torch.float32, device=query.device)
+            _WS_CACHE[key] = ws
+        return ws, ws.numel()
+    n = paged_attention_workspace_floats(H, Hkv, d, bs)
     if workspace.dtype != torch.float32 or workspace.numel() < n or not workspace.is_cuda:
         raise ValueError(f"workspace must be a CUDA float32 tensor of >= {n} elements")
     return workspace, workspace.numel()
+
+
+def _required_workspace(query, H, Hkv, d, bs, workspace):
+    ws, n = _workspace(query, H, Hkv, d, bs, workspace)
+    if ws is None:
+        raise RuntimeError("the first call on a stream that is being captured needs an "
+                           "explicit workspace (make one eager call first, or pass one)")
+    return ws, n
+
+
+def _persistent_decode_ok(query, key_cache, value_cache, out, d, block_size, kv_layout):
+    """Shapes the persistent split-KV decode takes (else the generic fp32 kernel)."""
+    if d not in (64, 128) or block_size not in (16, 32):
+        return False
+    if query.dtype == torch.float32:
+        return (kv_layout == "flat" and key_cache.data_ptr() % 16 == 0
+                and value_cache.data_ptr() % 16 == 0
+                and query.data_ptr() % (16 if d == 128 else 8) == 0)
+    return True
 
 
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
@@ -160,10 +220,15 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
       "flat" -- K and V [num_blocks, Hkv, block_size, d] (the reference's fp32 layout);
       "vllm" -- K [num_blocks, Hkv, d/8, block_size, 8], V [num_blocks, Hkv, d,
                 block_size] (vLLM's x-packed layout; bf16/fp16, block_size 16).
-    bf16 / fp16 use the split-KV kernel (``version`` "auto"/"v2") with a zero-filled
-    float32 ``workspace`` of ``paged_attention_workspace_floats(...)`` elements
-    (allocated here if not given; reuse one across calls), or the single-pass kernel
-    (``version="v1"``, no workspace). fp32 caches use the single-pass fp32 kernel.
+    The persistent split-KV kernel runs bf16, fp16 and fp32 caches (``version``
+    "auto"/"v2"; fp32 with head_dim 64 or 128, block size 16 or 32, 16-byte aligned
+    caches) on a zero-filled float32 ``workspace`` of
+    ``paged_attention_workspace_floats(...)`` elements. Without one, the call uses a
+    workspace cached for the current (device, stream), made on the first such call.
+    A first call on a stream that is being captured into a CUDA graph uses the stream's
+    slot of the library's own scratch instead (nothing is allocated during a capture).
+    ``version="v1"`` runs the single-pass kernel (no workspace). Other fp32 shapes run
+    the generic single-pass fp32 kernel.
 
     ``rope=(cos, sin)`` (bf16/fp16): float32 CUDA tables [max_pos, d/2]; each query is
     rotated at position context_len - 1 inside the kernel (pairs (2i, 2i+1), the
@@ -177,16 +242,20 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
     sc = _scale_arg(scale, d)
     if max_context_len is None:
         max_context_len = maxb * block_size
-    with torch.cuda.device(query.device):
-        if query.dtype == torch.float32:
-            if kv_layout != "flat":
-                raise ValueError("the fp32 decode takes the flat cache layout")
+    if query.dtype == torch.float32 and kv_layout != "flat":
+        raise ValueError("the fp32 decode takes the flat cache layout")
+    with _on(query.device):
+        if query.dtype == torch.float32 and not _persistent_decode_ok(
+                query, key_cache, value_cache, out, d, block_size, kv_layout):
+            if rope is not None:
+                raise ValueError("rope with an fp32 cache needs head_dim 64/128, block size "
+                                 "16/32 and 16-byte aligned tensors")
             _lib.check(_lib_c.fe_paged_attention_v1_fp32(
                 _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(out), _ptr(block_tables),
                 _ptr(context_lens), S, H, Hkv, d, block_size, int(max_context_len), maxb, nb, sc,
                 _stream()), "paged_attention")
-        elif query.dtype in (torch.bfloat16, torch.float16):
-            dt = 0 if query.dtype == torch.bfloat16 else 1
+        elif query.dtype in (torch.bfloat16, torch.float16, torch.float32):
+            dt = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}[query.dtype]
             lay = 0 if kv_layout == "flat" else 1
             if version == "v1":
                 ws, n = None, 0
@@ -221,12 +290,12 @@ def paged_decode_partials(query, key_cache, value_cache, block_tables, context_l
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
                                            context_lens, block_size)
     dev = query.device
-    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+    ws, n = _required_workspace(query, H, Hkv, d, block_size, workspace)
     if out is None:
         out = torch.empty((S, H, d), dtype=torch.float32, device=dev)
     if out_stats is None:
         out_stats = torch.empty((S, H, 2), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.check(_lib_c.fe_paged_decode_partials_bf16(
             _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
             _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
@@ -255,11 +324,11 @@ def paged_decode_kv_exchange(query, key_cache, value_cache, block_tables, contex
         raise TypeError("the KV-range exchange decode takes bf16")
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
                                            context_lens, block_size)
-    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+    ws, n = _required_workspace(query, H, Hkv, d, block_size, workspace)
     if out is None:
         out = torch.empty_like(query)
     arr = (ctypes.c_void_p * len(xbufs))(*[int(x) for x in xbufs])
-    with torch.cuda.device(query.device):
+    with _on(query.device):
         _lib.check(_lib_c.fe_paged_decode_kv_exchange_bf16(
             _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
             _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
@@ -282,7 +351,7 @@ def merge_partials(part_out, part_stats, ranks: int, parts_per_rank: int, out_dt
         out = torch.empty((rows, d), dtype=dt, device=part_out.device)
     if code == 2 and out_stats is None:
         out_stats = torch.empty((rows, 2), dtype=torch.float32, device=part_out.device)
-    with torch.cuda.device(part_out.device):
+    with _on(part_out.device):
         _lib.check(_lib_c.fe_merge_partials(
             _ptr(part_out), _ptr(part_stats), rows, ranks, parts_per_rank, d, _ptr(out),
             _ptr(out_stats) if out_stats is not None else None, code, _stream()),
@@ -311,7 +380,7 @@ def flash_decoding(query, key, value, num_splits: int = 4, scale: float | None =
         ss = torch.empty((B, H, num_splits, 2), dtype=torch.float32, device=query.device)
     else:
         so, ss = scratch
-    with torch.cuda.device(query.device):
+    with _on(query.device):
         _lib.check(_lib_c.fe_flash_decoding_forward_fp32(
             _ptr(query), _ptr(key), _ptr(value), _ptr(out), _ptr(so), _ptr(ss), B, H, M, d,
             int(num_splits), _scale_arg(scale, d), _stream()), "flash_decoding")

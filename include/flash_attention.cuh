@@ -33,18 +33,20 @@ struct TilingConfig {
   static constexpr int HEAD_DIM_ = HEAD_DIM;
 };
 
-// fp32: CUDA-core FA2 (1e-3 relative tolerance needs fp32 products). d <= 128.
+// fp32, d <= 128. d = 32, 64, 128 with 16-byte aligned tensors: tcgen05 tensor cores
+// with 3xTF32 products (each fp32 product split into TF32 high and low parts), which
+// hold the 1e-3 relative tolerance; other shapes: a CUDA-core FA2 kernel.
 cudaError_t launch_flash_attention_forward_fp32(const float* d_Q, const float* d_K,
                                                 const float* d_V, float* d_O,
                                                 const AttentionConfig& config,
                                                 cudaStream_t stream = nullptr);
 
-// fp16 in/out, fp32 accumulate: tcgen05 tensor cores. d in {64, 128}.
+// fp16 in/out, fp32 accumulate: tcgen05 tensor cores. d in {32, 64, 128}.
 cudaError_t launch_flash_attention_forward_fp16(const half* d_Q, const half* d_K, const half* d_V,
                                                 half* d_O, const AttentionConfig& config,
                                                 cudaStream_t stream = nullptr);
 
-// bf16 in/out, fp32 accumulate: tcgen05 tensor cores. d in {64, 128}. New.
+// bf16 in/out, fp32 accumulate: tcgen05 tensor cores. d in {32, 64, 128}. New.
 cudaError_t launch_flash_attention_forward_bf16(const __nv_bfloat16* d_Q,
                                                 const __nv_bfloat16* d_K,
                                                 const __nv_bfloat16* d_V, __nv_bfloat16* d_O,

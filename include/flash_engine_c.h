@@ -55,19 +55,24 @@ int fe_get_device_errors(unsigned int* errors_out);
  */
 
 /* fp32. Replaces launch_flash_attention_forward_fp32 (include/flash_attention.cuh:60-67,
- * src/flash_attention.cu:304-345). Any head_dim in 1..256 with head_dim % 4 == 0. */
+ * src/flash_attention.cu:304-345). Any head_dim in 1..128 (the reference dispatches 32,
+ * 64 and 128 and sends others to its naive kernel, which also stops at 128). head_dim
+ * 32, 64 and 128 with 16-byte aligned tensors run a 3xTF32 tcgen05 tensor-core kernel;
+ * other shapes a CUDA-core kernel. Both hold the 1e-3 relative fp32 tolerance. */
 int fe_flash_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
                                     int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                     int is_causal, float softmax_scale, void* stream);
 
 /* fp16 in/out, fp32 accumulate. Replaces launch_flash_attention_forward_fp16
- * (include/flash_attention.cuh:69-76, src/flash_attention.cu:486-524). head_dim 64 or 128. */
+ * (include/flash_attention.cuh:69-76, src/flash_attention.cu:486-524). head_dim 32, 64
+ * or 128 (32 runs the 64 kernel with zero-filled columns), as the reference dispatches
+ * (src/flash_attention.cu:514-521). */
 int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v, void* o,
                                     int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                     int is_causal, float softmax_scale, void* stream);
 
 /* bf16 in/out, fp32 accumulate (tcgen05 / TMEM / TMA kernel). New sibling of the fp16
- * entry with identical parameters. head_dim 64 or 128. */
+ * entry with identical parameters. head_dim 32, 64 or 128. */
 int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v, void* o,
                                     int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                     int is_causal, float softmax_scale, void* stream);
@@ -96,11 +101,10 @@ int fe_naive_attention_forward_fp32(const float* q, const float* k, const float*
 
 /* fp32 cache. Replaces launch_paged_attention_v1_fp32 (include/paged_attention.cuh:39-48,
  * src/paged_attention.cu:181-215). Any block_size >= 1, head_dim % 4 == 0, <= 256.
- * When max_blocks_per_seq * block_size exceeds 512, the key range runs in 512-token
- * splits that a merge kernel combines. The splits' partials go to fp32 scratch the
- * library owns, one block per (device, stream), allocated on the first such call
- * outside a stream capture. Inside a capture with no large enough block yet, the
- * single-pass kernel runs instead. */
+ * head_dim 64 or 128 with block_size 16 or 32 and 16-byte aligned q / caches runs the
+ * persistent split-KV decode of fe_paged_attention_v2_bf16 with fp32 arithmetic on the
+ * stream's library scratch slot (see fe_paged_attention_v1_bf16); other shapes run a
+ * single-pass CUDA-core kernel with one CTA per (sequence, KV head). */
 int fe_paged_attention_v1_fp32(const float* q, const float* k_cache, const float* v_cache,
                                float* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
@@ -120,11 +124,14 @@ int fe_paged_attention_v1_fp16(const void* q, const void* k_cache, const void* v
                                int block_size, int max_context_len, int max_blocks_per_seq,
                                int num_blocks, float scale, void* stream);
 
-/* General tensor-core paged decode: dtype 0 = bf16, 1 = fp16; kv_layout 0 = flat
+/* General paged decode: dtype 0 = bf16, 1 = fp16 (tensor cores), 2 = fp32 (CUDA
+ * cores; flat layout, 16-byte aligned q); kv_layout 0 = flat
  * [num_blocks, Hkv, block_size, d] (K and V), 1 = vLLM x-packed (K [num_blocks, Hkv,
  * d/8, block_size, 8], V [num_blocks, Hkv, d, block_size]; block_size 16). With a
  * workspace (fe_paged_attention_v2_workspace_floats floats) it runs the split-KV
- * path, without one (NULL) the single-pass path.
+ * path, without one (NULL) the single-pass path. workspace = NULL with
+ * workspace_floats = FE_WORKSPACE_LIBRARY runs the split-KV path on the stream's slot
+ * of the library's scratch, as the v1 entries do (see fe_paged_attention_v1_bf16).
  * rope_cos / rope_sin (NULL = off): fp32 tables [rope_max_pos, d/2]; the query of
  * sequence s is rotated at position context_lens[s] - 1 in the kernel prologue,
  * pairs (2i, 2i+1) as in the reference's src/fused_rope.cu:33-43 (the cached keys are
@@ -139,12 +146,19 @@ int fe_paged_attention_ex(const void* q, const void* k_cache, const void* v_cach
 
 /* bf16 cache, v1 calling convention (the caller passes no scratch). New bf16 sibling
  * of launch_paged_attention_v1_fp32. block_size 16 or 32, head_dim 64 or 128.
- * Runs the split-KV kernel of fe_paged_attention_v2_bf16 on a workspace the library
- * allocates on the first call on each (device, stream) (cudaMalloc, about 5 MB, kept
- * until the process exits). Calls made while the stream is being captured into a CUDA
- * graph, before any call on that stream outside the capture, run the single-pass
- * kernel instead (one unit of work per (sequence, KV head), no scratch). The
- * single-pass kernel is also what fe_paged_attention_ex runs without a workspace. */
+ * Runs the split-KV kernel of fe_paged_attention_v2_bf16 on scratch the library owns
+ * and never allocates: FE_STREAM_SCRATCH_SLOTS slots of a static device array (4 MiB
+ * each) that every GPU loading the library holds until the process exits. The first
+ * v1 call on a stream binds a free slot to that (device, stream) for the life of the
+ * process (the per-thread default stream is bound per calling thread); this needs no
+ * allocation and no synchronisation, so it also works while the stream is being
+ * captured into a CUDA graph. Calls on one stream are ordered and share its slot;
+ * a graph that captured a v1 call uses its stream's slot when replayed, so replays
+ * must not overlap other work on that stream. A stream whose handle is destroyed and
+ * reused by a new stream inherits the slot: destroy a stream only once its v1 work has
+ * finished. When every slot is bound, other streams run the single-pass kernel (one
+ * unit of work per (sequence, KV head), no scratch), which is also what
+ * fe_paged_attention_ex runs without a workspace. */
 int fe_paged_attention_v1_bf16(const void* q, const void* k_cache, const void* v_cache,
                                void* out, const int* block_tables, const int* context_lens,
                                int num_seqs, int num_heads, int num_kv_heads, int head_dim,
@@ -170,13 +184,22 @@ int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v
                                int num_blocks, float scale, float* workspace,
                                size_t workspace_floats, void* stream);
 
-/* Workspace floats fe_paged_attention_v2_bf16 and fe_paged_decode_partials_bf16 need
- * on the current device for this head configuration; 0 if the shape is not supported. */
+/* Scratch slots of the v1 entry points (see fe_paged_attention_v1_bf16). */
+#define FE_STREAM_SCRATCH_SLOTS 4
+/* workspace_floats value that asks fe_paged_attention_ex (with workspace = NULL) for the
+ * library's per-stream scratch slot. */
+#define FE_WORKSPACE_LIBRARY ((size_t)-1)
+
+/* Workspace floats the split-KV decode (fe_paged_attention_v2_bf16,
+ * fe_paged_attention_ex with any dtype, fe_paged_decode_partials_bf16) needs on the
+ * current device for this head configuration; 0 if the shape is not supported. */
 size_t fe_paged_attention_v2_workspace_floats(int num_heads, int num_kv_heads, int head_dim,
                                               int block_size);
 
-/* Maximum scratch of fe_paged_attention_v2_bf16_noalloc, in floats (16 MiB). */
-#define FE_NOALLOC_SCRATCH_FLOATS (4 * 1024 * 1024)
+/* Maximum scratch of fe_paged_attention_v2_bf16_noalloc, in floats (17 MiB): the
+ * workspace of the largest decode grid any GPU can launch (1024 CTAs of 16 query
+ * heads at head_dim 128), so the limit does not depend on the device. */
+#define FE_NOALLOC_SCRATCH_FLOATS (4352 * 1024)
 
 /* The split-KV bf16 decode of fe_paged_attention_v2_bf16 for callers that cannot
  * allocate device memory: plugin hosts that own every device buffer and hand a
@@ -192,8 +215,10 @@ size_t fe_paged_attention_v2_workspace_floats(int num_heads, int num_kv_heads, i
  *     current device; make that first call before any stream capture.
  *   - All calls share the one array: calls that can overlap on the GPU (other
  *     streams, other threads) race on it and must be serialised by the caller.
- *     Its arrival counters are zeroed by the first call on a device, and every
- *     call leaves them at zero.
+ *     The array is zero when the library is loaded and every call leaves its
+ *     arrival counters at zero; after two calls did overlap, the counters may stay
+ *     wrong for the rest of the process, and later calls can then return wrong
+ *     rows (some of them flagged as bit 3 of the device error word).
  * Other arguments and limits are those of fe_paged_attention_v2_bf16. */
 int fe_paged_attention_v2_bf16_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                        void* out, const int* block_tables,

@@ -83,8 +83,9 @@ def test_paged_fp32_random(H, Hkv, d):
 @pytest.mark.parametrize("H,Hkv,d", [(8, 2, 64), (32, 8, 128), (12, 4, 96), (64, 8, 128),
                                      (4, 4, 256)])
 def test_paged_fp32_long_contexts_split(H, Hkv, d):
-    """Contexts longer than one 512-token split: the fp32 entry cuts the key range into
-    splits over the block-table row and merges them (boundaries at 511/512/513)."""
+    """Long fp32 contexts (boundaries around 512 tokens): head_dim 64 and 128 run the
+    persistent split-KV decode, which cuts long sequences over several CTAs and merges
+    the pieces; head_dim 96 and 256 run the generic single-pass fp32 kernel."""
     lens = [0, 1, 511, 512, 513, 1500, 2049]
     p = O.make_paged_problem(19 + d, len(lens), H, Hkv, d, lens, bf16=False)
     ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
@@ -94,8 +95,9 @@ def test_paged_fp32_long_contexts_split(H, Hkv, d):
 
 
 def test_paged_fp32_misaligned_cache_generic_decoder():
-    """An fp32 cache that is only 4-byte aligned cannot take the vectorised decoder's
-    128-bit loads: the generic decoder runs, in both the split and single-pass kernels."""
+    """An fp32 cache that is only 4-byte aligned cannot take the persistent decode's bulk
+    page copies or the vectorised decoder's 128-bit loads: the generic single-pass
+    kernel runs."""
     import flash_engine
     for lens in ([900, 40, 1], [300, 17]):
         p = O.make_paged_problem(31, len(lens), 32, 8, 128, lens, bf16=False)
@@ -117,9 +119,10 @@ def test_paged_fp32_misaligned_cache_generic_decoder():
 
 
 def test_paged_fp32_split_in_graph_capture():
-    """fp32 paged decode inside a CUDA-graph capture: on a fresh stream (no library
-    scratch yet) it takes the single-pass kernel, after an eager call on that stream the
-    split kernel and merge; both replays match the oracle."""
+    """fp32 paged decode inside a CUDA-graph capture: on a fresh stream (no cached
+    workspace yet) the Python operator runs the split-KV kernel on the stream's slot of
+    the library scratch, after an eager call on that stream on the stream's cached
+    workspace; both replays match the oracle."""
     import flash_engine
     lens = [700, 1300, 64, 2000]
     p = O.make_paged_problem(77, len(lens), 16, 4, 128, lens, bf16=False)
@@ -389,8 +392,9 @@ def _v1_bf16(lib, x, out, stream):
 
 def test_v1_c_entry_splits_on_library_scratch_and_in_capture():
     """The reference's v1 calling convention (no scratch): the library runs the
-    split-KV kernel on its own per-stream workspace. A first call captured into a CUDA
-    graph on a new stream runs the single-pass kernel instead; both match the oracle."""
+    split-KV kernel on the stream's slot of its static scratch, which needs no
+    allocation, so a first call captured into a CUDA graph on a new stream splits too;
+    both match the oracle."""
     import ctypes
     from flash_engine import _lib
     lens = [4096, 1, 0, 3000, 700, 2049]
@@ -442,3 +446,76 @@ def test_more_sequences_than_one_launch():
         torch.cuda.synchronize()
         assert flash_engine.device_errors() == 0
         assert_bf16_close(host(out)[sel], ref)
+
+
+def _v1_fp32(lib, x, out, stream):
+    S = x["q"].shape[0]
+    return lib.fe_paged_attention_v1_fp32(
+        x["q"].data_ptr(), x["kc"].data_ptr(), x["vc"].data_ptr(), out.data_ptr(),
+        x["bt"].data_ptr(), x["lens"].data_ptr(), S, x["H"], x["Hkv"], x["d"], 16,
+        x["max_ctx"], x["bt"].shape[1], x["kc"].shape[0], 0.0, stream)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_v1_fp32_c_entry_capture_first_and_replay(d):
+    """The reference's fp32 v1 entry (launch_paged_attention_v1_fp32: no scratch
+    argument) on a stream whose first call is inside a CUDA-graph capture: the
+    persistent split-KV decode runs on the library's static scratch slot, so nothing is
+    allocated; the replays and a later eager call on the same stream match the oracle."""
+    import ctypes
+    from flash_engine import _lib
+    lens = [4096, 1, 0, 3000, 700, 2049, 513]
+    p = O.make_paged_problem(93 + d, len(lens), 32, 8, d, lens, bf16=False)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    x = dict(q=cuda(p["q"]), kc=cuda(p["k_cache"]), vc=cuda(p["v_cache"]),
+             bt=cuda(p["block_tables"]), lens=cuda(p["context_lens"]), H=32, Hkv=8, d=d,
+             max_ctx=max(lens))
+    lib = _lib.lib
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    out = torch.full_like(x["q"], float("nan"))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        assert _v1_fp32(lib, x, out, ctypes.c_void_p(side.cuda_stream)) == 0
+    for _ in range(2):
+        out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert _lib.device_errors() == 0
+        assert_fp32_close(host(out), ref)
+    out2 = torch.full_like(x["q"], float("nan"))
+    with torch.cuda.stream(side):
+        assert _v1_fp32(lib, x, out2, ctypes.c_void_p(side.cuda_stream)) == 0
+    torch.cuda.synchronize()
+    assert _lib.device_errors() == 0
+    assert_fp32_close(host(out2), ref)
+    del g
+
+
+def test_v1_entries_on_many_streams():
+    """More streams than the library has scratch slots call the v1 bf16 entry: the
+    first streams run the split-KV decode on their own slot, the rest the single-pass
+    kernel; all results match the oracle, and the slots' counters stay consistent
+    when the first stream is used again."""
+    import ctypes
+    from flash_engine import _lib
+    lens = [3000, 17, 2500, 0, 4096]
+    p = O.make_paged_problem(95, len(lens), 32, 8, 128, lens)
+    ref = O.paged_attention_gqa(p["q"], p["k_cache"], p["v_cache"], p["block_tables"],
+                                p["context_lens"])
+    x = dict(q=cuda(p["q"], torch.bfloat16), kc=cuda(p["k_cache"], torch.bfloat16),
+             vc=cuda(p["v_cache"], torch.bfloat16), bt=cuda(p["block_tables"]),
+             lens=cuda(p["context_lens"]), H=32, Hkv=8, d=128, max_ctx=max(lens))
+    lib = _lib.lib
+    streams = [torch.cuda.Stream() for _ in range(6)]
+    outs = [torch.full_like(x["q"], float("nan")) for _ in streams]
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+    for rep in range(2):
+        for s, o in zip(streams, outs):
+            assert _v1_bf16(lib, x, o, ctypes.c_void_p(s.cuda_stream)) == 0
+        torch.cuda.synchronize()
+        assert _lib.device_errors() == 0
+        for o in outs:
+            assert_bf16_close(host(o), ref)

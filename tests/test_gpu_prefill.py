@@ -118,7 +118,7 @@ def _bf16_case(B, H, N, M, d, causal, seed, dtype=torch.bfloat16):
     return host(out), ref
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [32, 64, 128])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M", [(128, 128), (256, 256), (300, 300), (1, 1), (77, 200),
                                  (200, 77), (512, 384)])
@@ -130,6 +130,15 @@ def test_bf16_tcgen05_shapes(d, causal, N, M):
 def test_fp16_tcgen05():
     out, ref = _bf16_case(2, 2, 384, 384, 128, True, 3, torch.float16)
     assert_bf16_close(out, ref, atol=5e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_head_dim_32_reference_dispatch(dtype):
+    """head_dim 32, which the reference's fp16 launcher dispatches
+    (src/flash_attention.cu:514-521): the d = 64 tensor-core kernel loads 64-column
+    boxes over the 32 real columns (zero-filled by TMA) and stores 32 columns."""
+    out, ref = _bf16_case(2, 3, 640, 520, 32, True, 32, dtype)
+    assert_bf16_close(out, ref, atol=5e-3 if dtype == torch.float16 else 2e-2)
 
 
 def test_bf16_config2_shape_slice():
