@@ -332,16 +332,17 @@ def _block_sets(lens, bs, R, seed):
 
 
 def _e2e_decode(q, kc, vc, bts, lens_t, bs, max_ctx, wsp, R, steps, ws, dev, elt):
-    """End to end through the public API with host buffers: every step moves that step's
+    """End to end through the public API with host buffers. Every step moves that step's
     q, block table and context lengths in from pinned host memory as ONE packed copy,
-    runs the decode and copies the output back to pinned host memory; two steps are in
-    flight (the host reuses a step's buffers only after that step's output is on the
-    host). Two forms, both on one stream:
-      graph -- the step (copy in, flash_engine.paged_attention, copy out) captured once
-               per (buffer, block set) into a CUDA graph and replayed, as a serving loop
-               replays its captured decode step;
-      eager -- the same three operations issued from Python every step.
-    Returns (graph_ms, eager_ms, h2d_bytes, d2h_bytes) per step on this rank."""
+    runs the decode (flash_engine.paged_attention) and copies its output back to pinned
+    host memory. Steps are pipelined over three device buffer sets: the CUDA graph of
+    step k runs the decode of step k and, on two forked streams, the input copy of step
+    k+1 and the output copy of step k-1 (as a serving loop overlaps its transfers with
+    the running step); the host replays one graph per step and waits for the graph of
+    step k-2 before it replays step k. The timed region includes the first step's input
+    copy and the last step's output copy. Also returned: the same three operations
+    issued eagerly from Python, one step at a time (no overlap).
+    Returns (pipelined_ms, eager_ms, h2d_bytes, d2h_bytes) per step on this rank."""
     import torch
     import flash_engine
 
@@ -361,60 +362,78 @@ def _e2e_decode(q, kc, vc, bts, lens_t, bs, max_ctx, wsp, R, steps, ws, dev, elt
         h[o_bt:o_bt + nbt].copy_(bts[r].cpu().contiguous().view(-1).view(torch.uint8))
         h[o_l:o_l + nl].copy_(lens_t.cpu().contiguous().view(torch.uint8))
         stage_h.append(h)
-    stage_d = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
+    NB = 3
+    in_d = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(NB)]
     views = [(sd[:nq].view(q.dtype).view(q.shape), sd[o_bt:o_bt + nbt].view(torch.int32)
-              .view(bts[0].shape), sd[o_l:o_l + nl].view(torch.int32)) for sd in stage_d]
-    outs_d = [torch.empty_like(q) for _ in range(2)]
-    outs_h = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2)]
-    evs = [torch.cuda.Event() for _ in range(2)]
+              .view(bts[0].shape), sd[o_l:o_l + nl].view(torch.int32)) for sd in in_d]
+    out_d = [torch.empty_like(q) for _ in range(NB)]
+    out_h = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(NB)]
+    evs = [torch.cuda.Event() for _ in range(NB)]
 
-    def body(b, r):
-        stage_d[b].copy_(stage_h[r], non_blocking=True)
+    def decode(b):
         qv, btv, lv = views[b]
         flash_engine.paged_attention(qv, kc, vc, btv, lv, bs, max_context_len=max_ctx,
-                                     out=outs_d[b], workspace=wsp)
-        outs_h[b].copy_(outs_d[b], non_blocking=True)
+                                     out=out_d[b], workspace=wsp)
 
-    # graphs: one per (buffer, block set)
-    for b in range(2):
-        body(b, 0)
+    # one graph per (buffer set of step k, block set of step k+1)
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    for b in range(NB):
+        in_d[b].copy_(stage_h[0])
+        decode(b)
     torch.cuda.synchronize()
     graphs = {}
     cap = torch.cuda.Stream(device=dev)
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
-        for b in range(2):
-            for r in range(R):
+        for b in range(NB):
+            for rn in range(R):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=cap):
-                    body(b, r)
-                graphs[(b, r)] = g
+                    s_in.wait_stream(cap)
+                    s_out.wait_stream(cap)
+                    with torch.cuda.stream(s_in):
+                        in_d[(b + 1) % NB].copy_(stage_h[rn], non_blocking=True)
+                    with torch.cuda.stream(s_out):
+                        out_h[(b - 1) % NB].copy_(out_d[(b - 1) % NB], non_blocking=True)
+                    decode(b)
+                    cap.wait_stream(s_in)
+                    cap.wait_stream(s_out)
+                graphs[(b, rn)] = g
     torch.cuda.current_stream().wait_stream(cap)
     torch.cuda.synchronize()
 
-    def run(n, graph):
-        for i in range(n):
-            b = i % 2
-            if i >= 2:
-                evs[b].synchronize()
-            if graph:
-                graphs[(b, i % R)].replay()
-            else:
-                body(b, i % R)
+    def pipelined(n):
+        in_d[0].copy_(stage_h[0], non_blocking=True)
+        for k in range(n):
+            b = k % NB
+            if k >= 2:
+                evs[(k - 2) % NB].synchronize()
+            graphs[(b, (k + 1) % R)].replay()
             evs[b].record()
+        lb = (n - 1) % NB
+        out_h[lb].copy_(out_d[lb], non_blocking=True)
         torch.cuda.synchronize()
+
+    def eager(n):
+        for k in range(n):
+            b = k % NB
+            in_d[b].copy_(stage_h[k % R], non_blocking=True)
+            decode(b)
+            out_h[b].copy_(out_d[b], non_blocking=True)
+            evs[b].record()
+            evs[b].synchronize()
 
     n = max(4, min(steps, 200))
     res = []
-    for graph in (True, False):
-        run(4, graph)
+    for fn in (pipelined, eager):
+        fn(4)
         _barrier(ws, dev)
         t0 = time.perf_counter()
-        run(n, graph)
+        fn(n)
         res.append(_max_over_ranks((time.perf_counter() - t0) * 1e3 / n, ws, dev))
-    # the outputs that came back must be the decode's
-    for b in range(2):
-        assert torch.equal(outs_h[b].to(dev), outs_d[b])
+    # the outputs that came back are the decode's
+    for b in range(NB):
+        assert torch.equal(out_h[b].to(dev), out_d[b])
     del graphs
     return res[0], res[1], nq + nbt + nl, nq
 
@@ -534,10 +553,13 @@ def bench_paged(a, ws, rank, local, cfg, steps, warmup, fp32=False):
                 "d2h_bytes_per_step": int(d2h),
                 "mode": "per step: one packed H2D copy of q, block table and lengths from "
                         "pinned memory, the public paged_attention call, one D2H copy of "
-                        "the output; captured per step into a CUDA graph and replayed, two "
-                        "steps in flight",
+                        "the output; one CUDA graph per step (decode of step k, input copy "
+                        "of step k+1 and output copy of step k-1 on forked streams), "
+                        "replayed by the host every step",
                 "eager_value": round(total / (ems * 1e-3) / 1e9, 2),
-                "eager_ms_per_step": round(ems, 4)},
+                "eager_ms_per_step": round(ems, 4),
+                "eager_mode": "the same three operations issued from Python, one step at a "
+                              "time"},
         "gpu_launches": steps,
         "clocks": sampler.summary(t0, t1),
     }
