@@ -33,6 +33,13 @@ inline float resolve_scale(float s, int d) { return s > 0.f ? s : 1.0f / sqrtf(s
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 constexpr int kMaxSeqsPerLaunch = 4096;
+// Pages of streaming that a sequence start inside a CTA's chunk costs the flat-mode
+// decode (segment change, partial writes, piece count-in), measured per CTA with
+// %globaltimer on the config 3 / 5 shard shapes: about 2.5-3.5 us, 6-8 pages.
+#ifndef FE_DECODE_SEG_COST
+#define FE_DECODE_SEG_COST 6
+#endif
+constexpr int kSegCostPages = FE_DECODE_SEG_COST;
 constexpr int kErr = static_cast<int>(cudaErrorInvalidValue);
 
 bool dense_args_ok(int B, int H, int N, int M, int d) {
@@ -174,6 +181,7 @@ int paged_tc_run(const PagedArgs& a, const DecodePlan& pl, float* ws, cudaStream
     p.tok_begin = pl.tok_begin;
     p.tok_end = pl.tok_end;
     p.pages_per_split = pl.flat ? 1 : INT_MAX / 2;
+    p.seg_cost_pages = pl.flat ? kSegCostPages : 0;
     p.flat = pl.flat ? 1 : 0;
     p.direct_final = pl.direct_final ? 1 : 0;
     p.scale_log2 = resolve_scale(a.scale, a.d) * fe::kLog2e;

@@ -126,6 +126,23 @@ __device__ __forceinline__ Window seq_window(int ctx, int tb, int te, int bs) {
   return w;
 }
 
+// Flat mode keeps, per sequence, its page prefix pre[] and the number of window tokens
+// in its last page (tail[], 1..BS) in shared memory, so the segment walk rebuilds a
+// window without reading context_lens again. The window starts at tok_begin, a multiple
+// of BS.
+__device__ __forceinline__ uint8_t last_page_tokens(const Window& w, int bs) {
+  return w.np > 0 ? static_cast<uint8_t>(w.hi - (w.pb + w.np - 1) * bs) : 0;
+}
+__device__ __forceinline__ Window flat_window(const int* pre, const uint8_t* tail, int s, int tb,
+                                              int bs) {
+  Window w;
+  w.np = pre[s + 1] - pre[s];
+  w.lo = max(tb, 0);
+  w.pb = w.lo / bs;
+  w.hi = w.np > 0 ? (w.pb + w.np - 1) * bs + tail[s] : w.lo;
+  return w;
+}
+
 // Number of unit-mode segments of a sequence: one per pages_per_split pages (at
 // least one, so that an empty sequence still gets its zero output row).
 __device__ __forceinline__ int unit_splits(const Window& w, int pps) {
@@ -170,35 +187,78 @@ __device__ __forceinline__ int find_seq(const int* pre, int S, long long r) {
   return lo;
 }
 
-// Flat-mode chunk length in pages (identical in the decode and merge kernels).
-__device__ __forceinline__ long long flat_chunk(long long T, int ctas, int chunk_min) {
-  long long c = (T + ctas - 1) / ctas;
-  if (c < chunk_min) c = chunk_min;
-  return c < 1 ? 1 : c;
-}
+// Flat-mode partition. The (KV-head group y, sequence s) units are laid out in a cost
+// space in which unit (y, s) takes beta virtual pages followed by its np(s) pages:
+// unit (y, s) starts at y * (Ptot + beta * S) + pre[s] + beta * s. The cost space is
+// cut into gridDim.x equal chunks, one per CTA, and a CTA streams the pages inside its
+// chunk. A sequence that starts inside a chunk costs the CTA a segment change (merge of
+// the warp states, partial writes, a piece to count in) that takes about as long as
+// streaming a few pages, so those beta pages are taken off that CTA's share. A CTA
+// whose chunk holds only virtual pages gets no pages; it can never sit between two
+// pieces of one unit, whose pages are contiguous. Kept in shared memory, one per CTA.
+struct FlatPartition {
+  const int* pre;
+  int S, Ptot, beta;
+  long long Cy;   // cost of one y: Ptot + beta * S
+  long long C;    // total cost: Y * Cy
+  long long cc;   // cost per CTA chunk
+  double inv_cc;  // 1 / cc
+  // Largest s in [0, S) with pre[s] + beta * s <= r.
+  __device__ __forceinline__ int unit_at(long long r) const {
+    int lo = 0, hi = S;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pre[mid] + static_cast<long long>(beta) * mid <= r) lo = mid; else hi = mid;
+    }
+    return lo;
+  }
+  // Global page index (y * Ptot + page) at cost position c (the first page at or after c).
+  __device__ __forceinline__ long long page_at(long long c) const {
+    if (c >= C) return static_cast<long long>(C / Cy) * Ptot;
+    const long long y = c / Cy;
+    const long long r = c - y * Cy;
+    const int s = unit_at(r);
+    const long long off = r - (pre[s] + static_cast<long long>(beta) * s);
+    return y * Ptot + pre[s] + (off > beta ? off - beta : 0);
+  }
+  // floor(c / cc) for 0 <= c < 2^52: a reciprocal multiply, corrected by one step.
+  __device__ __forceinline__ int chunk_of(long long c) const {
+    long long q = static_cast<long long>(static_cast<double>(c) * inv_cc);
+    if (q * cc > c) --q;
+    else if ((q + 1) * cc <= c) ++q;
+    return static_cast<int>(q);
+  }
+  // Cost position of the first page of unit (y, s).
+  __device__ __forceinline__ long long unit_cost(int y, int s) const {
+    return static_cast<long long>(y) * Cy + pre[s] + static_cast<long long>(beta) * (s + 1);
+  }
+};
 
 struct Seg {
   int seq, kvh, hc;
   int p0, p1;     // absolute pages [p0, p1)
   int lo, hi;     // valid tokens [lo, hi)
-  int slot;       // flat mode: 0 = first segment of the CTA's chunk, 1 = a later one
+  int slot;       // flat mode: fixup slot of a piece: 1 = the unit's first piece (the
+                  // last segment of its CTA), 0 = a continuation (the CTA's first segment)
   int nslots;     // chunks (segments) of this (sequence, head group); 1 = finalise here
   int cfirst;     // flat mode: chunk holding the first page of this (sequence, group)
-  int kfirst;     // flat mode: slot of the piece in chunk cfirst (1 if it starts mid-chunk)
 };
 
 // Walks the segments of one CTA. Producer and consumers run identical copies.
 struct SegIter {
   const Params* p;
   const int* pre;
+  const uint8_t* tail;  // flat mode
   int S, Y, HC, BS;
   bool flat;
   // unit mode
   int u, total_units;
   // flat mode
-  long long P, Pend, chunk;
+  long long P, Pend;
   int Ptot;
-  bool first_seg;
+  int y;           // KV-head group of page P, and y * Ptot
+  long long ybase;
+  const FlatPartition* fp;  // in shared memory (keeps the walk's registers few)
 
   __device__ __forceinline__ bool next(Seg& g) {
     if (!flat) {
@@ -218,19 +278,20 @@ struct SegIter {
       g.hi = w.hi;
       g.slot = split;
       g.nslots = pre[seq + 1] - pre[seq];
-      g.cfirst = g.kfirst = 0;
+      g.cfirst = 0;
       return true;
     }
     if (P >= Pend) return false;
-    const int y = static_cast<int>(P / Ptot);
-    const int r = static_cast<int>(P - static_cast<long long>(y) * Ptot);
+    while (P >= ybase + Ptot) {  // P only grows: no division
+      ybase += Ptot;
+      ++y;
+    }
+    const int r = static_cast<int>(P - ybase);
     const int seq = find_seq(pre, S, r);
-    const Window w = seq_window(__ldg(p->context_lens + seq), p->tok_begin, p->tok_end, BS);
+    const Window w = flat_window(pre, tail, seq, p->tok_begin, BS);
     const int in0 = r - pre[seq];
     const long long left = Pend - P;
     const int n = static_cast<int>(min(static_cast<long long>(w.np - in0), left));
-    const long long gstart = static_cast<long long>(y) * Ptot + pre[seq];
-    const long long gend = gstart + w.np - 1;
     g.seq = seq;
     g.kvh = y / HC;
     g.hc = y - g.kvh * HC;
@@ -238,12 +299,12 @@ struct SegIter {
     g.p1 = g.p0 + n;
     g.lo = w.lo;
     g.hi = w.hi;
-    const int cfirst = static_cast<int>(gstart / chunk);
-    g.nslots = static_cast<int>(gend / chunk) - cfirst + 1;
+    // chunks holding the unit's first and last page
+    const long long c0 = fp->unit_cost(y, seq);
+    const int cfirst = fp->chunk_of(c0);
+    g.nslots = fp->chunk_of(c0 + w.np - 1) - cfirst + 1;
     g.cfirst = cfirst;
-    g.kfirst = gstart != static_cast<long long>(cfirst) * chunk ? 1 : 0;
-    g.slot = first_seg ? 0 : 1;
-    first_seg = false;
+    g.slot = in0 == 0 ? 1 : 0;
     P += n;
     return true;
   }
@@ -372,8 +433,8 @@ __device__ __forceinline__ void lse_combine_warp(const float* __restrict__ part_
 // Per-CTA event times (globaltimer ns) of the last decode launch, for profiling
 // builds only: [0] entry, [1] prefix done, [2] first page issued, [3] first page
 // ready (consumer warp 0), [4] consumers done, [5] producer done issuing,
-// [6] SM id, [7] nanoseconds spent merging split sequences, [8..11] exchange-mode
-// end: before the peer-store fence, after it, after the CTA barrier, after the flags.
+// [6] SM id, [7] nanoseconds spent merging split sequences, [8] consumer warp 0 past
+// griddepcontrol.wait (the previous grid has completed), [9..11] unused.
 __device__ unsigned long long g_timeline[kCounterSlots][12];
 #define FE_TL(slot) (g_timeline[blockIdx.x][slot] = globaltimer_ns())
 #else
@@ -382,7 +443,7 @@ __device__ unsigned long long g_timeline[kCounterSlots][12];
 
 // A piece of a split (sequence, head group) written by this CTA (flat mode).
 struct Pending {
-  int cfirst, kfirst, nslots, seq, kvh, hc, last;
+  int cfirst, nslots, seq, kvh, hc, last;
 };
 
 template <typename T, int D, int BS, int NT, int NCW, int NSTAGE>
@@ -397,7 +458,8 @@ struct Cfg {
   static constexpr int COMB_BYTES = NCW * HPC * (2 + CSTRIDE) * 4;
   static constexpr int FIXED_SMEM = 1024 /*align slack*/ + NSTAGE * STAGE + COMB_BYTES +
                                     NSTAGE * 16 /*bars*/ + NSTAGE * 4 + 64;
-  static int smem_bytes(int num_seqs) { return FIXED_SMEM + (num_seqs + 1) * 4; }
+  // + pre[num_seqs + 1] ints and tail[num_seqs] bytes
+  static int smem_bytes(int num_seqs) { return FIXED_SMEM + (num_seqs + 1) * 4 + num_seqs + 16; }
 };
 
 // Two CTAs of NCW + 1 warps share an SM only if three warps fit one SM sub-partition's
@@ -439,8 +501,10 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
   uint64_t* empty = full + NSTAGE;
   int* stage_valid = reinterpret_cast<int*>(empty + NSTAGE);
   int* pre = stage_valid + NSTAGE;  // [num_seqs + 1]
+  uint8_t* tail = reinterpret_cast<uint8_t*>(pre + p.num_seqs + 1);  // [num_seqs] (flat mode)
   __shared__ int warp_tot[NCW + 1];
   __shared__ Pending pend[2];  // flat mode: pieces written as slot 0 / slot 1
+  __shared__ FlatPartition fpart;  // flat mode: the partition of the work over the CTAs
 
   // Programmatic dependent launch, both ways: the next kernel in the stream may start
   // its CTAs as soon as SM room frees up (it waits for this grid's results before
@@ -492,6 +556,7 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
   SegIter it;
   it.p = &p;
   it.pre = pre;
+  it.tail = tail;
   it.S = S;
   it.Y = Y;
   it.HC = HC;
@@ -499,14 +564,36 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
   it.flat = flat;
   if (flat) {
     block_prefix<NTH>(pre, S, warp_tot, [&](int i) {
-      return seq_window(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS).np;
+      const Window w = seq_window(__ldg(p.context_lens + i), p.tok_begin, p.tok_end, BS);
+      tail[i] = last_page_tokens(w, BS);  // written twice, the same value
+      return w.np;
     });
     it.Ptot = pre[S];
     const long long total_pages = static_cast<long long>(Y) * it.Ptot;
-    it.chunk = flat_chunk(total_pages, gridDim.x, p.pages_per_split);
-    it.P = min(total_pages, static_cast<long long>(blockIdx.x) * it.chunk);
-    it.Pend = min(total_pages, it.P + it.chunk);
-    it.first_seg = true;
+    if (tid == 0) {
+      FlatPartition& fp = fpart;
+      fp.pre = pre;
+      fp.S = S;
+      fp.Ptot = it.Ptot;
+      // beta only while it stays well below a chunk (and the chunk holds real pages)
+      fp.beta = p.seg_cost_pages;
+      for (int k = 0; k < 2; ++k) {
+        fp.Cy = it.Ptot + static_cast<long long>(fp.beta) * S;
+        fp.C = static_cast<long long>(Y) * fp.Cy;
+        fp.cc = (fp.C + gridDim.x - 1) / gridDim.x;
+        if (fp.cc < 1) fp.cc = 1;
+        if (4LL * fp.beta <= fp.cc) break;
+        fp.beta = 0;
+      }
+      fp.inv_cc = 1.0 / static_cast<double>(fp.cc);
+    }
+    __syncthreads();
+    it.fp = &fpart;
+    it.P = total_pages == 0 ? 0 : fpart.page_at(static_cast<long long>(blockIdx.x) * fpart.cc);
+    it.Pend =
+        total_pages == 0 ? 0 : fpart.page_at(static_cast<long long>(blockIdx.x + 1) * fpart.cc);
+    it.y = it.Ptot > 0 ? static_cast<int>(it.P / it.Ptot) : 0;
+    it.ybase = static_cast<long long>(it.y) * it.Ptot;
     it.u = it.total_units = 0;
   } else {
     block_prefix<NTH>(pre, S, warp_tot, [&](int i) {
@@ -516,9 +603,10 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
     it.u = blockIdx.x;
     it.total_units = pre[S] * Y;
     it.P = it.Pend = 0;
-    it.chunk = 1;
     it.Ptot = 0;
-    it.first_seg = true;
+    it.y = 0;
+    it.ybase = 0;
+    it.fp = nullptr;
   }
   if (tid == 0) FE_TL(1);
 
@@ -529,32 +617,44 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
       prefetch_tensormap(&vmap);
     }
     const uint64_t pol = l2_policy_evict_first();
-    // Block-table entries of one 32-page group of a segment (lane i: page base+i).
-    auto load_group = [&](const Seg& g, int base, int& phys, int& valid) {
-      phys = 0;
-      valid = 0;
+    // Block-table entries of one 32-page group of a segment (lane i: page base+i). The
+    // loads are only issued here; the entries are checked (check_group) one group later,
+    // when they have landed, so the producer never waits on them before issuing the
+    // current group's copies.
+    constexpr int kNoPage = INT_MIN;      // lane past the segment
+    constexpr int kPastRow = INT_MIN + 1; // page past the block-table row
+    auto load_group = [&](const Seg& g, int base, int& phys) {
+      phys = kNoPage;
       const int page = g.p0 + base + lane;
       if (page < g.p1) {
-        if (page >= p.max_blocks_per_seq) {
-          atomicOr(p.err, kErrBadBlock);  // context longer than the block-table row
-        } else {
-          phys = __ldg(p.block_tables + static_cast<size_t>(g.seq) * p.max_blocks_per_seq + page);
-          const long long row = (static_cast<long long>(phys) * Hkv + g.kvh) * BS;
-          valid = phys >= 0 && (p.num_phys_blocks <= 0 || phys < p.num_phys_blocks) &&
-                  row + BS <= static_cast<long long>(INT_MAX);
-          if (!valid) atomicOr(p.err, kErrBadBlock);
-        }
+        phys = page >= p.max_blocks_per_seq
+                   ? kPastRow
+                   : __ldg(p.block_tables + static_cast<size_t>(g.seq) * p.max_blocks_per_seq +
+                           page);
       }
+    };
+    auto check_group = [&](const Seg& g, int phys) -> int {
+      if (phys == kNoPage) return 0;
+      if (phys == kPastRow) {
+        atomicOr(p.err, kErrBadBlock);  // context longer than the block-table row
+        return 0;
+      }
+      const long long row = (static_cast<long long>(phys) * Hkv + g.kvh) * BS;
+      const int valid = phys >= 0 && (p.num_phys_blocks <= 0 || phys < p.num_phys_blocks) &&
+                        row + BS <= static_cast<long long>(INT_MAX);
+      if (!valid) atomicOr(p.err, kErrBadBlock);
+      return valid;
     };
     int gi = 0;
     bool ok = true;
     Seg cur;
     bool have = it.next(cur);
     int base = 0;
-    int ph_cur = 0, vd_cur = 0;
-    if (have) load_group(cur, 0, ph_cur, vd_cur);
+    int ph_cur = kNoPage;
+    if (have) load_group(cur, 0, ph_cur);
     griddep_wait();  // the KV cache may have been written by the previous kernel
     while (have && ok) {
+      const int vd_cur = check_group(cur, ph_cur);  // loaded one group ago
       // Look one 32-page group ahead and start its block-table loads now.
       Seg ns = cur;
       int nbase = base + 32;
@@ -563,8 +663,8 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
         have_n = it.next(ns);
         nbase = 0;
       }
-      int ph_n = 0, vd_n = 0;
-      if (have_n) load_group(ns, nbase, ph_n, vd_n);
+      int ph_n = kNoPage;
+      if (have_n) load_group(ns, nbase, ph_n);
       const int cnt = max(0, min(32, cur.p1 - cur.p0 - base));
       for (int k = 0; k < cnt; ++k) {
         const int ph = __shfl_sync(0xffffffffu, ph_cur, k);
@@ -616,7 +716,6 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
       cur = ns;
       base = nbase;
       ph_cur = ph_n;
-      vd_cur = vd_n;
       have = have_n;
     }
     // Drain: no bulk copy of this CTA may still be in flight when it exits.
@@ -635,6 +734,7 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
 
   // ======================================================= consumer warps
   griddep_wait();
+  if (tid == 0) FE_TL(8);
   using E = Elem<T>;
   const int g = lane >> 2, c = lane & 3;
   const T* __restrict__ qbase = reinterpret_cast<const T*>(p.q);
@@ -1146,7 +1246,6 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
       // A piece of a longer sequence: counted in after this CTA's last segment.
       Pending& pd = pend[sg.slot];
       pd.cfirst = sg.cfirst;
-      pd.kfirst = sg.kfirst;
       pd.nslots = sg.nslots;
       pd.seq = sg.seq;
       pd.kvh = sg.kvh;
@@ -1198,7 +1297,9 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
         lse_combine_warp<PER, 8>(
             part_o, part_ml, pd.nslots, D,
             [&](int j) -> size_t {
-              return (static_cast<size_t>(pd.cfirst + j) * 2 + (j == 0 ? pd.kfirst : 0)) * HPC +
+              // piece j sits in CTA cfirst + j: the first piece in slot 1, the
+              // continuations in slot 0
+              return (static_cast<size_t>(pd.cfirst + j) * 2 + (j == 0 ? 1 : 0)) * HPC +
                      hl;
             },
             [&](size_t slot) { return slot * D; }, [&](size_t slot) { return slot * 2; }, M, L,

@@ -60,7 +60,9 @@ struct Params {
   int num_phys_blocks;     // 0 = unknown (no range check)
   int head_chunks;         // ceil(G / (8 * NT))
   int tok_begin, tok_end;  // token window [tok_begin, tok_end) of every sequence
-  int pages_per_split;     // unit mode: pages per segment; flat mode: minimum chunk
+  int pages_per_split;     // unit mode: pages per segment
+  int seg_cost_pages;      // flat mode: pages a CTA's share shrinks by for each sequence
+                           // that starts in its chunk (see FlatPartition)
   int flat;                // 1: flat (stream-K) chunking, 0: unit mode
   int direct_final;        // 1: whole rows are written normalised to `out`;
                            // 0: as merged partials to merged_o / merged_ml

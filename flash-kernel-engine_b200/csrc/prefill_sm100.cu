@@ -56,7 +56,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 17;
+  static constexpr int NBARS = 19;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* o_done = bars + 13;  // [2]
   uint64_t* drain = bars + 15;
   uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
+  uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
+      mbar_init(&p_half[i], 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -285,16 +287,19 @@ __global__ void __launch_bounds__(384, 1)
         }
         tc::commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
+      // P V in two halves of 64 keys: the first starts as soon as the softmax has
+      // stored P of keys 0..63 (p_half), while it computes keys 64..127 (p_full).
+      auto issue_pv_half = [&](int t, int j, int half) {
         const uint32_t vb = sbase + C::V_OFF + (j & 1) * TILE;
         const uint32_t ptm = tmem + t * BN;              // P_t over the S_t columns
         const uint32_t otm = tmem + 2 * BN + t * D;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int k2 = 0; k2 < BN / 32; ++k2) {
+          const int kk = half * (BN / 32) + k2;
           tc::mma_ts(otm, ptm + kk * 8, tc::smem_desc_sw128(vb + kk * 16 * 128, HALF, 1024),
                      idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc::commit(&o_done[t]);
+        if (half == 1) tc::commit(&o_done[t]);
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
       bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
@@ -316,9 +321,12 @@ __global__ void __launch_bounds__(384, 1)
         const bool next_k = j + 1 < nmax;
         bool k_ready = false;
         if (j < nkv[0]) {
+          if (!mbar_wait(&p_half[0], j & 1)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_pv_half(0, j, 0);
           if (!mbar_wait(&p_full[0], j & 1)) { ok = false; break; }
           tc::fence_after_sync();
-          issue_pv(0, j);
+          issue_pv_half(0, j, 1);
           if (j + 1 < nkv[0]) {
             if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
@@ -326,9 +334,12 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         if (j < nkv[1]) {
+          if (!mbar_wait(&p_half[1], j & 1)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_pv_half(1, j, 0);
           if (!mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
           tc::fence_after_sync();
-          issue_pv(1, j);
+          issue_pv_half(1, j, 1);
           if (j + 1 < nkv[1]) {
             if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
@@ -394,8 +405,25 @@ __global__ void __launch_bounds__(384, 1)
       const float m_use = need ? m_new : m_run;
       const float mu = m_use == NEG_INF ? 0.f : m_use;
       const float corr = need ? ex2(m_run - mu) : 1.f;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_t must hold P V of tile j-1 before it is rescaled, and be rescaled before
+        // the first half of P V of tile j accumulates into it.
+        const bool got_o = mbar_wait(&o_done[t], (j - 1) & 1);
+        if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c4 = 0; c4 < D / 32; ++c4) {
+          uint32_t u[32];
+          tc::ld32(tO + c4 * 32, u);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+          tc::st32(tO + c4 * 32, u);
+        }
+      }
       // p = 2^(s*sl - m): one FFMA each, then the MUFU ex2, except one pair in every
       // kPolyEvery that uses a polynomial on the FMA pipe (splits the work over both).
+      // Each 64-key half of P is handed to the MMA warp as soon as it is stored.
       uint64_t acc2[4] = {0, 0, 0, 0};  // paired partial sums (0 bits = 0.0f, 0.0f)
       const uint64_t sl2 = f2(sl, sl), nmu2 = f2(-mu, -mu);
 #pragma unroll
@@ -420,6 +448,9 @@ __global__ void __launch_bounds__(384, 1)
           pk[i] = pack2<T>(a, b);
         }
         tc::st32(tS + c4 * 32, pk);
+        tc::wait_st();
+        tc::fence_before_sync();
+        mbar_arrive(c4 == 0 ? &p_half[t] : &p_full[t]);
       }
       float sum = 0.f;
 #pragma unroll
@@ -430,24 +461,6 @@ __global__ void __launch_bounds__(384, 1)
       }
       l_run = l_run * corr + sum;
       m_run = m_use;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O_t must hold P V of tile j-1 before it is rescaled.
-        const bool got_o = mbar_wait(&o_done[t], (j - 1) & 1);
-        if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c4 = 0; c4 < D / 32; ++c4) {
-          uint32_t u[32];
-          tc::ld32(tO + c4 * 32, u);
-          tc::wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
-          tc::st32(tO + c4 * 32, u);
-        }
-      }
-      tc::wait_st();
-      tc::fence_before_sync();
-      mbar_arrive(&p_full[t]);
     }
     if (!ok) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
