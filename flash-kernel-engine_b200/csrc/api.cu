@@ -35,9 +35,11 @@ inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintp
 constexpr int kMaxSeqsPerLaunch = 4096;
 // Pages of streaming that a sequence start inside a CTA's chunk costs the flat-mode
 // decode (segment change, partial writes, piece count-in), measured per CTA with
-// %globaltimer on the config 3 / 5 shard shapes: about 2.5-3.5 us, 6-8 pages.
+// %globaltimer on the config 3 / 5 shard shapes: about 2.5-3.5 us, 6-8 pages. Swept
+// over 0/6/8/10 on those shapes: 8 is the best (config 3: 108.0 -> 104.8 us at N = 1,
+// 22.3 -> 20.5 us on the N = 8 shard; config 5 N = 8 shard: 55.1 -> 47.5 us).
 #ifndef FE_DECODE_SEG_COST
-#define FE_DECODE_SEG_COST 6
+#define FE_DECODE_SEG_COST 8
 #endif
 constexpr int kSegCostPages = FE_DECODE_SEG_COST;
 constexpr int kErr = static_cast<int>(cudaErrorInvalidValue);

@@ -575,15 +575,15 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
       fp.pre = pre;
       fp.S = S;
       fp.Ptot = it.Ptot;
-      // beta only while it stays well below a chunk (and the chunk holds real pages)
+      // beta is halved until it is at most a quarter of a chunk (chunks of little work)
       fp.beta = p.seg_cost_pages;
-      for (int k = 0; k < 2; ++k) {
+      for (;;) {
         fp.Cy = it.Ptot + static_cast<long long>(fp.beta) * S;
         fp.C = static_cast<long long>(Y) * fp.Cy;
         fp.cc = (fp.C + gridDim.x - 1) / gridDim.x;
         if (fp.cc < 1) fp.cc = 1;
-        if (4LL * fp.beta <= fp.cc) break;
-        fp.beta = 0;
+        if (4LL * fp.beta <= fp.cc || fp.beta == 0) break;
+        fp.beta >>= 1;
       }
       fp.inv_cc = 1.0 / static_cast<double>(fp.cc);
     }
