@@ -521,10 +521,13 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
   PagedArgs a{q, kc, vc, nullptr, bt, lens, S, H, Hkv, d, bs, 0, maxb, num_blocks, scale};
   int rc = paged_check<__nv_bfloat16>(a);
   if (rc) return rc;
+  const bool lib = !workspace && workspace_floats == FE_WORKSPACE_LIBRARY;
   const long long need = workspace_floats_for(H, Hkv, d, bs);
-  if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
+  if (need <= 0 || (!lib && (!workspace || static_cast<long long>(workspace_floats) < need)))
+    return kErr;
   if (tb < 0 || te < tb || !mout || !mstats || tb % bs != 0) return kErr;
   if (S == 0) return 0;
+  cudaStream_t st = as_stream(stream);
   DecodePlan pl;
   pl.tok_begin = tb;
   pl.tok_end = te;
@@ -532,7 +535,11 @@ int fe_paged_decode_partials_bf16(const void* q, const void* kc, const void* vc,
   pl.direct_final = false;
   pl.merged_out = mout;
   pl.merged_stats = mstats;
-  return paged_tc_run<__nv_bfloat16>(a, pl, workspace, as_stream(stream));
+  if (lib) {  // the stream's slot of the library scratch, else one segment per row
+    pl.ws_slot = stream_slot(st);
+    pl.flat = pl.ws_slot >= 0;
+  }
+  return paged_tc_run<__nv_bfloat16>(a, pl, workspace, st);
 }
 
 int fe_paged_decode_kv_exchange_bf16(const void* q, const void* kc, const void* vc,
@@ -553,13 +560,19 @@ int fe_paged_decode_kv_exchange_bf16(const void* q, const void* kc, const void* 
   if (S == 0) return 0;
   cudaStream_t st = as_stream(stream);
   if (phases & 1) {
+    const bool lib = !workspace && workspace_floats == FE_WORKSPACE_LIBRARY;
     const long long need = workspace_floats_for(H, Hkv, d, bs);
-    if (need <= 0 || !workspace || static_cast<long long>(workspace_floats) < need) return kErr;
+    if (need <= 0 || (!lib && (!workspace || static_cast<long long>(workspace_floats) < need)))
+      return kErr;
     DecodePlan pl;
     pl.tok_begin = tb;
     pl.tok_end = te;
     pl.flat = true;
     pl.direct_final = false;
+    if (lib) {  // the stream's slot of the library scratch, else one segment per row
+      pl.ws_slot = stream_slot(st);
+      pl.flat = pl.ws_slot >= 0;
+    }
     for (int r = 0; r < world; ++r) pl.xbuf[r] = static_cast<char*>(xbufs[r]);
     pl.xworld = world;
     pl.xrank = rank;

@@ -190,14 +190,6 @@ def _workspace(query, H, Hkv, d, bs, workspace):
     return workspace, workspace.numel()
 
 
-def _required_workspace(query, H, Hkv, d, bs, workspace):
-    ws, n = _workspace(query, H, Hkv, d, bs, workspace)
-    if ws is None:
-        raise RuntimeError("the first call on a stream that is being captured needs an "
-                           "explicit workspace (make one eager call first, or pass one)")
-    return ws, n
-
-
 def _persistent_decode_ok(query, key_cache, value_cache, out, d, block_size, kv_layout):
     """Shapes the persistent split-KV decode takes (else the generic fp32 kernel)."""
     if d not in (64, 128) or block_size not in (16, 32):
@@ -290,7 +282,7 @@ def paged_decode_partials(query, key_cache, value_cache, block_tables, context_l
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
                                            context_lens, block_size)
     dev = query.device
-    ws, n = _required_workspace(query, H, Hkv, d, block_size, workspace)
+    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
     if out is None:
         out = torch.empty((S, H, d), dtype=torch.float32, device=dev)
     if out_stats is None:
@@ -299,7 +291,8 @@ def paged_decode_partials(query, key_cache, value_cache, block_tables, context_l
         _lib.check(_lib_c.fe_paged_decode_partials_bf16(
             _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
             _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
-            int(token_begin), int(token_end), _ptr(ws), n, _ptr(out), _ptr(out_stats),
+            int(token_begin), int(token_end), _ptr(ws) if ws is not None else None, n,
+            _ptr(out), _ptr(out_stats),
             _stream()), "paged_decode_partials")
     return out, out_stats
 
@@ -324,7 +317,7 @@ def paged_decode_kv_exchange(query, key_cache, value_cache, block_tables, contex
         raise TypeError("the KV-range exchange decode takes bf16")
     S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
                                            context_lens, block_size)
-    ws, n = _required_workspace(query, H, Hkv, d, block_size, workspace)
+    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
     if out is None:
         out = torch.empty_like(query)
     arr = (ctypes.c_void_p * len(xbufs))(*[int(x) for x in xbufs])
@@ -332,7 +325,8 @@ def paged_decode_kv_exchange(query, key_cache, value_cache, block_tables, contex
         _lib.check(_lib_c.fe_paged_decode_kv_exchange_bf16(
             _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
             _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
-            int(token_begin), int(token_end), _ptr(ws), n, arr, len(xbufs), int(rank),
+            int(token_begin), int(token_end), _ptr(ws) if ws is not None else None, n, arr,
+            len(xbufs), int(rank),
             int(max_rows), _ptr(out), int(phases), _stream()), "paged_decode_kv_exchange")
     return out
 

@@ -243,7 +243,9 @@ int fe_flash_decoding_forward_fp32(const float* q, const float* k, const float* 
  * merged partial per (sequence, query head) in merged_out [S, H, d] f32
  * (unnormalised O) and merged_stats [S, H, 2] (m in log2 units of the scaled score,
  * l = sum 2^(s*scale*log2e - m)); a sequence whose window is empty gets (0, -inf, 0).
- * The work is spread like fe_paged_attention_v2_bf16 and needs the same workspace.
+ * The work is spread like fe_paged_attention_v2_bf16 and needs the same workspace
+ * (or workspace = NULL with workspace_floats = FE_WORKSPACE_LIBRARY: the stream's slot of
+ * the library scratch, as for fe_paged_attention_ex; also in fe_paged_decode_kv_exchange_bf16).
  * token_begin must be a multiple of block_size. Used for KV-range sharding across
  * GPUs: each GPU runs its own window, the merged partials are all-gathered and
  * fe_merge_partials combines them. New (the reference has no paged split-KV). */

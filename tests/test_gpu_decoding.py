@@ -126,3 +126,34 @@ def test_kv_exchange_emulated_ranks_one_gpu(world):
         torch.cuda.synchronize()
         for b in bufs:
             L.fe_kv_exchange_free(b)
+
+
+def test_partials_captured_first_on_library_scratch():
+    """A KV-range step (partials of two windows + merge) captured into a CUDA graph with
+    no workspace given: on the capture stream nothing may be allocated, so the partials
+    run on the stream's slot of the library scratch; replays on new queries match the
+    oracle."""
+    import flash_engine
+    from flash_engine.graph import DecodeGraph
+    lens = [9, 300, 1024, 2000]
+    S, H, Hkv, d = len(lens), 32, 8, 128
+    p = O.make_paged_problem(54, S, H, Hkv, d, lens)
+    q, kc, vc = (cuda(p[x], torch.bfloat16) for x in ("q", "k_cache", "v_cache"))
+    bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
+
+    def step():
+        parts = [flash_engine.paged_decode_partials(q, kc, vc, bt, cl, tb, te)
+                 for tb, te in ((0, 1008), (1008, 2000))]
+        return flash_engine.merge_partials(torch.stack([o for o, _ in parts]),
+                                           torch.stack([s for _, s in parts]), 2, 1, "bf16")
+
+    g = DecodeGraph(step, warmup=0)
+    for seed in (55, 56):
+        q2 = O.make_paged_problem(seed, S, H, Hkv, d, lens)["q"]
+        q.copy_(cuda(q2, torch.bfloat16))
+        out = g.replay()
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        assert_bf16_close(host(out).reshape(S, H, d), ref)
