@@ -344,8 +344,8 @@ int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v,
   if (!dense_args_ok(B, H, N, M, d)) return kErr;
   if (B * H == 0 || N == 0) return 0;
   return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
-                                                      resolve_scale(scale, d), true,
-                                                      as_stream(stream)));
+                                                      resolve_scale(scale, d), true, nullptr,
+                                                      nullptr, 0, as_stream(stream)));
 }
 
 int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v, void* o, int B,
@@ -354,7 +354,21 @@ int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v,
   if (!dense_args_ok(B, H, N, M, d)) return kErr;
   if (B * H == 0 || N == 0) return 0;
   return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
-                                                      resolve_scale(scale, d), false,
+                                                      resolve_scale(scale, d), false, nullptr,
+                                                      nullptr, 0, as_stream(stream)));
+}
+
+int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o, int B,
+                                  int H, int N, int M, int d, int causal, float scale, int dtype,
+                                  const float* rope_cos, const float* rope_sin, int rope_max_pos,
+                                  void* stream) {
+  if (!dense_args_ok(B, H, N, M, d) || (dtype != 0 && dtype != 1)) return kErr;
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return kErr;
+  if (rope_cos && (rope_max_pos < N || rope_max_pos < M)) return kErr;
+  if (B * H == 0 || N == 0) return 0;
+  return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
+                                                      resolve_scale(scale, d), dtype == 0,
+                                                      rope_cos, rope_sin, rope_max_pos,
                                                       as_stream(stream)));
 }
 
@@ -433,6 +447,27 @@ int fe_paged_attention_v2_bf16(const void* q, const void* kc, const void* vc, vo
                                float* workspace, size_t workspace_floats, void* stream) {
   PagedArgs a{q, kc, vc, out, bt, lens, S, H, Hkv, d, bs, max_ctx, maxb, num_blocks, scale};
   return paged_v2_tc<__nv_bfloat16>(a, workspace, workspace_floats, as_stream(stream));
+}
+
+int fe_paged_kv_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                       const int* bt, const int* lens, int S, int Hkv, int d, int bs, int maxb,
+                       int num_blocks, int dtype, int kv_layout, const float* rope_cos,
+                       const float* rope_sin, int rope_max_pos, void* stream) {
+  if (S < 0 || Hkv <= 0 || d <= 0 || d % 2 != 0 || bs <= 0 || maxb < 0) return kErr;
+  if (kv_layout != fe::paged::kKvFlat && kv_layout != fe::paged::kKvVllm) return kErr;
+  if (kv_layout == fe::paged::kKvVllm && (dtype == 2 || d % 8 != 0)) return kErr;
+  if ((rope_cos == nullptr) != (rope_sin == nullptr) || (rope_cos && rope_max_pos < 1))
+    return kErr;
+  if (S == 0) return 0;
+  unsigned* err = fe::device_error_word();
+  if (!err) return static_cast<int>(cudaErrorInitializationError);
+  fe::paged::AppendParams ap{k_new, v_new, k_cache, v_cache, bt, lens, S, Hkv, d, bs, maxb,
+                             num_blocks, kv_layout, rope_cos, rope_sin, rope_max_pos, err};
+  cudaStream_t st = as_stream(stream);
+  if (dtype == 0) return static_cast<int>(fe::paged::launch_kv_append<__nv_bfloat16>(ap, st));
+  if (dtype == 1) return static_cast<int>(fe::paged::launch_kv_append<half>(ap, st));
+  if (dtype == 2) return static_cast<int>(fe::paged::launch_kv_append<float>(ap, st));
+  return kErr;
 }
 
 size_t fe_paged_attention_v2_workspace_floats(int H, int Hkv, int d, int bs) {

@@ -1623,6 +1623,85 @@ cudaError_t launch_xmerge(const XMergeParams& xp, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, kern, xp);
 }
 
+// ---------------------------------------------------------------------------
+// Cache append of the decode step's new token: K and V rows of sequence s (position
+// context_lens[s] - 1) are written into row pos % BS of physical block
+// block_tables[s, pos / BS], K rotated at that position first when tables are given
+// (pairs (2i, 2i+1): x0 c - x1 s, x0 s + x1 c, src/fused_rope.cu:33-43). One CTA per
+// sequence, one thread per (KV head, pair). Not launched with programmatic dependent
+// launch, so a decode that follows on the stream starts after it completes.
+template <typename T>
+__device__ __forceinline__ float to_f(T x) { return static_cast<float>(x); }
+template <typename T>
+__device__ __forceinline__ T from_f(float x) { return static_cast<T>(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ half from_f<half>(float x) { return __float2half_rn(x); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) kv_append_kernel(const AppendParams ap) {
+  const int s = blockIdx.x;
+  const int pos = __ldg(ap.context_lens + s) - 1;
+  if (pos < 0) return;
+  const int half_d = ap.head_dim / 2;
+  const int blk = pos / ap.block_size, off = pos % ap.block_size;
+  if (blk >= ap.max_blocks_per_seq) {
+    if (threadIdx.x == 0) atomicOr(ap.err, kErrBadBlock);
+    return;
+  }
+  const int phys = __ldg(ap.block_tables + static_cast<size_t>(s) * ap.max_blocks_per_seq + blk);
+  if (phys < 0 || (ap.num_blocks > 0 && phys >= ap.num_blocks)) {
+    if (threadIdx.x == 0) atomicOr(ap.err, kErrBadBlock);
+    return;
+  }
+  const bool rope = ap.rope_cos != nullptr;
+  if (rope && pos >= ap.rope_max_pos) {
+    if (threadIdx.x == 0) atomicOr(ap.err, kErrBadBlock);
+    return;
+  }
+  const T* kn = static_cast<const T*>(ap.k_new);
+  const T* vn = static_cast<const T*>(ap.v_new);
+  T* kc = static_cast<T*>(ap.k_cache);
+  T* vc = static_cast<T*>(ap.v_cache);
+  const int D = ap.head_dim, BS = ap.block_size;
+  for (int idx = threadIdx.x; idx < ap.num_kv_heads * half_d; idx += blockDim.x) {
+    const int h = idx / half_d, i = idx - h * half_d;
+    const size_t src = (static_cast<size_t>(s) * ap.num_kv_heads + h) * D + 2 * i;
+    float k0 = to_f(kn[src]), k1 = to_f(kn[src + 1]);
+    if (rope) {
+      const float c = __ldg(ap.rope_cos + static_cast<size_t>(pos) * half_d + i);
+      const float sn = __ldg(ap.rope_sin + static_cast<size_t>(pos) * half_d + i);
+      const float r0 = k0 * c - k1 * sn, r1 = k0 * sn + k1 * c;
+      k0 = r0;
+      k1 = r1;
+    }
+    const size_t page = static_cast<size_t>(phys) * ap.num_kv_heads + h;  // (block, KV head)
+    for (int e = 0; e < 2; ++e) {
+      const int dim = 2 * i + e;
+      size_t kd, vd;
+      if (ap.kv_layout == kKvFlat) {
+        kd = vd = (page * BS + off) * D + dim;
+      } else {  // vLLM: K [.., D/8, BS, 8], V [.., D, BS]
+        kd = ((page * (D / 8) + dim / 8) * BS + off) * 8 + dim % 8;
+        vd = (page * D + dim) * BS + off;
+      }
+      kc[kd] = from_f<T>(e == 0 ? k0 : k1);
+      vc[vd] = vn[src + e];
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_kv_append(const AppendParams& ap, cudaStream_t stream) {
+  if (ap.num_seqs <= 0) return cudaSuccess;
+  kv_append_kernel<T><<<ap.num_seqs, 256, 0, stream>>>(ap);
+  return cudaGetLastError();
+}
+template cudaError_t launch_kv_append<__nv_bfloat16>(const AppendParams&, cudaStream_t);
+template cudaError_t launch_kv_append<half>(const AppendParams&, cudaStream_t);
+template cudaError_t launch_kv_append<float>(const AppendParams&, cudaStream_t);
+
 #ifdef FE_TIMELINE
 extern "C" int fe_debug_timeline(unsigned long long* host, int ctas) {
   if (ctas > kCounterSlots) ctas = kCounterSlots;

@@ -124,6 +124,24 @@ cudaError_t launch_decode(const Params& p, int head_dim, int block_size, const v
 
 cudaError_t launch_merge(const MergeParams& mp, int head_dim, cudaStream_t stream);
 
+// Cache append of the new token of every sequence (kv_append_kernel).
+struct AppendParams {
+  const void* k_new;        // [S, Hkv, D] (T)
+  const void* v_new;        // [S, Hkv, D]
+  void* k_cache;            // flat [blocks, Hkv, BS, D] or vLLM K [blocks, Hkv, D/8, BS, 8]
+  void* v_cache;            // flat, or vLLM V [blocks, Hkv, D, BS]
+  const int* block_tables;  // [S, max_blocks_per_seq]
+  const int* context_lens;  // [S]; the new token sits at position context_lens[s] - 1
+  int num_seqs, num_kv_heads, head_dim, block_size, max_blocks_per_seq, num_blocks;
+  int kv_layout;
+  const float* rope_cos;    // optional [rope_max_pos, D/2]: K rotated at its position
+  const float* rope_sin;
+  int rope_max_pos;
+  unsigned* err;
+};
+template <typename T>
+cudaError_t launch_kv_append(const AppendParams& ap, cudaStream_t stream);
+
 // Flat-mode scratch: kCounterSlots int arrival counters at the start (the same
 // place for every shape, so a workspace shared by several shapes keeps them at
 // zero), then `slot_rows` fixup rows of O (D floats each) and of stats (2 each).

@@ -56,7 +56,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 19;
+  static constexpr int NBARS = 23;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -65,6 +65,10 @@ struct PParams {
   void* out;
   int N, M, BH;
   int d_out;  // head dim of the tensors: D, or 32 when the D = 64 kernel runs d = 32
+  // Optional rotary embedding of Q and K (NULL = off): fp32 tables [rope_max_pos, d/2];
+  // query row i and key row j are rotated at positions i and j.
+  const float* rope_cos;
+  const float* rope_sin;
   int causal;
   float scale_log2;
   unsigned* err;
@@ -138,6 +142,51 @@ __device__ __forceinline__ uint32_t pack2<half>(float lo, float hi) {
   return pack_f16x2(lo, hi);
 }
 
+// RoPE of one 16-byte chunk (8 elements = 4 pairs (2i, 2i+1)) of a 128B-swizzled tile
+// row in shared memory: (x0 c - x1 s, x0 s + x1 c) in fp32 (src/fused_rope.cu:33-43),
+// rounded back to T. cs / sn point at the 4 pairs' table entries (16-byte aligned).
+template <typename T>
+__device__ __forceinline__ void rope_chunk(uint8_t* addr, const float* cs, const float* sn) {
+  uint4 v = *reinterpret_cast<uint4*>(addr);
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cs));
+  const float4 s = __ldg(reinterpret_cast<const float4*>(sn));
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float x0, x1;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      x0 = __uint_as_float(w[k] << 16);
+      x1 = __uint_as_float(w[k] & 0xffff0000u);
+    } else {
+      x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] & 0xffffu)));
+      x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] >> 16)));
+    }
+    w[k] = pack2<T>(x0 * cc[k] - x1 * ss[k], x0 * ss[k] + x1 * cc[k]);
+  }
+  *reinterpret_cast<uint4*>(addr) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Rotates the 16-byte chunks first, first + step, ... (below last) of a [128][D] tile
+// of 16-bit elements stored as D/64 column halves of 128B-swizzled 128-byte rows (chunk
+// c is row c / (D/8)); row r has position pos0 + r. Columns at or past d (d = 32 on the
+// D = 64 kernel) and rows at or past `rows` (zero-filled) are left as they are.
+template <typename T, int D>
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int first, int last, int step,
+                                          int pos0, int rows, int d, const float* cos_t,
+                                          const float* sin_t) {
+  constexpr int CPR = D / 8;  // 16-byte chunks per row
+  for (int c = first; c < last; c += step) {
+    const int row = c / CPR, ch = c - row * CPR;
+    const int col = ch * 8;
+    if (pos0 + row >= rows || col >= d) continue;
+    const int h = col / 64, cc = (col % 64) / 8;
+    uint8_t* addr = tile + h * (128 * 128) + row * 128 + ((cc ^ (row & 7)) << 4);
+    const size_t e = static_cast<size_t>(pos0 + row) * (d / 2) + col / 2;
+    rope_chunk<T>(addr, cos_t + e, sin_t + e);
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(384, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -163,6 +212,9 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* drain = bars + 15;
   uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
   uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
+  uint64_t* q_rot = bars + 19;    // [2] RoPE: Q_t rotated in shared memory
+  uint64_t* k_rot = bars + 21;    // [2] RoPE: the K tile of that stage rotated
+  const bool rope = p.rope_cos != nullptr;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -208,6 +260,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_half[i], 128);
+      mbar_init(&q_rot[i], 128);
+      mbar_init(&k_rot[i], 1);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -230,7 +284,80 @@ __global__ void __launch_bounds__(384, 1)
    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
    if (warp == 8) {
     // ========================================================= TMA producer
-    if (lane == 0 && nmax > 0) {
+    if (rope && nmax > 0) {
+      // RoPE: the whole warp rotates each K tile in shared memory after it lands (lane 0
+      // issues the copies). Per step j: issue K_{j+1}, rotate K_j, then issue V_{j+1};
+      // V_{j+1} needs P V of step j-1 done, which needs S_1(j), which needs K_j rotated.
+      const uint64_t pol_keep = l2_policy_evict_last();
+      const uint64_t pol_once = l2_policy_evict_first();
+      if (lane == 0) {
+        prefetch_tensormap(&qmap);
+        prefetch_tensormap(&kmap);
+        prefetch_tensormap(&vmap);
+      }
+      auto load_q = [&](int t) {
+        uint64_t* bar = t == 0 ? q_full : q_full1;
+        mbar_arrive_expect_tx(bar, TILE);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::Q_OFF + t * TILE + h * HALF, &qmap, h * 64, m0[t], bh, bar,
+                      pol_once);
+      };
+      auto issue_k = [&](int j) -> bool {
+        const int st = j & 1, rnd = j >> 1;
+        if (rnd > 0 && !mbar_wait(&k_empty[st], (rnd - 1) & 1)) return false;
+        mbar_arrive_expect_tx(&k_full[st], TILE);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::K_OFF + st * TILE + h * HALF, &kmap, h * 64, j * BN, bh,
+                      &k_full[st], pol_keep);
+        return true;
+      };
+      auto issue_v = [&](int j) -> bool {
+        const int st = j & 1, rnd = j >> 1;
+        if (rnd > 0 && !mbar_wait(&v_empty[st], (rnd - 1) & 1)) return false;
+        mbar_arrive_expect_tx(&v_full[st], TILE);
+        for (int h = 0; h < HALVES; ++h)
+          tma_load_3d(smem + C::V_OFF + st * TILE + h * HALF, &vmap, h * 64, j * BN, bh,
+                      &v_full[st], pol_keep);
+        return true;
+      };
+      int issued_k = 0, issued_v = 0;
+      int good = 1;
+      if (lane == 0) {
+        if (nkv[0] > 0) load_q(0);
+        issue_k(0);
+        if (nkv[1] > 0) load_q(1);
+        issue_v(0);
+      }
+      issued_k = issued_v = 1;
+      for (int j = 0; j < nmax && good; ++j) {
+        if (j + 1 < nmax) {
+          if (lane == 0) good = issue_k(j + 1);
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) break;
+          ++issued_k;
+        }
+        const int st = j & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (j >> 1) & 1))) { good = 0; break; }
+        rope_tile<T, D>(smem + C::K_OFF + st * TILE, lane, 128 * (D / 8), 32, j * BN, p.M,
+                        p.d_out, p.rope_cos, p.rope_sin);
+        fence_proxy_async_smem();  // generic writes before the tensor core reads them
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&k_rot[st]);
+        if (j + 1 < nmax) {
+          if (lane == 0) good = issue_v(j + 1);
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) break;
+          ++issued_v;
+        }
+      }
+      if (lane == 0) {
+        if (!good) atomicOr(p.err, kErrWaitTimeout);
+        if (nkv[0] > 0) mbar_wait(q_full, 0);
+        if (nkv[1] > 0) mbar_wait(q_full1, 0);
+        for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1);
+        for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
+      }
+    } else if (lane == 0 && nmax > 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
@@ -302,13 +429,17 @@ __global__ void __launch_bounds__(384, 1)
         if (half == 1) tc::commit(&o_done[t]);
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
-      bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
+      // with RoPE, Q_t and K tiles are used once rotated
+      uint64_t* const q0_bar = rope ? &q_rot[0] : q_full;
+      uint64_t* const q1_bar = rope ? &q_rot[1] : q_full1;
+      uint64_t* const k_bar = rope ? k_rot : k_full;
+      bool ok = (nkv[0] == 0 || mbar_wait(q0_bar, 0)) && mbar_wait(&k_bar[0], 0);
       if (ok && nkv[0] > 0) {
         tc::fence_after_sync();
         issue_s(0, 0);
       }
       if (ok && nkv[1] > 0) {
-        ok = mbar_wait(q_full1, 0);
+        ok = mbar_wait(q1_bar, 0);
         if (ok) {
           tc::fence_after_sync();
           issue_s(1, 0);
@@ -328,7 +459,7 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
           issue_pv_half(0, j, 1);
           if (j + 1 < nkv[0]) {
-            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
             issue_s(0, j + 1);
           }
@@ -341,13 +472,13 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
           issue_pv_half(1, j, 1);
           if (j + 1 < nkv[1]) {
-            if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!k_ready && !mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
             issue_s(1, j + 1);
           }
         }
         if (next_k) {
-          if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+          if (!k_ready && !mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
           tc::commit(&k_empty[(j + 1) & 1]);
         }
         tc::commit(&v_empty[st]);
@@ -371,6 +502,17 @@ __global__ void __launch_bounds__(384, 1)
     const float sl = p.scale_log2;
     float m_run = NEG_INF, l_run = 0.f;
     bool ok = true;
+    if (rope && nkv[t] > 0) {
+      // RoPE: this thread rotates its own row of Q_t (position r) once it has landed
+      ok = __all_sync(0xffffffffu, mbar_wait(t == 0 ? q_full : q_full1, 0));
+      if (ok) {
+        constexpr int CPR = D / 8;
+        rope_tile<T, D>(smem + C::Q_OFF + t * TILE, row * CPR, (row + 1) * CPR, 1, m0[t], p.N,
+                        p.d_out, p.rope_cos, p.rope_sin);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&q_rot[t]);
+    }
     for (int j = 0; j < nkv[t] && ok; ++j) {
       const bool got = mbar_wait(&s_full[t], j & 1);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
@@ -509,7 +651,8 @@ __global__ void __launch_bounds__(384, 1)
 // stored.
 template <typename T, int D>
 static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o, int B, int H,
-                            int N, int M, int d, int causal, float scale, cudaStream_t st) {
+                            int N, int M, int d, int causal, float scale, const float* rope_cos,
+                            const float* rope_sin, cudaStream_t st) {
   using C = PCfg<D>;
   auto kern = fa_prefill_kernel<T, D>;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
@@ -528,6 +671,8 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
   p.N = N;
   p.M = M;
   p.d_out = d;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
   p.BH = static_cast<int>(BH);
   p.causal = causal;
   p.scale_log2 = scale * kLog2e;
@@ -554,19 +699,24 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
 
 cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o, int B, int H,
                            int N, int M, int d, int causal, float scale, bool is_bf16,
+                           const float* rope_cos, const float* rope_sin, int rope_max_pos,
                            cudaStream_t stream) {
   if (!(d == 32 || d == 64 || d == 128)) return cudaErrorInvalidValue;
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return cudaErrorInvalidValue;
+  if (rope_cos && (rope_max_pos < N || rope_max_pos < M ||
+                   ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15)))
+    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15)
     return cudaErrorInvalidValue;
   if (static_cast<long long>(B) * H > 65535) return cudaErrorInvalidValue;
   if (is_bf16) {
     if (d == 128)
-      return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
-    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+      return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
+    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
   }
-  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
-  return launch_d<half, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
+  return launch_d<half, 64>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
 }
 
 }  // namespace prefill

@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     paged_attention,
     paged_attention_workspace_floats,
     paged_decode_partials,
+    paged_kv_append,
 )
 
 __version__ = "1.2.0"
@@ -26,6 +27,7 @@ __all__ = [
     "flash_decoding",
     "naive_attention",
     "paged_decode_partials",
+    "paged_kv_append",
     "merge_partials",
     "paged_attention_workspace_floats",
     "device_errors",

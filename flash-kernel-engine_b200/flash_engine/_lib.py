@@ -36,11 +36,14 @@ _SIGS = {
     "fe_flash_attention_forward_fp16": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P], _I),
     "fe_flash_attention_forward_bf16": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P], _I),
     "fe_naive_attention_forward_fp32": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P], _I),
+    "fe_flash_attention_forward_ex": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P, _I,
+                                       _P], _I),
     "fe_paged_attention_v1_fp32": ([_P, _P, _P, _P, _P, _P] + [_I] * 8 + [_F, _P], _I),
     "fe_paged_attention_v1_fp16": ([_P, _P, _P, _P, _P, _P] + [_I] * 8 + [_F, _P], _I),
     "fe_paged_attention_v1_bf16": ([_P, _P, _P, _P, _P, _P] + [_I] * 8 + [_F, _P], _I),
     "fe_paged_attention_v2_bf16": ([_P] * 6 + [_I] * 8 + [_F, _P, ctypes.c_size_t, _P], _I),
     "fe_paged_attention_v2_workspace_floats": ([_I] * 4, ctypes.c_size_t),
+    "fe_paged_kv_append": ([_P] * 6 + [_I] * 8 + [_P, _P, _I, _P], _I),
     "fe_paged_attention_ex": ([_P] * 6 + [_I] * 7 + [_F, _I, _I, _P, _P, _I, _P,
                                                      ctypes.c_size_t, _P], _I),
     "fe_paged_attention_v2_bf16_noalloc": ([_P] * 6 + [_I] * 8 + [_F, _P], _I),

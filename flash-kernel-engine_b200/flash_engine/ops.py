@@ -64,11 +64,14 @@ def _scale_arg(scale, d):
 
 # --------------------------------------------------------------------------- prefill
 def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None, *,
-                    out=None):
+                    out=None, rope=None):
     """FA2 forward: softmax(q k^T * scale [+ top-left causal mask]) v.
 
     q: [B, H, N, d]; k, v: [B, H, M, d]; dtype float32, bfloat16 or float16. ``out``
-    (optional, new): a contiguous tensor like q to write into.
+    (optional, new): a contiguous tensor like q to write into. ``rope=(cos, sin)``
+    (optional, new; bf16/fp16): float32 CUDA tables [max_pos, d/2] with max_pos >= N, M;
+    query row i and key row j are rotated at positions i and j inside the kernel (the
+    reference's fused RoPE arithmetic, applied to Q and K).
     """
     _require_cuda(q, k, v)
     B, H, N, d = q.shape
@@ -81,6 +84,20 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
         out = torch.empty_like(q)
     elif out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous tensor like q")
+    if rope is not None:
+        if q.dtype not in (torch.bfloat16, torch.float16):
+            raise TypeError("rope is supported for bfloat16 / float16 attention")
+        rcos, rsin = rope
+        _require_cuda(rcos, rsin)
+        if rcos.dtype != torch.float32 or rcos.shape != rsin.shape or rcos.dim() != 2 or \
+                rcos.shape[1] != d // 2 or rcos.shape[0] < max(N, M):
+            raise ValueError("rope tables must be float32 [max_pos >= max(N, M), d/2]")
+        with _on(q.device):
+            _lib.check(_lib_c.fe_flash_attention_forward_ex(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
+                _scale_arg(scale, d), 0 if q.dtype == torch.bfloat16 else 1, _ptr(rcos),
+                _ptr(rsin), rcos.shape[0], _stream()), "flash_attention")
+        return out
     fn = {torch.float32: _lib_c.fe_flash_attention_forward_fp32,
           torch.bfloat16: _lib_c.fe_flash_attention_forward_bf16,
           torch.float16: _lib_c.fe_flash_attention_forward_fp16}.get(q.dtype)
@@ -268,6 +285,43 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens,
         else:
             raise TypeError(f"unsupported dtype {query.dtype}")
     return out
+
+
+def paged_kv_append(k_new, v_new, key_cache, value_cache, block_tables, context_lens,
+                    block_size: int = 16, *, kv_layout: str = "flat", rope=None):
+    """Writes the decode step's new token into the paged cache: K and V rows
+    k_new / v_new [S, Hkv, d] of sequence s go to position context_lens[s] - 1 (block
+    block_tables[s, pos // block_size], row pos % block_size). ``rope=(cos, sin)``: float32
+    CUDA tables [max_pos, d/2]; the key is rotated at that position first (the reference's
+    fused RoPE arithmetic), so with the same tables passed to ``paged_attention`` both the
+    query and the keys carry the embedding. Returns the caches."""
+    _require_cuda(k_new, v_new, key_cache, value_cache, block_tables, context_lens)
+    S, Hkv, d = k_new.shape
+    if v_new.shape != k_new.shape or k_new.dtype != key_cache.dtype or \
+            v_new.dtype != key_cache.dtype:
+        raise ValueError("k_new / v_new must be [S, Hkv, d] of the cache dtype")
+    dummy_q = k_new.new_empty((S, Hkv, d))
+    _, _, Hkv2, d2, nb, maxb = _paged_shapes(dummy_q, key_cache, value_cache, block_tables,
+                                             context_lens, block_size, kv_layout)
+    if Hkv2 != Hkv or d2 != d:
+        raise ValueError("k_new does not match the cache's KV heads / head_dim")
+    dt = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}.get(k_new.dtype)
+    if dt is None:
+        raise TypeError(f"unsupported dtype {k_new.dtype}")
+    rc, rs, rmax = None, None, 0
+    if rope is not None:
+        rcos, rsin = rope
+        _require_cuda(rcos, rsin)
+        if rcos.dtype != torch.float32 or rcos.shape != rsin.shape or rcos.dim() != 2 or \
+                rcos.shape[1] != d // 2:
+            raise ValueError("rope tables must be float32 [max_pos, d/2]")
+        rc, rs, rmax = _ptr(rcos), _ptr(rsin), rcos.shape[0]
+    with _on(k_new.device):
+        _lib.check(_lib_c.fe_paged_kv_append(
+            _ptr(k_new), _ptr(v_new), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+            _ptr(context_lens), S, Hkv, d, block_size, maxb, nb, dt,
+            0 if kv_layout == "flat" else 1, rc, rs, rmax, _stream()), "paged_kv_append")
+    return key_cache, value_cache
 
 
 def paged_decode_partials(query, key_cache, value_cache, block_tables, context_lens,

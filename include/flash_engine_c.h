@@ -77,6 +77,19 @@ int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v,
                                     int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                     int is_causal, float softmax_scale, void* stream);
 
+/* bf16 (dtype 0) or fp16 (dtype 1) FA2 forward of fe_flash_attention_forward_bf16 /
+ * _fp16 with an optional fused rotary embedding: rope_cos / rope_sin (NULL = off) are
+ * fp32 tables [rope_max_pos, head_dim/2] (16-byte aligned, rope_max_pos >= seq_q and
+ * >= seq_kv); query row i and key row j of every (batch, head) are rotated at positions
+ * i and j, pairs (2i, 2i+1), as the reference's fused RoPE does to Q and K
+ * (src/fused_rope.cu:13-69), inside the kernel after their tiles land in shared memory.
+ * New (the reference applies RoPE as a separate pass over Q and K). */
+int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o,
+                                  int batch, int heads, int seq_q, int seq_kv, int head_dim,
+                                  int is_causal, float softmax_scale, int dtype,
+                                  const float* rope_cos, const float* rope_sin, int rope_max_pos,
+                                  void* stream);
+
 /* Row-per-thread fp32 attention. Replaces launch_naive_attention_forward_fp32
  * (include/flash_attention.cuh:79-86, src/flash_attention.cu:86-104). */
 int fe_naive_attention_forward_fp32(const float* q, const float* k, const float* v, float* o,
@@ -183,6 +196,24 @@ int fe_paged_attention_v2_bf16(const void* q, const void* k_cache, const void* v
                                int block_size, int max_context_len, int max_blocks_per_seq,
                                int num_blocks, float scale, float* workspace,
                                size_t workspace_floats, void* stream);
+
+/* Cache append of the decode step's new token, with the rotary embedding of the key
+ * fused in: for every sequence s with context_lens[s] > 0, the K row k_new[s, h] (rotated
+ * at position context_lens[s] - 1 when rope_cos / rope_sin are given: fp32 tables
+ * [rope_max_pos, d/2], pairs (2i, 2i+1) as src/fused_rope.cu:33-43) and the V row
+ * v_new[s, h] ([S, Hkv, d] each) are written into row (ctx - 1) % block_size of physical
+ * block block_tables[s, (ctx - 1) / block_size] for every KV head h. dtype 0 bf16, 1
+ * fp16, 2 fp32; kv_layout 0 flat, 1 vLLM (16-bit types). Launched without programmatic
+ * completion, so a decode that follows on the stream reads the appended rows; with the
+ * decode's rope tables the query is rotated at the same position, so Q and K both carry
+ * the embedding. Out-of-range block-table entries set bit 1 of the device error word.
+ * New: the reference has no cache writer (its fused RoPE, src/fused_rope.cu:13-69,
+ * rotates a dense Q or K tensor). */
+int fe_paged_kv_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                       const int* block_tables, const int* context_lens, int num_seqs,
+                       int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq,
+                       int num_blocks, int dtype, int kv_layout, const float* rope_cos,
+                       const float* rope_sin, int rope_max_pos, void* stream);
 
 /* Scratch slots of the v1 entry points (see fe_paged_attention_v1_bf16). */
 #define FE_STREAM_SCRATCH_SLOTS 4

@@ -519,3 +519,56 @@ def test_v1_entries_on_many_streams():
         assert _lib.device_errors() == 0
         for o in outs:
             assert_bf16_close(host(o), ref)
+
+
+@pytest.mark.parametrize("dtype,kv_layout", [(torch.bfloat16, "flat"), (torch.bfloat16, "vllm"),
+                                             (torch.float16, "flat"), (torch.float32, "flat")])
+def test_kv_append_with_rope_then_decode(dtype, kv_layout):
+    """One decode step with RoPE on Q and K: the new token's key is rotated at position
+    ctx - 1 and written with its value into the paged cache (fe_paged_kv_append), then
+    the decode rotates the query at the same position. The cache's earlier keys were
+    stored rotated by earlier steps. Against the oracle with Q and every key rotated."""
+    import flash_engine
+    lens = [1, 17, 700, 2000, 0]
+    S, H, Hkv, d = len(lens), 32, 8, 128
+    p = O.make_paged_problem(81, S, H, Hkv, d, lens, bf16=dtype != torch.float32)
+    cos, sin = O.rope_tables(4096, d)
+    rnd = (lambda x: O.bf16_round(x.astype(np.float32))) if dtype == torch.bfloat16 else \
+        (lambda x: x.astype(np.float16).astype(np.float32)) if dtype == torch.float16 else \
+        (lambda x: x.astype(np.float32))
+    kc, vc = rnd(p["k_cache"]), rnd(p["v_cache"])
+    rng = np.random.default_rng(82)
+    k_new = rnd(rng.standard_normal((S, Hkv, d), dtype=np.float32))
+    v_new = rnd(rng.standard_normal((S, Hkv, d), dtype=np.float32))
+    # what the cache must hold after the append: the new key rotated at ctx - 1
+    kc_ref, vc_ref = kc.copy(), vc.copy()
+    for s, c in enumerate(lens):
+        if c <= 0:
+            continue
+        blk, off = p["block_tables"][s, (c - 1) // 16], (c - 1) % 16
+        kc_ref[blk, :, off] = rnd(O.rope_rotate(k_new[s], cos, sin, c - 1))
+        vc_ref[blk, :, off] = v_new[s]
+    pos = np.maximum(np.asarray(lens) - 1, 0)
+    q = rnd(p["q"])
+    q_rot = rnd(O.rope_rotate(q, cos, sin, pos[:, None]))
+    ref = O.paged_attention_gqa(q_rot, kc_ref, vc_ref, p["block_tables"], p["context_lens"])
+    kd, vd = kc, vc
+    if kv_layout == "vllm":
+        kd, vd = _to_vllm(kc, vc)
+    kd, vd = cuda(kd, dtype), cuda(vd, dtype)
+    bt, cl = cuda(p["block_tables"]), cuda(p["context_lens"])
+    tabs = (cuda(cos), cuda(sin))
+    flash_engine.paged_kv_append(cuda(k_new, dtype), cuda(v_new, dtype), kd, vd, bt, cl, 16,
+                                 kv_layout=kv_layout, rope=tabs)
+    out = flash_engine.paged_attention(cuda(q, dtype), kd, vd, bt, cl, 16, kv_layout=kv_layout,
+                                       rope=tabs)
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    if dtype == torch.float32:
+        assert_fp32_close(host(out), ref)
+    else:
+        assert_bf16_close(host(out), ref, atol=2e-2 if dtype == torch.bfloat16 else 5e-3)
+    # the appended rows landed where the oracle put them (flat layout: checked bit for bit)
+    if kv_layout == "flat":
+        np.testing.assert_array_equal(host(kd), kc_ref.astype(np.float32)
+                                      if dtype == torch.float32 else host(cuda(kc_ref, dtype)))

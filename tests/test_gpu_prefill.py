@@ -204,3 +204,47 @@ def test_bf16_first_call_inside_graph_capture():
     for h in (0, 11, 23):
         ref = O.flash_attention_sliced(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], True)
         assert_bf16_close(o[:, h:h + 1], ref)
+
+
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("N,M", [(300, 300), (128, 520), (640, 200)])
+def test_bf16_fused_rope_q_and_k(d, causal, N, M):
+    """RoPE of Q (row i at position i) and K (row j at position j) fused into the
+    tensor-core prefill, against the oracle rotating Q and K first (the reference's
+    fused RoPE arithmetic, src/fused_rope.cu:33-43) then attending."""
+    import flash_engine
+    rng = np.random.default_rng(N + M + d)
+    q = O.bf16_round(rng.standard_normal((2, 3, N, d), dtype=np.float32))
+    k = O.bf16_round(rng.standard_normal((2, 3, M, d), dtype=np.float32))
+    v = O.bf16_round(rng.standard_normal((2, 3, M, d), dtype=np.float32))
+    cos, sin = O.rope_tables(max(N, M) + 7, d)
+    qr = O.bf16_round(O.rope_rotate(q, cos, sin, np.arange(N)[:, None]).astype(np.float32))
+    kr = O.bf16_round(O.rope_rotate(k, cos, sin, np.arange(M)[:, None]).astype(np.float32))
+    ref = O.flash_attention_sliced(qr, kr, v, causal)
+    out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
+                                       cuda(v, torch.bfloat16), causal,
+                                       rope=(cuda(cos), cuda(sin)))
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out), ref)
+
+
+def test_fp16_fused_rope_config2_slice():
+    """Fused RoPE on the config 2 shape (causal, 4096 rows, d 128) in fp16, 2 heads."""
+    import flash_engine
+    rng = np.random.default_rng(7)
+    N, d = 4096, 128
+    q, k, v = (rng.standard_normal((1, 2, N, d), dtype=np.float32).astype(np.float16)
+               .astype(np.float32) for _ in range(3))
+    cos, sin = O.rope_tables(N, d)
+    pos = np.arange(N)[:, None]
+    qr = O.rope_rotate(q, cos, sin, pos).astype(np.float16).astype(np.float32)
+    kr = O.rope_rotate(k, cos, sin, pos).astype(np.float16).astype(np.float32)
+    ref = O.flash_attention_sliced(qr, kr, v, True)
+    out = flash_engine.flash_attention(cuda(q, torch.float16), cuda(k, torch.float16),
+                                       cuda(v, torch.float16), True,
+                                       rope=(cuda(cos), cuda(sin)))
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out), ref, atol=5e-3)
