@@ -187,7 +187,7 @@ __device__ __forceinline__ void rope_tile(uint8_t* tile, int first, int last, in
   }
 }
 
-template <typename T, int D>
+template <typename T, int D, bool ROPE>
 __global__ void __launch_bounds__(384, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kmap,
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
   uint64_t* q_rot = bars + 19;    // [2] RoPE: Q_t rotated in shared memory
   uint64_t* k_rot = bars + 21;    // [2] RoPE: the K tile of that stage rotated
-  const bool rope = p.rope_cos != nullptr;
+  constexpr bool rope = ROPE;  // a separate instantiation: the plain kernel carries none of it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(384, 1)
    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
    if (warp == 8) {
     // ========================================================= TMA producer
-    if (rope && nmax > 0) {
+    if constexpr (rope) {
+     if (nmax > 0) {
       // RoPE: the whole warp rotates each K tile in shared memory after it lands (lane 0
       // issues the copies). Per step j: issue K_{j+1}, rotate K_j, then issue V_{j+1};
       // V_{j+1} needs P V of step j-1 done, which needs S_1(j), which needs K_j rotated.
@@ -357,6 +358,7 @@ __global__ void __launch_bounds__(384, 1)
         for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1);
         for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
       }
+     }
     } else if (lane == 0 && nmax > 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
@@ -502,7 +504,7 @@ __global__ void __launch_bounds__(384, 1)
     const float sl = p.scale_log2;
     float m_run = NEG_INF, l_run = 0.f;
     bool ok = true;
-    if (rope && nkv[t] > 0) {
+    if (ROPE && nkv[t] > 0) {
       // RoPE: this thread rotates its own row of Q_t (position r) once it has landed
       ok = __all_sync(0xffffffffu, mbar_wait(t == 0 ? q_full : q_full1, 0));
       if (ok) {
@@ -654,7 +656,7 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
                             int N, int M, int d, int causal, float scale, const float* rope_cos,
                             const float* rope_sin, cudaStream_t st) {
   using C = PCfg<D>;
-  auto kern = fa_prefill_kernel<T, D>;
+  auto kern = rope_cos ? fa_prefill_kernel<T, D, true> : fa_prefill_kernel<T, D, false>;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
   if (e != cudaSuccess) return e;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;

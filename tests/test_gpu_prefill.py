@@ -219,8 +219,8 @@ def test_bf16_fused_rope_q_and_k(d, causal, N, M):
     k = O.bf16_round(rng.standard_normal((2, 3, M, d), dtype=np.float32))
     v = O.bf16_round(rng.standard_normal((2, 3, M, d), dtype=np.float32))
     cos, sin = O.rope_tables(max(N, M) + 7, d)
-    qr = O.bf16_round(O.rope_rotate(q, cos, sin, np.arange(N)[:, None]).astype(np.float32))
-    kr = O.bf16_round(O.rope_rotate(k, cos, sin, np.arange(M)[:, None]).astype(np.float32))
+    qr = O.bf16_round(O.rope_rotate(q, cos, sin, np.arange(N)).astype(np.float32))
+    kr = O.bf16_round(O.rope_rotate(k, cos, sin, np.arange(M)).astype(np.float32))
     ref = O.flash_attention_sliced(qr, kr, v, causal)
     out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
                                        cuda(v, torch.bfloat16), causal,
@@ -238,7 +238,7 @@ def test_fp16_fused_rope_config2_slice():
     q, k, v = (rng.standard_normal((1, 2, N, d), dtype=np.float32).astype(np.float16)
                .astype(np.float32) for _ in range(3))
     cos, sin = O.rope_tables(N, d)
-    pos = np.arange(N)[:, None]
+    pos = np.arange(N)
     qr = O.rope_rotate(q, cos, sin, pos).astype(np.float16).astype(np.float32)
     kr = O.rope_rotate(k, cos, sin, pos).astype(np.float16).astype(np.float32)
     ref = O.flash_attention_sliced(qr, kr, v, True)
