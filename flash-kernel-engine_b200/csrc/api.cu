@@ -26,6 +26,7 @@
 #include "paged_decode.h"
 #include "prefill.h"
 #include "ptx.cuh"
+#include "rope.h"
 
 namespace {
 
@@ -358,18 +359,38 @@ int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v,
                                                       nullptr, 0, as_stream(stream)));
 }
 
+int fe_rope_forward(const void* in, const float* cos_table, const float* sin_table, void* out,
+                    int B, int H, int seq_len, int head_dim, int dtype, void* stream) {
+  if (B < 0 || H < 0 || seq_len < 0 || head_dim < 2 || head_dim % 2 || dtype < 0 || dtype > 2 ||
+      !cos_table || !sin_table)
+    return kErr;
+  if (B * H == 0 || seq_len == 0) return 0;
+  return static_cast<int>(fe::rope::launch_rope(in, cos_table, sin_table, out, B, H, seq_len,
+                                                head_dim, dtype, as_stream(stream)));
+}
+
 int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o, int B,
                                   int H, int N, int M, int d, int causal, float scale, int dtype,
                                   const float* rope_cos, const float* rope_sin, int rope_max_pos,
-                                  void* stream) {
+                                  void* k_rotated, void* stream) {
   if (!dense_args_ok(B, H, N, M, d) || (dtype != 0 && dtype != 1)) return kErr;
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return kErr;
-  if (rope_cos && (rope_max_pos < N || rope_max_pos < M)) return kErr;
+  if (rope_cos && (rope_max_pos < N || rope_max_pos < M || !k_rotated)) return kErr;
   if (B * H == 0 || N == 0) return 0;
-  return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
+  cudaStream_t st = as_stream(stream);
+  const void* kk = k;
+  if (rope_cos) {
+    // K rotated once (each key tile is read by every query tile of its head), into the
+    // caller's buffer, which then holds the keys a KV cache stores; Q is rotated in the
+    // attention kernel as its tiles land.
+    const cudaError_t e = fe::rope::launch_rope(k, rope_cos, rope_sin, k_rotated, B, H, M, d,
+                                                dtype, st);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    kk = k_rotated;
+  }
+  return static_cast<int>(fe::prefill::launch_prefill(q, kk, v, o, B, H, N, M, d, causal,
                                                       resolve_scale(scale, d), dtype == 0,
-                                                      rope_cos, rope_sin, rope_max_pos,
-                                                      as_stream(stream)));
+                                                      rope_cos, rope_sin, rope_max_pos, st));
 }
 
 int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc, float* out,
@@ -864,6 +885,27 @@ cudaError_t launch_paged_decode_kv_range_bf16(
 }
 
 }  // namespace paged_attention
+
+namespace rope {
+
+cudaError_t launch_fused_rope_fp32(const float* d_in, const float* d_cos, const float* d_sin,
+                                   float* d_out, const RoPEConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_rope_forward(d_in, d_cos, d_sin, d_out, c.batch_size,
+                                                  c.num_heads, c.seq_len, c.head_dim, 2, s));
+}
+cudaError_t launch_fused_rope_bf16(const __nv_bfloat16* d_in, const float* d_cos,
+                                   const float* d_sin, __nv_bfloat16* d_out, const RoPEConfig& c,
+                                   cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_rope_forward(d_in, d_cos, d_sin, d_out, c.batch_size,
+                                                  c.num_heads, c.seq_len, c.head_dim, 0, s));
+}
+cudaError_t launch_fused_rope_fp16(const half* d_in, const float* d_cos, const float* d_sin,
+                                   half* d_out, const RoPEConfig& c, cudaStream_t s) {
+  return static_cast<cudaError_t>(fe_rope_forward(d_in, d_cos, d_sin, d_out, c.batch_size,
+                                                  c.num_heads, c.seq_len, c.head_dim, 1, s));
+}
+
+}  // namespace rope
 
 namespace decoding {
 

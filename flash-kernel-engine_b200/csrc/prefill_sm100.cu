@@ -56,7 +56,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 23;
+  static constexpr int NBARS = 21;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -65,8 +65,8 @@ struct PParams {
   void* out;
   int N, M, BH;
   int d_out;  // head dim of the tensors: D, or 32 when the D = 64 kernel runs d = 32
-  // Optional rotary embedding of Q and K (NULL = off): fp32 tables [rope_max_pos, d/2];
-  // query row i and key row j are rotated at positions i and j.
+  // Optional rotary embedding of Q (NULL = off): fp32 tables [rope_max_pos, d/2]; query
+  // row i is rotated at position i in shared memory. K arrives rotated (rope_forward).
   const float* rope_cos;
   const float* rope_sin;
   int causal;
@@ -213,7 +213,6 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
   uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
   uint64_t* q_rot = bars + 19;    // [2] RoPE: Q_t rotated in shared memory
-  uint64_t* k_rot = bars + 21;    // [2] RoPE: the K tile of that stage rotated
   constexpr bool rope = ROPE;  // a separate instantiation: the plain kernel carries none of it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
@@ -261,7 +260,6 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&p_full[i], 128);
       mbar_init(&p_half[i], 128);
       mbar_init(&q_rot[i], 128);
-      mbar_init(&k_rot[i], 1);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -284,82 +282,7 @@ __global__ void __launch_bounds__(384, 1)
    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
    if (warp == 8) {
     // ========================================================= TMA producer
-    if constexpr (rope) {
-     if (nmax > 0) {
-      // RoPE: the whole warp rotates each K tile in shared memory after it lands (lane 0
-      // issues the copies). Per step j: issue K_{j+1}, rotate K_j, then issue V_{j+1};
-      // V_{j+1} needs P V of step j-1 done, which needs S_1(j), which needs K_j rotated.
-      const uint64_t pol_keep = l2_policy_evict_last();
-      const uint64_t pol_once = l2_policy_evict_first();
-      if (lane == 0) {
-        prefetch_tensormap(&qmap);
-        prefetch_tensormap(&kmap);
-        prefetch_tensormap(&vmap);
-      }
-      auto load_q = [&](int t) {
-        uint64_t* bar = t == 0 ? q_full : q_full1;
-        mbar_arrive_expect_tx(bar, TILE);
-        for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(smem + C::Q_OFF + t * TILE + h * HALF, &qmap, h * 64, m0[t], bh, bar,
-                      pol_once);
-      };
-      auto issue_k = [&](int j) -> bool {
-        const int st = j & 1, rnd = j >> 1;
-        if (rnd > 0 && !mbar_wait(&k_empty[st], (rnd - 1) & 1)) return false;
-        mbar_arrive_expect_tx(&k_full[st], TILE);
-        for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(smem + C::K_OFF + st * TILE + h * HALF, &kmap, h * 64, j * BN, bh,
-                      &k_full[st], pol_keep);
-        return true;
-      };
-      auto issue_v = [&](int j) -> bool {
-        const int st = j & 1, rnd = j >> 1;
-        if (rnd > 0 && !mbar_wait(&v_empty[st], (rnd - 1) & 1)) return false;
-        mbar_arrive_expect_tx(&v_full[st], TILE);
-        for (int h = 0; h < HALVES; ++h)
-          tma_load_3d(smem + C::V_OFF + st * TILE + h * HALF, &vmap, h * 64, j * BN, bh,
-                      &v_full[st], pol_keep);
-        return true;
-      };
-      int issued_k = 0, issued_v = 0;
-      int good = 1;
-      if (lane == 0) {
-        if (nkv[0] > 0) load_q(0);
-        issue_k(0);
-        if (nkv[1] > 0) load_q(1);
-        issue_v(0);
-      }
-      issued_k = issued_v = 1;
-      for (int j = 0; j < nmax && good; ++j) {
-        if (j + 1 < nmax) {
-          if (lane == 0) good = issue_k(j + 1);
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) break;
-          ++issued_k;
-        }
-        const int st = j & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&k_full[st], (j >> 1) & 1))) { good = 0; break; }
-        rope_tile<T, D>(smem + C::K_OFF + st * TILE, lane, 128 * (D / 8), 32, j * BN, p.M,
-                        p.d_out, p.rope_cos, p.rope_sin);
-        fence_proxy_async_smem();  // generic writes before the tensor core reads them
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&k_rot[st]);
-        if (j + 1 < nmax) {
-          if (lane == 0) good = issue_v(j + 1);
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) break;
-          ++issued_v;
-        }
-      }
-      if (lane == 0) {
-        if (!good) atomicOr(p.err, kErrWaitTimeout);
-        if (nkv[0] > 0) mbar_wait(q_full, 0);
-        if (nkv[1] > 0) mbar_wait(q_full1, 0);
-        for (int j = max(0, issued_k - 2); j < issued_k; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1);
-        for (int j = max(0, issued_v - 2); j < issued_v; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
-      }
-     }
-    } else if (lane == 0 && nmax > 0) {
+    if (lane == 0 && nmax > 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
@@ -431,10 +354,10 @@ __global__ void __launch_bounds__(384, 1)
         if (half == 1) tc::commit(&o_done[t]);
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
-      // with RoPE, Q_t and K tiles are used once rotated
+      // with RoPE, Q_t is used once rotated (K comes rotated from the caller's buffer)
       uint64_t* const q0_bar = rope ? &q_rot[0] : q_full;
       uint64_t* const q1_bar = rope ? &q_rot[1] : q_full1;
-      uint64_t* const k_bar = rope ? k_rot : k_full;
+      uint64_t* const k_bar = k_full;
       bool ok = (nkv[0] == 0 || mbar_wait(q0_bar, 0)) && mbar_wait(&k_bar[0], 0);
       if (ok && nkv[0] > 0) {
         tc::fence_after_sync();

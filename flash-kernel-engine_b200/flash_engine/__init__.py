@@ -17,6 +17,7 @@ from .ops import (  # noqa: F401
     paged_attention_workspace_floats,
     paged_decode_partials,
     paged_kv_append,
+    rope,
 )
 
 __version__ = "1.2.0"
@@ -28,6 +29,7 @@ __all__ = [
     "naive_attention",
     "paged_decode_partials",
     "paged_kv_append",
+    "rope",
     "merge_partials",
     "paged_attention_workspace_floats",
     "device_errors",

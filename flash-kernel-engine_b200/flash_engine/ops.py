@@ -63,15 +63,40 @@ def _scale_arg(scale, d):
 
 
 # --------------------------------------------------------------------------- prefill
+def rope(x, cos, sin, out=None):
+    """Rotary position embedding of x [B, H, seq, d] (float32, bfloat16 or float16): row
+    (b, h, i) is rotated at position i, pairs (2j, 2j+1) -> (x0 c - x1 s, x0 s + x1 c) with
+    the float32 tables cos/sin [>= seq, d/2] (the reference's fused RoPE kernel,
+    src/fused_rope.cu:13-45). ``out`` may be x (in place). Returns out."""
+    _require_cuda(x, cos, sin)
+    B, H, N, d = x.shape
+    if cos.dtype != torch.float32 or cos.shape != sin.shape or cos.dim() != 2 or \
+            cos.shape[1] != d // 2 or cos.shape[0] < N:
+        raise ValueError("rope tables must be float32 [max_pos >= seq, d/2]")
+    dt = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}.get(x.dtype)
+    if dt is None:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    if out is None:
+        out = torch.empty_like(x)
+    elif out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor like x")
+    with _on(x.device):
+        _lib.check(_lib_c.fe_rope_forward(_ptr(x), _ptr(cos), _ptr(sin), _ptr(out), B, H, N, d,
+                                          dt, _stream()), "rope")
+    return out
+
+
 def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None, *,
-                    out=None, rope=None):
+                    out=None, rope=None, k_rotated=None):
     """FA2 forward: softmax(q k^T * scale [+ top-left causal mask]) v.
 
     q: [B, H, N, d]; k, v: [B, H, M, d]; dtype float32, bfloat16 or float16. ``out``
     (optional, new): a contiguous tensor like q to write into. ``rope=(cos, sin)``
     (optional, new; bf16/fp16): float32 CUDA tables [max_pos, d/2] with max_pos >= N, M;
-    query row i and key row j are rotated at positions i and j inside the kernel (the
-    reference's fused RoPE arithmetic, applied to Q and K).
+    query row i and key row j are rotated at positions i and j (the reference's fused
+    RoPE arithmetic, applied to Q and K): K once into ``k_rotated`` (a tensor like k, made
+    here if not given; it then holds the rotated keys a KV cache stores), Q inside the
+    attention kernel.
     """
     _require_cuda(q, k, v)
     B, H, N, d = q.shape
@@ -92,11 +117,16 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
         if rcos.dtype != torch.float32 or rcos.shape != rsin.shape or rcos.dim() != 2 or \
                 rcos.shape[1] != d // 2 or rcos.shape[0] < max(N, M):
             raise ValueError("rope tables must be float32 [max_pos >= max(N, M), d/2]")
+        if k_rotated is None:
+            k_rotated = torch.empty_like(k)
+        elif k_rotated.shape != k.shape or k_rotated.dtype != k.dtype or \
+                not k_rotated.is_contiguous():
+            raise ValueError("k_rotated must be a contiguous tensor like k")
         with _on(q.device):
             _lib.check(_lib_c.fe_flash_attention_forward_ex(
                 _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
                 _scale_arg(scale, d), 0 if q.dtype == torch.bfloat16 else 1, _ptr(rcos),
-                _ptr(rsin), rcos.shape[0], _stream()), "flash_attention")
+                _ptr(rsin), rcos.shape[0], _ptr(k_rotated), _stream()), "flash_attention")
         return out
     fn = {torch.float32: _lib_c.fe_flash_attention_forward_fp32,
           torch.bfloat16: _lib_c.fe_flash_attention_forward_bf16,

@@ -1,8 +1,9 @@
 // Umbrella header of the B200 inference-attention library -- drop-in for the
 // hot-path part of the reference's include/flash_engine.h:1-31: the attention
-// headers and the CUDA graph runner used to capture decode steps. The reference's
-// other kernels (RMSNorm, activations, speculative decoding, quantized GEMM,
-// cross-entropy) and its memory pool are not part of this library.
+// headers, the rotary embedding that feeds attention (fused_rope.cuh) and the CUDA
+// graph runner used to capture decode steps. The reference's other kernels (RMSNorm,
+// activations, speculative decoding, quantized GEMM, cross-entropy) and its memory pool
+// are not part of this library.
 #pragma once
 
 #include "cuda_graph_runner.h"
@@ -11,6 +12,7 @@
 #include "flash_decoding.cuh"
 #include "paged_attention.cuh"
 #include "flash_engine_c.h"
+#include "fused_rope.cuh"
 
 namespace flash_engine {
 

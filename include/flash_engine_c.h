@@ -77,18 +77,27 @@ int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v,
                                     int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                     int is_causal, float softmax_scale, void* stream);
 
+/* Rotary position embedding of a dense [batch, heads, seq_len, head_dim] tensor (dtype
+ * 0 bf16, 1 fp16, 2 fp32): row r of batch*heads*seq_len is rotated at position
+ * r % seq_len with fp32 tables [>= seq_len, head_dim/2]; out may be in. Replaces
+ * launch_fused_rope_fp32 (include/fused_rope.cuh:21-28, src/fused_rope.cu:13-69); the
+ * bf16 / fp16 types are new. */
+int fe_rope_forward(const void* in, const float* cos_table, const float* sin_table, void* out,
+                    int batch, int heads, int seq_len, int head_dim, int dtype, void* stream);
+
 /* bf16 (dtype 0) or fp16 (dtype 1) FA2 forward of fe_flash_attention_forward_bf16 /
- * _fp16 with an optional fused rotary embedding: rope_cos / rope_sin (NULL = off) are
- * fp32 tables [rope_max_pos, head_dim/2] (16-byte aligned, rope_max_pos >= seq_q and
+ * _fp16 with an optional rotary embedding of Q and K: rope_cos / rope_sin (NULL = off)
+ * are fp32 tables [rope_max_pos, head_dim/2] (16-byte aligned, rope_max_pos >= seq_q and
  * >= seq_kv); query row i and key row j of every (batch, head) are rotated at positions
- * i and j, pairs (2i, 2i+1), as the reference's fused RoPE does to Q and K
- * (src/fused_rope.cu:13-69), inside the kernel after their tiles land in shared memory.
- * New (the reference applies RoPE as a separate pass over Q and K). */
+ * i and j (pairs (2i, 2i+1), src/fused_rope.cu:33-43). K is rotated once into the
+ * caller's k_rotated buffer ([batch, heads, seq_kv, head_dim], may be k itself), which
+ * keeps the rotated keys for a KV cache; Q is rotated inside the attention kernel as its
+ * tiles land in shared memory. New (the reference rotates Q and K in separate passes). */
 int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o,
                                   int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                   int is_causal, float softmax_scale, int dtype,
                                   const float* rope_cos, const float* rope_sin, int rope_max_pos,
-                                  void* stream);
+                                  void* k_rotated, void* stream);
 
 /* Row-per-thread fp32 attention. Replaces launch_naive_attention_forward_fp32
  * (include/flash_attention.cuh:79-86, src/flash_attention.cu:86-104). */

@@ -210,9 +210,10 @@ def test_bf16_first_call_inside_graph_capture():
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M", [(300, 300), (128, 520), (640, 200)])
 def test_bf16_fused_rope_q_and_k(d, causal, N, M):
-    """RoPE of Q (row i at position i) and K (row j at position j) fused into the
-    tensor-core prefill, against the oracle rotating Q and K first (the reference's
-    fused RoPE arithmetic, src/fused_rope.cu:33-43) then attending."""
+    """RoPE of Q (row i at position i, rotated inside the tensor-core prefill) and K (row
+    j at position j, rotated once into k_rotated), against the oracle rotating Q and K
+    first (the reference's fused RoPE arithmetic, src/fused_rope.cu:33-43) then
+    attending."""
     import flash_engine
     rng = np.random.default_rng(N + M + d)
     q = O.bf16_round(rng.standard_normal((2, 3, N, d), dtype=np.float32))
@@ -222,12 +223,15 @@ def test_bf16_fused_rope_q_and_k(d, causal, N, M):
     qr = O.bf16_round(O.rope_rotate(q, cos, sin, np.arange(N)).astype(np.float32))
     kr = O.bf16_round(O.rope_rotate(k, cos, sin, np.arange(M)).astype(np.float32))
     ref = O.flash_attention_sliced(qr, kr, v, causal)
+    k_rot = torch.empty((2, 3, M, d), dtype=torch.bfloat16, device="cuda")
     out = flash_engine.flash_attention(cuda(q, torch.bfloat16), cuda(k, torch.bfloat16),
                                        cuda(v, torch.bfloat16), causal,
-                                       rope=(cuda(cos), cuda(sin)))
+                                       rope=(cuda(cos), cuda(sin)), k_rotated=k_rot)
     torch.cuda.synchronize()
     assert flash_engine.device_errors() == 0
     assert_bf16_close(host(out), ref)
+    # the rotated keys a KV cache would store
+    np.testing.assert_allclose(host(k_rot), kr, rtol=2 ** -7, atol=2 ** -7)
 
 
 def test_fp16_fused_rope_config2_slice():
@@ -248,3 +252,27 @@ def test_fp16_fused_rope_config2_slice():
     torch.cuda.synchronize()
     assert flash_engine.device_errors() == 0
     assert_bf16_close(host(out), ref, atol=5e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d", [64, 128, 6])
+def test_rope_forward(dtype, d):
+    """The dense RoPE pass (the reference's fused_rope_kernel_fp32 rule: row (b, h, i)
+    rotated at position i with the caller's tables), vector path (d % 8 == 0) and the
+    per-pair path (d = 6), out of place and in place."""
+    import flash_engine
+    rng = np.random.default_rng(d)
+    x = rng.standard_normal((2, 3, 77, d), dtype=np.float32)
+    rnd = (lambda a: O.bf16_round(a.astype(np.float32))) if dtype == torch.bfloat16 else \
+        (lambda a: a.astype(np.float16).astype(np.float32)) if dtype == torch.float16 else \
+        (lambda a: a.astype(np.float32))
+    x = rnd(x)
+    cos, sin = O.rope_tables(100, d)
+    ref = rnd(O.rope_rotate(x, cos, sin, np.arange(77)))
+    xt = cuda(x, dtype)
+    out = flash_engine.rope(xt, cuda(cos), cuda(sin))
+    flash_engine.rope(xt, cuda(cos), cuda(sin), out=xt)   # in place
+    torch.cuda.synchronize()
+    tol = {torch.float32: 1e-6, torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10}[dtype]
+    np.testing.assert_allclose(host(out), ref, rtol=tol, atol=tol)
+    np.testing.assert_array_equal(host(xt), host(out))
