@@ -142,48 +142,49 @@ __device__ __forceinline__ uint32_t pack2<half>(float lo, float hi) {
   return pack_f16x2(lo, hi);
 }
 
-// RoPE of one 16-byte chunk (8 elements = 4 pairs (2i, 2i+1)) of a 128B-swizzled tile
-// row in shared memory: (x0 c - x1 s, x0 s + x1 c) in fp32 (src/fused_rope.cu:33-43),
-// rounded back to T. cs / sn point at the 4 pairs' table entries (16-byte aligned).
-template <typename T>
-__device__ __forceinline__ void rope_chunk(uint8_t* addr, const float* cs, const float* sn) {
-  uint4 v = *reinterpret_cast<uint4*>(addr);
-  const float4 c = __ldg(reinterpret_cast<const float4*>(cs));
-  const float4 s = __ldg(reinterpret_cast<const float4*>(sn));
-  uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float x0, x1;
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      x0 = __uint_as_float(w[k] << 16);
-      x1 = __uint_as_float(w[k] & 0xffff0000u);
-    } else {
-      x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] & 0xffffu)));
-      x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] >> 16)));
-    }
-    w[k] = pack2<T>(x0 * cc[k] - x1 * ss[k], x0 * ss[k] + x1 * cc[k]);
-  }
-  *reinterpret_cast<uint4*>(addr) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// Rotates the 16-byte chunks first, first + step, ... (below last) of a [128][D] tile
-// of 16-bit elements stored as D/64 column halves of 128B-swizzled 128-byte rows (chunk
-// c is row c / (D/8)); row r has position pos0 + r. Columns at or past d (d = 32 on the
-// D = 64 kernel) and rows at or past `rows` (zero-filled) are left as they are.
+// RoPE of row `row` of a [128][D] tile of 16-bit elements in shared memory, stored as
+// D/64 column halves of 128B-swizzled 128-byte rows, at position pos: pair (2i, 2i+1)
+// becomes (x0 c - x1 s, x0 s + x1 c) in fp32 (src/fused_rope.cu:33-43), rounded back to
+// T. Columns at or past d (d = 32 on the D = 64 kernel) are left as they are. All the
+// row's shared-memory and table loads are issued before the arithmetic (one round trip).
 template <typename T, int D>
-__device__ __forceinline__ void rope_tile(uint8_t* tile, int first, int last, int step,
-                                          int pos0, int rows, int d, const float* cos_t,
-                                          const float* sin_t) {
-  constexpr int CPR = D / 8;  // 16-byte chunks per row
-  for (int c = first; c < last; c += step) {
-    const int row = c / CPR, ch = c - row * CPR;
-    const int col = ch * 8;
-    if (pos0 + row >= rows || col >= d) continue;
-    const int h = col / 64, cc = (col % 64) / 8;
-    uint8_t* addr = tile + h * (128 * 128) + row * 128 + ((cc ^ (row & 7)) << 4);
-    const size_t e = static_cast<size_t>(pos0 + row) * (d / 2) + col / 2;
-    rope_chunk<T>(addr, cos_t + e, sin_t + e);
+__device__ __forceinline__ void rope_row(uint8_t* tile, int row, int pos, int d,
+                                         const float* cos_t, const float* sin_t) {
+  constexpr int CPR = D / 8;  // 16-byte chunks (4 pairs) per row
+  uint4 v[CPR];
+  float4 c[CPR], sn[CPR];
+  const float* cr = cos_t + static_cast<size_t>(pos) * (d / 2);
+  const float* sr = sin_t + static_cast<size_t>(pos) * (d / 2);
+#pragma unroll
+  for (int ch = 0; ch < CPR; ++ch) {
+    if (ch * 8 >= d) break;
+    const int h = ch / 8, cc = ch % 8;
+    v[ch] = *reinterpret_cast<const uint4*>(tile + h * (128 * 128) + row * 128 +
+                                            ((cc ^ (row & 7)) << 4));
+    c[ch] = __ldg(reinterpret_cast<const float4*>(cr + ch * 4));
+    sn[ch] = __ldg(reinterpret_cast<const float4*>(sr + ch * 4));
+  }
+#pragma unroll
+  for (int ch = 0; ch < CPR; ++ch) {
+    if (ch * 8 >= d) break;
+    uint32_t w[4] = {v[ch].x, v[ch].y, v[ch].z, v[ch].w};
+    const float cc4[4] = {c[ch].x, c[ch].y, c[ch].z, c[ch].w};
+    const float ss4[4] = {sn[ch].x, sn[ch].y, sn[ch].z, sn[ch].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float x0, x1;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        x0 = __uint_as_float(w[k] << 16);
+        x1 = __uint_as_float(w[k] & 0xffff0000u);
+      } else {
+        x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] & 0xffffu)));
+        x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] >> 16)));
+      }
+      w[k] = pack2<T>(x0 * cc4[k] - x1 * ss4[k], x0 * ss4[k] + x1 * cc4[k]);
+    }
+    const int h = ch / 8, cc = ch % 8;
+    *reinterpret_cast<uint4*>(tile + h * (128 * 128) + row * 128 + ((cc ^ (row & 7)) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -430,11 +431,8 @@ __global__ void __launch_bounds__(384, 1)
     if (ROPE && nkv[t] > 0) {
       // RoPE: this thread rotates its own row of Q_t (position r) once it has landed
       ok = __all_sync(0xffffffffu, mbar_wait(t == 0 ? q_full : q_full1, 0));
-      if (ok) {
-        constexpr int CPR = D / 8;
-        rope_tile<T, D>(smem + C::Q_OFF + t * TILE, row * CPR, (row + 1) * CPR, 1, m0[t], p.N,
-                        p.d_out, p.rope_cos, p.rope_sin);
-      }
+      if (ok && r < p.N)
+        rope_row<T, D>(smem + C::Q_OFF + t * TILE, row, r, p.d_out, p.rope_cos, p.rope_sin);
       fence_proxy_async_smem();
       mbar_arrive(&q_rot[t]);
     }
