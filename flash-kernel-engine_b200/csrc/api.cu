@@ -345,8 +345,8 @@ int fe_flash_attention_forward_bf16(const void* q, const void* k, const void* v,
   if (!dense_args_ok(B, H, N, M, d)) return kErr;
   if (B * H == 0 || N == 0) return 0;
   return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
-                                                      resolve_scale(scale, d), true, nullptr,
-                                                      nullptr, 0, as_stream(stream)));
+                                                      resolve_scale(scale, d), true,
+                                                      as_stream(stream)));
 }
 
 int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v, void* o, int B,
@@ -355,8 +355,8 @@ int fe_flash_attention_forward_fp16(const void* q, const void* k, const void* v,
   if (!dense_args_ok(B, H, N, M, d)) return kErr;
   if (B * H == 0 || N == 0) return 0;
   return static_cast<int>(fe::prefill::launch_prefill(q, k, v, o, B, H, N, M, d, causal,
-                                                      resolve_scale(scale, d), false, nullptr,
-                                                      nullptr, 0, as_stream(stream)));
+                                                      resolve_scale(scale, d), false,
+                                                      as_stream(stream)));
 }
 
 int fe_rope_forward(const void* in, const float* cos_table, const float* sin_table, void* out,
@@ -372,25 +372,28 @@ int fe_rope_forward(const void* in, const float* cos_table, const float* sin_tab
 int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o, int B,
                                   int H, int N, int M, int d, int causal, float scale, int dtype,
                                   const float* rope_cos, const float* rope_sin, int rope_max_pos,
-                                  void* k_rotated, void* stream) {
+                                  void* q_rotated, void* k_rotated, void* stream) {
   if (!dense_args_ok(B, H, N, M, d) || (dtype != 0 && dtype != 1)) return kErr;
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return kErr;
-  if (rope_cos && (rope_max_pos < N || rope_max_pos < M || !k_rotated)) return kErr;
+  if (rope_cos && (rope_max_pos < N || rope_max_pos < M || !q_rotated || !k_rotated))
+    return kErr;
   if (B * H == 0 || N == 0) return 0;
   cudaStream_t st = as_stream(stream);
+  const void* qq = q;
   const void* kk = k;
   if (rope_cos) {
-    // K rotated once (each key tile is read by every query tile of its head), into the
-    // caller's buffer, which then holds the keys a KV cache stores; Q is rotated in the
-    // attention kernel as its tiles land.
-    const cudaError_t e = fe::rope::launch_rope(k, rope_cos, rope_sin, k_rotated, B, H, M, d,
-                                                dtype, st);
+    // Q and K rotated once each by the streaming RoPE pass into the caller's buffers
+    // (each key tile is read by every query tile of its head, so rotating it inside the
+    // attention kernel would repeat the work; k_rotated keeps the keys a KV cache stores)
+    cudaError_t e = fe::rope::launch_rope(q, rope_cos, rope_sin, q_rotated, B, H, N, d, dtype, st);
+    if (e == cudaSuccess)
+      e = fe::rope::launch_rope(k, rope_cos, rope_sin, k_rotated, B, H, M, d, dtype, st);
     if (e != cudaSuccess) return static_cast<int>(e);
+    qq = q_rotated;
     kk = k_rotated;
   }
-  return static_cast<int>(fe::prefill::launch_prefill(q, kk, v, o, B, H, N, M, d, causal,
-                                                      resolve_scale(scale, d), dtype == 0,
-                                                      rope_cos, rope_sin, rope_max_pos, st));
+  return static_cast<int>(fe::prefill::launch_prefill(qq, kk, v, o, B, H, N, M, d, causal,
+                                                      resolve_scale(scale, d), dtype == 0, st));
 }
 
 int fe_paged_attention_v1_fp32(const float* q, const float* kc, const float* vc, float* out,

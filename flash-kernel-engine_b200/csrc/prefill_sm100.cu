@@ -56,7 +56,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 21;
+  static constexpr int NBARS = 19;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -65,10 +65,6 @@ struct PParams {
   void* out;
   int N, M, BH;
   int d_out;  // head dim of the tensors: D, or 32 when the D = 64 kernel runs d = 32
-  // Optional rotary embedding of Q (NULL = off): fp32 tables [rope_max_pos, d/2]; query
-  // row i is rotated at position i in shared memory. K arrives rotated (rope_forward).
-  const float* rope_cos;
-  const float* rope_sin;
   int causal;
   float scale_log2;
   unsigned* err;
@@ -142,53 +138,7 @@ __device__ __forceinline__ uint32_t pack2<half>(float lo, float hi) {
   return pack_f16x2(lo, hi);
 }
 
-// RoPE of row `row` of a [128][D] tile of 16-bit elements in shared memory, stored as
-// D/64 column halves of 128B-swizzled 128-byte rows, at position pos: pair (2i, 2i+1)
-// becomes (x0 c - x1 s, x0 s + x1 c) in fp32 (src/fused_rope.cu:33-43), rounded back to
-// T. Columns at or past d (d = 32 on the D = 64 kernel) are left as they are. All the
-// row's shared-memory and table loads are issued before the arithmetic (one round trip).
 template <typename T, int D>
-__device__ __forceinline__ void rope_row(uint8_t* tile, int row, int pos, int d,
-                                         const float* cos_t, const float* sin_t) {
-  constexpr int CPR = D / 8;  // 16-byte chunks (4 pairs) per row
-  uint4 v[CPR];
-  float4 c[CPR], sn[CPR];
-  const float* cr = cos_t + static_cast<size_t>(pos) * (d / 2);
-  const float* sr = sin_t + static_cast<size_t>(pos) * (d / 2);
-#pragma unroll
-  for (int ch = 0; ch < CPR; ++ch) {
-    if (ch * 8 >= d) break;
-    const int h = ch / 8, cc = ch % 8;
-    v[ch] = *reinterpret_cast<const uint4*>(tile + h * (128 * 128) + row * 128 +
-                                            ((cc ^ (row & 7)) << 4));
-    c[ch] = __ldg(reinterpret_cast<const float4*>(cr + ch * 4));
-    sn[ch] = __ldg(reinterpret_cast<const float4*>(sr + ch * 4));
-  }
-#pragma unroll
-  for (int ch = 0; ch < CPR; ++ch) {
-    if (ch * 8 >= d) break;
-    uint32_t w[4] = {v[ch].x, v[ch].y, v[ch].z, v[ch].w};
-    const float cc4[4] = {c[ch].x, c[ch].y, c[ch].z, c[ch].w};
-    const float ss4[4] = {sn[ch].x, sn[ch].y, sn[ch].z, sn[ch].w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float x0, x1;
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        x0 = __uint_as_float(w[k] << 16);
-        x1 = __uint_as_float(w[k] & 0xffff0000u);
-      } else {
-        x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] & 0xffffu)));
-        x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(w[k] >> 16)));
-      }
-      w[k] = pack2<T>(x0 * cc4[k] - x1 * ss4[k], x0 * ss4[k] + x1 * cc4[k]);
-    }
-    const int h = ch / 8, cc = ch % 8;
-    *reinterpret_cast<uint4*>(tile + h * (128 * 128) + row * 128 + ((cc ^ (row & 7)) << 4)) =
-        make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
-
-template <typename T, int D, bool ROPE>
 __global__ void __launch_bounds__(384, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kmap,
@@ -213,8 +163,6 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* drain = bars + 15;
   uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
   uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
-  uint64_t* q_rot = bars + 19;    // [2] RoPE: Q_t rotated in shared memory
-  constexpr bool rope = ROPE;  // a separate instantiation: the plain kernel carries none of it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -260,7 +208,6 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_half[i], 128);
-      mbar_init(&q_rot[i], 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -355,17 +302,13 @@ __global__ void __launch_bounds__(384, 1)
         if (half == 1) tc::commit(&o_done[t]);
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
-      // with RoPE, Q_t is used once rotated (K comes rotated from the caller's buffer)
-      uint64_t* const q0_bar = rope ? &q_rot[0] : q_full;
-      uint64_t* const q1_bar = rope ? &q_rot[1] : q_full1;
-      uint64_t* const k_bar = k_full;
-      bool ok = (nkv[0] == 0 || mbar_wait(q0_bar, 0)) && mbar_wait(&k_bar[0], 0);
+      bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
       if (ok && nkv[0] > 0) {
         tc::fence_after_sync();
         issue_s(0, 0);
       }
       if (ok && nkv[1] > 0) {
-        ok = mbar_wait(q1_bar, 0);
+        ok = mbar_wait(q_full1, 0);
         if (ok) {
           tc::fence_after_sync();
           issue_s(1, 0);
@@ -385,7 +328,7 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
           issue_pv_half(0, j, 1);
           if (j + 1 < nkv[0]) {
-            if (!mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
             issue_s(0, j + 1);
           }
@@ -398,13 +341,13 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
           issue_pv_half(1, j, 1);
           if (j + 1 < nkv[1]) {
-            if (!k_ready && !mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
             issue_s(1, j + 1);
           }
         }
         if (next_k) {
-          if (!k_ready && !mbar_wait(&k_bar[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+          if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
           tc::commit(&k_empty[(j + 1) & 1]);
         }
         tc::commit(&v_empty[st]);
@@ -428,14 +371,6 @@ __global__ void __launch_bounds__(384, 1)
     const float sl = p.scale_log2;
     float m_run = NEG_INF, l_run = 0.f;
     bool ok = true;
-    if (ROPE && nkv[t] > 0) {
-      // RoPE: this thread rotates its own row of Q_t (position r) once it has landed
-      ok = __all_sync(0xffffffffu, mbar_wait(t == 0 ? q_full : q_full1, 0));
-      if (ok && r < p.N)
-        rope_row<T, D>(smem + C::Q_OFF + t * TILE, row, r, p.d_out, p.rope_cos, p.rope_sin);
-      fence_proxy_async_smem();
-      mbar_arrive(&q_rot[t]);
-    }
     for (int j = 0; j < nkv[t] && ok; ++j) {
       const bool got = mbar_wait(&s_full[t], j & 1);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
@@ -574,10 +509,9 @@ __global__ void __launch_bounds__(384, 1)
 // stored.
 template <typename T, int D>
 static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o, int B, int H,
-                            int N, int M, int d, int causal, float scale, const float* rope_cos,
-                            const float* rope_sin, cudaStream_t st) {
+                            int N, int M, int d, int causal, float scale, cudaStream_t st) {
   using C = PCfg<D>;
-  auto kern = rope_cos ? fa_prefill_kernel<T, D, true> : fa_prefill_kernel<T, D, false>;
+  auto kern = fa_prefill_kernel<T, D>;
   cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(kern), C::SMEM);
   if (e != cudaSuccess) return e;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -594,8 +528,6 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
   p.N = N;
   p.M = M;
   p.d_out = d;
-  p.rope_cos = rope_cos;
-  p.rope_sin = rope_sin;
   p.BH = static_cast<int>(BH);
   p.causal = causal;
   p.scale_log2 = scale * kLog2e;
@@ -622,24 +554,19 @@ static cudaError_t launch_d(const void* q, const void* k, const void* v, void* o
 
 cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o, int B, int H,
                            int N, int M, int d, int causal, float scale, bool is_bf16,
-                           const float* rope_cos, const float* rope_sin, int rope_max_pos,
                            cudaStream_t stream) {
   if (!(d == 32 || d == 64 || d == 128)) return cudaErrorInvalidValue;
-  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return cudaErrorInvalidValue;
-  if (rope_cos && (rope_max_pos < N || rope_max_pos < M ||
-                   ((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15)))
-    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15)
     return cudaErrorInvalidValue;
   if (static_cast<long long>(B) * H > 65535) return cudaErrorInvalidValue;
   if (is_bf16) {
     if (d == 128)
-      return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
-    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
+      return launch_d<__nv_bfloat16, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+    return launch_d<__nv_bfloat16, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
   }
-  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
-  return launch_d<half, 64>(q, k, v, o, B, H, N, M, d, causal, scale, rope_cos, rope_sin, stream);
+  if (d == 128) return launch_d<half, 128>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
+  return launch_d<half, 64>(q, k, v, o, B, H, N, M, d, causal, scale, stream);
 }
 
 }  // namespace prefill

@@ -37,7 +37,7 @@ _SIGS = {
     "fe_flash_attention_forward_bf16": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P], _I),
     "fe_naive_attention_forward_fp32": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P], _I),
     "fe_flash_attention_forward_ex": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P, _I,
-                                       _P, _P], _I),
+                                       _P, _P, _P], _I),
     "fe_rope_forward": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "fe_paged_attention_v1_fp32": ([_P, _P, _P, _P, _P, _P] + [_I] * 8 + [_F, _P], _I),
     "fe_paged_attention_v1_fp16": ([_P, _P, _P, _P, _P, _P] + [_I] * 8 + [_F, _P], _I),

@@ -94,9 +94,9 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
     (optional, new): a contiguous tensor like q to write into. ``rope=(cos, sin)``
     (optional, new; bf16/fp16): float32 CUDA tables [max_pos, d/2] with max_pos >= N, M;
     query row i and key row j are rotated at positions i and j (the reference's fused
-    RoPE arithmetic, applied to Q and K): K once into ``k_rotated`` (a tensor like k, made
-    here if not given; it then holds the rotated keys a KV cache stores), Q inside the
-    attention kernel.
+    RoPE arithmetic, applied to Q and K) by the streaming RoPE pass into a temporary
+    like q and into ``k_rotated`` (a tensor like k, made here if not given; it then holds
+    the rotated keys a KV cache stores), which the attention kernel reads.
     """
     _require_cuda(q, k, v)
     B, H, N, d = q.shape
@@ -126,7 +126,8 @@ def flash_attention(q, k, v, is_causal: bool = False, scale: float | None = None
             _lib.check(_lib_c.fe_flash_attention_forward_ex(
                 _ptr(q), _ptr(k), _ptr(v), _ptr(out), B, H, N, M, d, int(bool(is_causal)),
                 _scale_arg(scale, d), 0 if q.dtype == torch.bfloat16 else 1, _ptr(rcos),
-                _ptr(rsin), rcos.shape[0], _ptr(k_rotated), _stream()), "flash_attention")
+                _ptr(rsin), rcos.shape[0], _ptr(torch.empty_like(q)), _ptr(k_rotated),
+                _stream()), "flash_attention")
         return out
     fn = {torch.float32: _lib_c.fe_flash_attention_forward_fp32,
           torch.bfloat16: _lib_c.fe_flash_attention_forward_bf16,

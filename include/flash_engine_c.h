@@ -89,15 +89,16 @@ int fe_rope_forward(const void* in, const float* cos_table, const float* sin_tab
  * _fp16 with an optional rotary embedding of Q and K: rope_cos / rope_sin (NULL = off)
  * are fp32 tables [rope_max_pos, head_dim/2] (16-byte aligned, rope_max_pos >= seq_q and
  * >= seq_kv); query row i and key row j of every (batch, head) are rotated at positions
- * i and j (pairs (2i, 2i+1), src/fused_rope.cu:33-43). K is rotated once into the
- * caller's k_rotated buffer ([batch, heads, seq_kv, head_dim], may be k itself), which
- * keeps the rotated keys for a KV cache; Q is rotated inside the attention kernel as its
- * tiles land in shared memory. New (the reference rotates Q and K in separate passes). */
+ * i and j (pairs (2i, 2i+1), src/fused_rope.cu:33-43) by the streaming RoPE pass
+ * (fe_rope_forward) into the caller's q_rotated / k_rotated buffers (like q / k; they may
+ * be q / k themselves), which the attention kernel then reads; k_rotated keeps the
+ * rotated keys a KV cache stores. New: the reference runs its RoPE and attention
+ * kernels as separate calls. */
 int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, void* o,
                                   int batch, int heads, int seq_q, int seq_kv, int head_dim,
                                   int is_causal, float softmax_scale, int dtype,
                                   const float* rope_cos, const float* rope_sin, int rope_max_pos,
-                                  void* k_rotated, void* stream);
+                                  void* q_rotated, void* k_rotated, void* stream);
 
 /* Row-per-thread fp32 attention. Replaces launch_naive_attention_forward_fp32
  * (include/flash_attention.cuh:79-86, src/flash_attention.cu:86-104). */

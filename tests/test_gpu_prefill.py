@@ -210,10 +210,10 @@ def test_bf16_first_call_inside_graph_capture():
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M", [(300, 300), (128, 520), (640, 200)])
 def test_bf16_fused_rope_q_and_k(d, causal, N, M):
-    """RoPE of Q (row i at position i, rotated inside the tensor-core prefill) and K (row
-    j at position j, rotated once into k_rotated), against the oracle rotating Q and K
-    first (the reference's fused RoPE arithmetic, src/fused_rope.cu:33-43) then
-    attending."""
+    """RoPE of Q (row i at position i) and K (row j at position j) by the streaming RoPE
+    pass, then the tensor-core prefill, against the oracle rotating Q and K first (the
+    reference's fused RoPE arithmetic, src/fused_rope.cu:33-43) then attending; k_rotated
+    returns the rotated keys."""
     import flash_engine
     rng = np.random.default_rng(N + M + d)
     q = O.bf16_round(rng.standard_normal((2, 3, N, d), dtype=np.float32))
@@ -235,7 +235,7 @@ def test_bf16_fused_rope_q_and_k(d, causal, N, M):
 
 
 def test_fp16_fused_rope_config2_slice():
-    """Fused RoPE on the config 2 shape (causal, 4096 rows, d 128) in fp16, 2 heads."""
+    """RoPE + prefill on the config 2 shape (causal, 4096 rows, d 128) in fp16, 2 heads."""
     import flash_engine
     rng = np.random.default_rng(7)
     N, d = 4096, 128
