@@ -41,10 +41,38 @@ namespace prefill {
 constexpr float NEG_INF = -__builtin_huge_valf();
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
 // One exponential pair in every kPolyEvery goes to the FMA-pipe polynomial (0: none).
+// With P handed to the MMA warp in two halves, all-MUFU is the fastest at every
+// measured shape (config 2 and its 2-, 4- and 8-way head shards), so 0 is the default.
 #ifndef FE_PREFILL_POLY_EVERY
-#define FE_PREFILL_POLY_EVERY 8
+#define FE_PREFILL_POLY_EVERY 0
 #endif
 constexpr int kPolyEvery = FE_PREFILL_POLY_EVERY;
+// P of a key tile is handed to the MMA warp in kPChunks pieces (2 or 4; quarters
+// measured 2-4% slower than halves on config 2).
+#ifndef FE_PREFILL_P_CHUNKS
+#define FE_PREFILL_P_CHUNKS 2
+#endif
+constexpr int kPChunks = FE_PREFILL_P_CHUNKS;
+static_assert(kPChunks == 2 || kPChunks == 4, "P is handed over in halves or quarters");
+
+#ifdef FE_PF_TIMELINE
+// Per-CTA event times (globaltimer ns) of the last launch, profiling builds only:
+// [0] entry, [1] set up (barriers, tensor memory, previous grid complete), [2] first S
+// of tile 0 seen by the softmax, [3] softmax 0 done, [4] softmax 1 done, [5] epilogue 0
+// done, [6] epilogue 1 done, [7] exit, [8] SM id, [9] query-tile pair, [10] (batch, head).
+constexpr int kTimelineCtas = 4096;
+__device__ unsigned long long g_pf_timeline[kTimelineCtas][12];
+// Steps of the first 148 CTAs: [step][0/1] S of tile 0/1 seen, [2/3] P of tile 0/1 done,
+// [4/5] row max of tile 0/1 known.
+__device__ unsigned long long g_pf_steps[148][64][16];
+#define FE_PST(j, slot) \
+  do { if (blockIdx.x < 148 && (j) < 64) g_pf_steps[blockIdx.x][j][slot] = globaltimer_ns(); } while (0)
+#define FE_PTL(slot, v) \
+  do { if (blockIdx.x < kTimelineCtas) g_pf_timeline[blockIdx.x][slot] = (v); } while (0)
+#else
+#define FE_PTL(slot, v) do {} while (0)
+#define FE_PST(j, slot) do {} while (0)
+#endif
 
 template <int D>
 struct PCfg {
@@ -56,7 +84,7 @@ struct PCfg {
   static constexpr int K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
   static constexpr int BAR_OFF = V_OFF + 2 * TILE_BYTES;
-  static constexpr int NBARS = 19;
+  static constexpr int NBARS = 17 + 2 * (kPChunks - 1);
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   static constexpr int NTHREADS = 384;
 };
@@ -162,10 +190,16 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* o_done = bars + 13;  // [2]
   uint64_t* drain = bars + 15;
   uint64_t* q_full1 = bars + 16;  // Q1 (Q0 completes on q_full)
-  uint64_t* p_half = bars + 17;   // [2] per query tile: P of keys 0..63 is in tensor memory
+  // [kPChunks - 1][2]: chunk c of P_t (keys c * BN / kPChunks ...) is in tensor memory;
+  // the last chunk completes on p_full.
+  uint64_t* p_part = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) FE_PTL(0, globaltimer_ns());
+#ifdef FE_PF_TIMELINE
+  const long long clk_entry = clock64();
+#endif
   // Block mapping: the (batch, head)s are cut into groups of p.group whose K/V fit in
   // L2 together. CTAs are dispatched group by group; inside a group, the query-tile
   // pairs go longest-first across all of its heads, so the causal work is scheduled
@@ -207,7 +241,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&p_half[i], 128);
+      for (int c = 0; c < kPChunks - 1; ++c) mbar_init(&p_part[c * 2 + i], 128);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -225,6 +259,14 @@ __global__ void __launch_bounds__(384, 1)
   // and wait for the previous kernel's results before the first global access.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    FE_PTL(1, globaltimer_ns());
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    FE_PTL(8, smid);
+    FE_PTL(9, pair);
+    FE_PTL(10, bh);
+  }
 
   if (warp >= 8) {
    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
@@ -287,19 +329,30 @@ __global__ void __launch_bounds__(384, 1)
         }
         tc::commit(&s_full[t]);
       };
-      // P V in two halves of 64 keys: the first starts as soon as the softmax has
-      // stored P of keys 0..63 (p_half), while it computes keys 64..127 (p_full).
-      auto issue_pv_half = [&](int t, int j, int half) {
+      // P V in kPChunks pieces: each starts as soon as the softmax has stored that
+      // chunk of P (p_part), while it computes the next ones (the last: p_full).
+      auto issue_pv_part = [&](int t, int j, int c) {
         const uint32_t vb = sbase + C::V_OFF + (j & 1) * TILE;
         const uint32_t ptm = tmem + t * BN;              // P_t over the S_t columns
         const uint32_t otm = tmem + 2 * BN + t * D;
+        constexpr int KK = BN / 16 / kPChunks;            // 16-key MMAs per chunk
 #pragma unroll
-        for (int k2 = 0; k2 < BN / 32; ++k2) {
-          const int kk = half * (BN / 32) + k2;
+        for (int k2 = 0; k2 < KK; ++k2) {
+          const int kk = c * KK + k2;
           tc::mma_ts(otm, ptm + kk * 8, tc::smem_desc_sw128(vb + kk * 16 * 128, HALF, 1024),
                      idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        if (half == 1) tc::commit(&o_done[t]);
+        if (c == kPChunks - 1) tc::commit(&o_done[t]);
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+#pragma unroll
+        for (int c = 0; c < kPChunks; ++c) {
+          uint64_t* bar = c < kPChunks - 1 ? &p_part[c * 2 + t] : &p_full[t];
+          if (!mbar_wait(bar, j & 1)) return false;
+          tc::fence_after_sync();
+          issue_pv_part(t, j, c);
+        }
+        return true;
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
       bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
@@ -321,12 +374,7 @@ __global__ void __launch_bounds__(384, 1)
         const bool next_k = j + 1 < nmax;
         bool k_ready = false;
         if (j < nkv[0]) {
-          if (!mbar_wait(&p_half[0], j & 1)) { ok = false; break; }
-          tc::fence_after_sync();
-          issue_pv_half(0, j, 0);
-          if (!mbar_wait(&p_full[0], j & 1)) { ok = false; break; }
-          tc::fence_after_sync();
-          issue_pv_half(0, j, 1);
+          if (!issue_pv(0, j)) { ok = false; break; }
           if (j + 1 < nkv[0]) {
             if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
@@ -334,12 +382,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         if (j < nkv[1]) {
-          if (!mbar_wait(&p_half[1], j & 1)) { ok = false; break; }
-          tc::fence_after_sync();
-          issue_pv_half(1, j, 0);
-          if (!mbar_wait(&p_full[1], j & 1)) { ok = false; break; }
-          tc::fence_after_sync();
-          issue_pv_half(1, j, 1);
+          if (!issue_pv(1, j)) { ok = false; break; }
           if (j + 1 < nkv[1]) {
             if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
             k_ready = true;
@@ -374,12 +417,15 @@ __global__ void __launch_bounds__(384, 1)
     for (int j = 0; j < nkv[t] && ok; ++j) {
       const bool got = mbar_wait(&s_full[t], j & 1);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      if (j == 0 && t == 0 && threadIdx.x == 0) FE_PTL(2, globaltimer_ns());
+      if ((threadIdx.x & 127) == 0) FE_PST(j, t);
       tc::fence_after_sync();
       uint32_t u[BN];
 #pragma unroll
       for (int c4 = 0; c4 < BN / 32; ++c4)
         tc::ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c4 * 32]));
       tc::wait_ld();
+      if ((threadIdx.x & 127) == 0) FE_PST(j, 6 + t);
       const int c0 = j * BN;
       const bool need_mask = (p.causal && c0 + BN - 1 > m0[t]) || c0 + BN > p.M;
       if (need_mask) {
@@ -400,6 +446,7 @@ __global__ void __launch_bounds__(384, 1)
           m8[k] = max3(m8[k], __uint_as_float(u[i + 2 * k]), __uint_as_float(u[i + 2 * k + 1]));
       const float mx = max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]),
                             fmaxf(m8[6], m8[7])) * sl;
+      if ((threadIdx.x & 127) == 0) FE_PST(j, 4 + t);
       const float m_new = fmaxf(m_run, mx);
       const bool need = m_new > m_run + kRescaleThreshold;  // also true while m_run = -inf
       const float m_use = need ? m_new : m_run;
@@ -421,18 +468,20 @@ __global__ void __launch_bounds__(384, 1)
           tc::st32(tO + c4 * 32, u);
         }
       }
-      // p = 2^(s*sl - m): one FFMA each, then the MUFU ex2, except one pair in every
-      // kPolyEvery that uses a polynomial on the FMA pipe (splits the work over both).
-      // Each 64-key half of P is handed to the MMA warp as soon as it is stored.
+      // p = 2^(s*sl - m): one FFMA each, then the MUFU ex2 (with kPolyEvery > 0, one
+      // pair in every kPolyEvery uses a polynomial on the FMA pipe instead).
+      // Each chunk of P is handed to the MMA warp as soon as it is stored.
       uint64_t acc2[4] = {0, 0, 0, 0};  // paired partial sums (0 bits = 0.0f, 0.0f)
       const uint64_t sl2 = f2(sl, sl), nmu2 = f2(-mu, -mu);
+      if ((threadIdx.x & 127) == 0) FE_PST(j, 8 + t);
+      constexpr int CK = BN / kPChunks;  // keys per chunk
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 64; ++c4) {
-        uint32_t pk[32];
+      for (int c = 0; c < kPChunks; ++c) {
+        uint32_t pk[CK / 2];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint64_t x2 = fma2(f2(__uint_as_float(u[c4 * 64 + 2 * i]),
-                                      __uint_as_float(u[c4 * 64 + 2 * i + 1])),
+        for (int i = 0; i < CK / 2; ++i) {
+          const uint64_t x2 = fma2(f2(__uint_as_float(u[c * CK + 2 * i]),
+                                      __uint_as_float(u[c * CK + 2 * i + 1])),
                                    sl2, nmu2);
           float xa, xb;
           f2_split(x2, xa, xb);
@@ -447,10 +496,16 @@ __global__ void __launch_bounds__(384, 1)
           acc2[i & 3] = add2(acc2[i & 3], f2(a, b));
           pk[i] = pack2<T>(a, b);
         }
-        tc::st32(tS + c4 * 32, pk);
+        if constexpr (CK == 64) {
+          tc::st32(tS + c * 32, pk);
+        } else {
+          tc::st16(tS + c * 16, pk);
+        }
         tc::wait_st();
+        if ((threadIdx.x & 127) == 0 && c == 0) FE_PST(j, 12 + t);
+        if ((threadIdx.x & 127) == 0 && c == kPChunks - 1) FE_PST(j, 14 + t);
         tc::fence_before_sync();
-        mbar_arrive(c4 == 0 ? &p_half[t] : &p_full[t]);
+        mbar_arrive(c < kPChunks - 1 ? &p_part[c * 2 + t] : &p_full[t]);
       }
       float sum = 0.f;
 #pragma unroll
@@ -461,7 +516,9 @@ __global__ void __launch_bounds__(384, 1)
       }
       l_run = l_run * corr + sum;
       m_run = m_use;
+      if ((threadIdx.x & 127) == 0) FE_PST(j, 2 + t);
     }
+    if ((threadIdx.x & 127) == 0) FE_PTL(3 + t, globaltimer_ns());
     if (!ok) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
     } else if (nkv[t] > 0) {
@@ -492,10 +549,15 @@ __global__ void __launch_bounds__(384, 1)
         atomicOr(p.err, kErrWaitTimeout);
       }
     }
+    if ((threadIdx.x & 127) == 0) FE_PTL(5 + t, globaltimer_ns());
   }
 
   tc::fence_before_sync();
   __syncthreads();
+  if (threadIdx.x == 0) FE_PTL(7, globaltimer_ns());
+#ifdef FE_PF_TIMELINE
+  if (threadIdx.x == 0) FE_PTL(11, clock64() - clk_entry);
+#endif
   if (warp == 9) {
     tc::fence_after_sync();
     tc::tmem_dealloc<512>(tmem);
@@ -571,3 +633,15 @@ cudaError_t launch_prefill(const void* q, const void* k, const void* v, void* o,
 
 }  // namespace prefill
 }  // namespace fe
+
+#ifdef FE_PF_TIMELINE
+extern "C" int fe_debug_prefill_steps(unsigned long long* host) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, fe::prefill::g_pf_steps,
+                                               sizeof(fe::prefill::g_pf_steps)));
+}
+extern "C" int fe_debug_prefill_timeline(unsigned long long* host, int ctas) {
+  if (ctas > fe::prefill::kTimelineCtas) ctas = fe::prefill::kTimelineCtas;
+  return static_cast<int>(cudaMemcpyFromSymbol(host, fe::prefill::g_pf_timeline,
+                                               sizeof(unsigned long long) * 12 * ctas));
+}
+#endif

@@ -46,6 +46,20 @@ namespace tf32 {
 constexpr float NEG_INF = -__builtin_huge_valf();
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows > 2^8
 
+#ifdef FE_TF32_TIMELINE
+// Per-CTA event times (globaltimer ns) of the last launch, profiling builds only:
+// [0] entry, [1] set up, [2] Q landed, [3] K/V tile 0 split, [4] S_0 seen, [5] P_0 done,
+// [6] S_1 seen, [7] P_1 done, [8] final O, [9] partials stored, [10] cluster barrier 1
+// passed, [11] rows stored, [12] cluster barrier 2 passed, [13] SM id, [14] clock64
+// cycles entry -> [12].
+__device__ unsigned long long g_tf32_timeline[1024][16];
+#define FE_TTL(slot, v) \
+  do { if (blockIdx.x + blockIdx.y * gridDim.x < 1024) \
+         g_tf32_timeline[blockIdx.x + blockIdx.y * gridDim.x][slot] = (v); } while (0)
+#else
+#define FE_TTL(slot, v) do {} while (0)
+#endif
+
 template <int D>
 struct TCfg {
   // d = 128: Q hi / lo and two K/V stages of 64 keys do not fit shared memory, so the
@@ -223,6 +237,15 @@ __global__ void __launch_bounds__(320, 1)
                    const __grid_constant__ CUtensorMap vmap, const TParams p) {
   using C = TCfg<D>;
   constexpr int BM = C::BM, BN = C::BN, HALVES = C::HALVES;
+#ifdef FE_TF32_TIMELINE
+  const long long clk0 = clock64();
+  if (threadIdx.x == 0) {
+    FE_TTL(0, globaltimer_ns());
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    FE_TTL(13, smid);
+  }
+#endif
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -278,6 +301,7 @@ __global__ void __launch_bounds__(320, 1)
   // and wait for the previous kernel's results before the first global access.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) FE_TTL(1, globaltimer_ns());
 
   float m_run = NEG_INF, l_run = 0.f;  // softmax threads: this row's running max and sum
   bool have_o = false;                 // softmax threads: O in tensor memory is final
@@ -421,6 +445,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&kv_ready[st]);
+        if (sid == 0 && it == 0) FE_TTL(3, globaltimer_ns());
       }
       if (!ok && sid == 0) atomicOr(p.err, kErrWaitTimeout);
     }
@@ -438,6 +463,7 @@ __global__ void __launch_bounds__(320, 1)
     // Q is split here (these warps are idle until S_0) while warps 6-9 split K_0 / V_0.
     if (nloc > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0));
+      if (threadIdx.x == 0) FE_TTL(2, globaltimer_ns());
       if (ok) {
         if constexpr (C::QLO_TMEM) {
           // this thread's row: hi back in place, lo to tensor-memory columns T_QL + d
@@ -471,6 +497,7 @@ __global__ void __launch_bounds__(320, 1)
       const int b = it & 1;
       const bool got = mbar_wait(&s_full[b], (it >> 1) & 1);
       if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      if (threadIdx.x == 0 && it < 2) FE_TTL(4 + 2 * it, globaltimer_ns());
       tc::fence_after_sync();
       uint32_t u[BN];
 #pragma unroll
@@ -527,12 +554,14 @@ __global__ void __launch_bounds__(320, 1)
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(&p_full[b]);
+      if (threadIdx.x == 0 && it < 2) FE_TTL(5 + 2 * it, globaltimer_ns());
     }
     if (!ok) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
     } else if (nloc > 0) {
       const bool got = mbar_wait(&o_done[(nloc - 1) & 1], ((nloc - 1) >> 1) & 1);
       have_o = __all_sync(0xffffffffu, got);
+      if (threadIdx.x == 0) FE_TTL(8, globaltimer_ns());
       if (have_o) {
         tc::fence_after_sync();
       } else if (lane == 0) {
@@ -611,8 +640,10 @@ __global__ void __launch_bounds__(320, 1)
     pM[row] = m_run;
     pL[row] = l_run;
   }
+  if (threadIdx.x == 0) FE_TTL(9, globaltimer_ns());
   tc::fence_before_sync();
   cluster_sync_all();  // every partial of the cluster is in place
+  if (threadIdx.x == 0) FE_TTL(10, globaltimer_ns());
   if (warp == 5) {     // every tensor-memory read of this CTA is done
     tc::fence_after_sync();
     tc::tmem_dealloc<512>(tmem);
@@ -659,7 +690,14 @@ __global__ void __launch_bounds__(320, 1)
     *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c) =
         make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
   }
+  if (threadIdx.x == 0) FE_TTL(11, globaltimer_ns());
   cluster_sync_all();  // no CTA exits while a partner may still read its partials
+#ifdef FE_TF32_TIMELINE
+  if (threadIdx.x == 0) {
+    FE_TTL(12, globaltimer_ns());
+    FE_TTL(14, clock64() - clk0);
+  }
+#endif
 }
 
 // CTAs (one cluster) per 128-row tile: the most (up to 8 and up to the key-tile count)
@@ -753,3 +791,10 @@ cudaError_t launch_fa2_tf32(const float* q, const float* k, const float* v, floa
 
 }  // namespace simt
 }  // namespace fe
+
+#ifdef FE_TF32_TIMELINE
+extern "C" int fe_debug_tf32_timeline(unsigned long long* host) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, fe::tf32::g_tf32_timeline,
+                                               sizeof(fe::tf32::g_tf32_timeline)));
+}
+#endif
