@@ -9,22 +9,26 @@
 // (src/flash_attention.cu:111-345): O = softmax(Q K^T * scale [+ causal mask]) V over
 // [B, H, N|M, d] fp32 tensors, causal mask top-left aligned (query row i sees keys
 // j <= i, src/flash_attention.cu:224). Head dims 32, 64 and 128; the other head dims run
-// on the CUDA-core kernel of attention_fp32.cu. At d = 128 the key tile is 32 and Q lo
-// sits in tensor memory (shared memory holds Q hi and the two K/V stages).
+// on the CUDA-core kernel of attention_fp32.cu. Q hi and Q lo sit in tensor memory;
+// shared memory holds raw Q and two K/V stages (key tile 64, 32 at d = 128).
 //
 // A CTA owns one 128-row query tile of one (batch, head) and the 64-key tiles
 // t = split, split + nsplit, ... of it. The nsplit CTAs of a row tile form a thread-block
 // cluster and merge their (m, l, O) partials through distributed shared memory (the
-// log-sum-exp combine of src/flash_decoding.cu:151-223).
+// log-sum-exp combine of src/flash_decoding.cu:151-223): each CTA stores its partial
+// rows into the CTA that owns them, which merges them from its own shared memory.
 //  * warp 4 (TMA): Q once, then K_j and V_j (3-D TMA, 128-byte swizzle; rows past N or
 //    M read as zeros): tiles 0 and 1 straight into the two stages, later tiles into a
 //    landing buffer as soon as the split warps have read the previous one.
 //  * warps 6-9 (split): write each landed K / V tile into its stage as hi and lo; V is
 //    transposed on the way (V^T hi / lo), the K-major B operand of the P V product.
-//    The softmax warps split Q the same way before their first S tile.
-//  * warp 5 (MMA): allocates tensor memory [S0 | S1 | PL0 | PL1 | O] and, from one
-//    thread, issues
-//      S_j = Qhi Khi^T + Qhi Klo^T + Qlo Khi^T   (kind::tf32, A and B from shared memory)
+//    Keys are split first (K_0, K_1, V_0, V_1, then K and V of each later tile), each
+//    released on its own barrier, so S_j waits only for K_j.
+//    The softmax warps split Q the same way before their first S tile, each its row,
+//    into tensor memory.
+//  * warp 5 (MMA): allocates tensor memory [S0 | S1 | PL0 | PL1 | O | Qlo | Qhi] and,
+//    from one thread, issues
+//      S_j = Qhi Khi^T + Qhi Klo^T + Qlo Khi^T   (kind::tf32, A = Q from tensor memory)
 //      O  += Phi Vhi + Phi Vlo + Plo Vhi         (A = P from tensor memory, B = V^T)
 //    with S double-buffered, so S_{j+1} is computed while the softmax of tile j runs.
 //  * warps 0-3 (softmax): thread i owns query row i. It reads S_j, applies mask and
@@ -48,11 +52,12 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when m grows
 
 #ifdef FE_TF32_TIMELINE
 // Per-CTA event times (globaltimer ns) of the last launch, profiling builds only:
-// [0] entry, [1] set up, [2] Q landed, [3] K/V tile 0 split, [4] S_0 seen, [5] P_0 done,
-// [6] S_1 seen, [7] P_1 done, [8] final O, [9] partials stored, [10] cluster barrier 1
-// passed, [11] rows stored, [12] cluster barrier 2 passed, [13] SM id, [14] clock64
-// cycles entry -> [12].
-__device__ unsigned long long g_tf32_timeline[1024][16];
+// [0] entry, [1] set up, [2] Q landed, [3] K_0 split, [4] S_0 seen, [5] P_0 done,
+// [6] S_1 seen, [7] P_1 done, [8] final O, [9] cluster barrier 1 passed, [10] partials
+// pushed, [11] cluster barrier 2 passed, [12] rows stored, [13] SM id, [14] clock64
+// cycles entry -> [12], [15] MMA thread saw P_0, [16] PV_0 issued, [17] saw P_1, [18] PV_1
+// issued, [19] S_1 issued, [20] V_1 split, [21] Q split, [22] drain done.
+__device__ unsigned long long g_tf32_timeline[1024][24];
 #define FE_TTL(slot, v) \
   do { if (blockIdx.x + blockIdx.y * gridDim.x < 1024) \
          g_tf32_timeline[blockIdx.x + blockIdx.y * gridDim.x][slot] = (v); } while (0)
@@ -62,9 +67,9 @@ __device__ unsigned long long g_tf32_timeline[1024][16];
 
 template <int D>
 struct TCfg {
-  // d = 128: Q hi / lo and two K/V stages of 64 keys do not fit shared memory, so the
-  // key tile is 32 and Q lo lives in tensor memory (the A operand of its S pass).
-  static constexpr bool QLO_TMEM = D > 64;
+  // Q hi and Q lo live in tensor memory (the A operands of the S passes); shared memory
+  // holds raw Q as landed and two K/V stages. d = 128: two stages of 64 keys do not fit
+  // shared memory (nor tensor memory), so the key tile is 32.
   static constexpr int BM = 128, BN = D > 64 ? 32 : 64;
   static constexpr int HALVES = D / 32;  // 128-byte swizzle atom columns along d
   static constexpr int QH = BM * 128;    // bytes of one Q atom column
@@ -72,24 +77,24 @@ struct TCfg {
   static constexpr int VTH = D * 128;    // bytes of one V^T atom column (D rows)
   static constexpr int Q_BYTES = BM * D * 4;
   static constexpr int KV_BYTES = BN * D * 4;
-  static constexpr int Q_HI = 0, Q_LO = Q_BYTES;  // Q_LO: shared-memory Q lo (d <= 64)
+  static constexpr int Q_RAW = 0;  // raw Q as landed by TMA
   static constexpr int K_HI = 0, K_LO = KV_BYTES, V_HI = 2 * KV_BYTES, V_LO = 3 * KV_BYTES;
   static constexpr int STAGE = 4 * KV_BYTES;
-  static constexpr int ST_OFF = (QLO_TMEM ? 1 : 2) * Q_BYTES;  // stage s at ST_OFF + s*STAGE
+  static constexpr int ST_OFF = Q_BYTES;  // stage s at ST_OFF + s*STAGE
   // Landing buffer of raw K and V for key tiles 2, 3, ...: their copies need only the
   // previous tile's raw data to have been read, not a free stage.
   static constexpr int L_OFF = ST_OFF + 2 * STAGE, L_K = 0, L_V = KV_BYTES;
   static constexpr int BAR_OFF = L_OFF + 2 * KV_BYTES;
-  static constexpr int NBARS = 17;
+  static constexpr int NBARS = 19;
   static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
   // Dynamic shared memory requested at launch: enough that two CTAs never share an SM.
   // Each allocates all 512 tensor-memory columns, and two on one SM in one cluster would
   // wait on each other (one in tcgen05.alloc, the other at the cluster barrier).
   static constexpr int SMEM_LAUNCH = SMEM > 120 * 1024 ? SMEM : 120 * 1024;
   static constexpr int NTHREADS = 320;
-  // tensor-memory columns: S / P_hi double-buffered, P_lo double-buffered, O, Q lo
-  static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN, T_QL = T_O + D;
-  static_assert(T_QL + (QLO_TMEM ? D : 0) <= 512, "tensor memory");
+  // tensor-memory columns: S / P_hi double-buffered, P_lo double-buffered, O, Q lo, Q hi
+  static constexpr int T_S = 0, T_PL = 2 * BN, T_O = 4 * BN, T_QL = T_O + D, T_QH = T_QL + D;
+  static_assert(T_QH + D <= 512, "tensor memory");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -209,25 +214,20 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 // Every thread of every CTA of the cluster arrives; shared-memory writes before it
 // (local and remote) are visible to the whole cluster after it.
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile(
       "barrier.cluster.arrive.release.aligned;\n\t"
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float x, float y, float z, float w) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y),
+               "f"(z), "f"(w)
+               : "memory");
 }
 
 template <int D>
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* q_ready = bars + 1;
   uint64_t* kv_full = bars + 2;   // [2] TMA landed
-  uint64_t* kv_ready = bars + 4;  // [2] split into hi / lo
+  uint64_t* k_ready = bars + 4;   // [2] K_j split into hi / lo (S_j can start)
   uint64_t* kv_empty = bars + 6;  // [2] MMAs done with the stage
   uint64_t* s_full = bars + 8;    // [2] S_j in tensor memory
   uint64_t* p_full = bars + 10;   // [2] P_j in tensor memory
@@ -262,6 +262,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* drain = bars + 14;
   uint64_t* l_full = bars + 15;   // landing buffer holds the next tile's raw K / V
   uint64_t* l_empty = bars + 16;  // the split warps have read it
+  uint64_t* v_ready = bars + 17;  // [2] V_j split and transposed (P_j V_j can start)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -278,7 +279,8 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(q_ready, 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_ready[i], 128);
+      mbar_init(&k_ready[i], 128);
+      mbar_init(&v_ready[i], 128);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint64_t pol_once = l2_policy_evict_first();  // Q is read once
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
       for (int h = 0; h < HALVES; ++h)
-        tma_load_3d(smem + C::Q_HI + h * C::QH, &qmap, h * 32, m0, bh, q_full, pol_once);
+        tma_load_3d(smem + C::Q_RAW + h * C::QH, &qmap, h * 32, m0, bh, q_full, pol_once);
       bool ok = true;
       int issued = 0;
       // Tiles 0 and 1 land in their stages; later tiles in the landing buffer, each once
@@ -360,19 +362,14 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t kbase = sbase + C::ST_OFF + b * C::STAGE;
 #pragma unroll
         for (int pass = 0; pass < 3; ++pass) {
-          const uint32_t qa = sbase + (pass == 2 ? C::Q_LO : C::Q_HI);
+          const uint32_t qa = tmem + (pass == 2 ? C::T_QL : C::T_QH);  // A from tensor memory
           const uint32_t kb = kbase + (pass == 1 ? C::K_LO : C::K_HI);
 #pragma unroll
           for (int kk = 0; kk < D / 8; ++kk) {
-            const uint32_t qoff = (kk >> 2) * C::QH + (kk & 3) * 32;
             const uint32_t koff = (kk >> 2) * C::KH + (kk & 3) * 32;
-            const uint32_t acc = (pass > 0 || kk > 0) ? 1u : 0u;
-            if (C::QLO_TMEM && pass == 2)  // A = Q lo from tensor memory
-              tc::mma_ts_tf32(tmem + C::T_S + b * BN, tmem + C::T_QL + kk * 8,
-                              tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk, acc);
-            else
-              tc::mma_ss_tf32(tmem + C::T_S + b * BN, tc::smem_desc_sw128(qa + qoff, 16, 1024),
-                              tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk, acc);
+            tc::mma_ts_tf32(tmem + C::T_S + b * BN, qa + kk * 8,
+                            tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk,
+                            (pass > 0 || kk > 0) ? 1u : 0u);
           }
         }
         tc::commit(&s_full[b]);
@@ -396,25 +393,30 @@ __global__ void __launch_bounds__(320, 1)
       // S_{it+1} goes in before P_it V_it, so the tensor core computes it while the
       // softmax of tile it runs. MMAs from this thread execute in issue order, so
       // S_{it+2} overwrites P_it only after P_it V_it has read it.
-      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&kv_ready[0], 0);
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_ready[0], 0);
       if (ok) {
         tc::fence_after_sync();
         issue_s(0);
       }
       for (int it = 0; it < nloc && ok; ++it) {
         if (it + 1 < nloc) {
-          if (!mbar_wait(&kv_ready[(it + 1) & 1], ((it + 1) >> 1) & 1)) { ok = false; break; }
+          if (!mbar_wait(&k_ready[(it + 1) & 1], ((it + 1) >> 1) & 1)) { ok = false; break; }
           tc::fence_after_sync();
           issue_s(it + 1);
+          if (it == 0) FE_TTL(19, globaltimer_ns());
         }
-        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1) ||
+            !mbar_wait(&v_ready[it & 1], (it >> 1) & 1)) { ok = false; break; }
+        if (it < 2) FE_TTL(15 + 2 * it, globaltimer_ns());
         tc::fence_after_sync();
         issue_pv(it);
+        if (it < 2) FE_TTL(16 + 2 * it, globaltimer_ns());
       }
       if (!ok) atomicOr(p.err, kErrWaitTimeout);
       // Drain: all MMAs issued by this thread have completed.
       tc::commit(drain);
       mbar_wait(drain, 0);
+      FE_TTL(22, globaltimer_ns());
     }
   } else if (warp >= 6) {
     // ========================================================= hi / lo split
@@ -422,30 +424,44 @@ __global__ void __launch_bounds__(320, 1)
     if (nloc > 0) {
       // The 128 split threads meet on named barrier 1 (inside split_transpose_v), so they
       // take every go / give-up decision together: a wait result is AND-reduced first.
+      // Tiles 0 and 1 land in their stages and are split in place, keys first (K_0, K_1,
+      // then V_0, V_1): S_0 and S_1 need only the keys, and V_0 is needed only once the
+      // softmax of tile 0 is done.
       bool ok = true;
-      for (int it = 0; it < nloc && ok; ++it) {
+      const int nfirst = min(nloc, 2);
+      for (int it = 0; it < nfirst && ok; ++it) {
+        uint8_t* sb = smem + C::ST_OFF + it * C::STAGE;
+        if (!split_group_all(mbar_wait(&kv_full[it], 0))) { ok = false; break; }
+        split_tile<C::KV_BYTES, 128>(sb + C::K_HI, sb + C::K_LO, sid);
+        fence_proxy_async_smem();
+        mbar_arrive(&k_ready[it]);
+        if (sid == 0 && it == 0) FE_TTL(3, globaltimer_ns());
+      }
+      for (int it = 0; it < nfirst && ok; ++it) {
+        uint8_t* sb = smem + C::ST_OFF + it * C::STAGE;
+        split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
+        fence_proxy_async_smem();
+        mbar_arrive(&v_ready[it]);
+        if (sid == 0 && it == 1) FE_TTL(20, globaltimer_ns());
+      }
+      for (int it = 2; it < nloc && ok; ++it) {
+        // raw tile in the landing buffer; the stage is free once P V of tile it-2 is done
         const int st = it & 1;
         uint8_t* sb = smem + C::ST_OFF + st * C::STAGE;
-        if (it < 2) {  // raw tile in its stage: split in place
-          if (!split_group_all(mbar_wait(&kv_full[it], 0))) { ok = false; break; }
-          split_tile<C::KV_BYTES, 128>(sb + C::K_HI, sb + C::K_LO, sid);
-          split_transpose_v<D, BN>(sb + C::V_HI, sb + C::V_LO, sid);
-        } else {
-          // raw tile in the landing buffer; the stage is free once P V of tile it-2 is done
-          const bool got = mbar_wait(l_full, (it - 2) & 1) &&
-                           mbar_wait(&kv_empty[st], ((it >> 1) - 1) & 1);
-          if (!split_group_all(got)) { ok = false; break; }
-          float4 kx[C::KV_BYTES / 16 / 128];
-          float4 vx[v_per<D, BN>()];
-          load_tile<C::KV_BYTES, 128>(smem + C::L_OFF + C::L_K, kx, sid);
-          load_v<D, BN>(smem + C::L_OFF + C::L_V, vx, sid);
-          mbar_arrive(l_empty);  // this thread's reads of the landing buffer are done
-          store_split<C::KV_BYTES, 128>(kx, sb + C::K_HI, sb + C::K_LO, sid);
-          store_vt<D, BN>(vx, sb + C::V_HI, sb + C::V_LO, sid);
-        }
+        const bool got = mbar_wait(l_full, (it - 2) & 1) &&
+                         mbar_wait(&kv_empty[st], ((it >> 1) - 1) & 1);
+        if (!split_group_all(got)) { ok = false; break; }
+        float4 kx[C::KV_BYTES / 16 / 128];
+        float4 vx[v_per<D, BN>()];
+        load_tile<C::KV_BYTES, 128>(smem + C::L_OFF + C::L_K, kx, sid);
+        load_v<D, BN>(smem + C::L_OFF + C::L_V, vx, sid);
+        mbar_arrive(l_empty);  // this thread's reads of the landing buffer are done
+        store_split<C::KV_BYTES, 128>(kx, sb + C::K_HI, sb + C::K_LO, sid);
         fence_proxy_async_smem();
-        mbar_arrive(&kv_ready[st]);
-        if (sid == 0 && it == 0) FE_TTL(3, globaltimer_ns());
+        mbar_arrive(&k_ready[st]);
+        store_vt<D, BN>(vx, sb + C::V_HI, sb + C::V_LO, sid);
+        fence_proxy_async_smem();
+        mbar_arrive(&v_ready[st]);
       }
       if (!ok && sid == 0) atomicOr(p.err, kErrWaitTimeout);
     }
@@ -465,32 +481,33 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0));
       if (threadIdx.x == 0) FE_TTL(2, globaltimer_ns());
       if (ok) {
-        if constexpr (C::QLO_TMEM) {
-          // this thread's row: hi back in place, lo to tensor-memory columns T_QL + d
+        // this thread's row of raw Q -> hi and lo in tensor-memory columns T_QH / T_QL + d,
+        // 32 columns at a time, hi stored before lo is formed (32 values live, not 64)
 #pragma unroll
-          for (int a = 0; a < HALVES; ++a) {
-            uint32_t lo[32];
+        for (int a = 0; a < HALVES; ++a) {
+          uint32_t x[32];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              float4* q4 = reinterpret_cast<float4*>(smem + C::Q_HI + a * C::QH + row * 128 +
-                                                     ((c ^ (row & 7)) << 4));
-              const float4 x = *q4;
-              const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-              *q4 = h;
-              lo[c * 4 + 0] = __float_as_uint(x.x - h.x);
-              lo[c * 4 + 1] = __float_as_uint(x.y - h.y);
-              lo[c * 4 + 2] = __float_as_uint(x.z - h.z);
-              lo[c * 4 + 3] = __float_as_uint(x.w - h.w);
-            }
-            tc::st32(tmem + lane_off + C::T_QL + a * 32, lo);
+          for (int c = 0; c < 8; ++c) {
+            const float4 v4 = *reinterpret_cast<const float4*>(
+                smem + C::Q_RAW + a * C::QH + row * 128 + ((c ^ (row & 7)) << 4));
+            x[c * 4 + 0] = __float_as_uint(v4.x);
+            x[c * 4 + 1] = __float_as_uint(v4.y);
+            x[c * 4 + 2] = __float_as_uint(v4.z);
+            x[c * 4 + 3] = __float_as_uint(v4.w);
           }
-          tc::wait_st();
-          tc::fence_before_sync();
-        } else {
-          split_tile<C::Q_BYTES, 128>(smem + C::Q_HI, smem + C::Q_LO, threadIdx.x);
+          uint32_t h[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) h[e] = x[e] & 0xFFFFE000u;  // tf32_hi
+          tc::st32(tmem + lane_off + C::T_QH + a * 32, h);
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            x[e] = __float_as_uint(__uint_as_float(x[e]) - __uint_as_float(x[e] & 0xFFFFE000u));
+          tc::st32(tmem + lane_off + C::T_QL + a * 32, x);
         }
-        fence_proxy_async_smem();
+        tc::wait_st();
+        tc::fence_before_sync();
         mbar_arrive(q_ready);
+        if (threadIdx.x == 0) FE_TTL(21, globaltimer_ns());
       }
     }
     for (int it = 0; it < nloc && ok; ++it) {
@@ -607,20 +624,30 @@ __global__ void __launch_bounds__(320, 1)
     return;
   }
 
-  // ---- cluster combine. Each CTA leaves its partial rows (O unnormalised, m, l) in its
-  // own stage buffers, which are free: their copies landed and every MMA has completed
-  // (drained above). After a cluster barrier, CTA c reads rows [c*SR, (c+1)*SR) of every partner
-  // (consecutive threads take consecutive 16-byte words of a row) and writes them.
-  // (Sending the slices with bulk async copies into the partners' shared memory measured
-  // the same; the cluster barriers dominate this phase.)
+  // ---- cluster combine. CTA c owns rows [c*SR, (c+1)*SR) of the tile. Every CTA pushes
+  // its partial rows (O unnormalised, m, l) into the owners' stage buffers with
+  // distributed-shared-memory stores, then each owner merges its rows from its own
+  // shared memory and writes them.
+  //  * cluster barrier 1: every CTA's stage buffers are free -- its copies landed and its
+  //    MMAs completed (drained above);
+  //  * cluster barrier 2: every push is visible to its owner. After it no CTA touches
+  //    another CTA's shared memory, so a CTA may exit once it has merged its rows.
+  // (Signalling the two steps with remote mbarrier arrives instead of the cluster
+  // barriers measured slower.)
   constexpr int OS = D + 4;                                 // padded row stride (floats)
-  float* pO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [BM][OS] (both stages)
-  float* pM = pO + BM * OS;                                 // [BM]
-  float* pL = pM + BM;                                      // [BM]
+  const int SR = BM / nsplit;
+  float* rO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [nsplit][SR][OS]
+  float* rM = rO + BM * OS;                                 // [nsplit][SR]
+  float* rL = rM + BM;                                      // [nsplit][SR]
   static_assert((BM * OS + 2 * BM) * 4 <= 2 * C::STAGE, "combine buffer");
+  cluster_sync_all();  // every CTA's stage buffers are free
+  if (threadIdx.x == 0) FE_TTL(9, globaltimer_ns());
   if (warp < 4) {
     const int row = warp * 32 + lane;
+    const uint32_t owner = static_cast<uint32_t>(row / SR);
+    const int slot = split * SR + (row - static_cast<int>(owner) * SR);
     const uint32_t tO = tmem + (static_cast<uint32_t>(warp * 32) << 16) + C::T_O;
+    const uint32_t dst = cluster_map(smem_u32(rO + slot * OS), owner);
 #pragma unroll
     for (int c = 0; c < D / 32; ++c) {
       uint32_t w[32];
@@ -633,65 +660,44 @@ __global__ void __launch_bounds__(320, 1)
       }
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(pO + row * OS + c * 32 + i) =
-            make_float4(__uint_as_float(w[i]), __uint_as_float(w[i + 1]),
-                        __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
+        st_cluster_v4(dst + (c * 32 + i) * 4, __uint_as_float(w[i]), __uint_as_float(w[i + 1]),
+                      __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
     }
-    pM[row] = m_run;
-    pL[row] = l_run;
+    st_cluster_f32(cluster_map(smem_u32(rM + slot), owner), m_run);
+    st_cluster_f32(cluster_map(smem_u32(rL + slot), owner), l_run);
   }
-  if (threadIdx.x == 0) FE_TTL(9, globaltimer_ns());
   tc::fence_before_sync();
-  cluster_sync_all();  // every partial of the cluster is in place
   if (threadIdx.x == 0) FE_TTL(10, globaltimer_ns());
+  cluster_sync_all();  // every push has reached its owner
+  if (threadIdx.x == 0) FE_TTL(11, globaltimer_ns());
   if (warp == 5) {     // every tensor-memory read of this CTA is done
     tc::fence_after_sync();
     tc::tmem_dealloc<512>(tmem);
   }
-  const int SR = BM / nsplit;
   constexpr int C4 = D / 4;
   for (int idx = threadIdx.x; idx < SR * C4; idx += C::NTHREADS) {
     const int rr = idx / C4, c = (idx - rr * C4) * 4;
-    const int trow = split * SR + rr;
-    const int row = m0 + trow;
+    const int row = m0 + split * SR + rr;
     if (row >= p.N) continue;
-    const uint32_t a_m = smem_u32(pM + trow), a_l = smem_u32(pL + trow);
-    const uint32_t a_o = smem_u32(pO + trow * OS + c);
-    float ms[8], ls[8];
-    float4 os[8];
-#pragma unroll
-    for (int s2 = 0; s2 < 8; ++s2) {
-      if (s2 < nsplit) {
-        ms[s2] = ld_cluster_f32(cluster_map(a_m, s2));
-        ls[s2] = ld_cluster_f32(cluster_map(a_l, s2));
-        os[s2] = ld_cluster_v4(cluster_map(a_o, s2));
-      }
-    }
     float mx = NEG_INF;
-#pragma unroll
-    for (int s2 = 0; s2 < 8; ++s2)
-      if (s2 < nsplit) mx = fmaxf(mx, ms[s2]);
+    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, rM[s2 * SR + rr]);
     float tot = 0.f;
     float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (mx != NEG_INF) {
-#pragma unroll
-      for (int s2 = 0; s2 < 8; ++s2) {
-        if (s2 < nsplit) {
-          const float w = ex2(ms[s2] - mx);
-          tot = fmaf(ls[s2], w, tot);
-          o4.x = fmaf(w, os[s2].x, o4.x);
-          o4.y = fmaf(w, os[s2].y, o4.y);
-          o4.z = fmaf(w, os[s2].z, o4.z);
-          o4.w = fmaf(w, os[s2].w, o4.w);
-        }
+      for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float w = ex2(rM[s2 * SR + rr] - mx);
+        const float4 os = *reinterpret_cast<const float4*>(rO + (s2 * SR + rr) * OS + c);
+        tot = fmaf(rL[s2 * SR + rr], w, tot);
+        o4.x = fmaf(w, os.x, o4.x);
+        o4.y = fmaf(w, os.y, o4.y);
+        o4.z = fmaf(w, os.z, o4.z);
+        o4.w = fmaf(w, os.w, o4.w);
       }
     }
     const float inv = tot > 0.f ? 1.f / tot : 0.f;
     *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c) =
         make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
   }
-  if (threadIdx.x == 0) FE_TTL(11, globaltimer_ns());
-  cluster_sync_all();  // no CTA exits while a partner may still read its partials
 #ifdef FE_TF32_TIMELINE
   if (threadIdx.x == 0) {
     FE_TTL(12, globaltimer_ns());
