@@ -86,7 +86,16 @@ struct TCfg {
   static constexpr int L_OFF = ST_OFF + 2 * STAGE, L_K = 0, L_V = KV_BYTES;
   static constexpr int BAR_OFF = L_OFF + 2 * KV_BYTES;
   static constexpr int NBARS = 19;
-  static constexpr int SMEM = 1024 + BAR_OFF + NBARS * 8 + 16;
+  static constexpr int BAR_END = BAR_OFF + NBARS * 8 + 32;  // + tensor-memory slot, flags
+  // Receive buffer of the cluster merge ([BM] rows of D floats, then m and l): a region of
+  // its own where it fits (d <= 64), so partners push into it without waiting for this
+  // CTA's stage buffers to be free; else (d = 128) the stage buffers.
+  static constexpr int RECV_BYTES = (BM * D + 2 * BM) * 4;
+  static constexpr int RECV_OWN_OFF = (BAR_END + 127) / 128 * 128;
+  static constexpr bool RECV_OWN = 1024 + RECV_OWN_OFF + RECV_BYTES <= 232448;
+  static constexpr int RECV_OFF = RECV_OWN ? RECV_OWN_OFF : ST_OFF;
+  static_assert(RECV_OWN || RECV_BYTES <= 2 * STAGE, "combine buffer");
+  static constexpr int SMEM = 1024 + (RECV_OWN ? RECV_OWN_OFF + RECV_BYTES : BAR_END);
   // Dynamic shared memory requested at launch: enough that two CTAs never share an SM.
   // Each allocates all 512 tensor-memory columns, and two on one SM in one cluster would
   // wait on each other (one in tcgen05.alloc, the other at the cluster barrier).
@@ -264,6 +273,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* l_empty = bars + 16;  // the split warps have read it
   uint64_t* v_ready = bars + 17;  // [2] V_j split and transposed (P_j V_j can start)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+  int* o_valid = reinterpret_cast<int*>(tmem_slot + 1);  // [4] softmax warp w read its final O
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsplit = p.nsplit;
@@ -299,6 +309,10 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // Cluster merge into a receive buffer of its own: this arrive, waited on just before
+  // the first remote store, makes sure every CTA of the cluster is running by then.
+  if (C::RECV_OWN && nsplit > 1)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   // Programmatic dependent launch: let the next kernel place its CTAs as ours retire,
   // and wait for the previous kernel's results before the first global access.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -589,6 +603,7 @@ __global__ void __launch_bounds__(320, 1)
       m_run = NEG_INF;
       l_run = 0.f;
     }
+    if (lane == 0) o_valid[warp] = have_o ? 1 : 0;
     if (nsplit == 1) {
       // O / l straight from tensor memory, 32 columns at a time
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -625,33 +640,45 @@ __global__ void __launch_bounds__(320, 1)
   }
 
   // ---- cluster combine. CTA c owns rows [c*SR, (c+1)*SR) of the tile. Every CTA pushes
-  // its partial rows (O unnormalised, m, l) into the owners' stage buffers with
+  // its partial rows (O unnormalised, m, l) into the owners' receive buffers with
   // distributed-shared-memory stores, then each owner merges its rows from its own
   // shared memory and writes them.
-  //  * cluster barrier 1: every CTA's stage buffers are free -- its copies landed and its
-  //    MMAs completed (drained above);
-  //  * cluster barrier 2: every push is visible to its owner. After it no CTA touches
-  //    another CTA's shared memory, so a CTA may exit once it has merged its rows.
-  // (Signalling the two steps with remote mbarrier arrives instead of the cluster
-  // barriers measured slower.)
-  constexpr int OS = D + 4;                                 // padded row stride (floats)
+  //  * with a receive buffer of its own (d <= 64) a CTA pushes as soon as its O is final;
+  //    with the stage buffers as receive buffer (d = 128) a cluster barrier first makes
+  //    sure every CTA's stage buffers are free (copies landed, MMAs drained above);
+  //  * a cluster barrier then makes every push visible to its owner. After it no CTA
+  //    touches another CTA's shared memory, so a CTA may exit once it has merged its rows.
+  // (Signalling with remote mbarrier arrives instead of the cluster barriers measured
+  // slower.) Rows are D floats apart, their 16-byte chunks XOR-swizzled by row & 7 so
+  // that neither the pushes (a warp stores one chunk of 32 rows) nor the merge reads
+  // conflict on banks.
   const int SR = BM / nsplit;
-  float* rO = reinterpret_cast<float*>(smem + C::ST_OFF);   // [nsplit][SR][OS]
-  float* rM = rO + BM * OS;                                 // [nsplit][SR]
-  float* rL = rM + BM;                                      // [nsplit][SR]
-  static_assert((BM * OS + 2 * BM) * 4 <= 2 * C::STAGE, "combine buffer");
-  cluster_sync_all();  // every CTA's stage buffers are free
+  float* rO = reinterpret_cast<float*>(smem + C::RECV_OFF);  // [nsplit * SR][D]
+  float* rM = rO + BM * D;                                   // [nsplit * SR]
+  float* rL = rM + BM;                                       // [nsplit * SR]
+  if (C::RECV_OWN) {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA running
+  } else {
+    cluster_sync_all();  // every CTA's stage buffers are free
+  }
   if (threadIdx.x == 0) FE_TTL(9, globaltimer_ns());
-  if (warp < 4) {
-    const int row = warp * 32 + lane;
+  // Warps 0-7 push: warp w reads tensor-memory lanes 32 (w & 3) .. + 31 (the rows it may
+  // access) and, for d >= 64, half of the columns ((w >> 2) selects the half).
+  constexpr int PUSH_WARPS = D >= 64 ? 8 : 4;
+  constexpr int PCOLS = D / (PUSH_WARPS / 4);
+  if (warp < PUSH_WARPS) {
+    const int row = (warp & 3) * 32 + lane;
+    const int h = warp >> 2;
     const uint32_t owner = static_cast<uint32_t>(row / SR);
     const int slot = split * SR + (row - static_cast<int>(owner) * SR);
-    const uint32_t tO = tmem + (static_cast<uint32_t>(warp * 32) << 16) + C::T_O;
-    const uint32_t dst = cluster_map(smem_u32(rO + slot * OS), owner);
+    const uint32_t tO = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + C::T_O + h * PCOLS;
+    const uint32_t dst = cluster_map(smem_u32(rO + slot * D), owner);
+    const bool valid = o_valid[warp & 3] != 0;
+    tc::fence_after_sync();  // the MMAs' writes of O (drained before the CTA barrier)
 #pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < PCOLS / 32; ++c) {
       uint32_t w[32];
-      if (have_o) {
+      if (valid) {
         tc::ld32(tO + c * 32, w);
         tc::wait_ld();
       } else {
@@ -659,12 +686,17 @@ __global__ void __launch_bounds__(320, 1)
         for (int i = 0; i < 32; ++i) w[i] = 0u;
       }
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        st_cluster_v4(dst + (c * 32 + i) * 4, __uint_as_float(w[i]), __uint_as_float(w[i + 1]),
-                      __uint_as_float(w[i + 2]), __uint_as_float(w[i + 3]));
+      for (int i = 0; i < 32; i += 4) {
+        const int chunk = (h * PCOLS + c * 32 + i) >> 2;
+        st_cluster_v4(dst + ((chunk ^ (slot & 7)) << 4), __uint_as_float(w[i]),
+                      __uint_as_float(w[i + 1]), __uint_as_float(w[i + 2]),
+                      __uint_as_float(w[i + 3]));
+      }
     }
-    st_cluster_f32(cluster_map(smem_u32(rM + slot), owner), m_run);
-    st_cluster_f32(cluster_map(smem_u32(rL + slot), owner), l_run);
+    if (h == 0) {
+      st_cluster_f32(cluster_map(smem_u32(rM + slot), owner), m_run);
+      st_cluster_f32(cluster_map(smem_u32(rL + slot), owner), l_run);
+    }
   }
   tc::fence_before_sync();
   if (threadIdx.x == 0) FE_TTL(10, globaltimer_ns());
@@ -676,26 +708,39 @@ __global__ void __launch_bounds__(320, 1)
   }
   constexpr int C4 = D / 4;
   for (int idx = threadIdx.x; idx < SR * C4; idx += C::NTHREADS) {
-    const int rr = idx / C4, c = (idx - rr * C4) * 4;
+    const int rr = idx / C4, c4 = idx - rr * C4;
     const int row = m0 + split * SR + rr;
     if (row >= p.N) continue;
+    float ms[8], ls[8];
+    float4 os[8];
     float mx = NEG_INF;
-    for (int s2 = 0; s2 < nsplit; ++s2) mx = fmaxf(mx, rM[s2 * SR + rr]);
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < nsplit) {
+        const int slot = s2 * SR + rr;
+        ms[s2] = rM[slot];
+        ls[s2] = rL[slot];
+        os[s2] = *reinterpret_cast<const float4*>(rO + slot * D + ((c4 ^ (slot & 7)) << 2));
+        mx = fmaxf(mx, ms[s2]);
+      }
+    }
     float tot = 0.f;
     float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (mx != NEG_INF) {
-      for (int s2 = 0; s2 < nsplit; ++s2) {
-        const float w = ex2(rM[s2 * SR + rr] - mx);
-        const float4 os = *reinterpret_cast<const float4*>(rO + (s2 * SR + rr) * OS + c);
-        tot = fmaf(rL[s2 * SR + rr], w, tot);
-        o4.x = fmaf(w, os.x, o4.x);
-        o4.y = fmaf(w, os.y, o4.y);
-        o4.z = fmaf(w, os.z, o4.z);
-        o4.w = fmaf(w, os.w, o4.w);
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (s2 < nsplit) {
+          const float w = ex2(ms[s2] - mx);
+          tot = fmaf(ls[s2], w, tot);
+          o4.x = fmaf(w, os[s2].x, o4.x);
+          o4.y = fmaf(w, os[s2].y, o4.y);
+          o4.z = fmaf(w, os[s2].z, o4.z);
+          o4.w = fmaf(w, os[s2].w, o4.w);
+        }
       }
     }
     const float inv = tot > 0.f ? 1.f / tot : 0.f;
-    *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c) =
+    *reinterpret_cast<float4*>(p.out + (static_cast<size_t>(bh) * p.N + row) * D + c4 * 4) =
         make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
   }
 #ifdef FE_TF32_TIMELINE

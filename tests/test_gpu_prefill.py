@@ -206,6 +206,59 @@ def test_bf16_first_call_inside_graph_capture():
         assert_bf16_close(o[:, h:h + 1], ref)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("N,M", [(300, 300), (520, 200), (256, 700)])
+def test_bf16_many_pairs_repeated_and_second_stream(d, causal, N, M):
+    """More query-tile pairs than SMs (several waves of CTAs, longest-first over head
+    groups). N = 300 leaves the last pair without its second tile. Three launches in a
+    row and one on a second stream; every (batch, head) against the oracle."""
+    import flash_engine
+    B, H = 3, 56
+    rng = np.random.default_rng(N * 3 + M + d + causal)
+    q = O.bf16_round(rng.standard_normal((B, H, N, d), dtype=np.float32))
+    k = O.bf16_round(rng.standard_normal((B, H, M, d), dtype=np.float32))
+    v = O.bf16_round(rng.standard_normal((B, H, M, d), dtype=np.float32))
+    ref = O.flash_attention(q, k, v, causal)
+    qd, kd, vd = (cuda(x, torch.bfloat16) for x in (q, k, v))
+    for _ in range(3):
+        out = flash_engine.flash_attention(qd, kd, vd, causal)
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        assert_bf16_close(host(out), ref)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        out = flash_engine.flash_attention(qd, kd, vd, causal)
+    torch.cuda.synchronize()
+    assert flash_engine.device_errors() == 0
+    assert_bf16_close(host(out), ref)
+
+
+def test_bf16_many_pairs_graph_replays():
+    """More query-tile pairs than SMs, captured into a CUDA graph as the first call on a
+    new stream and replayed three times (the output zeroed before each replay)."""
+    import flash_engine
+    B, H, N, d = 2, 48, 1100, 64
+    q, k, v = _heads_case(B, H, N, d, 9)
+    qd, kd, vd = (cuda(x, torch.bfloat16) for x in (q, k, v))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        out = flash_engine.flash_attention(qd, kd, vd, True)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert flash_engine.device_errors() == 0
+        o = host(out)
+        for b, h in ((0, 0), (1, 47), (0, 30)):
+            ref = O.flash_attention_sliced(q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1],
+                                           v[b:b + 1, h:h + 1], True)
+            assert_bf16_close(o[b:b + 1, h:h + 1], ref)
+
+
 @pytest.mark.parametrize("d", [32, 64, 128])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("N,M", [(300, 300), (128, 520), (640, 200)])
