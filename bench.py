@@ -616,15 +616,19 @@ def bench_splitkv(a, ws, rank, local, steps, warmup):
         return sharding.paged_decode_kv_range(qq, kc, vc, bb, ll, M, bs, workspace=wsp)
 
     # A step (decode, all-gather and merge at N > 1) is one CUDA-graph replay, except
-    # with the peer-memory exchange: its two launches are not CPU-bound, and replaying
-    # them as a graph measured slower at N = 8 (88 vs 70 us a step), so they are issued
-    # directly.
+    # with the peer-memory exchange: replaying its two launches as a graph measured slower
+    # at N = 8 (88 vs 70 us a step), so they are issued directly, through the exchange's
+    # prepared step (arguments checked and converted once; issuing through the checking
+    # wrapper cost as much host time as the step's GPU work at N = 8).
     from flash_engine.graph import DecodeGraph
     graph = DecodeGraph(lambda: call(0)) if ex is None else None
+    fast = ex.prepare(q_all, kc, vc, bt_t, lens_t, M, bs, workspace=wsp) if ex is not None else None
 
     def step(i):
         if graph is not None:
             graph.replay()
+        elif fast is not None:
+            fast()
         else:
             call(i)
 

@@ -416,6 +416,48 @@ def paged_decode_kv_exchange(query, key_cache, value_cache, block_tables, contex
     return out
 
 
+def paged_decode_kv_exchange_prepared(query, key_cache, value_cache, block_tables,
+                                      context_lens, token_begin: int, token_end: int, xbufs,
+                                      rank: int, max_rows: int, block_size: int = 16,
+                                      scale: float | None = None, workspace=None, out=None):
+    """``paged_decode_kv_exchange`` (both phases) with its arguments checked and converted
+    once: returns a function of no arguments that runs one step on the stream current at
+    this call and returns ``out``. For loops that decode into the same tensors step after
+    step (their data may change, not their shapes or storage), where the per-call checks
+    and argument conversion would cost as much host time as the step's GPU work."""
+    import ctypes
+
+    _require_cuda(query, key_cache, value_cache, block_tables, context_lens)
+    if query.dtype != torch.bfloat16:
+        raise TypeError("the KV-range exchange decode takes bf16")
+    S, H, Hkv, d, nb, maxb = _paged_shapes(query, key_cache, value_cache, block_tables,
+                                           context_lens, block_size)
+    ws, n = _workspace(query, H, Hkv, d, block_size, workspace)
+    if out is None:
+        out = torch.empty_like(query)
+    arr = (ctypes.c_void_p * len(xbufs))(*[int(x) for x in xbufs])
+    with _on(query.device):
+        stream = _stream()
+    fn = _lib_c.fe_paged_decode_kv_exchange_bf16
+    args = [_ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables),
+            _ptr(context_lens), S, H, Hkv, d, block_size, maxb, nb, _scale_arg(scale, d),
+            int(token_begin), int(token_end), _ptr(ws) if ws is not None else None, n, arr,
+            len(xbufs), int(rank), int(max_rows), _ptr(out), 3, stream]
+    # convert once to the declared ctypes argument types
+    cargs = tuple(a if isinstance(a, ctypes.Array) or a is None else t(a)
+                  for a, t in zip(args, fn.argtypes))
+    keep = (query, key_cache, value_cache, block_tables, context_lens, ws, out, arr)
+
+    def step():
+        _ = keep
+        st = fn(*cargs)
+        if st != 0:
+            _lib.check(st, "paged_decode_kv_exchange")
+        return out
+
+    return step
+
+
 def merge_partials(part_out, part_stats, ranks: int, parts_per_rank: int, out_dtype: str = "bf16",
                    out=None, out_stats=None):
     """Log-sum-exp combine of partials laid out [ranks, rows, parts_per_rank, d]

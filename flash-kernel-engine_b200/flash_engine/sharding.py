@@ -162,6 +162,21 @@ class KVRangeExchange:
                                             context_lens, tb, te, self.ptrs, self.rank,
                                             self.max_rows, block_size, scale, workspace, out)
 
+    def prepare(self, query, key_cache, value_cache, block_tables, context_lens,
+                max_context_len: int, block_size: int = 16, scale=None, workspace=None,
+                out=None):
+        """``decode`` with its arguments checked and converted once: returns a function
+        of no arguments that runs one step (on the stream current at this call) into
+        ``out`` and returns it. Every rank must call the returned function the same number
+        of times, interleaved with its ``decode`` calls in the same order."""
+        from . import ops
+
+        tb, te = kv_range_bounds(max_context_len, self.world, self.rank, block_size)
+        return ops.paged_decode_kv_exchange_prepared(query, key_cache, value_cache,
+                                                     block_tables, context_lens, tb, te,
+                                                     self.ptrs, self.rank, self.max_rows,
+                                                     block_size, scale, workspace, out)
+
     def close(self):
         """Collective: unmap the peers' buffers and free this rank's own."""
         if self._own is None:

@@ -178,8 +178,8 @@ def nccl_graph_worker(rank, world, port, result_path):
 
 def p2p_exchange_worker(rank, world, port, result_path):
     """KV-range decode with the all-gather done by the decode kernel over peer memory
-    (KVRangeExchange): three eager steps on new query tokens, then two replays of the
-    step captured in a CUDA graph, each checked against the oracle."""
+    (KVRangeExchange): three eager steps on new query tokens, two replays of the step
+    captured in a CUDA graph, then two prepared steps, each checked against the oracle."""
     import torch
     import torch.distributed as dist
     import flash_engine
@@ -221,6 +221,14 @@ def p2p_exchange_worker(rank, world, port, result_path):
     for seed in (65, 66):
         q2 = check(seed)
         out = g.replay()
+        torch.cuda.synchronize()
+        ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
+                                    p["context_lens"])
+        errs.append(float(np.abs(out.float().cpu().numpy() - ref).max()))
+    step = ex.prepare(q, kc, vc, bt, cl, M, 16, workspace=ws)
+    for seed in (67, 68):
+        q2 = check(seed)
+        out = step()
         torch.cuda.synchronize()
         ref = O.paged_attention_gqa(q2, p["k_cache"], p["v_cache"], p["block_tables"],
                                     p["context_lens"])
