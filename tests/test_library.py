@@ -75,8 +75,11 @@ def test_ops_have_no_cpu_fallback():
         flash_engine.flash_attention(q, q, q)
     with pytest.raises(TypeError):
         flash_engine.flash_attention(np.zeros((1, 1, 4, 64), np.float32), q, q)
+    # the reference binding's checks (TORCH_CHECK raises RuntimeError with these messages)
     import flash_engine_cuda
-    with pytest.raises(TypeError):
+    with pytest.raises(RuntimeError, match="Q must be a CUDA tensor"):
         flash_engine_cuda.flash_attention_forward(q, q, q, False)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="query must be a CUDA tensor"):
+        flash_engine_cuda.paged_attention_forward(q, q, q, q, q)
+    with pytest.raises(RuntimeError, match="x must be a CUDA tensor"):
         flash_engine_cuda.fused_rmsnorm_forward(q, q, 1e-5)
