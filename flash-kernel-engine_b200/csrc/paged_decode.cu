@@ -542,6 +542,9 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
   // inputs that no kernel of this library writes, context_lens and block_tables: the
   // prefix over the sequences and the producer's first block-table group are read
   // while the previous grid (typically the previous decode step) is still finishing.
+  // This grid can start before the previous kernel in the stream has completed only if
+  // that kernel executed griddepcontrol.launch_dependents, which only this library's
+  // kernels do; after any other kernel (or a copy) it starts once that has completed.
   // q, the KV cache, the workspace, the exchange buffers and the outputs are accessed
   // only after the wait.
   if (tid == 0) {
