@@ -544,7 +544,8 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
   // while the previous grid (typically the previous decode step) is still finishing.
   // This grid can start before the previous kernel in the stream has completed only if
   // that kernel executed griddepcontrol.launch_dependents, which only this library's
-  // kernels do; after any other kernel (or a copy) it starts once that has completed.
+  // kernels do; inputs written by a copy, a host write or any kernel that does not
+  // trigger programmatic completion are complete before this grid starts.
   // q, the KV cache, the workspace, the exchange buffers and the outputs are accessed
   // only after the wait.
   if (tid == 0) {
