@@ -382,12 +382,11 @@ int fe_flash_attention_forward_ex(const void* q, const void* k, const void* v, v
   const void* qq = q;
   const void* kk = k;
   if (rope_cos) {
-    // Q and K rotated once each by the streaming RoPE pass into the caller's buffers
+    // Q and K rotated once each by one streaming RoPE launch into the caller's buffers
     // (each key tile is read by every query tile of its head, so rotating it inside the
     // attention kernel would repeat the work; k_rotated keeps the keys a KV cache stores)
-    cudaError_t e = fe::rope::launch_rope(q, rope_cos, rope_sin, q_rotated, B, H, N, d, dtype, st);
-    if (e == cudaSuccess)
-      e = fe::rope::launch_rope(k, rope_cos, rope_sin, k_rotated, B, H, M, d, dtype, st);
+    const cudaError_t e = fe::rope::launch_rope_qk(q, k, rope_cos, rope_sin, q_rotated, k_rotated,
+                                                   B, H, N, M, d, dtype, st);
     if (e != cudaSuccess) return static_cast<int>(e);
     qq = q_rotated;
     kk = k_rotated;
