@@ -331,7 +331,7 @@ def test_rope_forward(dtype, d):
     np.testing.assert_array_equal(host(xt), host(out))
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("d", [64, 128])
 def test_rope_forward_many_passes(dtype, d):
     """The row path of the dense RoPE pass when each thread covers several rows of a
@@ -341,7 +341,8 @@ def test_rope_forward_many_passes(dtype, d):
     rng = np.random.default_rng(d + 1)
     x = rng.standard_normal((3, 50, 333, d), dtype=np.float32)
     rnd = (lambda a: O.bf16_round(a.astype(np.float32))) if dtype == torch.bfloat16 else \
-        (lambda a: a.astype(np.float16).astype(np.float32))
+        (lambda a: a.astype(np.float16).astype(np.float32)) if dtype == torch.float16 else \
+        (lambda a: a.astype(np.float32))
     x = rnd(x)
     cos, sin = O.rope_tables(400, d)
     ref = rnd(O.rope_rotate(x, cos, sin, np.arange(333)))
@@ -349,6 +350,6 @@ def test_rope_forward_many_passes(dtype, d):
     out = flash_engine.rope(xt, cuda(cos), cuda(sin))
     flash_engine.rope(xt, cuda(cos), cuda(sin), out=xt)   # in place
     torch.cuda.synchronize()
-    tol = {torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10}[dtype]
+    tol = {torch.float32: 1e-6, torch.bfloat16: 2 ** -7, torch.float16: 2 ** -10}[dtype]
     np.testing.assert_allclose(host(out), ref, rtol=tol, atol=tol)
     np.testing.assert_array_equal(host(xt), host(out))
