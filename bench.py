@@ -56,7 +56,8 @@ for _p in (ROOT, PKG):
 import numpy as np  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
-WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32", "paged_fp32")
+WORKLOADS = ("decode", "serving", "splitkv", "prefill", "prefill_fp32", "paged_fp32",
+             "prefill_rope")
 NOMINAL_HBM_GBS = 8000.0       # B200 HBM3e (DGX figure)
 NOMINAL_BF16_TFLOPS = 2250.0   # B200 dense bf16 tensor
 BF16_ATOL = 2e-2
@@ -756,7 +757,9 @@ def prefill_flops(B, H, N, d, causal=True):
     return f / 2 if causal else f
 
 
-def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
+def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False, rope=False):
+    """Config 1 (fp32) or config 2 (bf16); with rope, config 2 with Q and K rotated
+    (the RoPE pass for both, then the attention) inside every step."""
     import torch
     import flash_engine
 
@@ -765,6 +768,11 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
         B, H, N, d, causal, dt = 1, 8, 512, 64, False, torch.float32
         name = "fa2_prefill_fp32_config1"
         metric = "FA2 forward fp32 TFLOP/s (config 1: [1, 8, 512, 64], non-causal)"
+    elif rope:
+        B, H, N, d, causal, dt = 4, 32, 4096, 128, True, torch.bfloat16
+        name = "fa2_prefill_rope_config2"
+        metric = ("FA2 prefill with RoPE on Q and K, attention TFLOP/s (config 2: bf16 causal "
+                  "[4, 32, 4096, 128])")
     else:
         B, H, N, d, causal, dt = 4, 32, 4096, 128, True, torch.bfloat16
         name = "fa2_prefill_config2"
@@ -782,9 +790,19 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
             for _ in range(nsets)]
     outs = [torch.empty_like(sets[0][0]) for _ in range(nsets)]
     q, k, v = sets[0]
+    tabs, krot = None, None
+    if rope:
+        # cos / sin [N, d/2] of angle p * 10000^(-2i/d), made on the device
+        inv = 10000.0 ** (-2.0 * torch.arange(d // 2, dtype=torch.float64, device=dev) / d)
+        ang = torch.arange(N, dtype=torch.float64, device=dev)[:, None] * inv[None, :]
+        tabs = (torch.cos(ang).float().contiguous(), torch.sin(ang).float().contiguous())
+        krot = [torch.empty_like(sets[0][1]) for _ in range(nsets)]
 
     def call(i):
         qq, kk, vv = sets[i % nsets]
+        if rope:
+            return flash_engine.flash_attention(qq, kk, vv, causal, out=outs[i % nsets],
+                                                rope=tabs, k_rotated=krot[i % nsets])
         return flash_engine.flash_attention(qq, kk, vv, causal, out=outs[i % nsets])
 
     # config 1 (fp32) runs for about as long as the host takes to issue one call, so its
@@ -839,7 +857,9 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
 
     def e2e_step(i):
         stage_d.copy_(stage_h, non_blocking=True)
-        o_h.copy_(flash_engine.flash_attention(qd, kd, vd, causal), non_blocking=True)
+        o = (flash_engine.flash_attention(qd, kd, vd, causal, rope=tabs) if rope
+             else flash_engine.flash_attention(qd, kd, vd, causal))
+        o_h.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     e2e_step(0)
@@ -865,10 +885,16 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
             err = 0.0
             for b, h in pairs:
                 sl = (slice(b, b + 1), slice(h, h + 1))
-                ref = O.flash_attention(q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy(),
-                                        v[sl].float().cpu().numpy(), causal)
+                qs, ks = q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy()
+                if rope:
+                    cs, sn = (t.cpu().numpy() for t in tabs)
+                    qs = O.bf16_round(O.rope_rotate(qs, cs, sn, np.arange(N)).astype(np.float32))
+                    ks = O.bf16_round(O.rope_rotate(ks, cs, sn, np.arange(N)).astype(np.float32))
+                ref = O.flash_attention(qs, ks, v[sl].float().cpu().numpy(), causal)
                 err = max(err, _err(o[sl].float().cpu().numpy(), ref, rel=False))
             smp = "2 seeded (batch, head) slices of each rank, all 4096 rows"
+            if rope:
+                smp += ", Q and K rotated by the oracle's RoPE"
         parity = _parity(err, FP32_RTOL if fp32 else BF16_ATOL, "rel" if fp32 else "abs",
                          smp + ", vs the CPU oracle", ws, dev)
 
@@ -877,7 +903,7 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
     # half the bf16 rate): its ceiling in fp32 FLOP/s is the bf16 peak / 6.
     pk, pk_sus, pk_nom = ((peak / 6, peak_sus / 6, NOMINAL_BF16_TFLOPS / 6) if fp32
                           else (peak, peak_sus, NOMINAL_BF16_TFLOPS))
-    tfile = None if fp32 or ws > 1 else "fa_prefill_config2_traffic.json"
+    tfile = None if fp32 or rope or ws > 1 else "fa_prefill_config2_traffic.json"
     traffic, tsrc = _traffic(tfile) if tfile else (None, None)
     roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(pk, 1),
             "unit": "TFLOP/s", "frac": round(achieved / pk, 4),
@@ -886,7 +912,9 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
             "peak_source": src + (" bf16 burst / 6: TF32 runs at half the bf16 rate "
                                   "and each fp32 product takes 3 TF32 products"
                                   if fp32 else " bf16 burst"),
-            "kernel": "fa_tf32_kernel (3xTF32 tcgen05)" if fp32 else "fa_prefill_kernel",
+            "kernel": ("fa_tf32_kernel (3xTF32 tcgen05)" if fp32 else
+                       "rope_row_kernel + fa_prefill_kernel (step time; FLOPs of the attention)"
+                       if rope else "fa_prefill_kernel"),
             "traffic": traffic}
     if tsrc:
         roof["traffic_source"] = tsrc
@@ -904,7 +932,7 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False):
                    "steps_per_graph": GSTEPS},
         "roofline": roof,
         "clocks": sampler.summary(t0, t1),
-        "gpu_launches": steps,
+        "gpu_launches": steps * (2 if rope else 1),
     }
     if parity:
         res["parity"] = parity
@@ -962,15 +990,22 @@ def cpu_baseline(name, a, budget_s):
                 "kind": "port",
                 "sample": f"one (sequence, KV head) of config 4 ({tok} tokens, {H // Hkv} query "
                           f"heads) per pass, {done} passes of {dt:.2f} s; bytes counted as bf16"}
-    if name in ("prefill", "prefill_fp32"):
+    if name in ("prefill", "prefill_fp32", "prefill_rope"):
         fp32 = name == "prefill_fp32"
+        rope = name == "prefill_rope"
         B, H, N, d, causal = (1, 8, 512, 64, False) if fp32 else (4, 32, 4096, 128, True)
         rng = np.random.default_rng(a.seed)
         q, k, v = (rng.standard_normal((1, 1, N, d), dtype=np.float32) for _ in range(3))
+        cs, sn = O.rope_tables(N, d) if rope else (None, None)
         t = time.perf_counter()
         done = 0
         while True:
-            O.flash_attention(q, k, v, causal)
+            if rope:  # the reference's fused RoPE on Q and K, then the attention
+                pos = np.arange(N)
+                O.flash_attention(O.rope_rotate(q, cs, sn, pos), O.rope_rotate(k, cs, sn, pos),
+                                  v, causal)
+            else:
+                O.flash_attention(q, k, v, causal)
             done += 1
             if time.perf_counter() - t > budget_s or done >= (8 if fp32 else 4):
                 break
@@ -978,7 +1013,8 @@ def cpu_baseline(name, a, budget_s):
         f = prefill_flops(1, 1, N, d, causal)
         return {"value": round(f / dt / 1e12, 6), "unit": "TFLOP/s", "cores": _cpu_threads(),
                 "kind": "port",
-                "sample": f"one (batch, head) slice [{N}, {d}] of the config per pass "
+                "sample": f"one (batch, head) slice [{N}, {d}] of the config per pass"
+                          f"{' (RoPE of Q and K included)' if rope else ''} "
                           f"({done} passes of {dt * 1e3:.1f} ms), FLOPs counted as on the GPU"}
     raise ValueError(name)
 
@@ -1038,6 +1074,8 @@ def run_workload(name, a, ws, rank, local, primary):
         return bench_splitkv(a, ws, rank, local, steps, warmup)
     if name == "prefill":
         return bench_prefill(a, ws, rank, local, steps, warmup)
+    if name == "prefill_rope":
+        return bench_prefill(a, ws, rank, local, steps, warmup, rope=True)
     return bench_prefill(a, ws, rank, local, steps, warmup, fp32=True)
 
 
