@@ -855,30 +855,58 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False, rope=False):
     achieved = rank_flops / (ms_rank * 1e-3) / 1e12
 
     # End to end through the public API: Q, K, V from pinned host memory (one packed
-    # copy) and O back, every step (the host link, not the kernel, bounds this number).
+    # copy) and O back, every step. Two buffer sets and three streams: the input copy
+    # of step k runs on its own stream, the call on the current one once that copy is in,
+    # and the output copy on a third once the call is done; the host issues step k once
+    # step k - 2 has reached the host, so step k's input copy overlaps the output copy
+    # of step k - 1 (the host link carries both directions at once) and the calls.
     elt = 4 if fp32 else 2
     nb = q.numel() * elt
     stage_h = torch.empty(3 * nb, dtype=torch.uint8).pin_memory()
     for j, x in enumerate((q, k, v)):
         stage_h[j * nb:(j + 1) * nb].copy_(x.cpu().view(-1).view(torch.uint8))
-    stage_d = torch.empty_like(stage_h, device=dev)
-    qd, kd, vd = (stage_d[j * nb:(j + 1) * nb].view(dt).view(q.shape) for j in range(3))
-    o_h = torch.empty(q.shape, dtype=dt).pin_memory()
+    NB = 2
+    stage_d = [torch.empty_like(stage_h, device=dev) for _ in range(NB)]
+    views = [tuple(sd[j * nb:(j + 1) * nb].view(dt).view(q.shape) for j in range(3))
+             for sd in stage_d]
+    o_d = [torch.empty_like(q) for _ in range(NB)]
+    o_h = [torch.empty(q.shape, dtype=dt).pin_memory() for _ in range(NB)]
+    main = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in, ev_call, done = ([torch.cuda.Event() for _ in range(NB)] for _ in range(3))
 
     def e2e_step(i):
-        stage_d.copy_(stage_h, non_blocking=True)
-        o = (flash_engine.flash_attention(qd, kd, vd, causal, rope=tabs) if rope
-             else flash_engine.flash_attention(qd, kd, vd, causal))
-        o_h.copy_(o, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        b = i % NB
+        done[b].synchronize()  # step i - 2 is on the host: buffer set b is free
+        with torch.cuda.stream(s_in):
+            stage_d[b].copy_(stage_h, non_blocking=True)
+            ev_in[b].record(s_in)
+        main.wait_event(ev_in[b])
+        qd, kd, vd = views[b]
+        if rope:
+            flash_engine.flash_attention(qd, kd, vd, causal, out=o_d[b], rope=tabs)
+        else:
+            flash_engine.flash_attention(qd, kd, vd, causal, out=o_d[b])
+        ev_call[b].record(main)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_call[b])
+            o_h[b].copy_(o_d[b], non_blocking=True)
+            done[b].record(s_out)
+
+    def e2e_drain():
+        for st in (s_in, main, s_out):
+            st.synchronize()
 
     e2e_step(0)
+    e2e_drain()
     _barrier(ws, dev)
     n_e2e = max(1, min(steps, 5 if not fp32 else 100))
     te0 = time.perf_counter()
     for i in range(n_e2e):
         e2e_step(i)
+    e2e_drain()
     e2e_ms = _max_over_ranks((time.perf_counter() - te0) * 1e3 / n_e2e, ws, dev)
+    assert torch.equal(o_h[(n_e2e - 1) % NB].to(dev), o_d[(n_e2e - 1) % NB])
 
     parity = None
     if not a.no_parity:
@@ -934,7 +962,9 @@ def bench_prefill(a, ws, rank, local, steps, warmup, fp32=False, rope=False):
         "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": int(3 * nb), "d2h_bytes_per_step": int(nb),
-                "mode": "one packed H2D copy of Q, K, V, the call, one D2H copy of O"},
+                "mode": "per step one packed H2D copy of Q, K, V, the call and one D2H copy "
+                        "of O, each on its own stream; two buffer sets, the host issues step "
+                        "k once step k - 2 is on the host"},
         "config": {"workload": name, "batch": B, "heads": H, "seq_len": N, "head_dim": d,
                    "causal": causal, "parallelism": f"head shard x{ws}",
                    "flops_per_step": total,
