@@ -314,7 +314,10 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 9) {
     // ========================================================= MMA issuer
-    if (lane == 0 && nmax > 0) {
+    // The whole warp runs the issue loop and its waits, so its state stays warp-uniform;
+    // one elected lane issues the MMAs and commits.
+    if (nmax > 0) {
+      const bool leader = elect_one();
       constexpr uint32_t idesc_qk = tc::idesc_f16(kBF16, BM, BN, false, false);
       constexpr uint32_t idesc_pv = tc::idesc_f16(kBF16, BM, D, false, true);
       const uint32_t sbase = smem_u32(smem);
@@ -324,10 +327,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-          tc::mma_ss(tmem + t * BN, tc::smem_desc_sw128(qa + off, 16, 1024),
-                     tc::smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+          if (leader)
+            tc::mma_ss(tmem + t * BN, tc::smem_desc_sw128(qa + off, 16, 1024),
+                       tc::smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
         }
-        tc::commit(&s_full[t]);
+        if (leader) tc::commit(&s_full[t]);
       };
       // P V in kPChunks pieces: each starts as soon as the softmax has stored that
       // chunk of P (p_part), while it computes the next ones (the last: p_full).
@@ -339,44 +343,49 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int k2 = 0; k2 < KK; ++k2) {
           const int kk = c * KK + k2;
-          tc::mma_ts(otm, ptm + kk * 8, tc::smem_desc_sw128(vb + kk * 16 * 128, HALF, 1024),
-                     idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          if (leader)
+            tc::mma_ts(otm, ptm + kk * 8, tc::smem_desc_sw128(vb + kk * 16 * 128, HALF, 1024),
+                       idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        if (c == kPChunks - 1) tc::commit(&o_done[t]);
+        if (c == kPChunks - 1 && leader) tc::commit(&o_done[t]);
       };
       auto issue_pv = [&](int t, int j) -> bool {
 #pragma unroll
         for (int c = 0; c < kPChunks; ++c) {
           uint64_t* bar = c < kPChunks - 1 ? &p_part[c * 2 + t] : &p_full[t];
-          if (!mbar_wait(bar, j & 1)) return false;
+          if (!__all_sync(0xffffffffu, mbar_wait(bar, j & 1))) return false;
           tc::fence_after_sync();
           issue_pv_part(t, j, c);
         }
         return true;
       };
       // prologue: S0(0) as soon as Q0 and K_0 are in, then S1(0) once Q1 is
-      bool ok = (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0);
+      bool ok = __all_sync(0xffffffffu,
+                           (nkv[0] == 0 || mbar_wait(q_full, 0)) && mbar_wait(&k_full[0], 0));
       if (ok && nkv[0] > 0) {
         tc::fence_after_sync();
         issue_s(0, 0);
       }
       if (ok && nkv[1] > 0) {
-        ok = mbar_wait(q_full1, 0);
+        ok = __all_sync(0xffffffffu, mbar_wait(q_full1, 0));
         if (ok) {
           tc::fence_after_sync();
           issue_s(1, 0);
         }
       }
-      if (ok) tc::commit(&k_empty[0]);
+      if (ok && leader) tc::commit(&k_empty[0]);
       for (int j = 0; j < nmax && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (j >> 1) & 1))) { ok = false; break; }
         const bool next_k = j + 1 < nmax;
         bool k_ready = false;
         if (j < nkv[0]) {
           if (!issue_pv(0, j)) { ok = false; break; }
           if (j + 1 < nkv[0]) {
-            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) {
+              ok = false;
+              break;
+            }
             k_ready = true;
             issue_s(0, j + 1);
           }
@@ -384,20 +393,28 @@ __global__ void __launch_bounds__(384, 1)
         if (j < nkv[1]) {
           if (!issue_pv(1, j)) { ok = false; break; }
           if (j + 1 < nkv[1]) {
-            if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
+            if (!k_ready &&
+                !__all_sync(0xffffffffu, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) {
+              ok = false;
+              break;
+            }
             k_ready = true;
             issue_s(1, j + 1);
           }
         }
         if (next_k) {
-          if (!k_ready && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) { ok = false; break; }
-          tc::commit(&k_empty[(j + 1) & 1]);
+          if (!k_ready &&
+              !__all_sync(0xffffffffu, mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) {
+            ok = false;
+            break;
+          }
+          if (leader) tc::commit(&k_empty[(j + 1) & 1]);
         }
-        tc::commit(&v_empty[st]);
+        if (leader) tc::commit(&v_empty[st]);
       }
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
-      // Drain: all MMAs issued by this thread have completed.
-      tc::commit(drain);
+      if (!ok && leader) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: all MMAs issued by the leader have completed.
+      if (leader) tc::commit(drain);
       mbar_wait(drain, 0);
     }
    }

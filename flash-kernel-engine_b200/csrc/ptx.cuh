@@ -149,6 +149,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// True in one lane of the warp (elect.sync over all 32 lanes, which must all be active).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA / tensor core) accesses of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {
