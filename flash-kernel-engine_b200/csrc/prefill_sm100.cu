@@ -12,7 +12,7 @@
 //  * warp 8 (TMA): loads Q0/Q1 once, then K_j and V_j tiles (128 keys x d) into
 //    two-stage rings with 3-D TMA (128-byte swizzle; out-of-range rows zero-fill).
 //  * warp 9 (MMA): allocates 512 tensor-memory columns
-//    [S0 | S1 | O0 | O1] and, from one thread, issues
+//    [S0 | S1 | O0 | O1] and, from one elected lane of the warp-wide loop, issues
 //      S_t = Q_t K_j^T   (tcgen05.mma, A and B from shared memory)
 //      O_t += P_t V_j    (tcgen05.mma, A = P_t from tensor memory, B = V_j)
 //    in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ..., so the tensor

@@ -367,7 +367,10 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 5) {
     // ========================================================= MMA issuer
-    if (lane == 0 && nloc > 0) {
+    // The whole warp runs the issue loop and its waits, so its state stays warp-uniform;
+    // one elected lane issues the MMAs and commits.
+    if (nloc > 0) {
+      const bool leader = elect_one();
       constexpr uint32_t idesc_qk = tc::idesc_tf32(BM, BN, false, false);
       constexpr uint32_t idesc_pv = tc::idesc_tf32(BM, D, false, false);
       const uint32_t sbase = smem_u32(smem);
@@ -381,12 +384,13 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int kk = 0; kk < D / 8; ++kk) {
             const uint32_t koff = (kk >> 2) * C::KH + (kk & 3) * 32;
-            tc::mma_ts_tf32(tmem + C::T_S + b * BN, qa + kk * 8,
-                            tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk,
-                            (pass > 0 || kk > 0) ? 1u : 0u);
+            if (leader)
+              tc::mma_ts_tf32(tmem + C::T_S + b * BN, qa + kk * 8,
+                              tc::smem_desc_sw128(kb + koff, 16, 1024), idesc_qk,
+                              (pass > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        tc::commit(&s_full[b]);
+        if (leader) tc::commit(&s_full[b]);
       };
       auto issue_pv = [&](int it) {
         const int b = it & 1;
@@ -397,40 +401,50 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t vb = vbase + (pass == 1 ? C::V_LO : C::V_HI);
 #pragma unroll
           for (int kk = 0; kk < BN / 8; ++kk)
-            tc::mma_ts_tf32(tmem + C::T_O, pa + kk * 8,
-                            tc::smem_desc_sw128(vb + (kk >> 2) * C::VTH + (kk & 3) * 32, 16, 1024),
-                            idesc_pv, (it > 0 || pass > 0 || kk > 0) ? 1u : 0u);
+            if (leader)
+              tc::mma_ts_tf32(tmem + C::T_O, pa + kk * 8,
+                              tc::smem_desc_sw128(vb + (kk >> 2) * C::VTH + (kk & 3) * 32, 16,
+                                                  1024),
+                              idesc_pv, (it > 0 || pass > 0 || kk > 0) ? 1u : 0u);
         }
-        tc::commit(&o_done[b]);
-        tc::commit(&kv_empty[b]);
+        if (leader) {
+          tc::commit(&o_done[b]);
+          tc::commit(&kv_empty[b]);
+        }
       };
       // S_{it+1} goes in before P_it V_it, so the tensor core computes it while the
       // softmax of tile it runs. MMAs from this thread execute in issue order, so
       // S_{it+2} overwrites P_it only after P_it V_it has read it.
-      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_ready[0], 0);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(q_ready, 0) && mbar_wait(&k_ready[0], 0));
       if (ok) {
         tc::fence_after_sync();
         issue_s(0);
       }
       for (int it = 0; it < nloc && ok; ++it) {
         if (it + 1 < nloc) {
-          if (!mbar_wait(&k_ready[(it + 1) & 1], ((it + 1) >> 1) & 1)) { ok = false; break; }
+          if (!__all_sync(0xffffffffu, mbar_wait(&k_ready[(it + 1) & 1], ((it + 1) >> 1) & 1))) {
+            ok = false;
+            break;
+          }
           tc::fence_after_sync();
           issue_s(it + 1);
-          if (it == 0) FE_TTL(19, globaltimer_ns());
+          if (it == 0 && leader) FE_TTL(19, globaltimer_ns());
         }
-        if (!mbar_wait(&p_full[it & 1], (it >> 1) & 1) ||
-            !mbar_wait(&v_ready[it & 1], (it >> 1) & 1)) { ok = false; break; }
-        if (it < 2) FE_TTL(15 + 2 * it, globaltimer_ns());
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_full[it & 1], (it >> 1) & 1) &&
+                                         mbar_wait(&v_ready[it & 1], (it >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        if (it < 2 && leader) FE_TTL(15 + 2 * it, globaltimer_ns());
         tc::fence_after_sync();
         issue_pv(it);
-        if (it < 2) FE_TTL(16 + 2 * it, globaltimer_ns());
+        if (it < 2 && leader) FE_TTL(16 + 2 * it, globaltimer_ns());
       }
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
-      // Drain: all MMAs issued by this thread have completed.
-      tc::commit(drain);
+      if (!ok && leader) atomicOr(p.err, kErrWaitTimeout);
+      // Drain: all MMAs issued by the leader have completed.
+      if (leader) tc::commit(drain);
       mbar_wait(drain, 0);
-      FE_TTL(22, globaltimer_ns());
+      if (leader) FE_TTL(22, globaltimer_ns());
     }
   } else if (warp >= 6) {
     // ========================================================= hi / lo split
