@@ -651,6 +651,7 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
     };
     int gi = 0;
     bool ok = true;
+    const bool leader = elect_one();
     Seg cur;
     bool have = it.next(cur);
     int base = 0;
@@ -673,14 +674,14 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
       for (int k = 0; k < cnt; ++k) {
         const int ph = __shfl_sync(0xffffffffu, ph_cur, k);
         const int vd = __shfl_sync(0xffffffffu, vd_cur, k);
-        int good = 1;
-        if (lane == 0) {
-          const SO so(gi);
-          const int s = so.s;
-          if (so.round > 0 && !mbar_wait(&empty[s], (so.round - 1) & 1)) {
-            atomicOr(p.err, kErrWaitTimeout);
-            good = 0;
-          } else {
+        // the whole warp waits for the slot; the elected lane issues its copies
+        const SO so(gi);
+        const int s = so.s;
+        int good = so.round == 0 ||
+                   __all_sync(0xffffffffu, mbar_wait(&empty[s], (so.round - 1) & 1));
+        if (!good && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+        if (good && leader) {
+          {
             stage_valid[s] = vd;
             uint8_t* ks = smem + s * STAGE;
             uint8_t* vs = ks + TILE;
@@ -710,7 +711,6 @@ __global__ void __maxnreg__((DecodeRegs<T, NT>::value))
             }
           }
         }
-        good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) {
           ok = false;
           break;
