@@ -33,7 +33,9 @@
 //    Hkv, d, 16]): one contiguous bulk copy per page of K and of V; that layout is
 //    already conflict-free for ldmatrix (K chunks of 8 tokens are 128 contiguous
 //    bytes, V is stored as V^T rows). L2 evict-first; single-CTA destinations.
-//    Block-table entries are fetched 32 at a time, one 32-page group ahead.
+//    Block-table entries are fetched 32 at a time, one 32-page group ahead. The
+//    whole warp runs the loop and waits for each ring slot; one elected lane issues
+//    the copies.
 //  * NCW consumer warps, each with a private ring of DEPTH stages (page gi of the
 //    CTA belongs to warp gi % NCW). Per 16 tokens a warp computes S^T = K Q^T with
 //    mma.m16n8k16 (tokens x query heads: all G query heads of the group share
